@@ -1,0 +1,453 @@
+"""Benchmark: Qwen3-8B-shaped W4A16 MTP verify step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload per GPU (independent replicas, weak scaling): 32 sequences with 8192-token
+synthetic prompts, MTP depth k=2 -> 96 verify rows per step, page size 16,
+random-init Qwen3-8B-shaped weights (hidden 4096, 36 layers, 32 Q / 8 KV heads,
+head_dim 128, SwiGLU 12288, vocab 151936), W4A16 group-128 for every linear incl.
+the tied LM head.  The prompts' K/V pages are filled with seeded random values
+(prefill is not part of the verify path); drafts are seeded random token ids.
+
+A step = one verify pass: embedding, 36 decoder layers over the 96 rows (fused
+QKV / O / gate-up / down W4 linears, QK-norm + RoPE + KV append, paged attention
+over ~8.2K keys per sequence), final norm, LM head, row argmax, greedy accept and
+rollback.  `value` times K such steps on device-resident inputs with CUDA events
+(max over ranks); `e2e` times K steps of the public engine call
+MTPVerifyEngine.verify_step with host drafts in, host accept results out.
+
+--impl reference times the reference's own CPU kernels (oracle/_ref/libecpu.so,
+built from the reference sources) on a bounded sample of the same workload on the
+host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "verified tok/s/GPU, Qwen3-8B W4A16 MTP verify; quant-GEMM HBM GB/s vs peak"
+SEQS, PROMPT, K_DRAFT, PAGE = 32, 8192, 2, 16
+GEN_HEADROOM = 512
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from pilm_b200 import bindings
+    from pilm_b200.engine import MTPVerifyEngine
+    from pilm_b200.qwen3 import QWEN3_8B, PagedKVCache, Qwen3Verifier, Qwen3Weights, attention_bytes
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    bindings.init()
+    shape = QWEN3_8B
+    seed = 1234 + rank
+    weights = Qwen3Weights.synthetic(shape, seed, dev)
+    pages_per_seq = (PROMPT + GEN_HEADROOM + PAGE - 1) // PAGE
+    num_blocks = SEQS * pages_per_seq + 1
+    kv = PagedKVCache(shape, num_blocks, dev, fill="random", seed=seed)
+    max_rows = SEQS * (K_DRAFT + 1)
+    ver = Qwen3Verifier(weights, kv, max_rows=max_rows, max_pos=PROMPT + GEN_HEADROOM + 64, device=dev)
+    eng = MTPVerifyEngine(ver, num_blocks=num_blocks, max_model_len=PROMPT + GEN_HEADROOM + 64)
+    g = torch.Generator().manual_seed(seed)
+    for _ in range(SEQS):
+        sid = eng.add_request(torch.randint(0, shape.vocab, (PROMPT,), generator=g).tolist(),
+                              max_new_tokens=GEN_HEADROOM)
+        eng.admit_prefilled(sid)
+    # state after prefill: the first generated token is pending (verify row 0) at
+    # position 8192, the first slot of a fresh page, so k=2 drafts fit (engine.py:399-401)
+    for s in eng.sched.running:
+        t = int(torch.randint(0, shape.vocab, (1,), generator=g))
+        s.tokens.append(t)
+        s.outputs.append(t)
+
+    def drafts_for_step():
+        return {s.seq_id: torch.randint(0, shape.vocab, (K_DRAFT,), generator=g).tolist() for s in eng.sched.running}
+
+    # ---- device-resident verify step (value) -------------------------------------
+    seqs = list(eng.sched.running)
+    d0 = drafts_for_step()
+    for s in seqs:
+        s.tokens.extend(d0[s.seq_id])
+        eng.pages.allocate(s, 1 + K_DRAFT, eng.max_pages)
+    starts = [s.num_computed for s in seqs]
+    batch = eng.build_batch(seqs, starts, [1 + K_DRAFT] * len(seqs))
+    i32 = dict(dtype=torch.int32, device=dev)
+    acc = torch.empty(len(seqs), **i32)
+    nxt = torch.empty(len(seqs), **i32)
+    ctx_work = batch.context_lens.clone()
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ctx_work.copy_(batch.context_lens, non_blocking=True)
+        ver.verify_greedy(batch, acc, nxt, ctx_work)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ver.op_timing = True  # per-kernel CUDA events around attention / linears during the timed steps
+    ver.op_events.clear()
+    sampler = ClockSampler(local_rank)
+    if world > 1:
+        dist.barrier()
+    sampler.start()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ver.op_timing = False
+    ms = e0.elapsed_time(e1) / args.steps
+    op_ms = ver.collect_op_times()
+    rows_per_step = batch.total_q
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # ---- end to end through the engine API (e2e) -----------------------------------
+    for s in seqs:  # undo the resident step's draft rows
+        del s.tokens[s.num_computed + 1:]
+    h2d = 0
+    for _ in range(max(1, args.warmup)):
+        eng.verify_step(drafts_for_step())
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_rows = 0
+    t0 = time.perf_counter()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        rows_before = eng.stats["verified_rows"]
+        eng.verify_step(drafts_for_step())
+        e2e_rows += eng.stats["verified_rows"] - rows_before
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
+    wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    e2e_t = torch.tensor([e2e_ms, e2e_rows], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t[:1], op=dist.ReduceOp.MAX)
+        rows_all = torch.tensor([float(e2e_rows)], dtype=torch.float64, device=dev)
+        dist.all_reduce(rows_all, op=dist.ReduceOp.SUM)
+        e2e_rows_all = float(rows_all.item())
+    else:
+        e2e_rows_all = float(e2e_rows)
+    e2e_ms_max = float(e2e_t[0].item())
+    maxp = max(len(s.pages) for s in eng.sched.running)
+    h2d = 4 * (3 * rows_per_step + SEQS * maxp + 2 * SEQS + 1) + 0
+    d2h = 4 * 2 * SEQS
+
+    if rank != 0:
+        return None
+
+    # ---- roofline of the dominant kernel (paged attention) -------------------------
+    pk = peaks()
+    ctx = batch.context_lens.tolist()
+    att_bytes = attention_bytes(shape, ctx, [1 + K_DRAFT] * SEQS)
+    att_ms = op_ms.get("attention")
+    att_gbs = att_bytes / (att_ms * 1e-3) / 1e9 if att_ms else None
+    lin_bytes = weights.linear_bytes
+    lin_ms = op_ms.get("linear_total")
+    lin_gbs = lin_bytes / (lin_ms * 1e-3) / 1e9 if lin_ms else None
+    step_bytes = att_bytes * shape.layers + lin_bytes + 2 * rows_per_step * shape.hidden * 2
+    profile = ROOT / "profiles" / "attn_traffic.json"
+    traffic = None
+    if profile.exists():
+        try:
+            traffic = json.loads(profile.read_text()).get("bytes_per_launch_scaled")
+        except Exception:
+            traffic = None
+    cpu = cpu_baseline_sample(args) if not args.no_cpu else None
+    value = rows_per_step * world / (ms_max * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "verified tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations x int4 weights, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights, random prompt KV pages, random drafts)",
+        "config": {
+            "workload": "Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])",
+            "seqs_per_gpu": SEQS, "prompt_len": PROMPT, "draft_k": K_DRAFT, "rows_per_step": rows_per_step,
+            "page_size": PAGE, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (about 40 GB KV + 4 GB weights read per step)",
+        },
+        "per_gpu": round(value / world, 2),
+        "e2e": {
+            "value": round(e2e_rows_all / (e2e_ms_max * 1e-3), 2),
+            "unit": "verified tok/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(e2e_ms_max, 4),
+            "host_wall_ms_per_step": round(wall_ms, 4),
+            "call": "pilm_b200.engine.MTPVerifyEngine.verify_step (host drafts -> host accept results)",
+        },
+        "roofline": {
+            "kernel": "attn_verify (+ merge), per layer",
+            "bound": "hbm",
+            "achieved": round(att_gbs, 1) if att_gbs else None,
+            "peak": pk["hbm_gbs"],
+            "peak_source": pk["source"],
+            "unit": "GB/s",
+            "frac": round(att_gbs / pk["hbm_gbs"], 4) if att_gbs else None,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": att_bytes,
+            "avg_launch_ms": round(att_ms, 5) if att_ms else None,
+        },
+        "quant_gemm": {
+            "bytes_per_step": lin_bytes,
+            "ms_per_step": round(lin_ms, 4) if lin_ms else None,
+            "achieved_gbs": round(lin_gbs, 1) if lin_gbs else None,
+            "frac_of_peak": round(lin_gbs / pk["hbm_gbs"], 4) if lin_gbs else None,
+            "rows": rows_per_step,
+        },
+        "step_roofline": {
+            "algorithmic_bytes": step_bytes,
+            "achieved_gbs": round(step_bytes / (ms_max * 1e-3) / 1e9, 1),
+            "frac": round(step_bytes / (ms_max * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+        },
+        "op_ms_per_step": {k: round(v, 4) for k, v in op_ms.items()},
+        "gpu_launches": ver.launches_per_step() * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "acceptance": {"attempts": eng.stats["attempts"], "accepts": eng.stats["accepts"]},
+    }
+    return line
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the reference's own C kernels on the host cores
+# ---------------------------------------------------------------------------------------
+
+def _ref_linear_ms(lib, M, N, K, threads_note) -> float:
+    import numpy as np
+    from oracle import reflib
+    rng = np.random.default_rng(N + K)
+    x = rng.integers(0, 65535, (M, K), dtype=np.uint16) & 0x3FFF | 0x3C00  # finite bf16 values
+    qw = rng.integers(0, 256, (N, (K + 1) // 2), dtype=np.uint8)
+    s = (rng.random((N, (K + 127) // 128), dtype=np.float32) * 0.01).astype(np.float32)
+    out = np.empty((M, N), np.uint16)
+    d = reflib.LinearDesc(M, N, K)
+    t0 = time.perf_counter()
+    rc = lib.ekernel_linear_w4a16g128_bf16(ctypes.byref(d), x.ctypes.data, qw.ctypes.data, s.ctypes.data,
+                                           out.ctypes.data, 1)
+    assert rc == 0
+    return (time.perf_counter() - t0) * 1e3
+
+
+def cpu_baseline_sample(args) -> dict | None:
+    """Bounded sample: one Qwen3-8B decoder layer's five W4 g128 linears and the LM head
+    at M = 96 verify rows through the reference's ekernel_linear_w4a16g128_bf16
+    (oracle/_ref/libecpu.so, OpenMP over all host threads), plus one layer of the
+    reference attention arithmetic (torch, oracle restatement) for the 32 sequences;
+    extrapolated to 36 layers + head."""
+    from oracle import reflib
+    if not reflib.available():
+        return None
+    import torch
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    torch.set_num_threads(threads)
+    lib = reflib.lib()
+    M = SEQS * (K_DRAFT + 1)
+    H, I, V = 4096, 12288, 151936
+    t_layer = 0.0
+    for (N, K) in ((4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (I, H), (I, H), (H, I)):
+        t_layer += _ref_linear_ms(lib, M, N, K, threads)
+    t_head = _ref_linear_ms(lib, M, V, H, threads)
+    t_att = _cpu_attention_layer_ms()
+    step_ms = 36 * (t_layer + t_att) + t_head
+    return {
+        "value": round(M / (step_ms * 1e-3), 3),
+        "unit": "verified tok/s",
+        "cores": threads,
+        "kind": "reference",
+        "isa": reflib.isa_name(),
+        "sample": (f"1 of 36 layers (q/k/v/o/gate/up/down W4 g128 linears at M={M} through the reference "
+                   f"ekernel_linear_w4a16g128_bf16: {t_layer:.0f} ms; torch attention of the reference "
+                   f"arithmetic over 32 seqs x {PROMPT + 3} keys: {t_att:.0f} ms) + LM head ({t_head:.0f} ms), "
+                   f"extrapolated to a {step_ms / 1e3:.1f} s step"),
+    }
+
+
+def _cpu_attention_layer_ms() -> float:
+    """One layer of the reference attention arithmetic for all sequences (oracle
+    restatement of attention.py:98-139: gather, GQA expand, bf16 bmm, softmax, bmm)."""
+    import math
+    import torch
+    g = torch.Generator().manual_seed(0)
+    nkv, nh, hd, q = 8, 32, 128, K_DRAFT + 1
+    ctx = PROMPT + q
+    k = torch.randn((ctx, nkv, hd), generator=g).to(torch.bfloat16)
+    v = torch.randn((ctx, nkv, hd), generator=g).to(torch.bfloat16)
+    qs = torch.randn((q, nh, hd), generator=g).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    for _ in range(SEQS):
+        fk = k.unsqueeze(2).expand(-1, -1, nh // nkv, -1).reshape(ctx, nh, hd).transpose(0, 1)
+        fv = v.unsqueeze(2).expand(-1, -1, nh // nkv, -1).reshape(ctx, nh, hd).transpose(0, 1)
+        s = torch.bmm(qs.transpose(0, 1), fk.transpose(1, 2)) * (1.0 / math.sqrt(hd))
+        mask = torch.triu(torch.ones(q, ctx, dtype=torch.bool), diagonal=ctx - q + 1)
+        s = s.masked_fill(mask.unsqueeze(0), float("-inf"))
+        a = torch.softmax(s.to(torch.float32), dim=-1).to(torch.bfloat16)
+        torch.bmm(a, fv)
+    return (time.perf_counter() - t0) * 1e3
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    from oracle import reflib
+    if not reflib.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libecpu.so was not built (reference sources absent)"}
+    samples = []
+    cpu = None
+    for _ in range(max(1, args.steps)):
+        cpu = cpu_baseline_sample(args)
+        samples.append(cpu["value"])
+    value = statistics.median(samples)
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "verified tok/s",
+        "n_gpus": 0,
+        "steps": args.steps,
+        "warmup": 0,
+        "ms_per_step": round((SEQS * (K_DRAFT + 1)) / value * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations x int4 weights, fp32 accumulate (AVX2)",
+        "data": "synthetic",
+        "config": {"workload": "Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])",
+                   "seqs_per_gpu": SEQS, "prompt_len": PROMPT, "draft_k": K_DRAFT,
+                   "rows_per_step": SEQS * (K_DRAFT + 1)},
+        "cpu_baseline": dict(cpu, value=value),
+        "e2e": {"value": value, "unit": "verified tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

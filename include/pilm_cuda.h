@@ -1,0 +1,308 @@
+/*
+ * libpilm_cuda -- B200 (sm_100a) implementation of piLM's MTP speculative-verify path.
+ *
+ * C ABI, drop-in for the piLM CPU library (libecpu) on the calls the verify path
+ * makes: the same symbol names, descriptor structs and return codes as the
+ * reference headers src/ecpu/include/{ecpu_base.h, ecpu.h, device/api.h,
+ * kernel/api.h}, as bound by src/abi/bindings.py:59-233.  Differences:
+ *   - every data pointer is a DEVICE pointer (cudaMalloc / torch CUDA tensors);
+ *   - calls are enqueued on the library stream (ekernel_set_stream) and return
+ *     without waiting, unless PILM_CUDA_SYNC=1 is set, in which case each call
+ *     synchronises and reports execution errors like the synchronous reference;
+ *   - the `isa` argument is ignored, exactly as in the reference ((void)isa).
+ * Entry points after the "verify-path extensions" banner have no counterpart in
+ * the reference; each comment names the reference code whose work it takes over.
+ *
+ * Return codes (ecpu_base.h:11-16): 0 ok, -1 bad parameter, -2 out of memory,
+ * -3 device error, -4 kernel launch/execution error, -5 unsupported.
+ * ecpu_last_error() returns the message of the last failure (or NULL).
+ */
+#ifndef PILM_CUDA_H
+#define PILM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- ecpu_base.h:11-26 -------------------------------------------------------- */
+#define ECPU_OK 0
+#define ECPU_ERR_PARAM (-1)
+#define ECPU_ERR_MEM (-2)
+#define ECPU_ERR_DEVICE (-3)
+#define ECPU_ERR_KERNEL (-4)
+#define ECPU_ERR_UNSUPPORTED (-5)
+
+typedef enum {
+    ECPU_PRECISION_F32 = 0,
+    ECPU_PRECISION_F16 = 1,
+    ECPU_PRECISION_BF16 = 2,
+    ECPU_PRECISION_F8_E4M3 = 3,
+    ECPU_PRECISION_F8_E5M2 = 4,
+    ECPU_PRECISION_I8 = 5,
+    ECPU_PRECISION_I4 = 6,
+} ecpu_precision_t;
+
+/* ---- device/api.h:10-53 -------------------------------------------------------- */
+typedef enum { EDEV_ECPU = 0, EDEV_CUDA = 1, EDEV_COUNT } edevice_t;
+
+typedef enum {
+    EDEV_CAP_NONE = 0,
+    EDEV_CAP_F16 = 1 << 0,
+    EDEV_CAP_BF16 = 1 << 1,
+    EDEV_CAP_FP8 = 1 << 2,
+    EDEV_CAP_INT8_AMX = 1 << 3,
+    EDEV_CAP_AVX512 = 1 << 4,
+    EDEV_CAP_AVX2 = 1 << 5,
+    EDEV_CAP_NEON = 1 << 6,
+    EDEV_CAP_SVE = 1 << 7,
+    EDEV_CAP_NUMA = 1 << 8,
+    EDEV_CAP_UNIFIED_MEM = 1 << 9,
+} edevice_caps_t;
+
+typedef struct edevice_vtable {
+    const char *name;
+    edevice_t id;
+    uint64_t caps;
+    void *(*alloc)(size_t bytes, size_t alignment);
+    void (*free)(void *ptr);
+    void (*memcpy_h2d)(void *dst, const void *src, size_t n);
+    void (*memcpy_d2h)(void *dst, const void *src, size_t n);
+    void (*memcpy_d2d)(void *dst, const void *src, size_t n);
+    int (*synchronize)(void);
+    size_t (*mem_total)(void);
+    size_t (*mem_free)(void);
+    int (*init)(void);
+    int (*shutdown)(void);
+} edevice_vtable_t;
+
+/* device/api.h:48-53.  Slot EDEV_CUDA holds the B200 device (cudaMalloc & co.);
+ * slot EDEV_ECPU holds a host-memory device so callers that enumerate both work. */
+const edevice_vtable_t *edevice_get(edevice_t dev);
+int edevice_register(edevice_t dev, const edevice_vtable_t *vtable);
+int edevice_set_active(edevice_t dev);
+const edevice_vtable_t *edevice_active(void);
+int edevice_init_all(void);
+void edevice_shutdown_all(void);
+
+/* ---- ecpu.h:15-39 -------------------------------------------------------------- */
+typedef struct {
+    int n_threads;
+    int numa_policy;
+    int disable_amx;
+    int disable_avx512;
+    size_t eram_budget_bytes;
+    size_t kv_cache_budget_bytes;
+    edevice_t device_type;
+} ecpu_config_t;
+
+ecpu_config_t ecpu_config_default(void); /* device_type = EDEV_CUDA here */
+int ecpu_init(const ecpu_config_t *config);
+void ecpu_shutdown(void);
+int ecpu_is_initialized(void);
+const char *ecpu_version(void);
+const char *ecpu_last_error(void);
+
+/* ---- kernel/api.h:14-24 -------------------------------------------------------- */
+typedef enum {
+    EKERNEL_ISA_SCALAR = 0,
+    EKERNEL_ISA_AVX2 = 1,
+    EKERNEL_ISA_AVX512 = 2,
+    EKERNEL_ISA_AMX = 3,
+    EKERNEL_ISA_NEON = 4,
+    EKERNEL_ISA_SVE = 5,
+    EKERNEL_ISA_SM100A = 16, /* not in the reference enum: this library's target */
+} ekernel_isa_t;
+
+ekernel_isa_t ekernel_detect_isa(void);          /* always EKERNEL_ISA_SM100A */
+const char *ekernel_isa_name(ekernel_isa_t isa); /* "sm_100a" for 16 */
+
+/* ---- kernel/api.h:26-50 -------------------------------------------------------- */
+typedef struct {
+    size_t M, N, K;
+    ecpu_precision_t a_prec;
+    ecpu_precision_t b_prec;
+    ecpu_precision_t out_prec;
+    int transpose_a;
+    int transpose_b;
+} ekernel_gemm_desc_t;
+
+typedef struct {
+    size_t M, N, K;
+} ekernel_linear_w8a32_desc_t;
+
+typedef struct {
+    size_t M;
+    size_t hidden_size;
+    size_t intermediate_size;
+    size_t gate_up_in_features;
+    size_t down_in_features;
+} ekernel_w4a16_swiglu_desc_t;
+
+/* kernel/api.h:35-38 (kernels.c:396-435): F32 GEMM, C[M,N] = op(A) op(B). */
+int ekernel_gemm(const ekernel_gemm_desc_t *desc, const void *A, const void *B, void *C, ekernel_isa_t isa);
+
+/* kernel/api.h:52-57 (kernels.c:437-467): fp32 A[M,K], int8 W[N,K], fp32 scales[N],
+ * fp32 C[M,N] = (A . W_n) * s_n. */
+int ekernel_linear_w8a32(const ekernel_linear_w8a32_desc_t *desc, const float *A, const int8_t *W,
+                         const float *scales, float *C, ekernel_isa_t isa);
+
+/* kernel/api.h:59-64 (kernels.c:469-656): bf16 A, int8 W, bf16 C = rne(dot * s_n). */
+int ekernel_linear_w8a16_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const int8_t *W,
+                              const float *scales, uint16_t *C, ekernel_isa_t isa);
+
+/* kernel/api.h:66-72 (kernels.c:658-737): M=1 argmax over bf16-rounded logits, first
+ * index on ties.  out_index / out_value are HOST pointers, as in the reference. */
+int ekernel_linear_w8a16_bf16_argmax(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                     const int8_t *W, const float *scales, size_t *out_index,
+                                     float *out_value, ekernel_isa_t isa);
+
+/* kernel/api.h:107-112 (kernels.c:1002-1087): packed int4 W[N, ceil(K/2)] (even k in the
+ * low nibble), fp32 scales[N]; bf16 C = rne(dot * s_n). */
+int ekernel_linear_w4a16_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                              const float *scales, uint16_t *C, ekernel_isa_t isa);
+
+/* kernel/api.h:114-119 (kernels.c:1141-1148): group-32 scales[N, ceil(K/32)]. */
+int ekernel_linear_w4a16g32_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                                 const float *scales, uint16_t *C, ekernel_isa_t isa);
+
+/* kernel/api.h:121-126 (kernels.c:1150-1157): group-128 scales[N, ceil(K/128)];
+ * C = rne(sum_g s[n,g] * dot_g).  M < 64 runs the register-dequant tensor-core GEMV;
+ * larger M runs the tiled GEMM. */
+int ekernel_linear_w4a16g128_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                                  const float *scales, uint16_t *C, ekernel_isa_t isa);
+
+/* kernel/api.h:180-186 (kernels.c:1485-1526): rne(x * rsqrt(mean(x^2)+eps) * (w [+1])). */
+int ekernel_rmsnorm_bf16(const uint16_t *x, uint16_t *out, const uint16_t *weight, size_t rows, size_t n,
+                         float eps, int add_one);
+
+/* kernel/api.h:196-199 (kernels.c:1580-1596): out = rne(silu(g) * u), fp32 math. */
+int ekernel_swiglu_bf16(const uint16_t *gate, const uint16_t *up, uint16_t *out, size_t n);
+
+/* kernel/api.h:205-212 (kernels.c:1598-1735): gate/up rows [0,I) and [I,2I) of one packed
+ * per-row-scaled W4 tensor, bf16 activation, then the down projection.  The reference
+ * supports M=1 only; this library accepts any M. */
+int ekernel_swiglu_w4a16_bf16(const ekernel_w4a16_swiglu_desc_t *desc, const uint16_t *A,
+                              const uint8_t *gate_up_W, const float *gate_up_scales, const uint8_t *down_W,
+                              const float *down_scales, uint16_t *C, ekernel_isa_t isa);
+
+/* ============================ verify-path extensions ============================ */
+
+/* Stream control.  `stream` is a cudaStream_t (NULL = legacy default stream).  The
+ * reference has no streams: its calls are synchronous (bindings.py:59-233). */
+int ekernel_set_stream(void *stream);
+void *ekernel_get_stream(void);
+int ekernel_synchronize(void);
+
+/* Number of kernels this library has launched since it was loaded (host-side count,
+ * one per launch; used to report how many of the library's kernels ran in a region). */
+unsigned long long ekernel_launch_count(void);
+
+/* Token embedding gather: out[r,:] = table[ids[r],:] (bf16).  Takes over
+ * nn.Embedding in Qwen3Model.forward (model.py:110). */
+int ekernel_embedding_bf16(const int32_t *ids, size_t rows, const uint16_t *table, size_t vocab, size_t hidden,
+                           uint16_t *out);
+
+/* Residual add + RMSNorm with the torch-module rounding of RMSNorm / GemmaRMSNorm
+ * (layers.py:94-98, 115-119): if delta != NULL, residual = rne(residual + delta) in
+ * place (TransformerBlock.forward, model.py:66-72); then
+ * out = rne( rne(residual * rsqrt(mean(residual^2)+eps)) * w' ), w' = w or rne(w+1). */
+int ekernel_add_rmsnorm_bf16(uint16_t *residual, const uint16_t *delta, const uint16_t *weight, size_t rows,
+                             size_t n, float eps, int add_one, uint16_t *out);
+
+/* SwiGLU activation with torch bf16 semantics (layers.py:193): h = rne(rne(silu(g)) * u)
+ * where gate_up is [rows, 2*inter] with gate in columns [0,inter) and up in
+ * [inter, 2*inter); out is [rows, inter]. */
+int ekernel_silu_mul_bf16(const uint16_t *gate_up, size_t rows, size_t inter, uint16_t *out);
+
+typedef struct {
+    size_t num_seqs;           /* B */
+    size_t total_q;            /* rows = sum of per-sequence query lengths */
+    size_t max_q_len;          /* upper bound of per-sequence query length */
+    size_t n_heads;            /* query heads */
+    size_t n_kv_heads;         /* KV heads (GQA); n_heads % n_kv_heads == 0 */
+    size_t head_dim;           /* 128 */
+    size_t block_size;         /* tokens per KV page (16) */
+    size_t num_blocks;         /* pages in the pool (bounds check) */
+    size_t max_blocks_per_seq; /* row stride of block_table */
+    size_t max_context;        /* upper bound of context_lens (sizes the KV split) */
+    size_t qkv_stride;         /* elements per row of the fused projection output */
+    size_t rope_rows;          /* rows of the cos/sin tables (positions) */
+    size_t rot_dim;            /* rotary dims, even, <= head_dim */
+    float eps;                 /* RMSNorm eps for q_norm / k_norm */
+    int add_one;               /* Gemma norms: weight + 1 */
+    int output_gate;           /* Qwen3.5 gated attention: q_proj is [q_h | gate_h] per head */
+} ekernel_paged_attn_desc_t;
+
+/* QK-RMSNorm + RoPE + paged KV append for the verify rows.  qkv: [total_q, qkv_stride]
+ * bf16 rows laid out [q section | k (n_kv*hd) | v (n_kv*hd)], the q section being
+ * n_heads*hd, or n_heads*2*hd with [q_h | gate_h] per head when output_gate.
+ * positions[total_q], slot_mapping[total_q] (= page*block_size + offset).  Writes the
+ * normed, rotated queries to q_out [total_q, n_heads, hd] and the gate half (if any)
+ * to gate_out [total_q, n_heads*hd]; writes K (normed, rotated) and V into the
+ * caches [num_blocks, block_size, n_kv, hd] (physical_kv.py:30-33 layout).
+ * Takes over attention.py:79-97 and layers.py:122-176. */
+int ekernel_qk_norm_rope_kv_append(const ekernel_paged_attn_desc_t *desc, const uint16_t *qkv,
+                                   const uint16_t *q_norm_w, const uint16_t *k_norm_w, const float *rope_cos,
+                                   const float *rope_sin, const int32_t *positions, const int32_t *slot_mapping,
+                                   uint16_t *k_cache, uint16_t *v_cache, uint16_t *q_out, uint16_t *gate_out);
+
+/* Paged attention over the verify rows.  q: [total_q, n_heads, hd] (from the call
+ * above), block_table [num_seqs, max_blocks_per_seq], cu_q [num_seqs+1] row offsets,
+ * context_lens [num_seqs] (keys per sequence, including the appended rows).  Row j of
+ * sequence b sits at position context_lens[b] - q_len_b + j and sees keys <= that
+ * position (the causal triu mask of attention.py:131-134).  Scores are rounded like
+ * the reference's bf16 bmm (rne(rne(q.k) * rne_scale)), softmax in fp32, split-KV
+ * partials merged in fp32; out [total_q, n_heads*hd] bf16, multiplied by
+ * rne(sigmoid(gate)) when output_gate (attention.py:135-139). */
+int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const uint16_t *q,
+                                   const uint16_t *k_cache, const uint16_t *v_cache, const int32_t *block_table,
+                                   const int32_t *cu_q, const int32_t *context_lens, const uint16_t *gate,
+                                   uint16_t *out);
+
+typedef struct {
+    size_t num_seqs; /* B */
+    size_t total_q;  /* logit rows */
+    size_t vocab;    /* V */
+} ekernel_accept_desc_t;
+
+/* Row-wise top-2 of fp32 logits [total_q, vocab]: top1 index (first maximum, like
+ * torch.argmax), top1 value and the top1-top2 gap.  Any output may be NULL. */
+int ekernel_argmax_top2_f32(const ekernel_accept_desc_t *desc, const float *logits, int32_t *top1,
+                            float *top1_val, float *margin);
+
+/* Same over bf16 logits [total_q, vocab] (the LM-head linear's output dtype; the
+ * reference casts these bf16 values to fp32 before argmax, engine.py:480). */
+int ekernel_argmax_top2_bf16(const ekernel_accept_desc_t *desc, const uint16_t *logits, int32_t *top1,
+                             float *top1_val, float *margin);
+
+/* Greedy MTP acceptance (engine.py:479-503, 551-557) + rollback of the verify slots.
+ * verify_ids [total_q] are the rows fed to the verify forward ([last, d1..dn] per
+ * sequence), top1 [total_q] their argmax.  Per sequence: accepted = number of leading
+ * drafts d_i == top1[row i-1]; next_token = top1 of the first mismatching row (or of
+ * the bonus row); context_lens[b] (in: keys incl. all verify rows) is rolled back to
+ * start + 1 + accepted, the reference's num_computed_tokens (engine.py:505-510);
+ * rejected verify slots in slot_mapping (may be NULL) are set to -1. */
+int ekernel_verify_accept_greedy(const ekernel_accept_desc_t *desc, const int32_t *verify_ids,
+                                 const int32_t *top1, const int32_t *cu_q, int32_t *accept_counts,
+                                 int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
+
+/* Rejection-sampling acceptance (no reference implementation; standard speculative
+ * sampling with a one-hot greedy draft).  p_i = softmax(logits_i / temperature)
+ * restricted to the nucleus {j : mass of strictly more probable tokens < top_p},
+ * renormalised.  Draft d_i is accepted iff uniforms[row,0] < p_i(d_i); at the first
+ * rejection the next token is sampled (inverse CDF in index order with
+ * uniforms[row,1]) from p_i with d_i removed, else the bonus row's p_n.  Outputs and
+ * rollback as in ekernel_verify_accept_greedy. */
+int ekernel_verify_accept_rejection(const ekernel_accept_desc_t *desc, const float *logits,
+                                    const int32_t *verify_ids, const int32_t *cu_q, const float *uniforms,
+                                    float temperature, float top_p, int32_t *accept_counts,
+                                    int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PILM_CUDA_H */

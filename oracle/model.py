@@ -197,6 +197,53 @@ def apply_rope(q: torch.Tensor, k: torch.Tensor, positions: torch.Tensor, cfg: Q
     return out[0], out[1]
 
 
+def attention_from_proj(c: Qwen3Config, qp: torch.Tensor, kp: torch.Tensor, vp: torch.Tensor,
+                        q_norm_w: torch.Tensor, k_norm_w: torch.Tensor, positions: torch.Tensor,
+                        kv_k: torch.Tensor, kv_v: torch.Tensor, block_ids: list[int], is_decode: bool) -> torch.Tensor:
+    """FullAttention.forward after the projections (attention.py:79-139) for one
+    sequence's rows, with the engine's block/slot choice (engine.py:428-434): the
+    rows never cross a page.  Writes K/V into the paged caches and returns the
+    (gated) attention output [seq, n_heads*hd] before o_proj."""
+    seq = qp.shape[0]
+    if c.gated:
+        qg = qp.view(seq, c.n_heads, c.head_dim * 2)
+        qs, gate = torch.chunk(qg, 2, dim=-1)
+        gate = gate.reshape(seq, -1)
+    else:
+        qs, gate = qp.view(seq, c.n_heads, c.head_dim), None
+    qs = rms_norm(qs, q_norm_w, c.eps, c.gemma_norm)
+    ks = rms_norm(kp.view(seq, c.n_kv_heads, c.head_dim), k_norm_w, c.eps, c.gemma_norm)
+    vs = vp.view(seq, c.n_kv_heads, c.head_dim)
+    qs, ks = apply_rope(qs, ks, positions, c)
+
+    bs = c.block_size
+    start = int(positions[0])
+    block_id = block_ids[start // bs]
+    slot = start % bs
+    kv_k[block_id, slot:slot + seq] = ks
+    kv_v[block_id, slot:slot + seq] = vs
+    cache_len = int(positions[-1]) + 1
+    needed = (cache_len + bs - 1) // bs
+    full_k = torch.cat([kv_k[b] for b in block_ids[:needed]], dim=0)[:cache_len]
+    full_v = torch.cat([kv_v[b] for b in block_ids[:needed]], dim=0)[:cache_len]
+
+    rep = c.n_heads // c.n_kv_heads
+    if rep > 1:
+        full_k = full_k.unsqueeze(2).expand(-1, -1, rep, -1).reshape(full_k.shape[0], c.n_heads, c.head_dim)
+        full_v = full_v.unsqueeze(2).expand(-1, -1, rep, -1).reshape(full_v.shape[0], c.n_heads, c.head_dim)
+    qt, kt, vt = qs.transpose(0, 1), full_k.transpose(0, 1), full_v.transpose(0, 1)
+    scores = torch.bmm(qt, kt.transpose(1, 2)) * (1.0 / math.sqrt(c.head_dim))
+    if not is_decode or seq > 1:
+        kv_len = full_k.shape[0]
+        mask = torch.triu(torch.ones(seq, kv_len, dtype=torch.bool), diagonal=kv_len - seq + 1)
+        scores = scores.masked_fill(mask.unsqueeze(0), float("-inf"))
+    attn = torch.softmax(scores.to(torch.float32), dim=-1).to(vt.dtype)
+    out = torch.bmm(attn, vt).transpose(0, 1).reshape(seq, -1)
+    if gate is not None:
+        out = out * torch.sigmoid(gate)
+    return out
+
+
 class OracleModel:
     """Qwen3Model (model.py:76-127) over a paged KV cache, one sequence per call
     (the reference runs one forward per request, engine.py:416-472)."""
@@ -218,48 +265,14 @@ class OracleModel:
 
     def attention(self, li: int, x: torch.Tensor, positions: torch.Tensor, kv_k: torch.Tensor,
                   kv_v: torch.Tensor, block_ids: list[int], is_decode: bool) -> torch.Tensor:
-        """FullAttention.forward (attention.py:68-141) with the engine's block/slot choice
-        (engine.py:428-434): the tokens of one call never cross a page."""
+        """FullAttention.forward (attention.py:68-141): projections, then
+        attention_from_proj, then o_proj."""
         c = self.cfg
-        seq = x.shape[0]
         qp = qlinear(x, self.q[f"l{li}.q_proj"], c.quant)
-        if c.gated:
-            qg = qp.view(seq, c.n_heads, c.head_dim * 2)
-            qs, gate = torch.chunk(qg, 2, dim=-1)
-            gate = gate.reshape(seq, -1)
-        else:
-            qs, gate = qp.view(seq, c.n_heads, c.head_dim), None
-        qs = rms_norm(qs, self.norms[f"l{li}.q_norm"], c.eps, c.gemma_norm)
-        ks = rms_norm(qlinear(x, self.q[f"l{li}.k_proj"], c.quant).view(seq, c.n_kv_heads, c.head_dim),
-                      self.norms[f"l{li}.k_norm"], c.eps, c.gemma_norm)
-        vs = qlinear(x, self.q[f"l{li}.v_proj"], c.quant).view(seq, c.n_kv_heads, c.head_dim)
-        qs, ks = apply_rope(qs, ks, positions, c)
-
-        bs = c.block_size
-        start = int(positions[0])
-        block_id = block_ids[start // bs]
-        slot = start % bs
-        kv_k[block_id, slot:slot + seq] = ks
-        kv_v[block_id, slot:slot + seq] = vs
-        cache_len = int(positions[-1]) + 1
-        needed = (cache_len + bs - 1) // bs
-        full_k = torch.cat([kv_k[b] for b in block_ids[:needed]], dim=0)[:cache_len]
-        full_v = torch.cat([kv_v[b] for b in block_ids[:needed]], dim=0)[:cache_len]
-
-        rep = c.n_heads // c.n_kv_heads
-        if rep > 1:
-            full_k = full_k.unsqueeze(2).expand(-1, -1, rep, -1).reshape(full_k.shape[0], c.n_heads, c.head_dim)
-            full_v = full_v.unsqueeze(2).expand(-1, -1, rep, -1).reshape(full_v.shape[0], c.n_heads, c.head_dim)
-        qt, kt, vt = qs.transpose(0, 1), full_k.transpose(0, 1), full_v.transpose(0, 1)
-        scores = torch.bmm(qt, kt.transpose(1, 2)) * (1.0 / math.sqrt(c.head_dim))
-        if not is_decode or seq > 1:
-            kv_len = full_k.shape[0]
-            mask = torch.triu(torch.ones(seq, kv_len, dtype=torch.bool), diagonal=kv_len - seq + 1)
-            scores = scores.masked_fill(mask.unsqueeze(0), float("-inf"))
-        attn = torch.softmax(scores.to(torch.float32), dim=-1).to(vt.dtype)
-        out = torch.bmm(attn, vt).transpose(0, 1).reshape(seq, -1)
-        if gate is not None:
-            out = out * torch.sigmoid(gate)
+        kp = qlinear(x, self.q[f"l{li}.k_proj"], c.quant)
+        vp = qlinear(x, self.q[f"l{li}.v_proj"], c.quant)
+        out = attention_from_proj(c, qp, kp, vp, self.norms[f"l{li}.q_norm"], self.norms[f"l{li}.k_norm"],
+                                  positions, kv_k, kv_v, block_ids, is_decode)
         return qlinear(out, self.q[f"l{li}.o_proj"], c.quant)
 
     def mlp(self, li: int, x: torch.Tensor) -> torch.Tensor:

@@ -1,0 +1,351 @@
+"""torch-facing wrappers for libpilm_cuda (CUDA tensors).
+
+Mirrors the reference's src/runtime/ckernel.py: same function names, argument
+meaning, shape checks and error behaviour (``ValueError`` for bad tensors,
+``RuntimeError(f"... failed: rc={rc}")`` for a non-zero return code), but the
+tensors must live on a CUDA device instead of the CPU.  There is no CPU
+fallback: a CPU tensor is rejected and a missing library raises on import of
+the first call.
+
+Also holds the verify-path wrappers (paged attention, acceptance) and on-device
+versions of the reference weight quantizers (ckernel.py:70-161), used to build
+large synthetic checkpoints directly in HBM.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import bindings as abi
+
+
+def _stream() -> None:
+    abi.set_stream(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(name: str, t: torch.Tensor, dtype: torch.dtype, ndim: Optional[int] = None) -> torch.Tensor:
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if ndim is not None and t.ndim != ndim:
+        raise ValueError(f"{name} must be {ndim}D, got shape={tuple(t.shape)}")
+    return t.contiguous()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed: rc={rc}: {abi.last_error()}")
+
+
+# ---------------------------------------------------------------------------------------
+# Reference-mirroring kernels (ckernel.py:24-679)
+# ---------------------------------------------------------------------------------------
+
+def gemm_f32(a: torch.Tensor, b: torch.Tensor, transpose_b: bool = False) -> torch.Tensor:
+    a = _cuda("a", a, torch.float32, 2)
+    b = _cuda("b", b, torch.float32, 2)
+    m, k = a.shape
+    n, kb = (b.shape if transpose_b else (b.shape[1], b.shape[0]))
+    if kb != k:
+        raise ValueError(f"incompatible GEMM shapes: a={tuple(a.shape)} b={tuple(b.shape)} transpose_b={transpose_b}")
+    out = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    _stream()
+    _check(abi.gemm_f32_ptr(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, False, transpose_b), "ekernel_gemm")
+    return out
+
+
+def linear_w8a32(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    x = _cuda("x", x, torch.float32, 2)
+    qweight = _cuda("qweight", qweight, torch.int8, 2)
+    scales = _cuda("scales", scales, torch.float32, 1)
+    m, k = x.shape
+    n, wk = qweight.shape
+    if wk != k or scales.shape[0] != n:
+        raise ValueError(f"incompatible W8A32 shapes: x={tuple(x.shape)} qweight={tuple(qweight.shape)} "
+                         f"scales={tuple(scales.shape)}")
+    out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    _stream()
+    _check(abi.linear_w8a32_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
+           "ekernel_linear_w8a32")
+    return out
+
+
+def linear_w8a16_bf16(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    x = _cuda("x", x, torch.bfloat16, 2)
+    qweight = _cuda("qweight", qweight, torch.int8, 2)
+    scales = _cuda("scales", scales, torch.float32, 1)
+    m, k = x.shape
+    n, wk = qweight.shape
+    if wk != k or scales.shape[0] != n:
+        raise ValueError(f"incompatible W8A16 shapes: x={tuple(x.shape)} qweight={tuple(qweight.shape)} "
+                         f"scales={tuple(scales.shape)}")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _stream()
+    _check(abi.linear_w8a16_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
+           "ekernel_linear_w8a16_bf16")
+    return out
+
+
+def linear_w8a16_bf16_argmax(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor) -> int:
+    x = _cuda("x", x, torch.bfloat16).reshape(1, -1)
+    qweight = _cuda("qweight", qweight, torch.int8, 2)
+    scales = _cuda("scales", scales, torch.float32, 1)
+    _stream()
+    rc, idx, _val = abi.linear_w8a16_bf16_argmax_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), 1,
+                                                     qweight.shape[0], x.shape[1])
+    _check(rc, "ekernel_linear_w8a16_bf16_argmax")
+    return idx
+
+
+def _w4_common(x, qweight, scales, in_features, scale_ndim, groups_of):
+    x = _cuda("x", x, torch.bfloat16, 2)
+    qweight = _cuda("qweight", qweight, torch.uint8, 2)
+    scales = _cuda("scales", scales, torch.float32, scale_ndim)
+    m, k = x.shape
+    n, packed_k = qweight.shape
+    if in_features is not None and int(in_features) != k:
+        raise ValueError(f"in_features={in_features} does not match x K={k}")
+    want = (n,) if groups_of is None else (n, (k + groups_of - 1) // groups_of)
+    if packed_k != (k + 1) // 2 or tuple(scales.shape) != want:
+        raise ValueError(f"incompatible W4A16 shapes: x={tuple(x.shape)} qweight={tuple(qweight.shape)} "
+                         f"scales={tuple(scales.shape)}")
+    return x, qweight, scales, m, n, k
+
+
+def linear_w4a16_bf16(x, qweight, scales, in_features=None) -> torch.Tensor:
+    x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 1, None)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _stream()
+    _check(abi.linear_w4a16_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
+           "ekernel_linear_w4a16_bf16")
+    return out
+
+
+def linear_w4a16g32_bf16(x, qweight, scales, in_features=None) -> torch.Tensor:
+    x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 2, 32)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _stream()
+    _check(abi.linear_w4a16g32_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n,
+                                        k), "ekernel_linear_w4a16g32_bf16")
+    return out
+
+
+def linear_w4a16g128_bf16(x, qweight, scales, in_features=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 2, 128)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _stream()
+    _check(abi.linear_w4a16g128_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n,
+                                         k), "ekernel_linear_w4a16g128_bf16")
+    return out
+
+
+def swiglu_bf16(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    gate = _cuda("gate", gate, torch.bfloat16)
+    up = _cuda("up", up, torch.bfloat16)
+    if tuple(gate.shape) != tuple(up.shape):
+        raise ValueError(f"gate/up shapes differ: gate={tuple(gate.shape)} up={tuple(up.shape)}")
+    out = torch.empty_like(gate)
+    _stream()
+    _check(abi.swiglu_bf16_ptr(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel()), "ekernel_swiglu_bf16")
+    return out
+
+
+def swiglu_w4a16_bf16(x, gate_up_qweight, gate_up_scales, down_qweight, down_scales, intermediate_size,
+                      gate_up_in_features=None, down_in_features=None) -> torch.Tensor:
+    """Fused W4 SwiGLU MLP (ckernel.py:585-647); any M here (the reference: M=1)."""
+    x = _cuda("x", x, torch.bfloat16, 2)
+    gate_up_qweight = _cuda("gate_up_qweight", gate_up_qweight, torch.uint8, 2)
+    down_qweight = _cuda("down_qweight", down_qweight, torch.uint8, 2)
+    gate_up_scales = _cuda("gate_up_scales", gate_up_scales, torch.float32, 1)
+    down_scales = _cuda("down_scales", down_scales, torch.float32, 1)
+    m, k = x.shape
+    inter = int(intermediate_size)
+    gk = k if gate_up_in_features is None else int(gate_up_in_features)
+    dk = inter if down_in_features is None else int(down_in_features)
+    hidden = int(down_qweight.shape[0])
+    if gk != k:
+        raise ValueError(f"gate_up_in_features={gk} does not match x K={k}")
+    if dk != inter:
+        raise ValueError("down_in_features must equal intermediate_size")
+    if tuple(gate_up_qweight.shape) != (2 * inter, (gk + 1) // 2):
+        raise ValueError(f"gate_up_qweight shape must be {(2 * inter, (gk + 1) // 2)}, "
+                         f"got {tuple(gate_up_qweight.shape)}")
+    if down_qweight.shape[1] != (dk + 1) // 2:
+        raise ValueError(f"down_qweight packed K does not match down_in_features={dk}")
+    if gate_up_scales.shape[0] != 2 * inter or down_scales.shape[0] != hidden:
+        raise ValueError("scale shapes do not match qweight rows")
+    out = torch.empty((m, hidden), dtype=torch.bfloat16, device=x.device)
+    _stream()
+    _check(abi.swiglu_w4a16_bf16_ptr(x.data_ptr(), gate_up_qweight.data_ptr(), gate_up_scales.data_ptr(),
+                                     down_qweight.data_ptr(), down_scales.data_ptr(), out.data_ptr(), m, hidden, inter,
+                                     gk, dk), "ekernel_swiglu_w4a16_bf16")
+    return out
+
+
+def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor, eps: float, add_one: bool = False) -> torch.Tensor:
+    if x.device.type != "cuda" or x.dtype != torch.bfloat16:
+        raise ValueError("x must be a CUDA torch.bfloat16 tensor")
+    weight = _cuda("weight", weight, torch.bfloat16, 1)
+    if x.shape[-1] != weight.shape[0]:
+        raise ValueError(f"incompatible RMSNorm shapes: x={tuple(x.shape)} weight={tuple(weight.shape)}")
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    out = torch.empty_like(x2)
+    _stream()
+    _check(abi.rmsnorm_bf16_ptr(x2.data_ptr(), out.data_ptr(), weight.data_ptr(), x2.shape[0], x2.shape[1],
+                                float(eps), bool(add_one)), "ekernel_rmsnorm_bf16")
+    return out.reshape(x.shape)
+
+
+# ---------------------------------------------------------------------------------------
+# Verify-path kernels
+# ---------------------------------------------------------------------------------------
+
+def embedding_bf16(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    ids = _cuda("ids", ids, torch.int32, 1)
+    table = _cuda("table", table, torch.bfloat16, 2)
+    if out is None:
+        out = torch.empty((ids.shape[0], table.shape[1]), dtype=torch.bfloat16, device=ids.device)
+    _stream()
+    _check(abi.lib().ekernel_embedding_bf16(ids.data_ptr(), ids.shape[0], table.data_ptr(), table.shape[0],
+                                            table.shape[1], out.data_ptr()), "ekernel_embedding_bf16")
+    return out
+
+
+def add_rmsnorm_bf16(residual: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, eps: float,
+                     add_one: bool, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """residual <- rne(residual + delta) (in place); returns the module-rounded RMSNorm."""
+    if residual.device.type != "cuda" or residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+        raise ValueError("residual must be a contiguous CUDA bfloat16 tensor")
+    rows, n = residual.shape
+    if out is None:
+        out = torch.empty_like(residual)
+    _stream()
+    _check(abi.lib().ekernel_add_rmsnorm_bf16(residual.data_ptr(), delta.data_ptr() if delta is not None else None,
+                                              weight.data_ptr(), rows, n, float(eps), int(add_one), out.data_ptr()),
+           "ekernel_add_rmsnorm_bf16")
+    return out
+
+
+def silu_mul_bf16(gate_up: torch.Tensor, inter: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    gate_up = _cuda("gate_up", gate_up, torch.bfloat16, 2)
+    rows = gate_up.shape[0]
+    if out is None:
+        out = torch.empty((rows, inter), dtype=torch.bfloat16, device=gate_up.device)
+    _stream()
+    _check(abi.lib().ekernel_silu_mul_bf16(gate_up.data_ptr(), rows, inter, out.data_ptr()), "ekernel_silu_mul_bf16")
+    return out
+
+
+def attn_desc(*, num_seqs, total_q, max_q_len, n_heads, n_kv_heads, head_dim, block_size, num_blocks,
+              max_blocks_per_seq, max_context, qkv_stride, rope_rows, rot_dim, eps, add_one, output_gate):
+    return abi.PagedAttnDesc(num_seqs, total_q, max_q_len, n_heads, n_kv_heads, head_dim, block_size, num_blocks,
+                             max_blocks_per_seq, max_context, qkv_stride, rope_rows, rot_dim, float(eps),
+                             int(add_one), int(output_gate))
+
+
+def _p(t: Optional[torch.Tensor]):
+    return t.data_ptr() if t is not None else None
+
+
+def qk_norm_rope_kv_append(desc, qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, positions, slot_mapping, k_cache,
+                           v_cache, q_out, gate_out=None) -> None:
+    _stream()
+    import ctypes
+    _check(abi.lib().ekernel_qk_norm_rope_kv_append(ctypes.byref(desc), _p(qkv), _p(q_norm_w), _p(k_norm_w),
+                                                    _p(rope_cos), _p(rope_sin), _p(positions), _p(slot_mapping),
+                                                    _p(k_cache), _p(v_cache), _p(q_out), _p(gate_out)),
+           "ekernel_qk_norm_rope_kv_append")
+
+
+def paged_attention_verify(desc, q, k_cache, v_cache, block_table, cu_q, context_lens, gate, out) -> None:
+    _stream()
+    import ctypes
+    _check(abi.lib().ekernel_paged_attention_verify(ctypes.byref(desc), _p(q), _p(k_cache), _p(v_cache),
+                                                    _p(block_table), _p(cu_q), _p(context_lens), _p(gate), _p(out)),
+           "ekernel_paged_attention_verify")
+
+
+def argmax_top2(logits: torch.Tensor, top1: torch.Tensor, top1_val=None, margin=None) -> None:
+    import ctypes
+    rows, vocab = logits.shape
+    d = abi.AcceptDesc(0, rows, vocab)
+    _stream()
+    if logits.dtype == torch.float32:
+        rc = abi.lib().ekernel_argmax_top2_f32(ctypes.byref(d), logits.data_ptr(), _p(top1), _p(top1_val), _p(margin))
+    elif logits.dtype == torch.bfloat16:
+        rc = abi.lib().ekernel_argmax_top2_bf16(ctypes.byref(d), logits.data_ptr(), _p(top1), _p(top1_val), _p(margin))
+    else:
+        raise ValueError("logits must be float32 or bfloat16")
+    _check(rc, "ekernel_argmax_top2")
+
+
+def verify_accept_greedy(num_seqs, verify_ids, top1, cu_q, accept_counts, next_tokens, context_lens,
+                         slot_mapping=None) -> None:
+    import ctypes
+    d = abi.AcceptDesc(num_seqs, verify_ids.shape[0], 0)
+    _stream()
+    _check(abi.lib().ekernel_verify_accept_greedy(ctypes.byref(d), _p(verify_ids), _p(top1), _p(cu_q),
+                                                  _p(accept_counts), _p(next_tokens), _p(context_lens),
+                                                  _p(slot_mapping)), "ekernel_verify_accept_greedy")
+
+
+def verify_accept_rejection(num_seqs, logits, verify_ids, cu_q, uniforms, temperature, top_p, accept_counts,
+                            next_tokens, context_lens, slot_mapping=None) -> None:
+    import ctypes
+    logits = _cuda("logits", logits, torch.float32, 2)
+    d = abi.AcceptDesc(num_seqs, logits.shape[0], logits.shape[1])
+    _stream()
+    _check(abi.lib().ekernel_verify_accept_rejection(ctypes.byref(d), logits.data_ptr(), _p(verify_ids), _p(cu_q),
+                                                     _p(uniforms), float(temperature), float(top_p),
+                                                     _p(accept_counts), _p(next_tokens), _p(context_lens),
+                                                     _p(slot_mapping)), "ekernel_verify_accept_rejection")
+
+
+# ---------------------------------------------------------------------------------------
+# On-device quantizers (same formats as ckernel.py:70-161)
+#
+# torch on CUDA turns `tensor / python_scalar` into a multiply by the reciprocal,
+# which rounds differently from the reference's CPU division; the divisors below are
+# device tensors so every quotient is a correctly rounded division, bit-identical to
+# the reference quantizer.
+# ---------------------------------------------------------------------------------------
+
+def _c(v: float, like: torch.Tensor) -> torch.Tensor:
+    return torch.full((), v, dtype=torch.float32, device=like.device)
+
+def _pack_i4(q: torch.Tensor) -> torch.Tensor:
+    if q.shape[1] % 2:
+        q = torch.nn.functional.pad(q, (0, 1))
+    lo = torch.bitwise_and(q[:, 0::2], 0x0F).to(torch.uint8)
+    hi = torch.bitwise_left_shift(torch.bitwise_and(q[:, 1::2], 0x0F), 4).to(torch.uint8)
+    return torch.bitwise_or(lo, hi).contiguous()
+
+
+def quantize_weight_i4_grouped(w: torch.Tensor, group_size: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """quantize_weight_i4_grouped_chunked (ckernel.py:124-161) on any device."""
+    w = w.to(torch.float32)
+    rows, cols = w.shape
+    groups = (cols + group_size - 1) // group_size
+    wp = torch.nn.functional.pad(w, (0, groups * group_size - cols)) if cols % group_size else w
+    g = wp.reshape(rows, groups, group_size)
+    s = torch.clamp(g.abs().amax(dim=2) / _c(7.0, g), min=1e-8)
+    q = torch.round(g / s.unsqueeze(2)).clamp(-7, 7).to(torch.int16).reshape(rows, groups * group_size)[:, :cols]
+    return _pack_i4(q), s.contiguous()
+
+
+def quantize_weight_i4_per_row(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quantize_weight_i4_per_row_chunked (ckernel.py:98-121) on any device."""
+    w = w.to(torch.float32)
+    s = torch.clamp(w.abs().amax(dim=1) / _c(7.0, w), min=1e-8)
+    q = torch.round(w / s.unsqueeze(1)).clamp(-7, 7).to(torch.int16)
+    return _pack_i4(q), s.contiguous()
+
+
+def quantize_weight_i8_per_row(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quantize_weight_i8_per_row (ckernel.py:70-75) on any device."""
+    w = w.to(torch.float32)
+    s = torch.clamp(w.abs().amax(dim=1) / _c(127.0, w), min=1e-8)
+    return torch.round(w / s.unsqueeze(1)).clamp(-127, 127).to(torch.int8).contiguous(), s.contiguous()

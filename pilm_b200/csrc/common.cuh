@@ -1,0 +1,85 @@
+// Shared device/host helpers for libpilm_cuda (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/pilm_cuda.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "libpilm_cuda targets sm_100a (B200) only"
+#endif
+
+namespace pilm {
+
+// ---------------------------------------------------------------------------------
+// Library state (defined in runtime.cu)
+// ---------------------------------------------------------------------------------
+cudaStream_t stream();
+int sync_mode();
+int num_sms();
+void set_error(const char *fmt, ...);
+// Device scratch owned by the library, one independent buffer per slot so nested
+// calls never alias (grown on demand, never inside stream capture).
+enum ScratchSlot { kScratchSplitK = 0, kScratchAux = 1, kScratchAttn = 2, kScratchSlots = 3 };
+void *scratch(int slot, size_t bytes);
+inline void *workspace(size_t bytes) { return scratch(kScratchSplitK, bytes); }
+int *counters(size_t n);  // zero-initialised, self-resetting arrival counters
+
+// W4 GEMM for M >= 64 (tcgen05 path, linear_tc.cu); returns ECPU_ERR_UNSUPPORTED
+// when the shape is not handled there, in which case the caller uses the GEMV.
+int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N,
+                 __nv_bfloat16 *Y, bool grouped, const char *what);
+// Quantized bf16 linear (linear.cu).  qf: 0 = W4 grouped (gs 32/128), 1 = W4 per-row,
+// 2 = W8 per-row.
+int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
+                const char *what);
+
+// Post-launch check: ECPU_ERR_KERNEL on a launch error; in synchronous mode
+// (PILM_CUDA_SYNC=1) also waits for the stream and reports execution errors.
+int check_launch(const char *what);
+
+// ---------------------------------------------------------------------------------
+// bf16 helpers.  The reference rounds fp32 -> bf16 to nearest-even
+// (kernels.c:19-25); __float2bfloat16_rn is the same rounding for finite values.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+__device__ __forceinline__ float bits2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint4 ldg_v4(const void *p) {
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace pilm
+
+#define PILM_REQUIRE(cond, code, ...)      \
+    do {                                   \
+        if (!(cond)) {                     \
+            pilm::set_error(__VA_ARGS__);  \
+            return (code);                 \
+        }                                  \
+    } while (0)

@@ -1,0 +1,527 @@
+// Quantized linears: W4A16 (group-128, group-32, per-row), W8A16, W8A32, F32 GEMM.
+//
+// Reference semantics (src/ecpu/src/kernel/kernels.c):
+//   W4 g128 / g32 (linear_w4a16g_bf16_impl, :1089-1139):
+//       C[m,n] = rne_bf16( sum_g s[n,g] * sum_{k in g} bf16(A[m,k]) * q[n,k] )
+//   W4 per-row (:1002-1087), W8A16 (:469-656):  C = rne_bf16( s[n] * sum_k A q )
+//   W8A32 (:437-467):                            C = s[n] * sum_k A q     (fp32)
+// q is the signed int4 nibble (even k in the low nibble, :43-46) or int8.
+//
+// Small M (the verify regime, M = batch*(k+1) < 64) is HBM-bound: the packed
+// weights are streamed once with 128-bit loads and dequantised in registers straight
+// into tensor-core A fragments (mma.sync m16n8k16, bf16 x bf16 -> fp32); the
+// activations form the B fragments.  The k order inside each 128-wide group is
+// permuted so that every thread's 16-byte weight load holds exactly the values its
+// fragments need (see w4_gemv_mma); the activations are permuted identically, so
+// each group's fp32 partial is the exact group dot of the reference, which is then
+// scaled by s[n,g] in fp32 like the reference.  Split-K partials are reduced in a
+// fixed order by the last-arriving CTA (deterministic, no spin-waits).
+#include "common.cuh"
+
+using namespace pilm;
+
+namespace {
+
+constexpr int kGemvWarps = 8;
+
+// (nibble ^ 8) | 0x4300 in both 16-bit halves: the bf16 value 136 + q, exact.
+__device__ __forceinline__ uint32_t nib_magic(uint32_t w) {
+    uint32_t t;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(t) : "r"(w), "r"(0x000F000Fu), "r"(0x43084308u));
+    return t;
+}
+
+// Two int4 nibbles at bits [0,4) and [16,20) -> bf16x2 (q_lo, q_hi), exact.
+__device__ __forceinline__ uint32_t dq_pair(uint32_t w) {
+    uint32_t t = nib_magic(w);
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&t);
+    const __nv_bfloat162 bias = __floats2bfloat162_rn(136.0f, 136.0f);
+    v = __hsub2(v, bias);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
+    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// Register-dequant W4 GEMV on tensor cores.
+//
+// Tile: a warp owns RT row tiles of 16 output rows and NT batch tiles of 8 rows of A.
+// Lane t = 4r + c.  For a 128-wide group g, thread c loads bytes [16c, 16c+16) of the
+// group (k in [32c, 32c+32)) for its weight rows r and r+8 of every row tile: four
+// 32-bit words, word i holding k = 32c + 8i + j at nibble j.  MMA step (i, h) uses
+// nibble pairs (2h, 2h+4) as A slots {2c, 2c+1} and (2h+1, 2h+5) as slots {2c+8, 2c+9};
+// the B fragment of the same thread carries A[m, k] for exactly those k (gathered
+// with byte permutes from one 16-byte load), so every MMA slot pairs W[n,k] with
+// A[m,k] for the same k and the 8 steps of a group sum the whole group.
+template <int RT, int NT, bool GROUPED>
+__global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
+    const __nv_bfloat16 *__restrict__ X, int M, int K, const uint8_t *__restrict__ W,
+    const float *__restrict__ S, int N, __nv_bfloat16 *__restrict__ Y, float *__restrict__ ws,
+    int *__restrict__ ctr, int splits, int groups_per_split) {
+    constexpr int ROWS = 16 * RT;
+    constexpr int NACC = RT * NT * 4;
+    __shared__ float red[kGemvWarps][NACC][32];
+    __shared__ int s_last;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const int row_base = blockIdx.x * ROWS;
+    const int G = K >> 7;
+    const int g0 = blockIdx.y * groups_per_split;
+    const int g1 = min(G, g0 + groups_per_split);
+    const size_t ldw = (size_t)K >> 1;
+
+    const uint8_t *wp[RT][2];
+    bool rv[RT][2];
+    int rows[RT][2];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int row = row_base + rt * 16 + h * 8 + r;
+            rows[rt][h] = row;
+            rv[rt][h] = row < N;
+            wp[rt][h] = W + (size_t)(row < N ? row : 0) * ldw + c * 16;
+        }
+    const __nv_bfloat16 *xp[NT];
+    bool xv[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        int m = nt * 8 + r;
+        xv[nt] = m < M;
+        xp[nt] = X + (size_t)(m < M ? m : 0) * K + c * 32;
+    }
+
+    float acc[RT][NT][4];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[rt][nt][j] = 0.f;
+
+    for (int g = g0 + warp; g < g1; g += kGemvWarps) {
+        uint4 wq[RT][2];
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                wq[rt][h] = rv[rt][h] ? ldg_nc_v4(wp[rt][h] + (size_t)g * 64) : make_uint4(0, 0, 0, 0);
+        float sc[RT][2];
+        if (GROUPED) {
+#pragma unroll
+            for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) sc[rt][h] = rv[rt][h] ? __ldg(S + (size_t)rows[rt][h] * G + g) : 0.f;
+        }
+        float part[RT][NT][4];
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) part[rt][nt][j] = 0.f;
+
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint4 xw[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+                xw[nt] = xv[nt] ? ldg_v4(xp[nt] + (size_t)g * 128 + i * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t b0[NT], b1[NT];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    uint32_t lo = hh ? xw[nt].y : xw[nt].x;
+                    uint32_t hi = hh ? xw[nt].w : xw[nt].z;
+                    b0[nt] = __byte_perm(lo, hi, 0x5410);
+                    b1[nt] = __byte_perm(lo, hi, 0x7632);
+                }
+#pragma unroll
+                for (int rt = 0; rt < RT; ++rt) {
+                    uint32_t wr = word_of(wq[rt][0], i), wr8 = word_of(wq[rt][1], i);
+                    uint32_t a0 = dq_pair(wr >> (8 * hh));
+                    uint32_t a1 = dq_pair(wr8 >> (8 * hh));
+                    uint32_t a2 = dq_pair(wr >> (8 * hh + 4));
+                    uint32_t a3 = dq_pair(wr8 >> (8 * hh + 4));
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) mma16816(part[rt][nt], a0, a1, a2, a3, b0[nt], b1[nt]);
+                }
+            }
+        }
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (GROUPED)  // reference: acc = acc + dot_g * s[n,g], product rounded first
+                        acc[rt][nt][j] = __fadd_rn(acc[rt][nt][j], __fmul_rn(part[rt][nt][j], sc[rt][j >> 1]));
+                    else
+                        acc[rt][nt][j] = __fadd_rn(acc[rt][nt][j], part[rt][nt][j]);
+                }
+    }
+
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) red[warp][(rt * NT + nt) * 4 + j][lane] = acc[rt][nt][j];
+    __syncthreads();
+
+    // Fixed-order reduction over warps; entry e -> (tile slot, lane) -> (row, m).
+    for (int e = threadIdx.x; e < NACC * 32; e += blockDim.x) {
+        const int idx = e >> 5, ln = e & 31;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) v += red[w][idx][ln];
+        const int rt = idx / (NT * 4), nt = (idx / 4) % NT, j = idx & 3;
+        const int row = row_base + rt * 16 + (ln >> 2) + ((j & 2) ? 8 : 0);
+        const int m = nt * 8 + 2 * (ln & 3) + (j & 1);
+        if (row < N && m < M) {
+            if (splits == 1) {
+                if (!GROUPED) v = v * __ldg(S + row);
+                Y[(size_t)m * N + row] = f2bf(v);
+            } else {
+                ws[((size_t)blockIdx.y * M + m) * N + row] = v;
+            }
+        }
+    }
+    if (splits == 1) return;
+
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int prev = atomicAdd(ctr + blockIdx.x, 1);
+        s_last = (prev == splits - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int e = threadIdx.x; e < ROWS * M; e += blockDim.x) {
+        const int m = e / ROWS, row = row_base + e % ROWS;
+        if (row >= N) continue;
+        float v = 0.f;
+        for (int s = 0; s < splits; ++s) v += __ldcg(ws + ((size_t)s * M + m) * N + row);
+        if (!GROUPED) v = v * __ldg(S + row);
+        Y[(size_t)m * N + row] = f2bf(v);
+    }
+    if (threadIdx.x == 0) ctr[blockIdx.x] = 0;  // self-reset for the next launch / graph replay
+}
+
+// Generic fallback (any K, any alignment): one warp per output row; lanes stride
+// over k; per scale group the lanes' partial dots are summed, then
+// acc = acc + dot_g * s[n,g] (QF 0), or the row dot is scaled once (QF 1: W4 per-row,
+// QF 2: W8 per-row).  Activations bf16; output bf16.
+template <int QF>
+__global__ void __launch_bounds__(256) linear_generic(const __nv_bfloat16 *__restrict__ X, int M, int K,
+                                                      const void *__restrict__ Wv, const float *__restrict__ S,
+                                                      int N, int gs, __nv_bfloat16 *__restrict__ Y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + warp;
+    if (n >= N) return;
+    const int G = QF == 0 ? (K + gs - 1) / gs : 1;
+    const int glen = QF == 0 ? gs : K;
+    const uint8_t *W4 = reinterpret_cast<const uint8_t *>(Wv) + (size_t)n * ((K + 1) / 2);
+    const int8_t *W8 = reinterpret_cast<const int8_t *>(Wv) + (size_t)n * K;
+    for (int m = 0; m < M; ++m) {
+        const __nv_bfloat16 *x = X + (size_t)m * K;
+        float acc = 0.f;
+        for (int g = 0; g < G; ++g) {
+            const int k0 = g * glen, k1 = min(K, k0 + glen);
+            float part = 0.f;
+            for (int k = k0 + lane; k < k1; k += 32) {
+                float q;
+                if (QF == 2) {
+                    q = (float)W8[k];
+                } else {
+                    int v = (W4[k >> 1] >> ((k & 1) * 4)) & 0xF;
+                    q = (float)(v >= 8 ? v - 16 : v);
+                }
+                part = fmaf(bf2f(x[k]), q, part);
+            }
+            part = warp_sum(part);
+            if (QF == 0)
+                acc = __fadd_rn(acc, __fmul_rn(part, __ldg(S + (size_t)n * G + g)));
+            else
+                acc += part;
+        }
+        if (QF != 0) acc = acc * __ldg(S + n);
+        if (lane == 0) Y[(size_t)m * N + n] = f2bf(acc);
+    }
+}
+
+// W8A32: fp32 activations, int8 weights, per-row scale, fp32 out.  One warp per row;
+// 16 int8 weights per lane per step when K % 16 == 0 (coalesced 16-byte loads).
+__global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, int M, int K,
+                                                  const int8_t *__restrict__ W, const float *__restrict__ S, int N,
+                                                  float *__restrict__ Y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 8 + warp;
+    if (n >= N) return;
+    const int8_t *w = W + (size_t)n * K;
+    const bool vec = ((K & 15) == 0) && ((((uintptr_t)W) & 15) == 0) && ((((uintptr_t)X) & 15) == 0);
+    for (int m0 = 0; m0 < M; m0 += 4) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (vec) {
+            for (int k = lane * 16; k < K; k += 512) {
+                uint4 q4 = ldg_nc_v4(w + k);
+                const int8_t *q = reinterpret_cast<const int8_t *>(&q4);
+#pragma unroll
+                for (int mm = 0; mm < 4; ++mm) {
+                    if (m0 + mm >= M) break;
+                    const float4 *xr = reinterpret_cast<const float4 *>(X + (size_t)(m0 + mm) * K + k);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        float4 xv = __ldg(xr + v);
+                        acc[mm] = fmaf(xv.x, (float)q[4 * v + 0], acc[mm]);
+                        acc[mm] = fmaf(xv.y, (float)q[4 * v + 1], acc[mm]);
+                        acc[mm] = fmaf(xv.z, (float)q[4 * v + 2], acc[mm]);
+                        acc[mm] = fmaf(xv.w, (float)q[4 * v + 3], acc[mm]);
+                    }
+                }
+            }
+        } else {
+            for (int k = lane; k < K; k += 32) {
+                float q = (float)w[k];
+                for (int mm = 0; mm < 4 && m0 + mm < M; ++mm) acc[mm] = fmaf(X[(size_t)(m0 + mm) * K + k], q, acc[mm]);
+            }
+        }
+        const float s = __ldg(S + n);
+#pragma unroll
+        for (int mm = 0; mm < 4; ++mm) {
+            float v = warp_sum(acc[mm]);
+            if (lane == 0 && m0 + mm < M) Y[(size_t)(m0 + mm) * N + n] = v * s;
+        }
+    }
+}
+
+__global__ void gemm_f32_naive(const float *A, const float *B, float *C, int M, int N, int K, int ta, int tb) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+    if (n >= N || m >= M) return;
+    const int lda = ta ? M : K, ldb = tb ? K : N;
+    float acc = 0.f;
+    for (int k = 0; k < K; ++k) {
+        float a = ta ? A[(size_t)k * lda + m] : A[(size_t)m * lda + k];
+        float b = tb ? B[(size_t)n * ldb + k] : B[(size_t)k * ldb + n];
+        acc = fmaf(a, b, acc);
+    }
+    C[(size_t)m * N + n] = acc;
+}
+
+__global__ void argmax_bf16_row(const __nv_bfloat16 *__restrict__ v, int n, int *out_idx, float *out_val) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float x = bf2f(v[i]);
+        if (x > best || (x == best && i < bi)) { best = x; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        best = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        if (lane == 0) { *out_idx = bi; *out_val = best; }
+    }
+}
+
+template <int RT, int NT, bool GROUPED>
+int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
+               const char *what) {
+    const int tiles = (N + 16 * RT - 1) / (16 * RT);
+    const int G = K >> 7;
+    const int target = 2 * pilm::num_sms();
+    int splits = 1;
+    if (tiles < target) {
+        splits = (target + tiles - 1) / tiles;
+        int max_splits = G / kGemvWarps;  // keep every warp busy
+        if (max_splits < 1) max_splits = 1;
+        if (splits > max_splits) splits = max_splits;
+    }
+    const int gps = (G + splits - 1) / splits;
+    splits = (G + gps - 1) / gps;
+    float *ws = nullptr;
+    int *ctr = nullptr;
+    if (splits > 1) {
+        ws = (float *)pilm::workspace((size_t)splits * M * N * sizeof(float));
+        ctr = pilm::counters((size_t)tiles);
+        PILM_REQUIRE(ws && ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+    }
+    dim3 grid(tiles, splits);
+    w4_gemv_mma<RT, NT, GROUPED><<<grid, kGemvWarps * 32, 0, pilm::stream()>>>(X, M, K, W, S, N, Y, ws, ctr, splits,
+                                                                                 gps);
+    return pilm::check_launch(what);
+}
+
+template <bool GROUPED>
+int dispatch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
+                 const char *what) {
+    if (M <= 8) return launch_mma<2, 1, GROUPED>(X, M, K, W, S, N, Y, what);
+    if (M <= 16) return launch_mma<2, 2, GROUPED>(X, M, K, W, S, N, Y, what);
+    if (M <= 32) return launch_mma<1, 4, GROUPED>(X, M, K, W, S, N, Y, what);
+    return launch_mma<1, 8, GROUPED>(X, M, K, W, S, N, Y, what);
+}
+
+bool aligned16(const void *p) { return (((uintptr_t)p) & 15) == 0; }
+
+}  // namespace
+
+namespace pilm {
+
+// Shared entry used by the ABI wrappers and by the fused SwiGLU path.
+// qf: 0 = W4 grouped (gs = 32 or 128), 1 = W4 per-row, 2 = W8 per-row.
+int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
+                const char *what) {
+    const __nv_bfloat16 *X = (const __nv_bfloat16 *)A;
+    __nv_bfloat16 *Y = (__nv_bfloat16 *)C;
+    if (M == 0 || N == 0) return ECPU_OK;
+    const bool mma_ok = (qf == 1 || (qf == 0 && gs == 128)) && (K % 128 == 0) && aligned16(A) && aligned16(W);
+    if (mma_ok) {
+        if (M >= 64) {
+            int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, what);
+            if (rc != ECPU_ERR_UNSUPPORTED) return rc;
+        }
+        // register-dequant GEMV, in slabs of at most 64 activation rows
+        for (int m0 = 0; m0 < M; m0 += 64) {
+            const int mm = M - m0 < 64 ? M - m0 : 64;
+            const __nv_bfloat16 *Xs = X + (size_t)m0 * K;
+            __nv_bfloat16 *Ys = Y + (size_t)m0 * N;
+            int rc = qf == 0 ? dispatch_mma<true>(Xs, mm, K, (const uint8_t *)W, S, N, Ys, what)
+                             : dispatch_mma<false>(Xs, mm, K, (const uint8_t *)W, S, N, Ys, what);
+            if (rc != ECPU_OK) return rc;
+        }
+        return ECPU_OK;
+    }
+    dim3 grid((N + 7) / 8);
+    switch (qf) {
+        case 0: linear_generic<0><<<grid, 256, 0, stream()>>>(X, M, K, W, S, N, gs, Y); break;
+        case 1: linear_generic<1><<<grid, 256, 0, stream()>>>(X, M, K, W, S, N, gs, Y); break;
+        default: linear_generic<2><<<grid, 256, 0, stream()>>>(X, M, K, W, S, N, gs, Y); break;
+    }
+    return check_launch(what);
+}
+
+}  // namespace pilm
+
+#define LINEAR_ARGS_OK(fn)                                                                   \
+    PILM_REQUIRE(desc &&A &&W &&scales &&C, ECPU_ERR_PARAM, fn ": null argument");            \
+    PILM_REQUIRE(desc->M <= 0x7fffffff && desc->N <= 0x7fffffff && desc->K <= 0x7fffffff, ECPU_ERR_PARAM, \
+                 fn ": dimension too large")
+
+extern "C" {
+
+int ekernel_gemm(const ekernel_gemm_desc_t *desc, const void *A, const void *B, void *C, ekernel_isa_t isa) {
+    (void)isa;
+    PILM_REQUIRE(desc && A && B && C, ECPU_ERR_PARAM, "ekernel_gemm: null argument");
+    PILM_REQUIRE(desc->a_prec == ECPU_PRECISION_F32 && desc->b_prec == ECPU_PRECISION_F32 &&
+                     desc->out_prec == ECPU_PRECISION_F32,
+                 ECPU_ERR_UNSUPPORTED, "ekernel_gemm: only F32 is supported");
+    if (desc->M == 0 || desc->N == 0) return ECPU_OK;
+    dim3 grid((unsigned)((desc->N + 127) / 128), (unsigned)desc->M);
+    gemm_f32_naive<<<grid, 128, 0, pilm::stream()>>>((const float *)A, (const float *)B, (float *)C, (int)desc->M,
+                                                     (int)desc->N, (int)desc->K, desc->transpose_a, desc->transpose_b);
+    return pilm::check_launch("ekernel_gemm");
+}
+
+int ekernel_linear_w8a32(const ekernel_linear_w8a32_desc_t *desc, const float *A, const int8_t *W,
+                         const float *scales, float *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w8a32");
+    if (desc->M == 0 || desc->N == 0) return ECPU_OK;
+    w8a32_gemv<<<(unsigned)((desc->N + 7) / 8), 256, 0, pilm::stream()>>>(A, (int)desc->M, (int)desc->K, W, scales,
+                                                                        (int)desc->N, C);
+    return pilm::check_launch("ekernel_linear_w8a32");
+}
+
+int ekernel_linear_w8a16_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const int8_t *W,
+                              const float *scales, uint16_t *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w8a16_bf16");
+    return pilm::linear_bf16(2, 0, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                             "ekernel_linear_w8a16_bf16");
+}
+
+int ekernel_linear_w8a16_bf16_argmax(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                     const int8_t *W, const float *scales, size_t *out_index, float *out_value,
+                                     ekernel_isa_t isa) {
+    (void)isa;
+    PILM_REQUIRE(desc && A && W && scales && out_index && out_value, ECPU_ERR_PARAM,
+                 "ekernel_linear_w8a16_bf16_argmax: null argument");
+    PILM_REQUIRE(desc->M == 1 && desc->N > 0 && desc->K > 0 && desc->N <= 0x7fffffff, ECPU_ERR_UNSUPPORTED,
+                 "ekernel_linear_w8a16_bf16_argmax: M must be 1");
+    const size_t n = desc->N;
+    char *ws = (char *)pilm::workspace(n * 2 + 64);
+    PILM_REQUIRE(ws, ECPU_ERR_MEM, "ekernel_linear_w8a16_bf16_argmax: workspace allocation failed");
+    int rc = pilm::linear_bf16(2, 0, A, 1, (int)desc->K, W, scales, (int)n, ws + 64,
+                               "ekernel_linear_w8a16_bf16_argmax");
+    if (rc != ECPU_OK) return rc;
+    argmax_bf16_row<<<1, 1024, 0, pilm::stream()>>>((const __nv_bfloat16 *)(ws + 64), (int)n, (int *)ws,
+                                                   (float *)(ws + 4));
+    rc = pilm::check_launch("ekernel_linear_w8a16_bf16_argmax");
+    if (rc != ECPU_OK) return rc;
+    int idx = 0;
+    float val = 0.f;
+    cudaMemcpyAsync(&idx, ws, 4, cudaMemcpyDeviceToHost, pilm::stream());
+    cudaMemcpyAsync(&val, ws + 4, 4, cudaMemcpyDeviceToHost, pilm::stream());
+    if (cudaStreamSynchronize(pilm::stream()) != cudaSuccess) {
+        pilm::set_error("ekernel_linear_w8a16_bf16_argmax: %s", cudaGetErrorString(cudaGetLastError()));
+        return ECPU_ERR_KERNEL;
+    }
+    *out_index = (size_t)idx;
+    *out_value = val;
+    return ECPU_OK;
+}
+
+int ekernel_linear_w4a16_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                              const float *scales, uint16_t *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w4a16_bf16");
+    return pilm::linear_bf16(1, 0, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                             "ekernel_linear_w4a16_bf16");
+}
+
+int ekernel_linear_w4a16g32_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                                 const float *scales, uint16_t *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w4a16g32_bf16");
+    return pilm::linear_bf16(0, 32, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                             "ekernel_linear_w4a16g32_bf16");
+}
+
+int ekernel_linear_w4a16g128_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                                  const float *scales, uint16_t *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16");
+    return pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                             "ekernel_linear_w4a16g128_bf16");
+}
+
+}  // extern "C"

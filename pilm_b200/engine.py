@@ -1,0 +1,187 @@
+"""Batched MTP speculative-verify engine on the B200 kernels.
+
+The reference runs one request per forward (src/engine.py:416-472); this engine
+verifies many sequences per step with the same per-sequence rules:
+
+* drafts appended per step are capped at
+  min(remaining output, tokens left in the current page - 1, pending drafts)
+  (engine.py:399-401), so verify rows never cross a page;
+* the verify rows are [last token, d1..dn] at positions num_computed..;
+* greedy acceptance counts leading drafts equal to the row argmax; the next
+  token is the argmax of the first mismatching row or of the bonus row
+  (engine.py:479-503, 551-557);
+* on rejection the sequence is rolled back to start + 1 + accepted tokens
+  (engine.py:505-510).  The page table is unchanged (no page boundary is ever
+  crossed).  The reference then re-runs the accepted prefix to refresh state;
+  for full-attention Qwen3 the verify pass already wrote identical K/V for those
+  rows and the accepted row's hidden state equals the re-run's (bit-identical in
+  bf16, checked against the reference), so no re-run is done here.
+
+Prefill runs through the same forward in page-aligned chunks of at most one
+page per sequence per pass (engine.py:218 uses 16-token chunks), or can be
+skipped for synthetic benchmarks whose KV pages are filled directly.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import ckernel as ck
+from .paging import PageTableManager, Sequence, Status, VerifyScheduler
+from .qwen3 import Qwen3Verifier, VerifyBatch
+
+
+def draft_limit(num_computed: int, block_size: int, remaining_output: int, n_pending: int) -> int:
+    """engine.py:399-401."""
+    block_remaining = block_size - (num_computed % block_size)
+    return max(0, min(remaining_output, block_remaining - 1, n_pending))
+
+
+@dataclass
+class StepResult:
+    seq_id: int
+    drafts: list[int]
+    accepted: int
+    next_token: int
+
+
+class MTPVerifyEngine:
+    def __init__(self, verifier: Qwen3Verifier, num_blocks: int, block_size: int = 16, max_model_len: int = 65536,
+                 max_pages_per_seq: Optional[int] = None, pin_memory: bool = True,
+                 max_num_batched_tokens: int = 1 << 30):
+        """max_num_batched_tokens is the scheduler's per-pass token budget; the reference
+        engine uses one page (16, engine.py:218), which also fixes its page order."""
+        self.v = verifier
+        self.device = verifier.device
+        self.block_size = block_size
+        self.pages = PageTableManager(num_blocks, block_size)
+        mp = max_pages_per_seq or (max_model_len + block_size - 1) // block_size
+        self.max_pages = mp
+        self.sched = VerifyScheduler(self.pages, max_num_batched_tokens=max_num_batched_tokens, max_num_seqs=1 << 20,
+                                     max_model_len=max_model_len, max_pages_per_seq=mp)
+        self._next_id = 0
+        self.pin = pin_memory and torch.cuda.is_available()
+        self.stats = {"attempts": 0, "accepts": 0, "rejects": 0, "steps": 0, "verified_rows": 0}
+
+    # ---- admission -------------------------------------------------------------------
+    def add_request(self, prompt: list[int], max_new_tokens: int = 256, eos_token_id: int = -1) -> int:
+        sid = self._next_id
+        self._next_id += 1
+        self.sched.add(Sequence(sid, list(prompt), max_new_tokens, eos_token_id))
+        return sid
+
+    def admit_prefilled(self, sid: int) -> None:
+        """Benchmark admission: take the pages of the whole prompt and mark it computed,
+        assuming its K/V are already in the pool (synthetic KV)."""
+        seq = self.sched.seqs[sid]
+        self.sched.waiting.remove(seq)
+        if self.pages.allocate(seq, seq.num_tokens, self.max_pages) is None:
+            raise RuntimeError("KV pool exhausted")
+        seq.num_computed = seq.num_tokens
+        seq.status = Status.RUNNING
+        self.sched.running.append(seq)
+
+    # ---- batch construction ------------------------------------------------------------
+    def _tensor(self, data, dtype=torch.int32) -> torch.Tensor:
+        t = torch.tensor(data, dtype=dtype, pin_memory=self.pin)
+        return t.to(self.device, non_blocking=True)
+
+    def build_batch(self, seqs: list[Sequence], starts: list[int], counts: list[int]) -> VerifyBatch:
+        ids, pos, slots, cu = [], [], [], [0]
+        bs = self.block_size
+        maxp = max(1, max(len(s.pages) for s in seqs))
+        table = []
+        ctx = []
+        for s, st, n in zip(seqs, starts, counts):
+            ids.extend(s.tokens[st:st + n])
+            pos.extend(range(st, st + n))
+            slots.extend(s.pages[p // bs] * bs + p % bs for p in range(st, st + n))
+            cu.append(cu[-1] + n)
+            table.append(s.pages + [0] * (maxp - len(s.pages)))
+            ctx.append(st + n)
+        return VerifyBatch(ids=self._tensor(ids), positions=self._tensor(pos), slots=self._tensor(slots),
+                           block_table=self._tensor(table), cu_q=self._tensor(cu), context_lens=self._tensor(ctx),
+                           max_q_len=max(counts), max_context=max(ctx))
+
+    # ---- prefill ----------------------------------------------------------------------
+    def prefill(self) -> dict[int, int]:
+        """Run every waiting prompt through the model in page-aligned chunks and take
+        the greedy first token of each.  First tokens are appended only after every
+        prompt is done, so no decode rows are mixed into the prefill passes.
+        Returns {seq_id: first_token}."""
+        first = {}
+        while self.sched.waiting or any(s.is_prefill for s in self.sched.running):
+            out = self.sched.schedule()
+            if out.is_empty:
+                raise RuntimeError("prefill could not be scheduled (KV pool too small?)")
+            seqs = [self.sched.seqs[c.seq_id] for c in out.scheduled]
+            starts = [c.positions[0] for c in out.scheduled]
+            counts = [c.num_tokens for c in out.scheduled]
+            b = self.build_batch(seqs, starts, counts)
+            h = self.v.forward(b)
+            done = [i for i, c in enumerate(out.scheduled) if not c.is_prefill_chunk]
+            if done:
+                ends = [sum(counts[:i + 1]) - 1 for i in done]
+                rows = torch.tensor(ends, device=self.device)
+                logits = self.v.lm_head(h.index_select(0, rows).contiguous())
+                top = torch.argmax(logits.float(), dim=-1).tolist()
+                for j, i in enumerate(done):
+                    first[out.scheduled[i].seq_id] = int(top[j])
+        for sid, t in first.items():
+            s = self.sched.seqs[sid]
+            s.tokens.append(t)
+            s.outputs.append(t)
+        return first
+
+    # ---- the verify step --------------------------------------------------------------
+    def verify_step(self, drafts: dict[int, list[int]]) -> list[StepResult]:
+        """One MTP verify step over every running sequence in decode state."""
+        seqs, starts, counts, used = [], [], [], []
+        for s in list(self.sched.running):
+            if s.num_uncomputed != 1 or s.is_prefill:
+                continue
+            d = drafts.get(s.seq_id, [])
+            remaining = s.max_new_tokens - len(s.outputs)
+            n = draft_limit(s.num_computed, self.block_size, remaining, len(d))
+            d = [int(t) for t in d[:n]]
+            s.tokens.extend(d)
+            if self.pages.allocate(s, 1 + n, self.max_pages) is None:
+                del s.tokens[len(s.tokens) - n:]
+                continue
+            seqs.append(s)
+            starts.append(s.num_computed)
+            counts.append(1 + n)
+            used.append(d)
+        if not seqs:
+            return []
+        b = self.build_batch(seqs, starts, counts)
+        B = len(seqs)
+        acc = torch.empty(B, dtype=torch.int32, device=self.device)
+        nxt = torch.empty(B, dtype=torch.int32, device=self.device)
+        ctx = b.context_lens.clone()
+        self.v.verify_greedy(b, acc, nxt, ctx)
+        res = torch.stack([acc, nxt]).to("cpu", non_blocking=False).tolist()
+        out = []
+        for i, s in enumerate(seqs):
+            a, t = int(res[0][i]), int(res[1][i])
+            st, d = starts[i], used[i]
+            accepted = d[:a]
+            del s.tokens[st + 1:]
+            s.tokens.extend(accepted)
+            s.outputs.extend(accepted)
+            s.num_computed = st + 1 + a
+            s.tokens.append(t)
+            s.outputs.append(t)
+            self.stats["attempts"] += min(len(d), a + 1)
+            self.stats["accepts"] += a
+            self.stats["rejects"] += 1 if a < len(d) else 0
+            out.append(StepResult(s.seq_id, d, a, t))
+        self.stats["steps"] += 1
+        self.stats["verified_rows"] += b.total_q
+        finished = [s for s in seqs if self.sched._check_stop(s)]
+        for s in finished:
+            self.sched.running.remove(s)
+            self.pages.free(s)
+        return out

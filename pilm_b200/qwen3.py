@@ -1,0 +1,378 @@
+"""Qwen3 verify forward on the B200 kernels.
+
+The batched counterpart of the reference's Qwen3Model.forward
+(src/models/qwen3/model.py:95-127) for the MTP verify step: all sequences' verify
+rows ([last, d1..dn] per sequence) go through one pass of every layer.  Per layer:
+
+    h   = RMSNorm(residual)                      add_rmsnorm   (layers.py:94-119)
+    qkv = W4 linear(h, [q_proj; k_proj; v_proj]) linear_w4a16g128 (linear.py:298-340)
+    q,k = QK-RMSNorm + RoPE, K/V -> page slots   qk_norm_rope_kv_append (attention.py:79-97)
+    a   = paged attention (+ sigmoid gate)       paged_attention_verify (attention.py:98-139)
+    o   = W4 linear(a, o_proj)
+    h   = RMSNorm(residual += o)                 add_rmsnorm
+    gu  = W4 linear(h, [gate; up])               one fused weight [2I, H]
+    m   = W4 linear(rne(rne(silu(g)) * u), down) silu_mul + linear (layers.py:192-193)
+    residual += m                                (fused into the next layer's add_rmsnorm)
+
+Weights are device-resident; q/k/v and gate/up are concatenated row-wise at load,
+which leaves every output element identical to the separate reference linears
+(each output row is an independent dot product).  KV pages use the reference
+layout [num_blocks, 16, n_kv, head_dim] per layer (physical_kv.py:30-33).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import bindings as abi
+from . import ckernel as ck
+
+
+@dataclass
+class Qwen3Shape:
+    hidden: int
+    layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    partial_rotary: float = 1.0
+    gated: bool = False        # Qwen3.5 gated attention (q_proj 2x wide)
+    gemma_norm: bool = False   # x * (w + 1) norms
+    block_size: int = 16
+
+    @property
+    def q_rows(self) -> int:
+        return self.n_heads * self.head_dim * (2 if self.gated else 1)
+
+    @property
+    def qkv_rows(self) -> int:
+        return self.q_rows + 2 * self.n_kv_heads * self.head_dim
+
+    @property
+    def rot_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary)
+
+
+QWEN3_8B = Qwen3Shape(hidden=4096, layers=36, n_heads=32, n_kv_heads=8, head_dim=128, intermediate=12288,
+                      vocab=151936)
+QWEN3_1_7B = Qwen3Shape(hidden=2048, layers=28, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=6144,
+                        vocab=151936)
+QWEN3_0_6B = Qwen3Shape(hidden=1024, layers=28, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=3072,
+                        vocab=151936)
+
+
+class W4Linear:
+    """Device-resident W4A16 group-128 linear in the reference packing
+    (qweight uint8 [N, ceil(K/2)], scales fp32 [N, ceil(K/128)])."""
+
+    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, in_features: int):
+        self.qweight = qweight.contiguous()
+        self.scales = scales.contiguous()
+        self.in_features = int(in_features)
+        self.out_features = int(qweight.shape[0])
+
+    @classmethod
+    def cat(cls, parts: list["W4Linear"]) -> "W4Linear":
+        return cls(torch.cat([p.qweight for p in parts]), torch.cat([p.scales for p in parts]), parts[0].in_features)
+
+    @property
+    def nbytes(self) -> int:
+        return self.qweight.numel() + self.scales.numel() * 4
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        m = x.shape[0]
+        if out is None:
+            out = torch.empty((m, self.out_features), dtype=torch.bfloat16, device=x.device)
+        rc = abi.linear_w4a16g128_bf16_ptr(x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(),
+                                           out.data_ptr(), m, self.out_features, self.in_features)
+        if rc != 0:
+            raise RuntimeError(f"ekernel_linear_w4a16g128_bf16 failed: rc={rc}: {abi.last_error()}")
+        return out
+
+
+class Qwen3Weights:
+    def __init__(self, shape: Qwen3Shape, embed: torch.Tensor, layers: list[dict], final_norm: torch.Tensor,
+                 lm_head: W4Linear):
+        self.shape = shape
+        self.embed = embed
+        self.layers = layers
+        self.final_norm = final_norm
+        self.lm_head = lm_head
+
+    @property
+    def linear_bytes(self) -> int:
+        n = self.lm_head.nbytes
+        for L in self.layers:
+            n += sum(L[k].nbytes for k in ("qkv", "o", "gate_up", "down"))
+        return n
+
+    @classmethod
+    def from_checkpoint(cls, shape: Qwen3Shape, ck_tensors: dict[str, torch.Tensor], device) -> "Qwen3Weights":
+        """Quantize a bf16 checkpoint dict (oracle.model.make_checkpoint naming) on the
+        device with the reference quantizer (group 128) and fuse q/k/v and gate/up."""
+        def q(name):
+            w = ck_tensors[name].to(device)
+            qw, s = ck.quantize_weight_i4_grouped(w, 128)
+            return W4Linear(qw, s, w.shape[1])
+
+        layers = []
+        for li in range(shape.layers):
+            p = f"l{li}."
+            layers.append({
+                "qkv": W4Linear.cat([q(p + "q_proj"), q(p + "k_proj"), q(p + "v_proj")]),
+                "o": q(p + "o_proj"),
+                "gate_up": W4Linear.cat([q(p + "gate"), q(p + "up")]),
+                "down": q(p + "down"),
+                "input_norm": ck_tensors[p + "input_norm"].to(device, torch.bfloat16).contiguous(),
+                "post_norm": ck_tensors[p + "post_norm"].to(device, torch.bfloat16).contiguous(),
+                "q_norm": ck_tensors[p + "q_norm"].to(device, torch.bfloat16).contiguous(),
+                "k_norm": ck_tensors[p + "k_norm"].to(device, torch.bfloat16).contiguous(),
+            })
+        embed = ck_tensors["embed"].to(device, torch.bfloat16).contiguous()
+        qw, s = ck.quantize_weight_i4_grouped(embed, 128)
+        return cls(shape, embed, layers, ck_tensors["final_norm"].to(device, torch.bfloat16).contiguous(),
+                   W4Linear(qw, s, shape.hidden))
+
+    @classmethod
+    def synthetic(cls, shape: Qwen3Shape, seed: int, device) -> "Qwen3Weights":
+        """Seeded random-init model generated and quantized on the device: N(0, 0.02)
+        weights rounded to bf16 (the checkpoint dtype), then group-128 int4; norm
+        weights ones (plain) or zeros (Gemma); tied LM head."""
+        g = torch.Generator(device=device).manual_seed(seed)
+
+        def lin(n, k):
+            w = (torch.randn((n, k), generator=g, device=device, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+            qw, s = ck.quantize_weight_i4_grouped(w, 128)
+            del w
+            return W4Linear(qw, s, k)
+
+        H, I = shape.hidden, shape.intermediate
+        init = torch.zeros if shape.gemma_norm else torch.ones
+        embed = (torch.randn((shape.vocab, H), generator=g, device=device, dtype=torch.float32) * 0.02).to(
+            torch.bfloat16)
+        layers = []
+        for _ in range(shape.layers):
+            layers.append({
+                "qkv": lin(shape.qkv_rows, H),
+                "o": lin(H, shape.n_heads * shape.head_dim),
+                "gate_up": lin(2 * I, H),
+                "down": lin(H, I),
+                "input_norm": init(H, dtype=torch.bfloat16, device=device),
+                "post_norm": init(H, dtype=torch.bfloat16, device=device),
+                "q_norm": init(shape.head_dim, dtype=torch.bfloat16, device=device),
+                "k_norm": init(shape.head_dim, dtype=torch.bfloat16, device=device),
+            })
+        qw, s = ck.quantize_weight_i4_grouped(embed, 128)
+        return cls(shape, embed, layers, init(H, dtype=torch.bfloat16, device=device), W4Linear(qw, s, H))
+
+
+def rope_tables(shape: Qwen3Shape, max_pos: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin [max_pos, rot_dim/2] fp32, computed on the host exactly like the reference
+    (_rope_inv_freq / _rope_cos_sin, layers.py:50-80) and uploaded."""
+    n_freq = shape.rot_dim // 2
+    inv_freq = 1.0 / (shape.rope_theta ** (torch.arange(0, n_freq, dtype=torch.float32) / n_freq))
+    pos = torch.arange(max_pos, dtype=torch.long).to(torch.float32)
+    freqs = pos.unsqueeze(1) * inv_freq.unsqueeze(0)
+    return torch.cos(freqs).contiguous().to(device), torch.sin(freqs).contiguous().to(device)
+
+
+class PagedKVCache:
+    """Device-resident paged KV: per layer K and V [num_blocks, block_size, n_kv, hd] bf16."""
+
+    def __init__(self, shape: Qwen3Shape, num_blocks: int, device, fill: Optional[str] = None, seed: int = 0):
+        self.num_blocks = num_blocks
+        self.block_size = shape.block_size
+        dims = (num_blocks, shape.block_size, shape.n_kv_heads, shape.head_dim)
+        self.k = []
+        self.v = []
+        g = torch.Generator(device=device).manual_seed(seed) if fill == "random" else None
+        for _ in range(shape.layers):
+            if fill == "random":
+                self.k.append(torch.randn(dims, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16))
+                self.v.append((torch.randn(dims, generator=g, device=device, dtype=torch.float32) * 0.02).to(
+                    torch.bfloat16))
+            else:
+                self.k.append(torch.zeros(dims, dtype=torch.bfloat16, device=device))
+                self.v.append(torch.zeros(dims, dtype=torch.bfloat16, device=device))
+
+    @property
+    def bytes_per_token(self) -> int:
+        return len(self.k) * 2 * self.k[0].shape[2] * self.k[0].shape[3] * 2
+
+
+@dataclass
+class VerifyBatch:
+    """Device metadata of one verify (or prefill-chunk) pass over B sequences."""
+    ids: torch.Tensor           # [T] int32 token ids of the rows
+    positions: torch.Tensor     # [T] int32
+    slots: torch.Tensor         # [T] int32 page * block_size + offset
+    block_table: torch.Tensor   # [B, max_blocks] int32
+    cu_q: torch.Tensor          # [B+1] int32 row offsets
+    context_lens: torch.Tensor  # [B] int32 keys per sequence incl. these rows
+    max_q_len: int
+    max_context: int
+
+    @property
+    def num_seqs(self) -> int:
+        return self.cu_q.shape[0] - 1
+
+    @property
+    def total_q(self) -> int:
+        return self.ids.shape[0]
+
+
+class Qwen3Verifier:
+    """Runs the batched verify forward, the LM head and the acceptance kernels."""
+
+    def __init__(self, weights: Qwen3Weights, kv: PagedKVCache, max_rows: int, max_pos: int, device):
+        self.w = weights
+        self.shape = weights.shape
+        self.kv = kv
+        self.device = device
+        self.max_rows = max_rows
+        s = self.shape
+        self.cos, self.sin = rope_tables(s, max_pos, device)
+        self.max_pos = max_pos
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.residual = torch.empty((max_rows, s.hidden), **bf)
+        self.h = torch.empty((max_rows, s.hidden), **bf)
+        self.qkv = torch.empty((max_rows, s.qkv_rows), **bf)
+        self.q = torch.empty((max_rows, s.n_heads * s.head_dim), **bf)
+        self.gate = torch.empty((max_rows, s.n_heads * s.head_dim), **bf) if s.gated else None
+        self.attn = torch.empty((max_rows, s.n_heads * s.head_dim), **bf)
+        self.o = torch.empty((max_rows, s.hidden), **bf)
+        self.gu = torch.empty((max_rows, 2 * s.intermediate), **bf)
+        self.act = torch.empty((max_rows, s.intermediate), **bf)
+        self.mlp = torch.empty((max_rows, s.hidden), **bf)
+        self.logits = torch.empty((max_rows, s.vocab), **bf)
+        i32 = dict(dtype=torch.int32, device=device)
+        self.top1 = torch.empty((max_rows,), **i32)
+        self.margin = torch.empty((max_rows,), dtype=torch.float32, device=device)
+        # optional CUDA-event timing of the attention and linear launches (bench.py)
+        self.op_timing = False
+        self.op_events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+        self._launches_before = None
+        self._last_step_launches = None
+
+    def _ev(self, name: str):
+        if not self.op_timing:
+            return None
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        self.op_events.append((name, a, b))
+        return b
+
+    def collect_op_times(self) -> dict:
+        """Average ms per launch for 'attention'; per-step sums for the linears."""
+        torch.cuda.synchronize()
+        tot: dict[str, float] = {}
+        cnt: dict[str, int] = {}
+        for name, a, b in self.op_events:
+            tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+            cnt[name] = cnt.get(name, 0) + 1
+        steps = max(1, cnt.get("lm_head", 1))
+        out = {}
+        if "attention" in tot:
+            out["attention"] = tot["attention"] / cnt["attention"]
+            out["attention_total"] = tot["attention"] / steps
+        lin = [k for k in tot if k.startswith("linear_")]
+        for k in lin:
+            out[k] = tot[k] / steps
+        if lin:
+            out["linear_total"] = sum(tot[k] for k in lin) / steps + tot.get("lm_head", 0.0) / steps
+        if "lm_head" in tot:
+            out["lm_head"] = tot["lm_head"] / steps
+        self.op_events.clear()
+        return out
+
+    def launches_per_step(self) -> int:
+        return int(self._last_step_launches or 0)
+
+    def _desc(self, b: VerifyBatch):
+        s = self.shape
+        return ck.attn_desc(num_seqs=b.num_seqs, total_q=b.total_q, max_q_len=b.max_q_len, n_heads=s.n_heads,
+                            n_kv_heads=s.n_kv_heads, head_dim=s.head_dim, block_size=s.block_size,
+                            num_blocks=self.kv.num_blocks, max_blocks_per_seq=b.block_table.shape[1],
+                            max_context=b.max_context, qkv_stride=s.qkv_rows, rope_rows=self.max_pos,
+                            rot_dim=s.rot_dim, eps=s.eps, add_one=s.gemma_norm, output_gate=s.gated)
+
+    def forward(self, b: VerifyBatch) -> torch.Tensor:
+        """Post-final-norm hidden states [T, H] (Qwen3Model.forward, return_last_hidden)."""
+        s = self.shape
+        T = b.total_q
+        if T > self.max_rows:
+            raise ValueError(f"{T} rows exceed max_rows={self.max_rows}")
+        desc = self._desc(b)
+        res, h = self.residual[:T], self.h[:T]
+        ck.embedding_bf16(b.ids, self.w.embed, out=res)
+        delta = None
+        for li, L in enumerate(self.w.layers):
+            ck.add_rmsnorm_bf16(res, delta, L["input_norm"], s.eps, s.gemma_norm, out=h)
+            e = self._ev("linear_qkv")
+            L["qkv"](h, out=self.qkv[:T])
+            if e is not None:
+                e.record()
+            ck.qk_norm_rope_kv_append(desc, self.qkv[:T], L["q_norm"], L["k_norm"], self.cos, self.sin, b.positions,
+                                      b.slots, self.kv.k[li], self.kv.v[li], self.q[:T],
+                                      self.gate[:T] if s.gated else None)
+            e = self._ev("attention")
+            ck.paged_attention_verify(desc, self.q[:T], self.kv.k[li], self.kv.v[li], b.block_table, b.cu_q,
+                                      b.context_lens, self.gate[:T] if s.gated else None, self.attn[:T])
+            if e is not None:
+                e.record()
+            e = self._ev("linear_o")
+            L["o"](self.attn[:T], out=self.o[:T])
+            if e is not None:
+                e.record()
+            ck.add_rmsnorm_bf16(res, self.o[:T], L["post_norm"], s.eps, s.gemma_norm, out=h)
+            e = self._ev("linear_gate_up")
+            L["gate_up"](h, out=self.gu[:T])
+            if e is not None:
+                e.record()
+            ck.silu_mul_bf16(self.gu[:T], s.intermediate, out=self.act[:T])
+            e = self._ev("linear_down")
+            L["down"](self.act[:T], out=self.mlp[:T])
+            if e is not None:
+                e.record()
+            delta = self.mlp[:T]
+        ck.add_rmsnorm_bf16(res, delta, self.w.final_norm, s.eps, s.gemma_norm, out=h)
+        return h
+
+    def lm_head(self, hidden: torch.Tensor) -> torch.Tensor:
+        T = hidden.shape[0]
+        e = self._ev("lm_head")
+        out = self.w.lm_head(hidden, out=self.logits[:T])
+        if e is not None:
+            e.record()
+        return out
+
+    def verify_greedy(self, b: VerifyBatch, accept_counts: torch.Tensor, next_tokens: torch.Tensor,
+                      context_lens: torch.Tensor, slots: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Verify forward + LM head + row argmax + greedy accept and rollback, all on the
+        stream; returns the logits buffer view (bf16)."""
+        n0 = abi.launch_count()
+        h = self.forward(b)
+        logits = self.lm_head(h)
+        T = b.total_q
+        ck.argmax_top2(logits, self.top1[:T], None, self.margin[:T])
+        ck.verify_accept_greedy(b.num_seqs, b.ids, self.top1[:T], b.cu_q, accept_counts, next_tokens, context_lens,
+                                slots)
+        self._last_step_launches = abi.launch_count() - n0
+        return logits
+
+
+def attention_bytes(shape: Qwen3Shape, context_lens: list[int], q_lens: list[int]) -> int:
+    """Algorithmic HBM bytes of one layer's paged attention: every key/value of each
+    sequence once, the queries and outputs, and the appended K/V rows."""
+    kv = sum(context_lens) * shape.n_kv_heads * shape.head_dim * 2 * 2
+    rows = sum(q_lens)
+    qo = rows * shape.n_heads * shape.head_dim * 2 * 2
+    app = rows * shape.n_kv_heads * shape.head_dim * 2 * 2
+    return kv + qo + app

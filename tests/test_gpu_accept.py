@@ -1,0 +1,80 @@
+"""GPU acceptance kernels: row top-2, greedy accept + rollback, rejection sampling
+against the oracle restatement with identical uniforms."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+from pilm_b200 import bindings as abi
+from pilm_b200 import ckernel as ck
+from tests._gpu import dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    abi.init()
+    yield
+
+
+def test_top2_matches_torch_first_max():
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((37, 151936), generator=g)
+    x[3, 1000] = x[3, 2000] = 50.0  # tie -> first index
+    top1 = torch.empty(37, dtype=torch.int32, device=dev())
+    margin = torch.empty(37, dtype=torch.float32, device=dev())
+    ck.argmax_top2(x.to(dev()), top1, None, margin)
+    assert top1.cpu().tolist() == torch.argmax(x, -1).tolist()
+    t = torch.topk(x, 2, -1).values
+    assert torch.allclose(margin.cpu(), t[:, 0] - t[:, 1])
+    xb = x.to(torch.bfloat16)
+    ck.argmax_top2(xb.to(dev()), top1, None, None)
+    assert top1.cpu().tolist() == torch.argmax(xb.float(), -1).tolist()
+
+
+def test_greedy_accept_and_rollback():
+    # 4 sequences: full accept, partial, immediate reject, no drafts
+    cu = [0, 4, 8, 11, 12]
+    ids = [5, 10, 11, 12, 6, 20, 21, 22, 7, 30, 31, 8]
+    top1 = [10, 11, 12, 99, 20, 77, 0, 0, 1, 2, 3, 44]
+    ctx = [104, 36, 23, 50]
+    i32 = dict(dtype=torch.int32, device=dev())
+    acc = torch.empty(4, **i32)
+    nxt = torch.empty(4, **i32)
+    c = torch.tensor(ctx, **i32)
+    slots = torch.arange(12, **i32)
+    ck.verify_accept_greedy(4, torch.tensor(ids, **i32), torch.tensor(top1, **i32), torch.tensor(cu, **i32), acc,
+                            nxt, c, slots)
+    assert acc.cpu().tolist() == [3, 1, 0, 0]
+    assert nxt.cpu().tolist() == [99, 77, 1, 44]
+    assert c.cpu().tolist() == [104, 34, 21, 50]
+    s = slots.cpu().tolist()
+    assert s[:4] == [0, 1, 2, 3] and s[4:8] == [4, 5, -1, -1] and s[8:11] == [8, -1, -1] and s[11] == 11
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_rejection_sampling_decisions_match_oracle(seed):
+    g = torch.Generator().manual_seed(seed)
+    B, k, V = 6, 3, 5000
+    logits = torch.randn((B * (k + 1), V), generator=g) * 4
+    uni = torch.rand((B * (k + 1), 2), generator=g)
+    ids = torch.randint(0, V, (B * (k + 1),), generator=g)
+    # make some drafts the argmax so that acceptance happens
+    for r in range(0, B * (k + 1), 2):
+        if (r + 1) % (k + 1):
+            ids[r + 1] = torch.argmax(logits[r])
+    cu = list(range(0, B * (k + 1) + 1, k + 1))
+    i32 = dict(dtype=torch.int32, device=dev())
+    acc = torch.empty(B, **i32)
+    nxt = torch.empty(B, **i32)
+    ctx = torch.full((B,), 100, **i32)
+    ck.verify_accept_rejection(B, logits.to(dev()), ids.to(torch.int32).to(dev()), torch.tensor(cu, **i32),
+                               uni.to(dev()), 0.8, 0.95, acc, nxt, ctx)
+    for b in range(B):
+        rows = slice(cu[b], cu[b + 1])
+        drafts = ids[rows][1:].tolist()
+        a, t = om.rejection_accept(logits[rows], drafts, uni[rows, 0].tolist(), uni[rows, 1].tolist(), 0.8, 0.95)
+        assert int(acc[b]) == a
+        assert int(nxt[b]) == t
+        assert int(ctx[b]) == 100 - (k + 1) + 1 + a

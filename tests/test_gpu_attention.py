@@ -1,0 +1,112 @@
+"""GPU parity of the fused QK-norm/RoPE/KV-append prologue and the paged verify
+attention against the oracle restatement of FullAttention (attention.py:79-139)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+from pilm_b200 import bindings as abi
+from pilm_b200 import ckernel as ck
+from tests._gpu import REL_TOL, bits_of, dev, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    abi.init()
+    yield
+
+
+def run_case(nh, nkv, ctxs, qlens, gated=False, gemma=False, seed=0, num_blocks=None, partial=1.0):
+    g = torch.Generator().manual_seed(seed)
+    cfg = om.Qwen3Config(n_heads=nh, n_kv_heads=nkv, gated=gated, gemma_norm=gemma, partial_rotary=partial)
+    hd, bs = 128, 16
+    B = len(ctxs)
+    pages = [(c + bs - 1) // bs for c in ctxs]
+    nb = num_blocks or (sum(pages) + 8)
+    perm = torch.randperm(nb - 1, generator=g)[: sum(pages)] + 1
+    tables, off = [], 0
+    for p in pages:
+        tables.append([int(x) for x in perm[off:off + p]])
+        off += p
+    maxp = max(pages)
+    kc = torch.randn((nb, bs, nkv, hd), generator=g).to(torch.bfloat16)
+    vc = (torch.randn((nb, bs, nkv, hd), generator=g) * 0.5).to(torch.bfloat16)
+    qrows = cfg.q_rows
+    T = sum(qlens)
+    qkv = (torch.randn((T, qrows + 2 * nkv * hd), generator=g) * 2).to(torch.bfloat16)
+    qn = (torch.randn(hd, generator=g) * 0.1 + (0 if gemma else 1)).to(torch.bfloat16)
+    kn = (torch.randn(hd, generator=g) * 0.1 + (0 if gemma else 1)).to(torch.bfloat16)
+    positions, slots, cu = [], [], [0]
+    for b in range(B):
+        st = ctxs[b] - qlens[b]
+        assert st % bs + qlens[b] <= bs, "verify rows never cross a page (engine.py:399-401)"
+        for j in range(qlens[b]):
+            p = st + j
+            positions.append(p)
+            slots.append(tables[b][p // bs] * bs + p % bs)
+        cu.append(cu[-1] + qlens[b])
+    # oracle, one sequence at a time on a copy of the caches
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    outs = []
+    for b in range(B):
+        rows = slice(cu[b], cu[b + 1])
+        x = qkv[rows]
+        qp, kp, vp = x[:, :qrows], x[:, qrows:qrows + nkv * hd], x[:, qrows + nkv * hd:]
+        outs.append(om.attention_from_proj(cfg, qp, kp, vp, qn, kn, torch.tensor(positions[rows]), kc_ref, vc_ref,
+                                           tables[b], True))
+    ref = torch.cat(outs)
+    # GPU
+    max_pos = max(ctxs) + 1
+    cos, sin = om.rope_tables(cfg, max_pos)
+    d = dev()
+    bt = torch.tensor([t + [0] * (maxp - len(t)) for t in tables], dtype=torch.int32, device=d)
+    desc = ck.attn_desc(num_seqs=B, total_q=T, max_q_len=max(qlens), n_heads=nh, n_kv_heads=nkv, head_dim=hd,
+                        block_size=bs, num_blocks=nb, max_blocks_per_seq=maxp, max_context=max(ctxs),
+                        qkv_stride=qkv.shape[1], rope_rows=max_pos, rot_dim=int(hd * partial), eps=1e-6,
+                        add_one=gemma, output_gate=gated)
+    kc_d, vc_d = kc.to(d), vc.to(d)
+    q_out = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d)
+    gate = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d) if gated else None
+    out = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d)
+    i32 = dict(dtype=torch.int32, device=d)
+    ck.qk_norm_rope_kv_append(desc, qkv.to(d), qn.to(d), kn.to(d), cos.to(d), sin.to(d),
+                              torch.tensor(positions, **i32), torch.tensor(slots, **i32), kc_d, vc_d, q_out, gate)
+    ck.paged_attention_verify(desc, q_out, kc_d, vc_d, bt, torch.tensor(cu, **i32),
+                              torch.tensor(ctxs, **i32), gate, out)
+    torch.cuda.synchronize()
+    # appended K/V: V is copied exactly; K within one bf16 rounding of the oracle
+    sl = torch.tensor(slots)
+    kv_ref_k = kc_ref.view(-1, nkv, hd)[sl].float()
+    kv_got_k = kc_d.view(-1, nkv, hd)[sl.to(d)].float().cpu()
+    assert rel_err(kv_got_k.numpy(), kv_ref_k.numpy()) <= REL_TOL
+    assert torch.equal(vc_d.view(-1, nkv, hd)[sl.to(d)].cpu(), vc_ref.view(-1, nkv, hd)[sl])
+    e = rel_err(out.float().cpu().numpy(), ref.float().numpy())
+    assert e <= REL_TOL, e
+    return e
+
+
+def test_verify_rows_gqa4_k2():
+    run_case(8, 2, ctxs=[40, 99, 16, 131], qlens=[3, 3, 1, 3])
+
+
+def test_verify_rows_gqa2_k3_gated_gemma():
+    run_case(4, 2, ctxs=[21, 64, 300], qlens=[4, 2, 4], gated=True, gemma=True, seed=1)
+
+
+def test_long_context_split_kv():
+    run_case(8, 2, ctxs=[2051, 4100], qlens=[3, 2], seed=2)
+
+
+def test_prefill_chunk_rows_two_mtiles():
+    # 16-token chunk with 4 query heads per KV head: 64 rows -> 2 row chunks of 32
+    run_case(8, 2, ctxs=[16, 45], qlens=[16, 13], seed=3)
+
+
+def test_partial_rotary():
+    run_case(4, 2, ctxs=[34, 51], qlens=[2, 3], seed=4, partial=0.25)
+
+
+def test_qwen3_8b_head_layout():
+    run_case(32, 8, ctxs=[531, 1000], qlens=[3, 3], seed=5)

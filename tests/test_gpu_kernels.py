@@ -1,0 +1,115 @@
+"""GPU parity of the quantized linears, norms and SwiGLU against the reference's
+golden outputs and the pinned oracle, through the C ABI (pilm_b200.bindings)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import kernels as ok
+from pilm_b200 import bindings as abi
+from pilm_b200 import ckernel as ck
+from tests import _golden as G
+from tests._gpu import REL_TOL, assert_bf16_close, bf16_from_bits, bits_of, dev, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    abi.init()
+    yield
+
+
+@pytest.fixture(scope="module")
+def kz():
+    return G.load("kernels.npz")
+
+
+def _shapes(kz):
+    return sorted({k.split(".")[0] for k in kz.files if k.startswith("s") and k.endswith(".shape")})
+
+
+def _t(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev())
+    return t if dtype is None else t.to(dtype)
+
+
+def test_linears_vs_reference_golden(kz):
+    for s in _shapes(kz):
+        x = bf16_from_bits(kz[f"{s}.x"])
+        for grp, fn in ((128, ck.linear_w4a16g128_bf16), (32, ck.linear_w4a16g32_bf16)):
+            y = fn(x, _t(kz[f"{s}.w4g{grp}.qw"]), _t(kz[f"{s}.w4g{grp}.s"]))
+            assert_bf16_close(bits_of(y), kz[f"{s}.w4g{grp}.y"], ulp_frac=0.99)
+        y = ck.linear_w4a16_bf16(x, _t(kz[f"{s}.w4row.qw"]), _t(kz[f"{s}.w4row.s"]))
+        assert_bf16_close(bits_of(y), kz[f"{s}.w4row.y"], ulp_frac=0.99)
+        y = ck.linear_w8a16_bf16(x, _t(kz[f"{s}.w8.qw"]), _t(kz[f"{s}.w8.s"]))
+        assert_bf16_close(bits_of(y), kz[f"{s}.w8a16.y"], ulp_frac=0.99)
+        y = ck.linear_w8a32(_t(kz[f"{s}.xf"]), _t(kz[f"{s}.w8.qw"]), _t(kz[f"{s}.w8.s"]))
+        assert rel_err(y.cpu().numpy(), kz[f"{s}.w8a32.y"]) <= 1e-5
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 12, 16, 24, 32, 48, 63, 64, 96, 130])
+@pytest.mark.parametrize("NK", [(256, 512), (384, 1024), (200, 4096)])
+def test_w4g128_vs_oracle_all_regimes(M, NK):
+    """Every GEMV tile configuration (M <= 8, 16, 32, 64) and the M >= 64 path,
+    including split-K (K=4096) and ragged N."""
+    N, K = NK
+    rng = np.random.default_rng(M * 7 + N)
+    x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    qw, s = ok.quantize_i4_grouped(w, 128)
+    ref = ok.linear_w4a16g_bf16(x, qw, s, 128)
+    y = ck.linear_w4a16g128_bf16(bf16_from_bits(x), _t(qw), _t(s))
+    assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
+    qr, sr = ok.quantize_i4_per_row(w)
+    ref = ok.linear_w4a16_bf16(x, qr, sr)
+    y = ck.linear_w4a16_bf16(bf16_from_bits(x), _t(qr), _t(sr))
+    assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
+
+
+def test_ragged_k_falls_back_and_matches():
+    rng = np.random.default_rng(3)
+    for (M, N, K) in [(3, 17, 130), (1, 5, 77), (6, 33, 200)]:
+        x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        qw, s = ok.quantize_i4_grouped(w, 128)
+        y = ck.linear_w4a16g128_bf16(bf16_from_bits(x), _t(qw), _t(s))
+        assert_bf16_close(bits_of(y), ok.linear_w4a16g_bf16(x, qw, s, 128), ulp_frac=0.99)
+
+
+def test_rmsnorm_and_swiglu_vs_golden(kz):
+    for s in _shapes(kz):
+        for add_one in (0, 1):
+            y = ck.rmsnorm_bf16(bf16_from_bits(kz[f"{s}.x"]), bf16_from_bits(kz[f"{s}.norm.w"]), 1e-6, bool(add_one))
+            assert_bf16_close(bits_of(y), kz[f"{s}.norm{add_one}.y"], ulp_frac=0.99)
+    y = ck.swiglu_bf16(bf16_from_bits(kz["swiglu.g"]), bf16_from_bits(kz["swiglu.u"]))
+    assert_bf16_close(bits_of(y), kz["swiglu.y"], ulp_frac=0.99)
+    H, I, K = [int(v) for v in kz["mlp.dims"]]
+    y = ck.swiglu_w4a16_bf16(bf16_from_bits(kz["mlp.x"]), _t(kz["mlp.gu_qw"]), _t(kz["mlp.gu_s"]),
+                             _t(kz["mlp.d_qw"]), _t(kz["mlp.d_s"]), I)
+    assert_bf16_close(bits_of(y), kz["mlp.y"], ulp_frac=0.98)
+
+
+def test_fused_swiglu_any_m_vs_oracle():
+    rng = np.random.default_rng(5)
+    H, I, K, M = 256, 384, 512, 5
+    x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    gq, gs = ok.quantize_i4_per_row((rng.standard_normal((2 * I, K)) * 0.02).astype(np.float32))
+    dq, ds = ok.quantize_i4_per_row((rng.standard_normal((H, I)) * 0.02).astype(np.float32))
+    ref = np.concatenate([ok.swiglu_w4a16_bf16(x[m], gq, gs, dq, ds, I) for m in range(M)])
+    y = ck.swiglu_w4a16_bf16(bf16_from_bits(x), _t(gq), _t(gs), _t(dq), _t(ds), I)
+    assert_bf16_close(bits_of(y), ref, ulp_frac=0.98)
+
+
+def test_gemm_known_answer_and_argmax():
+    a = torch.tensor([[1, 2], [3, 4]], dtype=torch.float32, device=dev())
+    b = torch.tensor([[5, 6], [7, 8]], dtype=torch.float32, device=dev())
+    assert ck.gemm_f32(a, b).cpu().tolist() == [[19, 22], [43, 50]]
+    rng = np.random.default_rng(9)
+    x = ok.f32_to_bf16(rng.standard_normal((1, 256)).astype(np.float32))
+    q8, s8 = ok.quantize_i8_per_row((rng.standard_normal((1000, 256)) * 0.02).astype(np.float32))
+    idx_ref, _ = ok.linear_w8a16_bf16_argmax(x, q8, s8)
+    assert ck.linear_w8a16_bf16_argmax(bf16_from_bits(x), _t(q8), _t(s8)) == idx_ref
+
+
+def test_sync_mode_reports_ok_and_errors_are_strings():
+    assert abi.lib().ekernel_synchronize() == 0

@@ -1,0 +1,124 @@
+"""End-to-end verify step on the GPU against the reference's golden traces:
+logits within 1e-2 relative, greedy accept counts / next tokens identical (near
+ties excused), page tables and slots exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+from pilm_b200 import bindings as abi
+from pilm_b200 import ckernel as ck
+from pilm_b200.engine import MTPVerifyEngine
+from pilm_b200.qwen3 import PagedKVCache, Qwen3Shape, Qwen3Verifier, Qwen3Weights, VerifyBatch
+from tests import _golden as G
+from tests._gpu import REL_TOL, argmax_agrees, bf16_from_bits, dev, rel_err
+
+pytestmark = pytest.mark.gpu
+BF16_VARIANTS = ["qwen3_w4g128", "qwen35_w4g128", "qwen3_w4g128_gqa4"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    abi.init()
+    yield
+
+
+def shape_of(cfg: om.Qwen3Config) -> Qwen3Shape:
+    return Qwen3Shape(hidden=cfg.hidden, layers=cfg.layers, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads,
+                      head_dim=cfg.head_dim, intermediate=cfg.intermediate, vocab=cfg.vocab, eps=cfg.eps,
+                      rope_theta=cfg.rope_theta, partial_rotary=cfg.partial_rotary, gated=cfg.gated,
+                      gemma_norm=cfg.gemma_norm, block_size=cfg.block_size)
+
+
+def build(variant):
+    z = G.load(f"model_{variant}.npz")
+    cfg, seed = G.model_config(z)
+    ckpt = om.make_checkpoint(cfg, seed)
+    w = Qwen3Weights.from_checkpoint(shape_of(cfg), ckpt, dev())
+    return z, cfg, ckpt, w
+
+
+def test_device_quantizer_matches_reference_format():
+    z, cfg, ckpt, w = build("qwen3_w4g128")
+    ref = om.quantize_linear(ckpt["l0.down"], "w4g128")
+    assert np.array_equal(w.layers[0]["down"].qweight.cpu().numpy(), ref["qweight"])
+    assert np.array_equal(w.layers[0]["down"].scales.cpu().numpy(), ref["scales"])
+
+
+@pytest.mark.parametrize("variant", BF16_VARIANTS)
+def test_verify_step_from_reference_kv(variant):
+    z, cfg, ckpt, w = build(variant)
+    B = G.num_seqs(z)
+    kv = PagedKVCache(w.shape, 32, dev())
+    for li in range(cfg.layers):
+        kv.k[li].copy_(bf16_from_bits(z[f"kv.k{li}"]))
+        kv.v[li].copy_(bf16_from_bits(z[f"kv.v{li}"]))
+    ver = Qwen3Verifier(w, kv, max_rows=64, max_pos=256, device=dev())
+    ids, pos, slots, cu, tables, ctx = [], [], [], [0], [], []
+    for b in range(B):
+        ids += G.ilist(z[f"b{b}.verify_ids"])
+        p = G.ilist(z[f"b{b}.positions"])
+        pos += p
+        slots += G.ilist(z[f"b{b}.slots"])
+        cu.append(cu[-1] + len(p))
+        tables.append(G.ilist(z[f"b{b}.block_ids"]))
+        ctx.append(p[-1] + 1)
+    maxp = max(len(t) for t in tables)
+    i32 = dict(dtype=torch.int32, device=dev())
+    batch = VerifyBatch(torch.tensor(ids, **i32), torch.tensor(pos, **i32), torch.tensor(slots, **i32),
+                        torch.tensor([t + [0] * (maxp - len(t)) for t in tables], **i32), torch.tensor(cu, **i32),
+                        torch.tensor(ctx, **i32), max(cu[i + 1] - cu[i] for i in range(B)), max(ctx))
+    acc = torch.empty(B, **i32)
+    nxt = torch.empty(B, **i32)
+    ctx_out = batch.context_lens.clone()
+    logits = ver.verify_greedy(batch, acc, nxt, ctx_out).float().cpu()
+    top1 = ver.top1[:batch.total_q].cpu()
+    for b in range(B):
+        ref = z[f"b{b}.logits"]
+        got = logits[cu[b]:cu[b + 1]].numpy()
+        assert rel_err(got, ref) <= REL_TOL
+        assert argmax_agrees(top1[cu[b]:cu[b + 1]].tolist(), ref)
+        ref_acc, ref_next = G.ilist(z[f"b{b}.accept"])
+        if argmax_agrees([int(t) for t in top1[cu[b]:cu[b + 1]]], ref) and \
+                top1[cu[b]:cu[b + 1]].tolist() == torch.as_tensor(ref).argmax(-1).tolist():
+            assert int(acc[b]) == ref_acc and int(nxt[b]) == ref_next
+        assert int(ctx_out[b]) == int(z[f"b{b}.num_computed_after"][0])
+
+
+@pytest.mark.parametrize("variant", ["qwen3_w4g128", "qwen35_w4g128"])
+def test_engine_prefill_and_verify_end_to_end(variant):
+    """Prompts prefilled on the GPU in page-aligned chunks, first token and the
+    verify step (golden drafts) compared with the reference trace."""
+    z, cfg, ckpt, w = build(variant)
+    B = G.num_seqs(z)
+    kv = PagedKVCache(w.shape, 32, dev())
+    ver = Qwen3Verifier(w, kv, max_rows=128, max_pos=256, device=dev())
+    eng = MTPVerifyEngine(ver, num_blocks=32, max_model_len=256, max_num_batched_tokens=16)
+    sids = [eng.add_request(G.ilist(z[f"b{b}.prompt"]), max_new_tokens=64) for b in range(B)]
+    first = eng.prefill()
+    res = eng.verify_step({sid: G.ilist(z[f"b{b}.drafts"]) for b, sid in enumerate(sids)})
+    for b, sid in enumerate(sids):
+        # same budget as the reference engine -> identical page tables
+        assert eng.sched.seqs[sid].pages == G.ilist(z[f"b{b}.block_ids"])
+    agree = 0
+    for b, sid in enumerate(sids):
+        if first[sid] != int(z[f"b{b}.first_token"][0]):
+            continue
+        r = next(x for x in res if x.seq_id == sid)
+        assert r.drafts == G.ilist(z[f"b{b}.drafts"])
+        agree += int([r.accepted, r.next_token] == G.ilist(z[f"b{b}.accept"]))
+    assert agree >= B - 1
+
+
+def test_verify_step_is_deterministic():
+    z, cfg, ckpt, w = build("qwen3_w4g128")
+    outs = []
+    for _ in range(2):
+        kv = PagedKVCache(w.shape, 32, dev())
+        ver = Qwen3Verifier(w, kv, max_rows=128, max_pos=256, device=dev())
+        eng = MTPVerifyEngine(ver, num_blocks=32, max_model_len=256)
+        sids = [eng.add_request(G.ilist(z[f"b{b}.prompt"]), max_new_tokens=64) for b in range(4)]
+        eng.prefill()
+        res = eng.verify_step({sid: G.ilist(z[f"b{b}.drafts"]) for b, sid in enumerate(sids)})
+        outs.append([(r.accepted, r.next_token) for r in res])
+    assert outs[0] == outs[1]

@@ -1,0 +1,81 @@
+"""Host paging logic against the reference scheduler's page-table trace."""
+import numpy as np
+
+from pilm_b200.engine import draft_limit
+from pilm_b200.paging import PagePool, PageTableManager, Sequence, VerifyScheduler
+from tests import _golden as G
+
+
+def test_page_tables_match_reference_scheduler_trace():
+    """Replays the request mix of make_golden.paging_trace through VerifyScheduler:
+    every scheduled chunk (sequence, size, start, prefill flag, page table) and every
+    preemption equals the reference Scheduler/KVCacheManager/BlockPool output."""
+    z = G.load("paging.npz")
+    nblocks, bs = [int(x) for x in z["pool"]]
+    rng = np.random.default_rng(7)
+    mgr = PageTableManager(nblocks, bs)
+    sched = VerifyScheduler(mgr, max_num_batched_tokens=16, max_num_seqs=8)
+    seqs = [Sequence(i + 1, [int(t) for t in rng.integers(0, 1000, int(n))], 6, -1) for i, n in enumerate(z["lens"])]
+    for s in seqs:
+        sched.add(s)
+    rows = []
+    for step in range(40):
+        out = sched.schedule()
+        if out.is_empty:
+            break
+        gen = {}
+        for c in out.scheduled:
+            rows.append([step, c.seq_id, c.num_tokens, c.positions[0], int(c.is_prefill)] + (c.pages + [-1] * 8)[:8])
+            s = sched.seqs[c.seq_id]
+            if not c.is_prefill_chunk and s.num_computed >= len(s.prompt):
+                gen[c.seq_id] = [int(rng.integers(0, 1000))]
+        for pid in out.preempted:
+            rows.append([step, -pid, 0, 0, 0] + [-1] * 8)
+        sched.update(out, gen)
+    assert np.array_equal(np.array(rows, np.int64), z["rows"])
+
+
+def test_pool_free_order_is_lifo_for_unhashed_pages():
+    p = PagePool(6)
+    a = p.take(3)
+    assert a == [1, 2, 3]
+    p.release([1, 2])
+    assert p.take(2) == [2, 1]
+
+
+def test_verify_rows_never_cross_a_page():
+    mgr = PageTableManager(64, 16)
+    for computed in range(0, 64):
+        for k in range(0, 5):
+            n = draft_limit(computed, 16, 100, k)
+            assert (computed % 16) + 1 + n <= 16
+    s = Sequence(0, list(range(31)))
+    s.num_computed = 31
+    assert mgr.allocate(s, 1) == [1, 2]
+
+
+def test_prefill_schedule_and_verify_pages_match_reference_engine():
+    """With the reference engine's one-page token budget (engine.py:218) the prefill
+    chunk schedule and the page tables of the verify step equal the reference's."""
+    for v in G.MODEL_VARIANTS:
+        z = G.load(f"model_{v}.npz")
+        mgr = PageTableManager(32, 16)
+        sch = VerifyScheduler(mgr, max_num_batched_tokens=16, max_num_seqs=1 << 20, max_model_len=256,
+                              max_pages_per_seq=16)
+        seqs = [Sequence(b, G.ilist(z[f"b{b}.prompt"]), 64) for b in range(G.num_seqs(z))]
+        for s in seqs:
+            sch.add(s)
+        chunks = []
+        while sch.waiting or any(s.is_prefill for s in sch.running):
+            for c in sch.schedule().scheduled:
+                chunks.append([c.seq_id, c.positions[0], c.num_tokens])
+        assert chunks == z["prefill_chunks"].tolist()
+        for s in seqs:
+            s.tokens.append(int(z[f"b{s.seq_id}.first_token"][0]))
+            d = G.ilist(z[f"b{s.seq_id}.drafts"])
+            assert len(d) == draft_limit(s.num_computed, 16, 64, 3)
+            s.tokens.extend(d)
+            mgr.allocate(s, 1 + len(d), 16)
+            assert s.pages == G.ilist(z[f"b{s.seq_id}.block_ids"])
+            slots = [s.slot(p, 16) for p in range(s.num_computed, s.num_computed + 1 + len(d))]
+            assert slots == G.ilist(z[f"b{s.seq_id}.slots"])
