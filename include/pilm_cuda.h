@@ -262,6 +262,26 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
                                    const int32_t *cu_q, const int32_t *context_lens, const uint16_t *gate,
                                    uint16_t *out);
 
+/* Allocation-free variant of ekernel_paged_attention_verify.  It has no counterpart in
+ * the reference.  It is for callers that cannot let a kernel library allocate GPU
+ * memory: an engine whose allocator owns the device and forbids side allocations, a
+ * serving loop that must never hit cudaMalloc's implicit synchronisation, or a host
+ * language that only passes in buffers it already owns.  Same arguments and result as
+ * ekernel_paged_attention_verify; the split-KV partials live in a fixed 8 MiB device
+ * array inside the library (held on every GPU that loads the library until exit)
+ * instead of library-allocated scratch, and no allocator is called.
+ *  - A call whose partials would exceed 8 MiB (splits x total_q x n_heads x 520 bytes)
+ *    is rejected with ECPU_ERR_PARAM and a message naming the needed size.
+ *  - The first call on each device looks up the array's device address with that
+ *    device current; make that first call before any stream capture.
+ *  - All calls share the one array and it keeps the previous call's contents (each
+ *    call resets the records it reads): calls that overlap on the GPU race, so issue
+ *    them on one stream or otherwise ordered. */
+int ekernel_paged_attention_verify_noalloc(const ekernel_paged_attn_desc_t *desc, const uint16_t *q,
+                                           const uint16_t *k_cache, const uint16_t *v_cache,
+                                           const int32_t *block_table, const int32_t *cu_q,
+                                           const int32_t *context_lens, const uint16_t *gate, uint16_t *out);
+
 typedef struct {
     size_t num_seqs; /* B */
     size_t total_q;  /* logit rows */

@@ -45,6 +45,7 @@ KERNEL_SYMBOLS = [
     "ekernel_silu_mul_bf16",
     "ekernel_qk_norm_rope_kv_append",
     "ekernel_paged_attention_verify",
+    "ekernel_paged_attention_verify_noalloc",
     "ekernel_argmax_top2_f32",
     "ekernel_argmax_top2_bf16",
     "ekernel_verify_accept_greedy",
@@ -176,6 +177,7 @@ def _configure(lib) -> None:
     lib.ekernel_silu_mul_bf16.argtypes = [_vp, _sz, _sz, _vp]
     lib.ekernel_qk_norm_rope_kv_append.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 11
     lib.ekernel_paged_attention_verify.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 8
+    lib.ekernel_paged_attention_verify_noalloc.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 8
     lib.ekernel_argmax_top2_f32.argtypes = [ctypes.POINTER(AcceptDesc), _vp, _vp, _vp, _vp]
     lib.ekernel_argmax_top2_bf16.argtypes = [ctypes.POINTER(AcceptDesc), _vp, _vp, _vp, _vp]
     lib.ekernel_verify_accept_greedy.argtypes = [ctypes.POINTER(AcceptDesc)] + [_vp] * 7

@@ -16,9 +16,16 @@
 //                 computes S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in,
 //                 fp32 accumulate) and keeps an fp32 online softmax; warps then merge.
 //   attn_merge    combines split partials (m, l, O) and applies the output gate.
+#include <mutex>
+
 #include "common.cuh"
 
 using namespace pilm;
+
+// Fixed device scratch for ekernel_paged_attention_verify_noalloc (see below).  Every
+// GPU that loads this library holds these bytes until the process exits.
+constexpr size_t kNoAllocAttnScratchBytes = (size_t)8 << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_noalloc_attn_scratch[kNoAllocAttnScratchBytes];
 
 namespace {
 
@@ -575,3 +582,129 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot let a kernel library allocate GPU memory: an engine whose
+// allocator owns the whole device and forbids side allocations, a caller that must
+// never hit cudaMalloc's implicit device-wide synchronisation on its serving path,
+// or a host written in another language that only hands over buffers it already
+// owns.  For them ekernel_paged_attention_verify_noalloc takes the same inputs and
+// outputs as ekernel_paged_attention_verify but keeps its split-KV partials in
+// g_noalloc_attn_scratch, a fixed 8 MiB array compiled into the library, and calls
+// no allocator at all.  The host cannot pass g_noalloc_attn_scratch itself to a
+// kernel (in host code that name is only a host-side stand-in), so the device address
+// is looked up once per device with cudaGetSymbolAddress and cached here.
+// ---------------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+void *g_noalloc_addr[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_attn_scratch on the current device (looked up on the
+// first call for that device, with that device current).
+int noalloc_scratch_address(void **out, const char *what) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    PILM_REQUIRE(e == cudaSuccess && dev >= 0 && dev < kNoAllocMaxDevices, ECPU_ERR_DEVICE,
+                 "%s: no usable current device (%s)", what, cudaGetErrorString(e));
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_noalloc_attn_scratch);
+        PILM_REQUIRE(e == cudaSuccess && ptr, ECPU_ERR_DEVICE, "%s: cudaGetSymbolAddress failed: %s", what,
+                     cudaGetErrorString(e));
+        g_noalloc_addr[dev] = ptr;
+    }
+    *out = g_noalloc_addr[dev];
+    return ECPU_OK;
+}
+
+}  // namespace
+
+extern "C" int ekernel_paged_attention_verify_noalloc(const ekernel_paged_attn_desc_t *desc, const uint16_t *q,
+                                                      const uint16_t *k_cache, const uint16_t *v_cache,
+                                                      const int32_t *block_table, const int32_t *cu_q,
+                                                      const int32_t *context_lens, const uint16_t *gate,
+                                                      uint16_t *out) {
+    const char *what = "ekernel_paged_attention_verify_noalloc";
+    int rc = check_desc(desc, what);
+    if (rc != ECPU_OK) return rc;
+    PILM_REQUIRE(q && k_cache && v_cache && block_table && cu_q && context_lens && out, ECPU_ERR_PARAM,
+                 "%s: null argument", what);
+    PILM_REQUIRE(!desc->output_gate || gate, ECPU_ERR_PARAM, "%s: gate required when output_gate", what);
+    if (desc->total_q == 0 || desc->num_seqs == 0) return ECPU_OK;
+
+    AttnParams p;
+    p.q = (const __nv_bfloat16 *)q;
+    p.kc = (const __nv_bfloat16 *)k_cache;
+    p.vc = (const __nv_bfloat16 *)v_cache;
+    p.block_table = block_table;
+    p.cu_q = cu_q;
+    p.ctx = context_lens;
+    p.gate = desc->output_gate ? (const __nv_bfloat16 *)gate : nullptr;
+    p.out = (__nv_bfloat16 *)out;
+    p.nh = (int)desc->n_heads;
+    p.nkv = (int)desc->n_kv_heads;
+    p.gsz = p.nh / p.nkv;
+    p.max_blocks = (int)desc->max_blocks_per_seq;
+    p.num_blocks = (int)desc->num_blocks;
+    p.total_q = (int)desc->total_q;
+    p.scale = (float)(1.0 / sqrt((double)kHD));
+
+    // the same split choice as ekernel_paged_attention_verify, so both give the same result
+    const int rows = (int)(desc->max_q_len ? desc->max_q_len : 1) * p.gsz;
+    const int MT = rows > 16 ? 2 : 1;
+    const int row_chunks = (rows + 16 * MT - 1) / (16 * MT);
+    const int max_pages = (int)((desc->max_context + 15) / 16);
+    const int base = (int)desc->num_seqs * p.nkv * row_chunks;
+    const int target = 2 * num_sms() * 2;
+    int splits = (target + base - 1) / base;
+    int max_splits = max_pages / (2 * kWarps);
+    if (max_splits < 1) max_splits = 1;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+    p.pages_per_split = (max_pages + splits - 1) / splits;
+    if (p.pages_per_split < 1) p.pages_per_split = 1;
+    splits = (max_pages + p.pages_per_split - 1) / p.pages_per_split;
+    if (splits < 1) splits = 1;
+    p.splits = splits;
+    p.row_chunk = 16 * MT;
+    p.part_o = nullptr;
+    p.part_ml = nullptr;
+    if (splits > 1) {
+        const size_t n_rec = (size_t)splits * desc->total_q * desc->n_heads;
+        const size_t need = n_rec * (kHD + 2) * sizeof(float);
+        PILM_REQUIRE(need <= kNoAllocAttnScratchBytes, ECPU_ERR_PARAM,
+                     "%s: this call needs %zu bytes of split-KV scratch (%d splits x %zu rows x %zu heads) but the "
+                     "allocation-free variant holds at most %zu bytes; use ekernel_paged_attention_verify",
+                     what, need, splits, desc->total_q, desc->n_heads, kNoAllocAttnScratchBytes);
+        void *base_ptr = nullptr;
+        rc = noalloc_scratch_address(&base_ptr, what);
+        if (rc != ECPU_OK) return rc;
+        p.part_o = (float *)base_ptr;
+        p.part_ml = p.part_o + n_rec * kHD;
+        // the array keeps the previous call's contents: reset every (m, l) record
+        attn_clear_ml<<<(int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096), 256, 0,
+                        stream()>>>(p.part_ml, n_rec * 2);
+        rc = check_launch(what);
+        if (rc != ECPU_OK) return rc;
+    }
+    const size_t ring = (size_t)kWarps * kStages * 2 * kPageBytes;
+    const size_t mergebuf = (size_t)kWarps * 16 * MT * (kHD + 2) * sizeof(float);
+    const size_t smem = ring > mergebuf ? ring : mergebuf;
+    dim3 grid(splits, p.nkv * row_chunks, (unsigned)desc->num_seqs);
+    if (MT == 1) {
+        cudaFuncSetAttribute(attn_verify<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_verify<1><<<grid, kWarps * 32, smem, stream()>>>(p);
+    } else {
+        cudaFuncSetAttribute(attn_verify<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_verify<2><<<grid, kWarps * 32, smem, stream()>>>(p);
+    }
+    rc = check_launch(what);
+    if (rc != ECPU_OK || splits == 1) return rc;
+    attn_merge<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
+    return check_launch(what);
+}
