@@ -116,6 +116,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     dev = torch.device("cuda", local_rank)
     bindings.init()
     shape = QWEN3_8B
+    if args.layers:  # reduced-depth case for profiling captures
+        from dataclasses import replace
+        shape = replace(shape, layers=args.layers)
+    SEQS, PROMPT = args.seqs, args.prompt
     seed = 1234 + rank
     weights = Qwen3Weights.synthetic(shape, seed, dev)
     pages_per_seq = (PROMPT + GEN_HEADROOM + PAGE - 1) // PAGE
@@ -168,10 +172,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     sampler.start()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -189,7 +195,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     for s in seqs:  # undo the resident step's draft rows
         del s.tokens[s.num_computed + 1:]
     h2d = 0
-    for _ in range(max(1, args.warmup)):
+    e2e_steps = 0 if args.no_e2e else args.steps
+    for _ in range(max(1, args.warmup) if e2e_steps else 0):
         eng.verify_step(drafts_for_step())
     torch.cuda.synchronize()
     if world > 1:
@@ -199,14 +206,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         rows_before = eng.stats["verified_rows"]
         eng.verify_step(drafts_for_step())
         e2e_rows += eng.stats["verified_rows"] - rows_before
     e_end.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e_start.elapsed_time(e_end) / args.steps
-    wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    e2e_ms = e_start.elapsed_time(e_end) / max(1, e2e_steps)
+    wall_ms = (time.perf_counter() - t0) * 1e3 / max(1, e2e_steps)
     e2e_t = torch.tensor([e2e_ms, e2e_rows], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(e2e_t[:1], op=dist.ReduceOp.MAX)
@@ -241,6 +248,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         except Exception:
             traffic = None
     cpu = cpu_baseline_sample(args) if not args.no_cpu else None
+    full = (SEQS, PROMPT, shape.layers) == (32, 8192, 36)
     value = rows_per_step * world / (ms_max * 1e-3)
     line = {
         "metric": METRIC,
@@ -256,14 +264,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "dtype": "bf16 activations x int4 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init weights, random prompt KV pages, random drafts)",
         "config": {
-            "workload": "Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])",
-            "seqs_per_gpu": SEQS, "prompt_len": PROMPT, "draft_k": K_DRAFT, "rows_per_step": rows_per_step,
+            "workload": ("Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])" if full else
+                         f"reduced profiling case: {shape.layers} layers, {SEQS} seqs x {PROMPT} tokens"),
+            "seqs_per_gpu": SEQS, "prompt_len": PROMPT, "layers": shape.layers, "draft_k": K_DRAFT,
+            "rows_per_step": rows_per_step,
             "page_size": PAGE, "parallelism": f"replicas x{world}",
             "l2": "inputs larger than L2 (about 40 GB KV + 4 GB weights read per step)",
         },
         "per_gpu": round(value / world, 2),
         "e2e": {
-            "value": round(e2e_rows_all / args.steps / (e2e_ms_max * 1e-3), 2),
+            "value": round(e2e_rows_all / max(1, e2e_steps) / (e2e_ms_max * 1e-3), 2) if e2e_steps else None,
             "unit": "verified tok/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
@@ -423,6 +433,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end engine leg (profiling runs)")
+    ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per GPU (default: the BASELINE config)")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens per sequence")
+    ap.add_argument("--layers", type=int, default=0, help="decoder layers (0 = all 36); profiling only")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
