@@ -144,6 +144,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         return {s.seq_id: torch.randint(0, shape.vocab, (K_DRAFT,), generator=g).tolist() for s in eng.sched.running}
 
     # ---- device-resident verify step (value) -------------------------------------
+    from pilm_b200.qwen3 import VerifyGraph
     seqs = list(eng.sched.running)
     d0 = drafts_for_step()
     for s in seqs:
@@ -151,21 +152,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         eng.pages.allocate(s, 1 + K_DRAFT, eng.max_pages)
     starts = [s.num_computed for s in seqs]
     batch = eng.build_batch(seqs, starts, [1 + K_DRAFT] * len(seqs))
-    i32 = dict(dtype=torch.int32, device=dev)
-    acc = torch.empty(len(seqs), **i32)
-    nxt = torch.empty(len(seqs), **i32)
-    ctx_work = batch.context_lens.clone()
     stream = torch.cuda.current_stream()
+    graph = VerifyGraph(ver, len(seqs), batch.total_q, batch.max_q_len, eng.max_pages, eng.max_model_len)
+    graph.load(batch)
+    graph.capture()
 
     def step():
-        ctx_work.copy_(batch.context_lens, non_blocking=True)
-        ver.verify_greedy(batch, acc, nxt, ctx_work)
+        graph.replay()
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    ver.op_timing = True  # per-kernel CUDA events around attention / linears during the timed steps
-    ver.op_events.clear()
     sampler = ClockSampler(local_rank)
     if world > 1:
         dist.barrier()
@@ -182,21 +179,25 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    ver.op_timing = False
     ms = e0.elapsed_time(e1) / args.steps
-    op_ms = ver.collect_op_times()
     rows_per_step = batch.total_q
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
+    # per-kernel timings for the rooflines (CUDA events, same stream, back-to-back launches)
+    op_ms = {"attention": ver.time_attention(graph.batch)}
+    op_ms["attention_total"] = op_ms["attention"] * shape.layers
+    op_ms.update(ver.time_linears(rows_per_step))
 
     # ---- end to end through the engine API (e2e) -----------------------------------
     for s in seqs:  # undo the resident step's draft rows
         del s.tokens[s.num_computed + 1:]
     h2d = 0
     e2e_steps = 0 if args.no_e2e else args.steps
-    for _ in range(max(1, args.warmup) if e2e_steps else 0):
+    # at least one page of warm-up steps, so every verify-row count the page-boundary cap
+    # produces (k+1 rows per sequence down to 1) has its graph captured before timing
+    for _ in range(max(args.warmup, PAGE) if e2e_steps else 0):
         eng.verify_step(drafts_for_step())
     torch.cuda.synchronize()
     if world > 1:
@@ -306,7 +307,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "frac": round(step_bytes / (ms_max * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
         },
         "op_ms_per_step": {k: round(v, 4) for k, v in op_ms.items()},
-        "gpu_launches": ver.launches_per_step() * args.steps,
+        "gpu_launches": graph.launches * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
         "acceptance": {"attempts": eng.stats["attempts"], "accepts": eng.stats["accepts"]},

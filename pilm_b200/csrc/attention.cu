@@ -175,7 +175,7 @@ struct AttnParams {
     float *part_o;               // [splits, total_q, nh, 128]
     float *part_ml;              // [splits, total_q, nh, 2]
     int nh, nkv, gsz, max_blocks, num_blocks, total_q;
-    int splits, pages_per_split, row_chunk;  // rows per CTA = 16 * MT
+    int splits, pages_per_split, row_chunk;  // rows per CTA = 16 * MT; pages_per_split: host sizing only
     float scale;                 // rne_bf16-compatible fp32 value of 1/sqrt(head_dim)
 };
 
@@ -196,9 +196,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const AttnParams p
     const int row_base = rc * 16 * MT;
     if (row_base >= R || q_len <= 0 || ctx <= 0) return;
     const int p0 = ctx - q_len;  // position of the first verify row
+    // every sequence divides its own pages evenly over the splits, so the split count
+    // (chosen on the host from a context bound) never leaves a long sequence's work on
+    // one CTA or a short one spread thin
     const int P = (ctx + 15) >> 4;
-    const int pg0 = split * p.pages_per_split;
-    const int pg1 = min(P, pg0 + p.pages_per_split);
+    const int pps = (P + p.splits - 1) / p.splits;
+    const int pg0 = split * pps;
+    const int pg1 = min(P, pg0 + pps);
     // the last row of this CTA sees keys up to p0 + jmax
     const int jmax = min(q_len - 1, (row_base + 16 * MT - 1) / p.gsz);
     const int pg_vis = min(pg1, ((p0 + jmax) >> 4) + 1);

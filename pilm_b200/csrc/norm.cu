@@ -73,6 +73,73 @@ __global__ void add_rmsnorm_kernel(__nv_bfloat16 *__restrict__ res, const __nv_b
     }
 }
 
+// Same semantics as add_rmsnorm_kernel, one CTA (256 threads) per row with the row
+// held in registers: 16-byte loads/stores, one read of the residual and delta, one
+// block reduction.  n % 8 == 0 and n <= 256 * 8 * VPT.
+template <int VPT>
+__global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__restrict__ res,
+                                                              const __nv_bfloat16 *__restrict__ delta,
+                                                              const __nv_bfloat16 *__restrict__ w, int n, float eps,
+                                                              int add_one, __nv_bfloat16 *__restrict__ out) {
+    __shared__ float red[8];
+    const int row = blockIdx.x;
+    __nv_bfloat16 *r = res + (size_t)row * n;
+    const __nv_bfloat16 *d = delta ? delta + (size_t)row * n : nullptr;
+    float x[VPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = (v * 256 + threadIdx.x) * 8;
+        if (i < n) {
+            uint4 rv = *reinterpret_cast<const uint4 *>(r + i);
+            const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
+            if (d) {
+                uint4 dv = *reinterpret_cast<const uint4 *>(d + i);
+                const __nv_bfloat16 *de = reinterpret_cast<const __nv_bfloat16 *>(&dv);
+                uint4 o;
+                __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&o);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    oe[j] = f2bf(__fadd_rn(bf2f(re[j]), bf2f(de[j])));
+                    x[v][j] = bf2f(oe[j]);
+                }
+                *reinterpret_cast<uint4 *>(r + i) = o;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[v][j] = bf2f(re[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(x[v][j], x[v][j], ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red[k];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+    __nv_bfloat16 *o = out + (size_t)row * n;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = (v * 256 + threadIdx.x) * 8;
+        if (i < n) {
+            uint4 wv = *reinterpret_cast<const uint4 *>(w + i);
+            const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv);
+            uint4 ov;
+            __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&ov);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float xn = bf16_round(__fmul_rn(x[v][j], inv));
+                float wf = bf2f(we[j]);
+                if (add_one) wf = bf16_round(__fadd_rn(wf, 1.0f));
+                oe[j] = f2bf(__fmul_rn(xn, wf));
+            }
+            *reinterpret_cast<uint4 *>(o + i) = ov;
+        }
+    }
+}
+
 __device__ __forceinline__ float silu_f(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
 // ekernel_swiglu_bf16 (kernels.c:1580-1596): rne(silu(g) * u), fp32 math.
@@ -149,6 +216,18 @@ int ekernel_add_rmsnorm_bf16(uint16_t *residual, const uint16_t *delta, const ui
                              size_t n, float eps, int add_one, uint16_t *out) {
     PILM_REQUIRE(residual && weight && out && rows > 0 && n > 0, ECPU_ERR_PARAM,
                  "ekernel_add_rmsnorm_bf16: bad argument");
+    const bool vec = (n % 8) == 0 && n <= 256 * 8 * 4 && ((((uintptr_t)residual) | ((uintptr_t)out) |
+                                                          ((uintptr_t)weight) | ((uintptr_t)delta)) & 15) == 0;
+    if (vec) {
+        const __nv_bfloat16 *dl = (const __nv_bfloat16 *)delta;
+        if (n <= 256 * 8 * 2)
+            add_rmsnorm_row_kernel<2><<<(unsigned)rows, 256, 0, stream()>>>(
+                (__nv_bfloat16 *)residual, dl, (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out);
+        else
+            add_rmsnorm_row_kernel<4><<<(unsigned)rows, 256, 0, stream()>>>(
+                (__nv_bfloat16 *)residual, dl, (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out);
+        return check_launch("ekernel_add_rmsnorm_bf16");
+    }
     add_rmsnorm_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, stream()>>>(
         (__nv_bfloat16 *)residual, (const __nv_bfloat16 *)delta, (const __nv_bfloat16 *)weight, (int)rows, (int)n,
         eps, add_one, (__nv_bfloat16 *)out);

@@ -30,7 +30,7 @@ import torch
 
 from . import ckernel as ck
 from .paging import PageTableManager, Sequence, Status, VerifyScheduler
-from .qwen3 import Qwen3Verifier, VerifyBatch
+from .qwen3 import Qwen3Verifier, VerifyBatch, VerifyGraph
 
 
 def draft_limit(num_computed: int, block_size: int, remaining_output: int, n_pending: int) -> int:
@@ -50,9 +50,11 @@ class StepResult:
 class MTPVerifyEngine:
     def __init__(self, verifier: Qwen3Verifier, num_blocks: int, block_size: int = 16, max_model_len: int = 65536,
                  max_pages_per_seq: Optional[int] = None, pin_memory: bool = True,
-                 max_num_batched_tokens: int = 1 << 30):
+                 max_num_batched_tokens: int = 1 << 30, use_graphs: bool = True):
         """max_num_batched_tokens is the scheduler's per-pass token budget; the reference
-        engine uses one page (16, engine.py:218), which also fixes its page order."""
+        engine uses one page (16, engine.py:218), which also fixes its page order.
+        use_graphs replays each verify-step shape (sequences, rows) from a captured CUDA
+        graph instead of launching ~15 kernels per layer from Python."""
         self.v = verifier
         self.device = verifier.device
         self.block_size = block_size
@@ -62,6 +64,9 @@ class MTPVerifyEngine:
         self.sched = VerifyScheduler(self.pages, max_num_batched_tokens=max_num_batched_tokens, max_num_seqs=1 << 20,
                                      max_model_len=max_model_len, max_pages_per_seq=mp)
         self._next_id = 0
+        self.max_model_len = max_model_len
+        self.use_graphs = use_graphs
+        self.graphs: dict[tuple[int, int, int], VerifyGraph] = {}
         self.pin = pin_memory and torch.cuda.is_available()
         self.stats = {"attempts": 0, "accepts": 0, "rejects": 0, "steps": 0, "verified_rows": 0}
 
@@ -88,7 +93,8 @@ class MTPVerifyEngine:
         t = torch.tensor(data, dtype=dtype, pin_memory=self.pin)
         return t.to(self.device, non_blocking=True)
 
-    def build_batch(self, seqs: list[Sequence], starts: list[int], counts: list[int]) -> VerifyBatch:
+    def build_batch(self, seqs: list[Sequence], starts: list[int], counts: list[int],
+                    on_device: bool = True) -> VerifyBatch:
         ids, pos, slots, cu = [], [], [], [0]
         bs = self.block_size
         maxp = max(1, max(len(s.pages) for s in seqs))
@@ -101,9 +107,24 @@ class MTPVerifyEngine:
             cu.append(cu[-1] + n)
             table.append(s.pages + [0] * (maxp - len(s.pages)))
             ctx.append(st + n)
-        return VerifyBatch(ids=self._tensor(ids), positions=self._tensor(pos), slots=self._tensor(slots),
-                           block_table=self._tensor(table), cu_q=self._tensor(cu), context_lens=self._tensor(ctx),
-                           max_q_len=max(counts), max_context=max(ctx))
+        mk = self._tensor if on_device else (lambda d: torch.tensor(d, dtype=torch.int32, pin_memory=self.pin))
+        return VerifyBatch(ids=mk(ids), positions=mk(pos), slots=mk(slots), block_table=mk(table), cu_q=mk(cu),
+                           context_lens=mk(ctx), max_q_len=max(counts), max_context=max(ctx))
+
+    def graph_for(self, b: VerifyBatch) -> VerifyGraph:
+        """Captured verify step for this batch shape; captured on first use (the capture
+        runs the step once eagerly on the loaded batch, which the replay then repeats
+        with identical results: K/V writes and the rollback are idempotent)."""
+        key = (b.num_seqs, b.total_q, b.max_q_len)
+        g = self.graphs.get(key)
+        if g is None:
+            g = VerifyGraph(self.v, b.num_seqs, b.total_q, b.max_q_len, self.max_pages, self.max_model_len)
+            g.load(b)
+            g.capture()
+            self.graphs[key] = g
+        else:
+            g.load(b)
+        return g
 
     # ---- prefill ----------------------------------------------------------------------
     def prefill(self) -> dict[int, int]:
@@ -156,12 +177,18 @@ class MTPVerifyEngine:
             used.append(d)
         if not seqs:
             return []
-        b = self.build_batch(seqs, starts, counts)
         B = len(seqs)
-        acc = torch.empty(B, dtype=torch.int32, device=self.device)
-        nxt = torch.empty(B, dtype=torch.int32, device=self.device)
-        ctx = b.context_lens.clone()
-        self.v.verify_greedy(b, acc, nxt, ctx)
+        if self.use_graphs:
+            b = self.build_batch(seqs, starts, counts, on_device=False)
+            g = self.graph_for(b)
+            g.replay()
+            acc, nxt = g.acc, g.next
+        else:
+            b = self.build_batch(seqs, starts, counts)
+            acc = torch.empty(B, dtype=torch.int32, device=self.device)
+            nxt = torch.empty(B, dtype=torch.int32, device=self.device)
+            ctx = b.context_lens.clone()
+            self.v.verify_greedy(b, acc, nxt, ctx)
         res = torch.stack([acc, nxt]).to("cpu", non_blocking=False).tolist()
         out = []
         for i, s in enumerate(seqs):

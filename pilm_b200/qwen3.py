@@ -90,6 +90,7 @@ class W4Linear:
         m = x.shape[0]
         if out is None:
             out = torch.empty((m, self.out_features), dtype=torch.bfloat16, device=x.device)
+        ck._stream()  # launch on the caller's current stream (graph capture included)
         rc = abi.linear_w4a16g128_bf16_ptr(x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(),
                                            out.data_ptr(), m, self.out_features, self.in_features)
         if rc != 0:
@@ -345,6 +346,56 @@ class Qwen3Verifier:
         ck.add_rmsnorm_bf16(res, delta, self.w.final_norm, s.eps, s.gemma_norm, out=h)
         return h
 
+    def time_attention(self, b: VerifyBatch, reps: int = 2) -> float:
+        """Average ms per paged-attention launch: every layer's attention over the batch,
+        launched back to back (reps x layers launches) between two CUDA events."""
+        s = self.shape
+        T = b.total_q
+        desc = self._desc(b)
+        gate = self.gate[:T] if s.gated else None
+        run = lambda li: ck.paged_attention_verify(desc, self.q[:T], self.kv.k[li], self.kv.v[li], b.block_table,
+                                                   b.cu_q, b.context_lens, gate, self.attn[:T])
+        run(0)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for li in range(s.layers):
+                run(li)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (reps * s.layers)
+
+    def time_linears(self, T: int, reps: int = 5) -> dict:
+        """ms per verify step spent in the W4 linears (all layers + LM head at T rows),
+        replayed from a captured graph of just those launches."""
+        def body():
+            for L in self.w.layers:
+                L["qkv"](self.h[:T], out=self.qkv[:T])
+                L["o"](self.attn[:T], out=self.o[:T])
+                L["gate_up"](self.h[:T], out=self.gu[:T])
+                L["down"](self.act[:T], out=self.mlp[:T])
+            self.w.lm_head(self.h[:T], out=self.logits[:T])
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            body()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            body()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return {"linear_total": e0.elapsed_time(e1) / reps}
+
     def lm_head(self, hidden: torch.Tensor) -> torch.Tensor:
         T = hidden.shape[0]
         e = self._ev("lm_head")
@@ -366,6 +417,69 @@ class Qwen3Verifier:
                                 slots)
         self._last_step_launches = abi.launch_count() - n0
         return logits
+
+
+class VerifyGraph:
+    """The whole verify step (forward, LM head, argmax, accept + rollback) captured as
+    one CUDA graph for a fixed (sequences, rows, rows-per-sequence bound).
+
+    Inputs live in static device buffers; ``load`` copies a batch's metadata into them
+    (page tables are zero-padded to the captured width) and ``replay`` runs the graph.
+    The attention split count is fixed at capture from ``max_context`` (a capacity), so
+    any batch whose contexts stay within it can be replayed."""
+
+    def __init__(self, verifier: "Qwen3Verifier", num_seqs: int, total_q: int, max_q_len: int, max_pages: int,
+                 max_context: int):
+        dev = verifier.device
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.v = verifier
+        self.batch = VerifyBatch(ids=torch.zeros(total_q, **i32), positions=torch.zeros(total_q, **i32),
+                                 slots=torch.full((total_q,), -1, **i32),
+                                 block_table=torch.zeros((num_seqs, max_pages), **i32),
+                                 cu_q=torch.zeros(num_seqs + 1, **i32), context_lens=torch.zeros(num_seqs, **i32),
+                                 max_q_len=max_q_len, max_context=max_context)
+        self.acc = torch.zeros(num_seqs, **i32)
+        self.next = torch.zeros(num_seqs, **i32)
+        self.ctx_out = torch.zeros(num_seqs, **i32)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.launches = 0
+
+    def load(self, b: VerifyBatch) -> None:
+        s = self.batch
+        if b.total_q != s.total_q or b.num_seqs != s.num_seqs:
+            raise ValueError("batch shape differs from the captured graph")
+        s.ids.copy_(b.ids, non_blocking=True)
+        s.positions.copy_(b.positions, non_blocking=True)
+        s.slots.copy_(b.slots, non_blocking=True)
+        s.cu_q.copy_(b.cu_q, non_blocking=True)
+        s.context_lens.copy_(b.context_lens, non_blocking=True)
+        w = b.block_table.shape[1]
+        s.block_table[:, :w].copy_(b.block_table, non_blocking=True)
+        if w < s.block_table.shape[1]:
+            s.block_table[:, w:].zero_()
+
+    def _body(self) -> None:
+        self.ctx_out.copy_(self.batch.context_lens)
+        self.v.verify_greedy(self.batch, self.acc, self.next, self.ctx_out)
+
+    def capture(self) -> None:
+        """One eager run (sizes the library's scratch memory, which must not grow
+        while capturing), then the capture."""
+        side = torch.cuda.Stream(device=self.v.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self._body()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        n0 = abi.launch_count()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._body()
+        self.launches = abi.launch_count() - n0
+        self.graph = g
+
+    def replay(self) -> None:
+        self.graph.replay()
 
 
 def attention_bytes(shape: Qwen3Shape, context_lens: list[int], q_lens: list[int]) -> int:

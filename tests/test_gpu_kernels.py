@@ -47,7 +47,7 @@ def test_linears_vs_reference_golden(kz):
         assert rel_err(y.cpu().numpy(), kz[f"{s}.w8a32.y"]) <= 1e-5
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 12, 16, 24, 32, 48, 63, 64, 96, 130])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 12, 16, 24, 32, 48, 63, 64, 96, 100, 128, 130, 256])
 @pytest.mark.parametrize("NK", [(256, 512), (384, 1024), (200, 4096)])
 def test_w4g128_vs_oracle_all_regimes(M, NK):
     """Every GEMV tile configuration (M <= 8, 16, 32, 64) and the M >= 64 path,
@@ -64,6 +64,19 @@ def test_w4g128_vs_oracle_all_regimes(M, NK):
     ref = ok.linear_w4a16_bf16(x, qr, sr)
     y = ck.linear_w4a16_bf16(bf16_from_bits(x), _t(qr), _t(sr))
     assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
+
+
+@pytest.mark.parametrize("M", [64, 96, 200])
+def test_large_m_qwen3_8b_shapes(M):
+    """The M >= 64 tensor-core path on the Qwen3-8B projection shapes that fit a test:
+    fused QKV (4096 -> 6144) and down (12288 -> 4096)."""
+    rng = np.random.default_rng(M)
+    for (N, K) in [(6144, 4096), (4096, 12288)]:
+        x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        qw, s = ok.quantize_i4_grouped(w, 128)
+        y = ck.linear_w4a16g128_bf16(bf16_from_bits(x), _t(qw), _t(s))
+        assert_bf16_close(bits_of(y), ok.linear_w4a16g_bf16(x, qw, s, 128), ulp_frac=0.99)
 
 
 def test_ragged_k_falls_back_and_matches():
