@@ -8,20 +8,28 @@
 // the product rounded before the add, as the reference does.
 //
 // CTA tile: 128 weight rows (the MMA M dimension, TMEM lanes) x up to 128 activation
-// rows (the MMA N dimension, TMEM columns), over a range of quant groups (split-K).
-// Warp roles (352 threads):
-//   warp 0      TMA: packed weight tile [128 rows x 64 B] per group -> raw ring (4 deep)
+// rows (the MMA N dimension), over a range of quant groups (split-K).  Warp roles
+// (384 threads):
+//   warp 0      TMA: packed weight tile [128 rows x 64 B] per group -> raw ring
 //   warp 1      TMA: activation tile [Nm rows x 128 k] (two SWIZZLE_128B boxes) -> X ring
-//               (4 deep: every CTA reads the same activation lines from L2, so this
-//               load has the longest latency of the pipeline)
-//   warp 2      TMEM owner + MMA issuer: 8 x tcgen05.mma (M=128, N=Nm, K=16) per group
-//               into one of two TMEM partial buffers, then tcgen05.commit to the
-//               barriers that free the A/X stages and publish the partial
-//   warps 3-6   dequant: raw int4 -> bf16 A tile in the K-major SWIZZLE_128B layout
-//   warps 7-10  epilogue: tcgen05.ld of the partial, acc = acc + part * s[n,g]
+//   warp 2      TMEM owner + MMA issuer: 8 x tcgen05.mma (M=128, N=Nm, K=16) per group,
+//               A from TMEM, B from shared memory, into one of three TMEM partials
+//   warp 3      TMA: group scales, [128 rows x 16 groups] fp32 tiles
+//   warps 4-11  compute: warp w owns TMEM lane quadrant w%4 and half (w-4)/4 of the
+//               work there.  Step i of a compute warp: wait for the MMAs of group i-2,
+//               dequantize its half-row of group i (32 packed bytes -> 64 bf16, k in
+//               [64h, 64h+64)) into the A stage those MMAs released (tcgen05.st), signal
+//               the MMA issuer, then fold group i-2's partial into its accumulators
+//               (tcgen05.ld, acc + rn(part * s[n,g]) for activation-row chunks h, h+2).  Two compute warps share each SM
+//               sub-partition; one warp's TMEM and shared-memory latencies hide behind
+//               the other's arithmetic.  Keeping A in TMEM (not shared memory) halves
+//               the shared-memory traffic per group.
+// The MMA issuer pays for one barrier wait and one commit per group: the issuing thread
+// is held while its MMAs execute, so every extra wait there leaves the tensor pipe idle.
 // Every mbarrier wait is bounded: on timeout the CTA records an error, drains, frees
 // its TMEM and returns, and the host reports ECPU_ERR_KERNEL.
 #include <cuda.h>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -32,33 +40,52 @@ namespace {
 
 constexpr int kTileRows = 128;   // weight rows per CTA
 constexpr int kMaxNm = 128;      // activation rows per CTA
-constexpr int kRawStages = 4;
+constexpr int kRawStages = 8;
 constexpr int kXStages = 4;
-constexpr int kAStages = 2;
+constexpr int kAStages = 2;                          // A buffers in TMEM (64 columns each)
 constexpr int kRawBytes = kTileRows * 64;            // one group of packed weights
-constexpr int kASubBytes = kTileRows * 128;          // 128 rows x 64 k bf16
-constexpr int kABytes = 2 * kASubBytes;              // one group (128 k)
 constexpr int kXSubBytes = kMaxNm * 128;             // Nm rows x 64 k bf16 (max)
 constexpr int kXBytes = 2 * kXSubBytes;
-constexpr int kThreads = 352;
-constexpr int kTBufs = 4;                            // TMEM partial buffers (MMA runs 3 groups ahead)
-constexpr int kTmemCols = 512;                       // kTBufs x 128 columns
-constexpr uint32_t kWaitLimit = 1u << 22;            // bounded wait (try_wait re-checks on completion)
+constexpr int kThreads = 384;
+constexpr int kComputeWarps = 8;
+constexpr int kTBufs = 3;                            // TMEM partial buffers (MMA runs 2 groups ahead)
+constexpr int kTmemCols = 512;
+constexpr int kAColBase = 0;                         // TMEM columns [0, 128): A stages
+constexpr int kAccColBase = 128;                     // TMEM columns [128, 512): partials
+constexpr uint32_t kWaitLimit = 1u << 20;            // polls before a wait gives up (bounded wait)
+constexpr uint32_t kSleepHintNs = 2000;              // longest sleep of one poll
+
+// Every mbarrier operation costs a few hundred cycles inside this kernel, so each group
+// has exactly three, all on rings indexed by slot i % kSlots:
+//   in_full[q]   both TMA copies of group i (packed weights and activations) complete
+//                here: the compute warps' one wait for their inputs
+//   op_full[q]   the MMA issuer's one wait: one arrival per compute warp once its part of
+//                A is in TMEM.  Partial buffer i % kTBufs is free by then (the same warps
+//                folded group i - 3 out of it one step earlier).  The weight producer
+//                also waits here before reusing raw slot i % kRawStages (group i - 8).
+//   mma_done[q]  the issuer's one commit: the compute warps wait for group i - 2 (partial
+//                ready, A stage i % 2 free), the activation producer for group i - 4
+// A waiter's parity is (j / kSlots) & 1 for the group j it needs.  No waiter can fall
+// kSlots or more completions behind: every later phase of its slot needs work that the
+// waiter itself has not released yet, so parities never alias.
+constexpr int kSlots = 8;
+static_assert(kSlots == kRawStages && kXStages == 4 && kAStages == 2 && kTBufs == 3, "pipeline depths");
 
 struct __align__(8) Barriers {
-    uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-    uint64_t x_full[kXStages], x_empty[kXStages];
-    uint64_t a_full[kAStages], a_empty[kAStages];
-    uint64_t t_full[kTBufs], t_empty[kTBufs];
+    uint64_t in_full[kSlots];
+    uint64_t op_full[kSlots], mma_done[kSlots];
+    uint64_t s_full[2], s_empty[2];
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
 };
 
 constexpr size_t kSmemRaw = 0;
-constexpr size_t kSmemX = kSmemRaw + (size_t)kRawStages * kRawBytes;   // 32 KB, 1024-aligned
-constexpr size_t kSmemA = kSmemX + (size_t)kXStages * kXBytes;         // +128 KB
-constexpr size_t kSmemBar = kSmemA + (size_t)kAStages * kABytes;       // +64 KB
+constexpr size_t kSmemX = kSmemRaw + (size_t)kRawStages * kRawBytes;   // 64 KB, 1024-aligned
+constexpr int kScaleChunk = 16;                      // groups per scale tile [128 rows x 16 groups] fp32
+constexpr int kScaleBytes = kTileRows * kScaleChunk * 4;
+constexpr size_t kSmemScale = kSmemX + (size_t)kXStages * kXBytes;     // +128 KB
+constexpr size_t kSmemBar = kSmemScale + 2 * (size_t)kScaleBytes;      // +16 KB (two scale tiles)
 constexpr size_t kSmemTotal = kSmemBar + sizeof(Barriers) + 1024;      // + alignment slack
 
 // ---- PTX wrappers ---------------------------------------------------------------------
@@ -84,14 +111,46 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps until the phase completes (or
+// the hint elapses) instead of re-issuing the poll, leaving issue slots to working warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity), "r"(kSleepHintNs)
+        : "memory");
+    return ok != 0;
+}
 // Bounded wait: returns false (and raises the CTA abort flag) if the phase never completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+// The MMA issuer polls (its waits are nearly always already satisfied); every other role
+// sleeps between polls.  The abort flag is read every 16 polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag,
+                                          bool sleep = true) {
+    if (mbar_try_wait(b, parity)) return true;  // already complete: no suspend
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
-        if (mbar_try_wait(b, parity)) return true;
-        if (*abort_flag) return false;
+        if (sleep ? mbar_try_wait_sleep(b, parity) : mbar_try_wait(b, parity)) return true;
+        if ((i & 15) == 15 && *abort_flag) return false;
     }
     *abort_flag = 1;
     return false;
+}
+
+// Bounded wait that ignores the abort flag: used to drain copies already issued, which
+// always complete, before the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint64_t *b, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(b, parity)) return;
+}
+
+// Warp-collective bounded wait: every lane waits (each gets the acquire), then the warp
+// reconverges before the .sync.aligned tcgen05 instructions that follow; a timeout in
+// any lane makes the whole warp give up together.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+    const bool ok = mbar_wait(b, parity, abort_flag);
+    return __all_sync(0xffffffffu, ok);
 }
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
@@ -102,7 +161,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -123,15 +181,28 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem desc]   (A: 128 lanes x K/2 columns, two bf16 per column)
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -181,10 +252,12 @@ struct TcParams {
     int splits, gps;    // number of K splits, groups per split
     uint32_t idesc;
     int grouped;
+    int scale_tma;      // group scales arrive by TMA (G % 4 == 0, group offsets 16-byte aligned)
 };
 
 __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant__ CUtensorMap wmap,
                                                          const __grid_constant__ CUtensorMap xmap,
+                                                         const __grid_constant__ CUtensorMap smap,
                                                          const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -195,24 +268,18 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     const int row0 = tile_n * kTileRows, m0 = tile_m * kMaxNm;
     const int g0 = split * p.gps, g1 = min(p.G, g0 + p.gps);
     const int ng = g1 - g0;
+    const int nchunks = p.scale_tma ? (ng + kScaleChunk - 1) / kScaleChunk : 0;
 
     if (threadIdx.x == 0) {
         // consumer-side barriers take one arrival per warp (lane 0 after __syncwarp)
-        for (int i = 0; i < kRawStages; ++i) {
-            mbar_init(&bar->raw_full[i], 1);
-            mbar_init(&bar->raw_empty[i], 4);
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(&bar->in_full[i], 2);  // the two producers' arrive.expect_tx
+            mbar_init(&bar->op_full[i], kComputeWarps);
+            mbar_init(&bar->mma_done[i], 1);
         }
-        for (int i = 0; i < kXStages; ++i) {
-            mbar_init(&bar->x_full[i], 1);
-            mbar_init(&bar->x_empty[i], 1);
-        }
-        for (int i = 0; i < kAStages; ++i) {
-            mbar_init(&bar->a_full[i], 4);
-            mbar_init(&bar->a_empty[i], 1);
-        }
-        for (int i = 0; i < kTBufs; ++i) {
-            mbar_init(&bar->t_full[i], 1);
-            mbar_init(&bar->t_empty[i], 4);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bar->s_full[i], 1);
+            mbar_init(&bar->s_empty[i], kComputeWarps);
         }
         mbar_init(&bar->drain, 1);
         bar->abort_flag = 0;
@@ -224,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
 
-    float acc[kMaxNm];
+    float2 acc[kMaxNm / 4];  // fp32 pairs: one packed multiply and one packed add per pair
     const int x_bytes = 2 * p.Nm * 128;
 
     if (warp == 0) {
@@ -234,15 +301,21 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             int issued = 0;
             for (int i = 0; i < ng; ++i) {
                 const int s = i % kRawStages;
-                const uint32_t ph = (uint32_t)(i / kRawStages) & 1u;
-                if (i >= kRawStages && !mbar_wait(&bar->raw_empty[s], ph ^ 1u, abort_flag)) break;
-                mbar_expect_tx(&bar->raw_full[s], kRawBytes);
-                tma_load_2d(smem + kSmemRaw + (size_t)s * kRawBytes, &wmap, &bar->raw_full[s], (g0 + i) * 64, row0);
+                // raw slot s held group i - kRawStages, read by every compute warp before it
+                // arrived on that group's op_full
+                if (i >= kRawStages && !mbar_wait(&bar->op_full[(i - kRawStages) % kSlots],
+                                                  (uint32_t)((i - kRawStages) / kSlots) & 1u, abort_flag))
+                    break;
+                mbar_expect_tx(&bar->in_full[i % kSlots], kRawBytes);
+                tma_load_2d(smem + kSmemRaw + (size_t)s * kRawBytes, &wmap, &bar->in_full[i % kSlots], (g0 + i) * 64,
+                            row0);
                 ++issued;
             }
-            // drain: every issued copy has landed before the CTA may exit
-            for (int i = issued > kRawStages ? issued - kRawStages : 0; i < issued; ++i)
-                mbar_wait(&bar->raw_full[i % kRawStages], (uint32_t)(i / kRawStages) & 1u, abort_flag);
+            // drain: every issued copy has landed before the CTA may exit (after an abort a
+            // phase may lack the other producer's arrival: the bounded drain then just waits
+            // out its limit, far longer than any copy takes)
+            for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
+                mbar_drain(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -252,130 +325,164 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             int issued = 0;
             for (int i = 0; i < ng; ++i) {
                 const int s = i % kXStages;
-                const uint32_t ph = (uint32_t)(i / kXStages) & 1u;
-                if (i >= kXStages && !mbar_wait(&bar->x_empty[s], ph ^ 1u, abort_flag)) break;
-                mbar_expect_tx(&bar->x_full[s], (uint32_t)x_bytes);
+                // X stage s is free once the MMAs of group i - kXStages have completed
+                if (i >= kXStages && !mbar_wait(&bar->mma_done[(i - kXStages) % kSlots],
+                                                (uint32_t)((i - kXStages) / kSlots) & 1u, abort_flag))
+                    break;
+                uint64_t *full = &bar->in_full[i % kSlots];
+                mbar_expect_tx(full, (uint32_t)x_bytes);
                 uint8_t *dst = smem + kSmemX + (size_t)s * kXBytes;
-                tma_load_2d(dst, &xmap, &bar->x_full[s], (g0 + i) * 128, m0);
-                tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, &bar->x_full[s], (g0 + i) * 128 + 64, m0);
+                tma_load_2d(dst, &xmap, full, (g0 + i) * 128, m0);
+                tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, full, (g0 + i) * 128 + 64, m0);
                 ++issued;
             }
             for (int i = issued > kXStages ? issued - kXStages : 0; i < issued; ++i)
-                mbar_wait(&bar->x_full[i % kXStages], (uint32_t)(i / kXStages) & 1u, abort_flag);
+                mbar_drain(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
         }
         __syncwarp();
     } else if (warp == 2) {
         // ---- MMA issuer ----
         if (lane == 0) {
             for (int i = 0; i < ng; ++i) {
-                const int sa = i % kAStages, sx = i % kXStages, b = i % kTBufs;
-                if (!mbar_wait(&bar->a_full[sa], (uint32_t)(i / kAStages) & 1u, abort_flag)) break;
-                if (!mbar_wait(&bar->x_full[sx], (uint32_t)(i / kXStages) & 1u, abort_flag)) break;
-                if (i >= kTBufs && !mbar_wait(&bar->t_empty[b], ((uint32_t)(i / kTBufs) & 1u) ^ 1u, abort_flag))
-                    break;
+                const int q = i % kSlots, sa = i % kAStages, sx = i % kXStages, b = i % kTBufs;
+                if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag, false)) break;
                 tc_fence_after();
-                const uint32_t a_base = smem_u32(smem + kSmemA + (size_t)sa * kABytes);
+                const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * 64);
                 const uint32_t x_base = smem_u32(smem + kSmemX + (size_t)sx * kXBytes);
-                const uint32_t d = tmem + (uint32_t)(b * kMaxNm);
+                const uint32_t d = tmem + (uint32_t)(kAccColBase + b * kMaxNm);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint64_t ad = sw128_desc(a_base + h * kASubBytes);
                     const uint64_t bd = sw128_desc(x_base + h * p.Nm * 128);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        umma_bf16(d, ad + 2 * k, bd + 2 * k, p.idesc, (h | k) ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k)  // K=16 per MMA: 8 TMEM columns of A, 32 B of B
+                        umma_bf16_ts(d, a_col + (uint32_t)(8 * (4 * h + k)), bd + 2 * k, p.idesc,
+                                     (h | k) ? 1u : 0u);
                 }
-                umma_commit(&bar->a_empty[sa]);
-                umma_commit(&bar->x_empty[sx]);
-                umma_commit(&bar->t_full[b]);
+                umma_commit(&bar->mma_done[q]);
             }
             // drain: all issued MMAs have completed before TMEM is released
             umma_commit(&bar->drain);
-            mbar_wait(&bar->drain, 0, abort_flag);
+            mbar_drain(&bar->drain, 0);
         }
         __syncwarp();
-    } else if (warp >= 3 && warp <= 6) {
-        // ---- dequant: raw [128 rows x 64 B] -> A [2 x (128 rows x 128 B)] SWIZZLE_128B ----
-        const int wq = warp - 3;           // rows 32*wq .. 32*wq+31
-        const int c = lane & 3;            // 16-byte chunk of the 64-byte row (k = 32c..32c+31)
-        const int rsub = lane >> 2;        // row within an 8-row slab
-        for (int i = 0; i < ng; ++i) {
-            const int s = i % kRawStages, sa = i % kAStages;
-            if (!mbar_wait(&bar->raw_full[s], (uint32_t)(i / kRawStages) & 1u, abort_flag)) break;
-            if (i >= kAStages && !mbar_wait(&bar->a_empty[sa], ((uint32_t)(i / kAStages) & 1u) ^ 1u, abort_flag))
-                break;
-            const uint8_t *raw = smem + kSmemRaw + (size_t)s * kRawBytes;
-            uint8_t *a = smem + kSmemA + (size_t)sa * kABytes + (c >> 1) * kASubBytes;
-            uint4 v[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = 32 * wq + 8 * j + rsub;
-                v[j] = *reinterpret_cast<const uint4 *>(raw + r * 64 + c * 16);
+    } else if (warp == 3) {
+        // ---- group scales: TMA, [128 rows x 16 groups] tiles into a two-slot ring.  A slot
+        // is refilled once every compute warp has finished the tile's last group. ----
+        if (lane == 0 && nchunks > 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
+            int issued = 0;
+            for (int c = 0; c < nchunks; ++c) {
+                const int slot = c & 1;
+                if (c >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((c - 2) >> 1) & 1u, abort_flag)) break;
+                mbar_expect_tx(&bar->s_full[slot], kScaleBytes);
+                tma_load_2d(smem + kSmemScale + (size_t)slot * kScaleBytes, &smap, &bar->s_full[slot],
+                            g0 + kScaleChunk * c, row0);
+                ++issued;
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar->raw_empty[s]);  // raw slot consumed (values in registers)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = 32 * wq + 8 * j + rsub;
-                uint8_t *rowp = a + r * 128;
-                const uint32_t words[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int chunk = ((c & 1) * 4 + q) ^ (r & 7);  // 8 bf16 (k = 32c + 8q ..) per chunk
-                    *reinterpret_cast<uint4 *>(rowp + chunk * 16) = dq_word(words[q]);
-                }
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar->a_full[sa]);
+            for (int c = issued > 2 ? issued - 2 : 0; c < issued; ++c)
+                mbar_drain(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u);
         }
+        __syncwarp();
     } else {
-        // ---- epilogue: warps 7..10 own TMEM lanes 32*(warp%4) .. +31 ----
+        // ---- compute warps ----
         const int quad = warp & 3;
-        const int row = row0 + 32 * quad + lane;
+        const int half = (warp - 4) >> 2;
+        const int rloc = 32 * quad + lane;  // this thread's weight row in the tile = TMEM lane
+        const int row = row0 + rloc;
         const bool row_ok = row < p.N;
-#pragma unroll
-        for (int j = 0; j < kMaxNm; ++j) acc[j] = 0.f;
-        // group scales are prefetched one group ahead (they are the only DRAM reads here)
+        const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
         const float *srow = p.S + (size_t)(row_ok ? row : 0) * p.G + g0;
-        float sc_next = (row_ok && p.grouped) ? __ldg(srow) : 1.0f;
-        for (int i = 0; i < ng; ++i) {
-            const int b = i % kTBufs;
-            const float sc = sc_next;
-            if (p.grouped && row_ok && i + 1 < ng) sc_next = __ldg(srow + i + 1);
-            if (!mbar_wait(&bar->t_full[b], (uint32_t)(i / kTBufs) & 1u, abort_flag)) break;
+        const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
+#pragma unroll
+        for (int j = 0; j < kMaxNm / 4; ++j) acc[j] = make_float2(0.f, 0.f);
+        // per-row scales (no group scales) or the fallback path: one group ahead by __ldg
+        float sc_next = (p.grouped && !p.scale_tma) ? __ldg(srow) : 1.0f;
+        float4 sc4 = make_float4(1.f, 1.f, 1.f, 1.f);  // four groups' scales of this row
+
+        for (int i = 0; i < ng + 2; ++i) {
+            const int j = i - 2;  // the group folded in this step
+            const int c = j / kScaleChunk, ci = j % kScaleChunk;
+            // the MMAs of group j have completed: their partial is ready and A stage i % 2 is free
+            if (i >= 2 && !mbar_wait_warp(&bar->mma_done[j % kSlots], (uint32_t)(j / kSlots) & 1u, abort_flag)) break;
             tc_fence_after();
-            const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)(b * kMaxNm);
+            // -- dequantize this warp's half of group i into A stage i % 2, then release the
+            // group to the MMA issuer before folding: the fold is off the MMA's critical path --
+            if (i < ng) {
+                const int s = i % kRawStages, sa = i % kAStages;
+                if (!mbar_wait_warp(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
+                // raw tile written with SWIZZLE_64B: 16-byte chunk c of row r sits at chunk
+                // c ^ ((r >> 1) & 3), so 8 consecutive rows hit 8 distinct bank groups
+                const uint8_t *rowp = smem + kSmemRaw + (size_t)s * kRawBytes + rloc * 64;
+                const int sw = (rloc >> 1) & 3;
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(rowp + (((2 * half) ^ sw) << 4));
+                const uint4 v1 = *reinterpret_cast<const uint4 *>(rowp + (((2 * half + 1) ^ sw) << 4));
+                uint32_t cols[32];
+                const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-            for (int cb = 0; cb < kMaxNm / 32; ++cb) {
-                if (cb * 32 < p.Nm) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + cb * 32, r);
-                    tmem_ld_wait();
+                for (int q = 0; q < 8; ++q) {  // 8 k values per word -> 4 columns
+                    const uint4 o = dq_word(words[q]);
+                    cols[4 * q + 0] = o.x;
+                    cols[4 * q + 1] = o.y;
+                    cols[4 * q + 2] = o.z;
+                    cols[4 * q + 3] = o.w;
+                }
+                tmem_st32(tmem + lane_addr + (uint32_t)(kAColBase + sa * 64 + 32 * half), cols);
+                tmem_st_wait();
+                // partial buffer i % 3 is free: group i - 3 was folded last step
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar->op_full[i % kSlots]);
+            }
+            // -- fold group j into the accumulators --
+            if (i >= 2) {
+                float sc = sc_next;
+                if (p.scale_tma) {
+                    if (ci == 0 && !mbar_wait_warp(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u, abort_flag)) break;
+                    if ((ci & 3) == 0)
+                        sc4 = *reinterpret_cast<const float4 *>(
+                            &sring[(size_t)(c & 1) * (kTileRows * kScaleChunk) + rloc * kScaleChunk + ci]);
+                    const int k4 = ci & 3;
+                    sc = k4 == 0 ? sc4.x : k4 == 1 ? sc4.y : k4 == 2 ? sc4.z : sc4.w;
+                } else if (p.grouped && j + 1 < ng) {
+                    sc_next = __ldg(srow + j + 1);
+                }
+                const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (j % kTBufs) * kMaxNm);
+                const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const float part = __uint_as_float(r[e]);
-                        acc[cb * 32 + e] = p.grouped ? __fadd_rn(acc[cb * 32 + e], __fmul_rn(part, sc))
-                                                     : __fadd_rn(acc[cb * 32 + e], part);
+                for (int u = 0; u < 2; ++u) {
+                    const int cb = 2 * u + half;
+                    if (cb * 32 < p.Nm) {
+                        uint32_t r[32];
+                        tmem_ld32(taddr + cb * 32, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {  // acc += rn(part * s), per element as the reference
+                            const float2 part = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                            acc[u * 16 + e] = __fadd2_rn(acc[u * 16 + e], p.grouped ? __fmul2_rn(part, sc2) : part);
+                        }
                     }
                 }
+                tc_fence_before();  // the loads are complete before the buffer is handed back
+                if (p.scale_tma && (ci == kScaleChunk - 1 || j == ng - 1)) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar->s_empty[c & 1]);  // done with scale tile c
+                }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar->t_empty[b]);
         }
         // ---- write out: direct (no split) or fp32 partial for the split-K reduction ----
         if (!*abort_flag && row_ok) {
             const float sr = p.grouped ? 1.0f : __ldg(p.S + row);
             const int mlim = min(p.Nm, p.M - m0);
 #pragma unroll
-            for (int j = 0; j < kMaxNm; ++j) {
-                if (j < mlim) {
-                    const int m = m0 + j;
+            for (int j = 0; j < kMaxNm / 2; ++j) {
+                const int ml = (2 * (j >> 5) + half) * 32 + (j & 31);  // activation row in the tile
+                const float a = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
+                if (ml < mlim) {
+                    const int m = m0 + ml;
                     if (p.splits == 1)
-                        p.Y[(size_t)m * p.N + row] = f2bf(acc[j] * sr);
+                        p.Y[(size_t)m * p.N + row] = f2bf(a * sr);
                     else
-                        p.ws[((size_t)split * p.M + m) * p.N + row] = acc[j];
+                        p.ws[((size_t)split * p.M + m) * p.N + row] = a;
                 }
             }
         }
@@ -488,7 +595,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         cuuint32_t box[2] = {64, (cuuint32_t)kTileRows};
         cuuint32_t es[2] = {1, 1};
         if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)W, dims, strides, box, es,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return ECPU_ERR_UNSUPPORTED;
     }
@@ -512,8 +619,25 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         if (splits > G) splits = G;
         if (splits < 1) splits = 1;
     }
-    const int gps = (G + splits - 1) / splits;
+    // group scales by TMA: the row stride (G floats) must be a multiple of 16 bytes and every
+    // split's first group (the tile's x coordinate) a multiple of 4 floats
+    const bool scale_tma = grouped && (G % 4) == 0 && ((uintptr_t)S & 15) == 0;
+    int gps = (G + splits - 1) / splits;
+    if (scale_tma) gps = (gps + 3) & ~3;
     splits = (G + gps - 1) / gps;
+
+    CUtensorMap smap;
+    memset(&smap, 0, sizeof(smap));
+    bool smap_ok = false;
+    if (scale_tma) {
+        cuuint64_t dims[2] = {(cuuint64_t)G, (cuuint64_t)N};
+        cuuint64_t strides[1] = {(cuuint64_t)G * 4};
+        cuuint32_t box[2] = {(cuuint32_t)kScaleChunk, (cuuint32_t)kTileRows};
+        cuuint32_t es[2] = {1, 1};
+        smap_ok = enc(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)S, dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
 
     TcParams p;
     p.S = S;
@@ -529,6 +653,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     p.splits = splits;
     p.gps = gps;
     p.grouped = grouped ? 1 : 0;
+    p.scale_tma = smap_ok ? 1 : 0;
     // kind::f16 instruction descriptor: D fp32, A/B bf16, K-major both, N = Nm, M = 128
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Nm >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     if (splits > 1) {
@@ -542,7 +667,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         attr_set = true;
     }
     dim3 grid(tiles_n, tiles_m, splits);
-    w4_gemm_tc<<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, p);
+    w4_gemm_tc<<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     if (sync_mode()) {

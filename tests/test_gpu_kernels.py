@@ -48,10 +48,11 @@ def test_linears_vs_reference_golden(kz):
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 12, 16, 24, 32, 48, 63, 64, 96, 100, 128, 130, 256])
-@pytest.mark.parametrize("NK", [(256, 512), (384, 1024), (200, 4096)])
+@pytest.mark.parametrize("NK", [(256, 512), (384, 1024), (200, 4096), (136, 1152)])
 def test_w4g128_vs_oracle_all_regimes(M, NK):
     """Every GEMV tile configuration (M <= 8, 16, 32, 64) and the M >= 64 path,
-    including split-K (K=4096) and ragged N."""
+    including split-K (K=4096), ragged N, and a group count that is not a multiple of
+    4 (K=1152: the tensor-core path loads group scales directly instead of by TMA)."""
     N, K = NK
     rng = np.random.default_rng(M * 7 + N)
     x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
@@ -66,17 +67,23 @@ def test_w4g128_vs_oracle_all_regimes(M, NK):
     assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
 
 
-@pytest.mark.parametrize("M", [64, 96, 200])
+@pytest.mark.parametrize("M", [64, 96, 128, 200])
 def test_large_m_qwen3_8b_shapes(M):
     """The M >= 64 tensor-core path on the Qwen3-8B projection shapes that fit a test:
-    fused QKV (4096 -> 6144) and down (12288 -> 4096)."""
+    fused QKV (4096 -> 6144) and down (12288 -> 4096), one activation tile (M <= 128)
+    and two (M = 200), with and without split-K.  Each shape runs three times in a row:
+    the pipeline's warps race one another, and a result that depends on their timing
+    differs between calls."""
     rng = np.random.default_rng(M)
     for (N, K) in [(6144, 4096), (4096, 12288)]:
         x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
         w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
         qw, s = ok.quantize_i4_grouped(w, 128)
-        y = ck.linear_w4a16g128_bf16(bf16_from_bits(x), _t(qw), _t(s))
-        assert_bf16_close(bits_of(y), ok.linear_w4a16g_bf16(x, qw, s, 128), ulp_frac=0.99)
+        ref = ok.linear_w4a16g_bf16(x, qw, s, 128)
+        xd, qd, sd = bf16_from_bits(x), _t(qw), _t(s)
+        for _ in range(3):
+            y = ck.linear_w4a16g128_bf16(xd, qd, sd)
+            assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
 
 
 def test_ragged_k_falls_back_and_matches():
