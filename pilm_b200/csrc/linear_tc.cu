@@ -9,20 +9,21 @@
 //
 // CTA tile: 128 weight rows (the MMA M dimension, TMEM lanes) x up to 128 activation
 // rows (the MMA N dimension), over a range of quant groups (split-K).  Warp roles
-// (384 threads):
+// (640 threads):
 //   warp 0      TMA: packed weight tile [128 rows x 64 B] per group -> raw ring
 //   warp 1      TMA: activation tile [Nm rows x 128 k] (two SWIZZLE_128B boxes) -> X ring
 //   warp 2      TMEM owner + MMA issuer: 8 x tcgen05.mma (M=128, N=Nm, K=16) per group,
 //               A from TMEM, B from shared memory, into one of three TMEM partials
 //   warp 3      TMA: group scales, [128 rows x 16 groups] fp32 tiles
-//   warps 4-11  compute: warp w owns TMEM lane quadrant w%4 and half (w-4)/4 of the
+//   warps 4-19  compute: warp w owns TMEM lane quadrant w%4 and quarter q = (w-4)/4 of the
 //               work there.  Step i of a compute warp: wait for the MMAs of group i-2,
-//               dequantize its half-row of group i (32 packed bytes -> 64 bf16, k in
-//               [64h, 64h+64)) into the A stage those MMAs released (tcgen05.st), signal
+//               dequantize its quarter-row of group i (16 packed bytes -> 32 bf16, k in
+//               [32q, 32q+32)) into the A stage those MMAs released (tcgen05.st), signal
 //               the MMA issuer, then fold group i-2's partial into its accumulators
-//               (tcgen05.ld, acc + rn(part * s[n,g]) for activation-row chunks h, h+2).  Two compute warps share each SM
-//               sub-partition; one warp's TMEM and shared-memory latencies hide behind
-//               the other's arithmetic.  Keeping A in TMEM (not shared memory) halves
+//               (tcgen05.ld, acc + rn(part * s[n,g]) for activation-row chunk q).  Four
+//               compute warps share each SM sub-partition: the work of one step is a
+//               short dependent chain, and the other warps' arithmetic hides its TMEM,
+//               shared-memory and barrier latencies.  Keeping A in TMEM (not shared memory) halves
 //               the shared-memory traffic per group.
 // The MMA issuer pays for one barrier wait and one commit per group: the issuing thread
 // is held while its MMAs execute, so every extra wait there leaves the tensor pipe idle.
@@ -46,8 +47,8 @@ constexpr int kAStages = 2;                          // A buffers in TMEM (64 co
 constexpr int kRawBytes = kTileRows * 64;            // one group of packed weights
 constexpr int kXSubBytes = kMaxNm * 128;             // Nm rows x 64 k bf16 (max)
 constexpr int kXBytes = 2 * kXSubBytes;
-constexpr int kThreads = 384;
-constexpr int kComputeWarps = 8;
+constexpr int kThreads = 640;
+constexpr int kComputeWarps = 16;
 constexpr int kTBufs = 3;                            // TMEM partial buffers (MMA runs 2 groups ahead)
 constexpr int kTmemCols = 512;
 constexpr int kAColBase = 0;                         // TMEM columns [0, 128): A stages
@@ -191,15 +192,20 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, u
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
-        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
-        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
-        "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -208,16 +214,6 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // int4 nibble pair at bits [0,4) and [16,20) -> bf16x2, exact (see linear.cu)
@@ -245,7 +241,6 @@ struct TcParams {
     const float *S;     // scales [N, G]
     __nv_bfloat16 *Y;   // [M, N]
     float *ws;          // split-K partials [splits, M, N]
-    int *ctr;           // arrival counters per (tile_n, tile_m)
     int *err;           // device error word
     int M, N, K, G;
     int Nm;             // activation rows per CTA (multiple of 16, <= 128)
@@ -291,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
 
-    float2 acc[kMaxNm / 4];  // fp32 pairs: one packed multiply and one packed add per pair
+    float2 acc[16];  // one 32-column chunk as fp32 pairs: one packed multiply and add per pair
     const int x_bytes = 2 * p.Nm * 128;
 
     if (warp == 0) {
@@ -386,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     } else {
         // ---- compute warps ----
         const int quad = warp & 3;
-        const int half = (warp - 4) >> 2;
+        const int part = (warp - 4) >> 2;  // k quarter of the dequant, activation-row chunk of the fold
         const int rloc = 32 * quad + lane;  // this thread's weight row in the tile = TMEM lane
         const int row = row0 + rloc;
         const bool row_ok = row < p.N;
@@ -394,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         const float *srow = p.S + (size_t)(row_ok ? row : 0) * p.G + g0;
         const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
 #pragma unroll
-        for (int j = 0; j < kMaxNm / 4; ++j) acc[j] = make_float2(0.f, 0.f);
+        for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.f, 0.f);
         // per-row scales (no group scales) or the fallback path: one group ahead by __ldg
         float sc_next = (p.grouped && !p.scale_tma) ? __ldg(srow) : 1.0f;
         float4 sc4 = make_float4(1.f, 1.f, 1.f, 1.f);  // four groups' scales of this row
@@ -405,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             // the MMAs of group j have completed: their partial is ready and A stage i % 2 is free
             if (i >= 2 && !mbar_wait_warp(&bar->mma_done[j % kSlots], (uint32_t)(j / kSlots) & 1u, abort_flag)) break;
             tc_fence_after();
-            // -- dequantize this warp's half of group i into A stage i % 2, then release the
+            // -- dequantize this warp's quarter of group i into A stage i % 2, then release the
             // group to the MMA issuer before folding: the fold is off the MMA's critical path --
             if (i < ng) {
                 const int s = i % kRawStages, sa = i % kAStages;
@@ -414,19 +409,18 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // c ^ ((r >> 1) & 3), so 8 consecutive rows hit 8 distinct bank groups
                 const uint8_t *rowp = smem + kSmemRaw + (size_t)s * kRawBytes + rloc * 64;
                 const int sw = (rloc >> 1) & 3;
-                const uint4 v0 = *reinterpret_cast<const uint4 *>(rowp + (((2 * half) ^ sw) << 4));
-                const uint4 v1 = *reinterpret_cast<const uint4 *>(rowp + (((2 * half + 1) ^ sw) << 4));
-                uint32_t cols[32];
-                const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(rowp + ((part ^ sw) << 4));
+                uint32_t cols[16];
+                const uint32_t words[4] = {v0.x, v0.y, v0.z, v0.w};
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {  // 8 k values per word -> 4 columns
+                for (int q = 0; q < 4; ++q) {  // 8 k values per word -> 4 columns
                     const uint4 o = dq_word(words[q]);
                     cols[4 * q + 0] = o.x;
                     cols[4 * q + 1] = o.y;
                     cols[4 * q + 2] = o.z;
                     cols[4 * q + 3] = o.w;
                 }
-                tmem_st32(tmem + lane_addr + (uint32_t)(kAColBase + sa * 64 + 32 * half), cols);
+                tmem_st16(tmem + lane_addr + (uint32_t)(kAColBase + sa * 64 + 16 * part), cols);
                 tmem_st_wait();
                 // partial buffer i % 3 is free: group i - 3 was folded last step
                 tc_fence_before();
@@ -448,17 +442,16 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
                 const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (j % kTBufs) * kMaxNm);
                 const float2 sc2 = make_float2(sc, sc);
+                if (part * 32 < p.Nm) {
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int cb = 2 * u + half;
-                    if (cb * 32 < p.Nm) {
-                        uint32_t r[32];
-                        tmem_ld32(taddr + cb * 32, r);
+                    for (int u = 0; u < 2; ++u) {
+                        uint32_t r[16];
+                        tmem_ld16(taddr + part * 32 + u * 16, r);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {  // acc += rn(part * s), per element as the reference
-                            const float2 part = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-                            acc[u * 16 + e] = __fadd2_rn(acc[u * 16 + e], p.grouped ? __fmul2_rn(part, sc2) : part);
+                        for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
+                            const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                            acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
                         }
                     }
                 }
@@ -474,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             const float sr = p.grouped ? 1.0f : __ldg(p.S + row);
             const int mlim = min(p.Nm, p.M - m0);
 #pragma unroll
-            for (int j = 0; j < kMaxNm / 2; ++j) {
-                const int ml = (2 * (j >> 5) + half) * 32 + (j & 31);  // activation row in the tile
+            for (int j = 0; j < 32; ++j) {
+                const int ml = part * 32 + j;  // activation row in the tile
                 const float a = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
                 if (ml < mlim) {
                     const int m = m0 + ml;
@@ -493,51 +486,45 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     __syncthreads();
     if (*abort_flag) {
         if (threadIdx.x == 0) atomicExch(p.err, 1);
-    } else if (p.splits > 1) {
-        // split-K: every CTA has written its fp32 partial; the last CTA to arrive for this
-        // tile sums the partials of its cells in split order (deterministic) and rounds.
-        __shared__ int s_last;
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const int prev = atomicAdd(p.ctr + blockIdx.y * gridDim.x + blockIdx.x, 1);
-            s_last = (prev == p.splits - 1);
-        }
-        __syncthreads();
-        if (s_last) {
-            // all threads: 8 cells per thread per pass, every partial load issued up front
-            __threadfence();
-            const int mlim = min(p.Nm, p.M - m0);
-            const int cells = kTileRows * mlim;
-            for (int base = threadIdx.x; base < cells; base += 8 * kThreads) {
-                float v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = 0.f;
-                for (int sp = 0; sp < p.splits; ++sp) {
-                    float t[8];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const int e = base + u * kThreads;
-                        const int r = row0 + (e % kTileRows), m = m0 + e / kTileRows;
-                        t[u] = (e < cells && r < p.N) ? __ldcg(p.ws + ((size_t)sp * p.M + m) * p.N + r) : 0.f;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) v[u] += t[u];
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int e = base + u * kThreads;
-                    const int r = row0 + (e % kTileRows), m = m0 + e / kTileRows;
-                    if (e < cells && r < p.N) p.Y[(size_t)m * p.N + r] = f2bf(p.grouped ? v[u] : v[u] * __ldg(p.S + r));
-                }
-            }
-        }
-        if (s_last && threadIdx.x == 0) p.ctr[blockIdx.y * gridDim.x + blockIdx.x] = 0;
     }
     if (warp == 2) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+}
+
+// Split-K combine: Y[m, n] = rn_bf16((0 + P_0 + P_1 + ... + P_{s-1}) * sr[n]), the partials
+// summed in split order (K order), as a separate fully parallel pass (8 outputs per thread).
+// sr is the per-row scale of the ungrouped format (nullptr: grouped, already applied).
+__global__ void __launch_bounds__(256) splitk_combine(const float *__restrict__ ws, int splits, int M, int N,
+                                                      const float *__restrict__ sr, __nv_bfloat16 *__restrict__ Y) {
+    const size_t total8 = (size_t)M * N / 8;
+    const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= total8) return;
+    const size_t base = t * 8;  // N % 8 == 0: the 8 outputs share one row m
+    const size_t plane = (size_t)M * N;
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = 0.f;
+    for (int sp = 0; sp < splits; ++sp) {
+        const float4 a = __ldcs(reinterpret_cast<const float4 *>(ws + sp * plane + base));
+        const float4 b = __ldcs(reinterpret_cast<const float4 *>(ws + sp * plane + base + 4));
+        v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        v[4] += b.x; v[5] += b.y; v[6] += b.z; v[7] += b.w;
+    }
+    const int n0 = (int)(base % (size_t)N);
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        float x0 = v[2 * u], x1 = v[2 * u + 1];
+        if (sr) {
+            x0 *= __ldg(sr + n0 + 2 * u);
+            x1 *= __ldg(sr + n0 + 2 * u + 1);
+        }
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        o[u] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    *reinterpret_cast<uint4 *>(Y + base) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // ---- host side ---------------------------------------------------------------------------
@@ -610,21 +597,33 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
             return ECPU_ERR_UNSUPPORTED;
     }
 
-    // split K so that the grid covers the SMs once (one CTA per SM: shared memory)
+    // Split K by a cost model in units of one group's pipeline time: every wave of CTAs pays
+    // its groups per CTA plus a fixed prologue and pipeline fill (about 2 groups), and a
+    // split adds one combine pass (about 3).  Group scales by TMA need every split's first
+    // group (the scale tile's x coordinate) at a multiple of 4; the combine pass wants
+    // N % 8 == 0 and 16-byte aligned output rows.
+    const bool scale_tma = grouped && (G % 4) == 0 && ((uintptr_t)S & 15) == 0;
     const int base = tiles_n * tiles_m;
     const int sms = num_sms();
-    int splits = 1;
-    if (base < sms) {
-        splits = sms / base;
-        if (splits > G) splits = G;
-        if (splits < 1) splits = 1;
+    int splits = 1, gps = G;
+    {
+        double best = 1e30;
+        const bool can_split = (N % 8) == 0 && (((uintptr_t)Y) & 15) == 0;
+        const int max_splits = can_split ? (G < 16 ? G : 16) : 1;
+        for (int s = 1; s <= max_splits; ++s) {
+            int g = (G + s - 1) / s;
+            if (scale_tma) g = (g + 3) & ~3;
+            const int se = (G + g - 1) / g;
+            if (se != s) continue;
+            const int waves = (base * se + sms - 1) / sms;
+            const double est = waves * (g + 2.0) + (se > 1 ? 3.0 : 0.0);
+            if (est < best - 1e-9) {
+                best = est;
+                splits = se;
+                gps = g;
+            }
+        }
     }
-    // group scales by TMA: the row stride (G floats) must be a multiple of 16 bytes and every
-    // split's first group (the tile's x coordinate) a multiple of 4 floats
-    const bool scale_tma = grouped && (G % 4) == 0 && ((uintptr_t)S & 15) == 0;
-    int gps = (G + splits - 1) / splits;
-    if (scale_tma) gps = (gps + 3) & ~3;
-    splits = (G + gps - 1) / gps;
 
     CUtensorMap smap;
     memset(&smap, 0, sizeof(smap));
@@ -643,7 +642,6 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     p.S = S;
     p.Y = Y;
     p.ws = nullptr;
-    p.ctr = nullptr;
     p.err = err;
     p.M = M;
     p.N = N;
@@ -658,8 +656,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Nm >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     if (splits > 1) {
         p.ws = (float *)workspace((size_t)splits * M * N * sizeof(float));
-        p.ctr = counters((size_t)tiles_n * tiles_m);
-        PILM_REQUIRE(p.ws && p.ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+        PILM_REQUIRE(p.ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
     static bool attr_set = false;
     if (!attr_set) {
@@ -670,6 +667,13 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     w4_gemm_tc<<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
+    if (splits > 1) {
+        const size_t total8 = (size_t)M * N / 8;
+        splitk_combine<<<(unsigned)((total8 + 255) / 256), 256, 0, stream()>>>(p.ws, splits, M, N,
+                                                                            grouped ? nullptr : S, Y);
+        rc = check_launch(what);
+        if (rc != ECPU_OK) return rc;
+    }
     if (sync_mode()) {
         int h = 0;
         cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost);
