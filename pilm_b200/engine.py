@@ -26,6 +26,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Optional
 
+import numpy as np
 import torch
 
 from . import ckernel as ck
@@ -69,6 +70,11 @@ class MTPVerifyEngine:
         self.graphs: dict[tuple[int, int, int], VerifyGraph] = {}
         self.pin = pin_memory and torch.cuda.is_available()
         self.stats = {"attempts": 0, "accepts": 0, "rejects": 0, "steps": 0, "verified_rows": 0}
+        # host side of the verify step: per-sequence page rows kept as int32 arrays and
+        # extended in place (page lists only grow until they are released), and pinned
+        # staging buffers reused every step
+        self._page_rows: dict[int, tuple[int, np.ndarray, int]] = {}
+        self._staging: dict[str, torch.Tensor] = {}
 
     # ---- admission -------------------------------------------------------------------
     def add_request(self, prompt: list[int], max_new_tokens: int = 256, eos_token_id: int = -1) -> int:
@@ -93,8 +99,35 @@ class MTPVerifyEngine:
         t = torch.tensor(data, dtype=dtype, pin_memory=self.pin)
         return t.to(self.device, non_blocking=True)
 
+    def _page_row(self, s: Sequence) -> np.ndarray:
+        """The sequence's page list as int32, zero-padded to max_pages; rebuilt only after
+        the list was released, otherwise extended by the pages appended since."""
+        n = len(s.pages)
+        c = self._page_rows.get(s.seq_id)
+        if c is None or c[0] != s.page_gen or c[2] > n or c[1].shape[0] < n:
+            arr = np.zeros(max(self.max_pages, n), dtype=np.int32)
+            arr[:n] = s.pages
+            self._page_rows[s.seq_id] = (s.page_gen, arr, n)
+            return arr
+        gen, arr, m = c
+        if m < n:
+            arr[m:n] = s.pages[m:n]
+            self._page_rows[s.seq_id] = (gen, arr, n)
+        return arr
+
+    def _stage(self, name: str, shape: tuple[int, ...]) -> torch.Tensor:
+        """A pinned int32 host buffer of at least this shape (a view of it)."""
+        numel = int(np.prod(shape))
+        t = self._staging.get(name)
+        if t is None or t.numel() < numel:
+            t = torch.empty(max(numel, 1), dtype=torch.int32, pin_memory=self.pin)
+            self._staging[name] = t
+        return t[:numel].view(shape)
+
     def build_batch(self, seqs: list[Sequence], starts: list[int], counts: list[int],
                     on_device: bool = True) -> VerifyBatch:
+        if not on_device:
+            return self._build_host_batch(seqs, starts, counts)
         ids, pos, slots, cu = [], [], [], [0]
         bs = self.block_size
         maxp = max(1, max(len(s.pages) for s in seqs))
@@ -110,6 +143,34 @@ class MTPVerifyEngine:
         mk = self._tensor if on_device else (lambda d: torch.tensor(d, dtype=torch.int32, pin_memory=self.pin))
         return VerifyBatch(ids=mk(ids), positions=mk(pos), slots=mk(slots), block_table=mk(table), cu_q=mk(cu),
                            context_lens=mk(ctx), max_q_len=max(counts), max_context=max(ctx))
+
+    def _build_host_batch(self, seqs: list[Sequence], starts: list[int], counts: list[int]) -> VerifyBatch:
+        """The verify step's metadata in pinned host buffers (copied to the graph's device
+        buffers by VerifyGraph.load).  The buffers are rewritten by the next step, which
+        starts only after this step's results were read back, so after its copies."""
+        bs = self.block_size
+        B = len(seqs)
+        T = int(sum(counts))
+        maxp = max(1, max(len(s.pages) for s in seqs))
+        ids, pos, slots = self._stage("ids", (T,)), self._stage("pos", (T,)), self._stage("slots", (T,))
+        cu, ctx = self._stage("cu", (B + 1,)), self._stage("ctx", (B,))
+        table = self._stage("table", (B, maxp))
+        ids_n, pos_n, slots_n = ids.numpy(), pos.numpy(), slots.numpy()
+        cu_n, ctx_n, table_n = cu.numpy(), ctx.numpy(), table.numpy()
+        o = 0
+        cu_n[0] = 0
+        for i, (s, st, n) in enumerate(zip(seqs, starts, counts)):
+            row = self._page_row(s)
+            table_n[i] = row[:maxp]
+            ids_n[o:o + n] = s.tokens[st:st + n]
+            p = np.arange(st, st + n, dtype=np.int32)
+            pos_n[o:o + n] = p
+            slots_n[o:o + n] = row[p // bs] * bs + p % bs
+            o += n
+            cu_n[i + 1] = o
+            ctx_n[i] = st + n
+        return VerifyBatch(ids=ids, positions=pos, slots=slots, block_table=table, cu_q=cu, context_lens=ctx,
+                           max_q_len=max(counts), max_context=int(ctx_n.max()))
 
     def graph_for(self, b: VerifyBatch) -> VerifyGraph:
         """Captured verify step for this batch shape; captured on first use (the capture
@@ -211,4 +272,5 @@ class MTPVerifyEngine:
         for s in finished:
             self.sched.running.remove(s)
             self.pages.free(s)
+            self._page_rows.pop(s.seq_id, None)
         return out

@@ -89,6 +89,7 @@ class Sequence:
     pages: list[int] = field(default_factory=list)
     status: int = Status.WAITING
     pending_drafts: list[int] = field(default_factory=list)
+    page_gen: int = 0  # bumped whenever the page list is released (pages only grow between)
 
     def __post_init__(self):
         if not self.tokens:
@@ -133,6 +134,7 @@ class PageTableManager:
     def free(self, seq: Sequence) -> None:
         self.pool.release(list(seq.pages))
         seq.pages = []
+        seq.page_gen += 1
 
 
 @dataclass

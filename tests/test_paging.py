@@ -79,3 +79,63 @@ def test_prefill_schedule_and_verify_pages_match_reference_engine():
             assert s.pages == G.ilist(z[f"b{s.seq_id}.block_ids"])
             slots = [s.slot(p, 16) for p in range(s.num_computed, s.num_computed + 1 + len(d))]
             assert slots == G.ilist(z[f"b{s.seq_id}.slots"])
+
+
+def test_host_verify_batch_matches_list_build_across_growth_preemption_and_finish():
+    """The engine's per-step host metadata (incrementally extended page rows, pinned
+    staging buffers) equals a from-scratch build of the same batch, step after step,
+    while pages are appended, a sequence is preempted and re-allocated (its page list
+    released and rebuilt) and another finishes."""
+    import random
+
+    from pilm_b200.engine import MTPVerifyEngine
+
+    class _NoDevice:
+        device = "cpu"
+
+    eng = MTPVerifyEngine(_NoDevice(), num_blocks=4000, pin_memory=False, max_model_len=4096)
+    rnd = random.Random(1)
+    seqs = []
+    for i in range(5):
+        s = Sequence(i, list(range(100 + 37 * i)), 64)
+        eng.pages.allocate(s, s.num_tokens, eng.max_pages)
+        s.num_computed = s.num_tokens - 1
+        seqs.append(s)
+
+    def scratch_build(seqs, starts, counts):
+        bs = eng.block_size
+        maxp = max(len(s.pages) for s in seqs)
+        ids, pos, slots, table, cu, ctx = [], [], [], [], [0], []
+        for s, st, n in zip(seqs, starts, counts):
+            ids += s.tokens[st:st + n]
+            pos += list(range(st, st + n))
+            slots += [s.pages[p // bs] * bs + p % bs for p in range(st, st + n)]
+            table.append(s.pages + [0] * (maxp - len(s.pages)))
+            cu.append(cu[-1] + n)
+            ctx.append(st + n)
+        return [ids, pos, slots, table, cu, ctx]
+
+    for step in range(30):
+        starts, counts = [], []
+        for s in seqs:
+            n = rnd.randint(1, 3)
+            s.tokens.extend(rnd.randint(0, 999) for _ in range(n - 1))
+            assert eng.pages.allocate(s, n, eng.max_pages) is not None
+            starts.append(s.num_computed)
+            counts.append(n)
+        b = eng.build_batch(seqs, starts, counts, on_device=False)
+        got = [b.ids.tolist(), b.positions.tolist(), b.slots.tolist(), b.block_table.tolist(), b.cu_q.tolist(),
+               b.context_lens.tolist()]
+        assert got == scratch_build(seqs, starts, counts), f"step {step}"
+        assert b.max_context == max(b.context_lens.tolist()) and b.max_q_len == max(counts)
+        for s, st, n in zip(seqs, starts, counts):
+            s.num_computed = st + n
+            del s.tokens[s.num_computed:]
+            s.tokens.append(rnd.randint(0, 999))
+        if step == 10:  # preemption: the page list is released, then rebuilt from new pages
+            victim = seqs[2]
+            eng.pages.free(victim)
+            eng.pages.allocate(victim, victim.num_computed + 1, eng.max_pages)
+        if step == 20:  # a finished sequence leaves the batch
+            eng.pages.free(seqs[4])
+            seqs.pop(4)
