@@ -38,6 +38,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "verified tok/s/GPU, Qwen3-8B W4A16 MTP verify; quant-GEMM HBM GB/s vs peak"
 SEQS, PROMPT, K_DRAFT, PAGE = 32, 8192, 2, 16
+# ncu capture of one attn_verify launch: 16 sequences x 8195 keys, 8 KV heads x 128 bf16,
+# DRAM read + write bytes, and the K/V bytes of that launch
+ATTN_TRAFFIC_CAPTURE = (537.568256e6 + 5.998336e6, 16 * 8195 * 8 * 128 * 2 * 2)
 GEN_HEADROOM = 512
 
 
@@ -241,13 +244,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     lin_ms = op_ms.get("linear_total")
     lin_gbs = lin_bytes / (lin_ms * 1e-3) / 1e9 if lin_ms else None
     step_bytes = att_bytes * shape.layers + lin_bytes + 2 * rows_per_step * shape.hidden * 2
-    profile = ROOT / "profiles" / "attn_traffic.json"
-    traffic = None
-    if profile.exists():
-        try:
-            traffic = json.loads(profile.read_text()).get("bytes_per_launch_scaled")
-        except Exception:
-            traffic = None
+    # DRAM traffic of one attn_verify launch: an ncu capture of the same kernel on a
+    # 16-sequence case (dram__bytes_read.sum + dram__bytes_write.sum), scaled by this
+    # launch's K/V bytes, with which the kernel's traffic grows (it reads each K/V byte once)
+    kv_bytes = sum(ctx) * shape.n_kv_heads * shape.head_dim * 2 * 2
+    traffic = round(ATTN_TRAFFIC_CAPTURE[0] * kv_bytes / ATTN_TRAFFIC_CAPTURE[1])
     cpu = cpu_baseline_sample(args) if not args.no_cpu else None
     full = (SEQS, PROMPT, shape.layers) == (32, 8192, 36)
     value = rows_per_step * world / (ms_max * 1e-3)
