@@ -12,10 +12,13 @@
 //                 row chunk); its query rows are all q_len x (n_heads / n_kv) rows that
 //                 share the kv head, so every K/V byte of the split is read from HBM
 //                 once per CTA.  Each of the 4 warps streams every 4th page of the split
-//                 through a private cp.async ring (3 pages deep, XOR-swizzled smem),
-//                 computes S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in,
-//                 fp32 accumulate) and keeps an fp32 online softmax; warps then merge.
+//                 through a private TMA ring (3 pages deep): one page of one KV head is
+//                 four cp.async.bulk.tensor loads (K and V, two 128-byte SWIZZLE_128B
+//                 halves each) completing on the stage's mbarrier.  The warp computes
+//                 S = Q K^T and O += P V with mma.sync m16n8k16 (bf16 in, fp32
+//                 accumulate) and keeps an fp32 online softmax; warps then merge.
 //   attn_merge    combines split partials (m, l, O) and applies the output gate.
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -33,6 +36,7 @@ constexpr int kHD = 128;         // head_dim supported by the tensor-core path
 constexpr int kWarps = 4;        // warps per attention CTA
 constexpr int kStages = 3;       // pages in flight per warp
 constexpr int kPageBytes = 16 * kHD * 2;  // one K (or V) tile of a 16-token page
+constexpr uint32_t kAttnWaitLimit = 1u << 22;  // polls before a page wait gives up
 
 // ---------------------------------------------------------------------------------
 // Prologue: q/k RMSNorm + RoPE, KV append
@@ -146,22 +150,55 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t 
                  : "r"(addr));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// byte offset of 16-byte chunk `ch` (0..15) of row `row` (0..15) inside a 4 KB tile
-__device__ __forceinline__ uint32_t swz(int row, int ch) { return (uint32_t)(row * 256 + ((ch ^ (row & 7)) << 4)); }
+// Byte offset of 16-byte chunk `ch` (0..15, dims 8ch..8ch+7) of key row `row` (0..15) in a
+// 4 KB K or V tile as TMA writes it: two halves of 16 rows x 128 B (dims 0-63, 64-127), each
+// SWIZZLE_128B (chunk c of row r at c ^ (r & 7); the tile is 1024-byte aligned).
+__device__ __forceinline__ uint32_t swz(int row, int ch) {
+    return (uint32_t)(((ch >> 3) << 11) + row * 128 + (((ch & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"((uint32_t)__cvta_generic_to_shared(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"((uint32_t)__cvta_generic_to_shared(b)) : "memory");
+}
+// bounded wait; false if the phase did not complete within the poll limit
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *b, uint32_t parity) {
+    for (uint32_t i = 0; i < kAttnWaitLimit; ++i)
+        if (mbar_try_wait(b, parity)) return true;
+    return false;
+}
+// 3-D tile copy global -> shared (no multicast), completing on an mbarrier
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            dst),
+        "l"(map), "r"((uint32_t)__cvta_generic_to_shared(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
 
 struct AttnParams {
     const __nv_bfloat16 *q;      // [total_q, nh, 128]
@@ -174,15 +211,21 @@ struct AttnParams {
     __nv_bfloat16 *out;          // [total_q, nh*128]
     float *part_o;               // [splits, total_q, nh, 128]
     float *part_ml;              // [splits, total_q, nh, 2]
+    int *err;                    // device error word: set when a page wait gave up
     int nh, nkv, gsz, max_blocks, num_blocks, total_q;
     int splits, pages_per_split, row_chunk;  // rows per CTA = 16 * MT; pages_per_split: host sizing only
     float scale;                 // rne_bf16-compatible fp32 value of 1/sqrt(head_dim)
 };
 
-// grid: (splits, nkv * row_chunks, B); block: 128 threads
+// grid: (splits, nkv * row_chunks, B); block: 128 threads.  kmap / vmap: the K and V
+// caches as 3-D tensors (dim, kv head, slot) with 64 x 1 x 16 SWIZZLE_128B boxes.
 template <int MT>
-__global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const AttnParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const __grid_constant__ CUtensorMap kmap,
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             const AttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kWarps][kStages];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = lane >> 2, c = lane & 3;
     const int split = blockIdx.x;
@@ -247,44 +290,72 @@ __global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const AttnParams p
         lrow[mt][0] = lrow[mt][1] = 0.f;
     }
 
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < kWarps; ++w)
+            for (int st = 0; st < kStages; ++st) mbar_init(&full_bar[w][st], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
     uint8_t *ring = smem + (size_t)warp * kStages * 2 * kPageBytes;
     const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
     const int32_t *bt = p.block_table + (size_t)b * p.max_blocks;
-    const size_t kv_row_stride = (size_t)p.nkv * kHD;  // elements between consecutive slots
 
     // pages handled by this warp: pg0 + warp, pg0 + warp + 4, ... (< pg_vis)
+    const int n_it = pg_vis > pg0 + warp ? (pg_vis - (pg0 + warp) + kWarps - 1) / kWarps : 0;
+    int issued = 0;  // lane 0's count of pages put in flight
+    // lane 0 loads page `it` of this warp into `stage`: K and V of this KV head, 8 KB.
+    // The stage's previous contents were read (ldmatrix) or written (zeroing) through
+    // the generic proxy, which the proxy fence orders before the TMA's writes.
     auto issue = [&](int it, int stage) {
+        if (lane != 0 || it >= n_it) return;
         const int pg = pg0 + warp + it * kWarps;
-        const uint32_t kdst = ring_s + stage * 2 * kPageBytes, vdst = kdst + kPageBytes;
-        if (pg < pg_vis) {
-            int blk = bt[pg];
-            const bool blk_ok = blk >= 0 && blk < p.num_blocks;
-            if (!blk_ok) blk = 0;
-            const int valid = min(16, ctx - pg * 16);  // tokens of this page inside the context
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int idx = lane + 32 * e;  // 256 chunks: row = idx / 16, ch = idx % 16
-                const int row = idx >> 4, ch = idx & 15;
-                const int bytes = (blk_ok && row < valid) ? 16 : 0;
-                const size_t off = ((size_t)blk * 16 + row) * kv_row_stride + (size_t)kvh * kHD + ch * 8;
-                cp_async16(kdst + swz(row, ch), p.kc + off, bytes);
-                cp_async16(vdst + swz(row, ch), p.vc + off, bytes);
-            }
-        }
-        cp_async_commit();
+        int blk = bt[pg];
+        if (blk < 0 || blk >= p.num_blocks) blk = 0;  // zeroed after it lands
+        const uint32_t dst = ring_s + stage * 2 * kPageBytes;
+        uint64_t *bar = &full_bar[warp][stage];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bar, 2 * kPageBytes);
+        tma_load_3d(dst, &kmap, bar, 0, kvh, blk * 16);
+        tma_load_3d(dst + kPageBytes / 2, &kmap, bar, 64, kvh, blk * 16);
+        tma_load_3d(dst + kPageBytes, &vmap, bar, 0, kvh, blk * 16);
+        tma_load_3d(dst + kPageBytes + kPageBytes / 2, &vmap, bar, 64, kvh, blk * 16);
+        ++issued;
     };
 
-    const int n_it = pg_vis > pg0 + warp ? (pg_vis - (pg0 + warp) + kWarps - 1) / kWarps : 0;
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) issue(s, s);
 
+    int consumed = 0;
     for (int it = 0; it < n_it; ++it) {
         issue(it + kStages - 1, (it + kStages - 1) % kStages);
-        cp_async_wait<kStages - 1>();
-        __syncwarp();
         const int stage = it % kStages;
+        const bool landed = mbar_wait_bounded(&full_bar[warp][stage], (uint32_t)(it / kStages) & 1u);
+        if (!__all_sync(0xffffffffu, landed)) {
+            if (lane == 0) atomicExch(p.err, 1);
+            break;
+        }
+        consumed = it + 1;
         const uint32_t ks_base = ring_s + stage * 2 * kPageBytes, vs_base = ks_base + kPageBytes;
         const int pg = pg0 + warp + it * kWarps;
+        {
+            // keys past the context get P = 0, so their V rows must be finite: zero them
+            // (and the whole page for an invalid block id, whose K then scores 0)
+            const int blk = bt[pg];
+            const bool blk_ok = blk >= 0 && blk < p.num_blocks;
+            const int valid = min(16, ctx - pg * 16);
+            if (!blk_ok || valid < 16) {
+                const int r0 = blk_ok ? valid : 0;
+                uint8_t *kp = ring + (size_t)stage * 2 * kPageBytes, *vp = kp + kPageBytes;
+                for (int idx = lane; idx < (16 - r0) * 16; idx += 32) {
+                    const int row = r0 + (idx >> 4), ch = idx & 15;
+                    const size_t off = (size_t)((ch >> 3) << 11) + row * 128 + ((ch & 7) << 4);
+                    *reinterpret_cast<uint4 *>(vp + off) = make_uint4(0u, 0u, 0u, 0u);
+                    if (!blk_ok) *reinterpret_cast<uint4 *>(kp + off) = make_uint4(0u, 0u, 0u, 0u);
+                }
+                __syncwarp();
+            }
+        }
 
         // ---- S = Q K^T over the 16 keys of the page ----
         float sacc[MT][2][4];
@@ -371,7 +442,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const AttnParams p
         }
         __syncwarp();
     }
-    cp_async_wait<0>();
+    if (lane == 0) {  // after a failed wait: the copies still in flight land before the CTA exits
+        for (int j = consumed; j < issued; ++j) mbar_wait_bounded(&full_bar[warp][j % kStages], (uint32_t)(j / kStages) & 1u);
+    }
+    __syncwarp();
     __syncthreads();
 
     // ---- merge the 4 warps: smem holds per-warp m, l and O (fp32) ----
@@ -462,11 +536,548 @@ __global__ void attn_merge(const AttnParams p) {
     p.out[(size_t)item * kHD + d] = f2bf(v);
 }
 
+// ---------------------------------------------------------------------------------
+// Whole-page persistent attention.
+//
+// Reading one KV head at a time touches 256 of every 2048 bytes of a slot row (the other
+// heads' bytes go to other CTAs), which holds a read-only stream near 5.9 TB/s on B200;
+// reading whole pages (16 slots x all KV heads, 32 KB of K and 32 KB of V contiguous)
+// reaches about 6.8 TB/s.  So here one CTA per SM takes a contiguous range of the batch's
+// page list (every sequence's pages, in sequence order): a producer warp streams whole
+// pages through a TMA ring, and consumer warp h computes KV head h's query rows against
+// them with the same per-page math as attn_verify.  A sequence lying entirely inside one
+// CTA's range is finished there; a sequence cut by range boundaries leaves one partial
+// (m, l, O) per CTA (slot 0 if it is the CTA's first sequence, else slot 1), which
+// attn_merge_pages combines in CTA order.  The ranges come from the context lengths on
+// the device, so a captured launch stays valid as contexts grow.
+// ---------------------------------------------------------------------------------
+constexpr int kPMaxKv = 8;       // KV heads per CTA (one consumer warp each)
+constexpr int kPStages = 3;      // pages in flight
+constexpr int kPMaxSeqs = 1024;  // sequences per call (page prefix kept in shared memory)
+
+struct PageAttnParams {
+    const __nv_bfloat16 *q;      // [total_q, nh, 128]
+    const int32_t *block_table;  // [B, max_blocks]
+    const int32_t *cu_q;         // [B+1]
+    const int32_t *ctx;          // [B]
+    const __nv_bfloat16 *gate;   // [total_q, nh*128] or null
+    __nv_bfloat16 *out;          // [total_q, nh*128]
+    float *part;                 // [G][2][max_q][nh][128 + 2]: O, m, l
+    int *prefix;                 // [B+1] pages before each sequence (CTA 0 writes it for the merge)
+    int *err;                    // device error word
+    int nh, nkv, gsz, max_blocks, num_blocks, B, max_q, G, total_q;
+    float scale;
+};
+
+// CTA whose page range [c*T/G, (c+1)*T/G) holds page x
+__device__ __forceinline__ int cta_of_page(long long x, long long T, int G) {
+    int c = (int)((x * G) / T);
+    if (c >= G) c = G - 1;
+    while (c + 1 < G && ((long long)(c + 1) * T) / G <= x) ++c;
+    while (c > 0 && ((long long)c * T) / G > x) --c;
+    return c;
+}
+
+// byte offset of 16-byte chunk ch of key row `row` in one head's tile of a page stage:
+// the tile's two 128-byte halves are hs bytes apart (SWIZZLE_128B, 1024-byte aligned)
+__device__ __forceinline__ uint32_t pswz(int row, int ch, uint32_t hs) {
+    return (uint32_t)((ch >> 3) * hs + row * 128 + (((ch & 7) ^ (row & 7)) << 4));
+}
+
+// grid: G (one CTA per SM); block: (nkv + 1) warps, warp nkv is the producer.  kmap / vmap:
+// the caches as (dim, slot, head) tensors with 64 x 16 x nkv SWIZZLE_128B boxes.
+template <int MT>
+__global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid_constant__ CUtensorMap kmap,
+                                                                    const __grid_constant__ CUtensorMap vmap,
+                                                                    const PageAttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ int s_prefix[kPMaxSeqs + 1];
+    __shared__ __align__(8) uint64_t full_bar[kPStages], empty_bar[kPStages];
+    __shared__ int s_blk_ok[kPStages];  // the stage's block id was valid (else zero its tiles)
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkv = p.nkv;
+    const int cta = blockIdx.x;
+    const uint32_t hs = (uint32_t)nkv * 2048;       // bytes of one 128-byte half for all heads
+    const uint32_t stage_bytes = 4 * hs;             // K (2 halves) + V (2 halves)
+
+    if (warp == 0) {  // page prefix over the sequences, 32 per pass
+        int carry = 0;
+        if (lane == 0) s_prefix[0] = 0;
+        for (int b0 = 0; b0 < p.B; b0 += 32) {
+            const int b = b0 + lane;
+            int pages = 0;
+            if (b < p.B) {
+                const int cx = p.ctx[b];
+                pages = cx > 0 ? (cx + 15) >> 4 : 0;
+            }
+            int incl = pages;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (b < p.B) s_prefix[b + 1] = carry + incl;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+    }
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kPStages; ++st) {
+            mbar_init(&full_bar[st], 1);
+            mbar_init(&empty_bar[st], (uint32_t)nkv);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (cta == 0)
+        for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.prefix[i] = s_prefix[i];
+    const long long T = s_prefix[p.B];
+    const long long s_c = ((long long)cta * T) / p.G, e_c = ((long long)(cta + 1) * T) / p.G;
+    if (s_c >= e_c) return;
+    // largest b with prefix[b] <= x (sequences without pages are skipped)
+    auto seq_of = [&](long long x) {
+        int lo = 0, hi = p.B - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_prefix[mid] <= x) lo = mid; else hi = mid - 1;
+        }
+        return lo;
+    };
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(smem);
+
+    if (warp == nkv) {
+        // ---- producer: whole pages (K and V of every KV head) into the ring.  The warp
+        // fetches the block ids of 32 pages at once (one per lane); lane 0 issues. ----
+        int b = seq_of(s_c);
+        int issued = 0;
+        bool stop = false;
+        for (long long xb = s_c; xb < e_c && !stop; xb += 32) {
+            const long long x = xb + lane;
+            int blk = -1, bb = b;
+            if (x < e_c) {
+                while (x >= s_prefix[bb + 1]) ++bb;
+                blk = p.block_table[(size_t)bb * p.max_blocks + (int)(x - s_prefix[bb])];
+            }
+            b = __shfl_sync(0xffffffffu, bb, 31);  // sequence of the chunk's last lane (>= any page issued)
+            const int n = (int)min((long long)32, e_c - xb);
+            for (int k = 0; k < n; ++k) {
+                const int blk_k = __shfl_sync(0xffffffffu, blk, k);
+                int ok = 1;
+                if (lane == 0) {
+                    const int st = issued % kPStages;
+                    // stage st held page issued - kPStages: every consumer warp has released it
+                    if (issued >= kPStages &&
+                        !mbar_wait_bounded(&empty_bar[st], (uint32_t)((issued / kPStages) - 1) & 1u)) {
+                        atomicExch(p.err, 1);
+                        ok = 0;
+                    } else {
+                        const bool valid = blk_k >= 0 && blk_k < p.num_blocks;
+                        const int blk_use = valid ? blk_k : 0;  // zeroed by the consumers
+                        s_blk_ok[st] = valid ? 1 : 0;           // published by the arrive below
+                        const uint32_t base = ring_s + (uint32_t)st * stage_bytes;
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        mbar_expect_tx(&full_bar[st], stage_bytes);
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {  // one box: half hf of the page, all heads
+                            tma_load_3d(base + hf * hs, &kmap, &full_bar[st], 64 * hf, blk_use * 16, 0);
+                            tma_load_3d(base + (2 + hf) * hs, &vmap, &full_bar[st], 64 * hf, blk_use * 16, 0);
+                        }
+                        ++issued;
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    stop = true;
+                    break;
+                }
+            }
+        }
+        if (lane == 0)  // every copy issued has landed before the CTA may exit
+            for (int j = issued > kPStages ? issued - kPStages : 0; j < issued; ++j)
+                mbar_wait_bounded(&full_bar[j % kPStages], (uint32_t)(j / kPStages) & 1u);
+        __syncwarp();
+        return;
+    }
+
+    // ---- consumer warp h: query rows of KV head h against every page of the range ----
+    const int h = warp;
+    const int r = lane >> 2, c = lane & 3;
+    int b = seq_of(s_c);
+    long long x = s_c;
+    int i = 0;  // pages consumed by this warp
+    while (x < e_c) {
+        while (x >= s_prefix[b + 1]) ++b;
+        const long long seg0 = x, seg1 = min(e_c, (long long)s_prefix[b + 1]);
+        const bool whole = seg0 == s_prefix[b] && seg1 == s_prefix[b + 1];
+        const int slot = seg0 == s_c ? 0 : 1;
+        const int q0 = p.cu_q[b], q_len = p.cu_q[b + 1] - q0, ctx = p.ctx[b];
+        const int R = q_len * p.gsz;
+        const bool active = q_len > 0 && R <= 16 * MT;
+        const int p0 = ctx - q_len;
+
+        uint32_t qf[MT][8][4];
+        int qpos[MT][2];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const int rho = mt * 16 + r + hh * 8;
+                const bool ok = active && rho < R;
+                const int j = ok ? rho / p.gsz : 0, g = ok ? rho % p.gsz : 0;
+                qpos[mt][hh] = ok ? p0 + j : -1;
+                const __nv_bfloat16 *qrow = p.q + ((size_t)(q0 + j) * p.nh + (size_t)h * p.gsz + g) * kHD;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    qf[mt][ks][hh] = ok ? *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + 2 * c) : 0u;
+                    qf[mt][ks][2 + hh] = ok ? *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + 8 + 2 * c) : 0u;
+                }
+            }
+        float o[MT][16][4];
+        float mrow[MT][2], lrow[MT][2];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+            for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o[mt][nt][j] = 0.f;
+            mrow[mt][0] = mrow[mt][1] = -INFINITY;
+            lrow[mt][0] = lrow[mt][1] = 0.f;
+        }
+
+        bool failed = false;
+        for (; x < seg1; ++x, ++i) {
+            const int st = i % kPStages;
+            const bool landed = mbar_wait_bounded(&full_bar[st], (uint32_t)(i / kPStages) & 1u);
+            if (!__all_sync(0xffffffffu, landed)) {
+                if (lane == 0) atomicExch(p.err, 1);
+                failed = true;
+                break;
+            }
+            const int pg = (int)(x - s_prefix[b]);
+            uint8_t *kp = smem + (size_t)st * stage_bytes + h * 2048;
+            uint8_t *vp = kp + 2 * hs;
+            {
+                // keys past the context get P = 0, so their V rows must be finite: zero them
+                // (and this head's whole page for an invalid block id, whose K then scores 0)
+                const bool blk_ok = s_blk_ok[st] != 0;
+                const int valid = min(16, ctx - pg * 16);
+                if (!blk_ok || valid < 16) {
+                    const int r0 = blk_ok ? valid : 0;
+                    for (int idx = lane; idx < (16 - r0) * 16; idx += 32) {
+                        const int row = r0 + (idx >> 4), ch = idx & 15;
+                        const size_t off = (size_t)(ch >> 3) * hs + row * 128 + ((ch & 7) << 4);
+                        *reinterpret_cast<uint4 *>(vp + off) = make_uint4(0u, 0u, 0u, 0u);
+                        if (!blk_ok) *reinterpret_cast<uint4 *>(kp + off) = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                    __syncwarp();
+                }
+            }
+            if (active) {
+                const uint32_t ks_base = (uint32_t)__cvta_generic_to_shared(kp);
+                const uint32_t vs_base = (uint32_t)__cvta_generic_to_shared(vp);
+                float sacc[MT][2][4];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) sacc[mt][nt][j] = 0.f;
+                {
+                    const int qm = lane >> 3, i8 = lane & 7;
+                    const int key = (qm >= 2 ? 8 : 0) + i8;
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks) {
+                        uint32_t b00, b01, b10, b11;
+                        ldsm_x4(ks_base + pswz(key, 2 * ks + (qm & 1), hs), b00, b01, b10, b11);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            mma16816(sacc[mt][0], qf[mt][ks], b00, b01);
+                            mma16816(sacc[mt][1], qf[mt][ks], b10, b11);
+                        }
+                    }
+                }
+                uint32_t pa[MT][4];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float mx = -INFINITY;
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int kpos = pg * 16 + nt * 8 + 2 * c + e;
+                                float sv = sacc[mt][nt][hh * 2 + e];
+                                // scores = bmm(q, k^T) in bf16, then * scale in bf16 (attention.py:128-129)
+                                sv = bf16_round(__fmul_rn(bf16_round(sv), p.scale));
+                                if (kpos > qpos[mt][hh] || kpos >= ctx) sv = -INFINITY;
+                                sacc[mt][nt][hh * 2 + e] = sv;
+                                mx = fmaxf(mx, sv);
+                            }
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                        const float mnew = fmaxf(mrow[mt][hh], mx);
+                        const float alpha = (mnew == -INFINITY) ? 1.f : expf(mrow[mt][hh] - mnew);
+                        mrow[mt][hh] = mnew;
+                        float ls = 0.f;
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const float sv = sacc[mt][nt][hh * 2 + e];
+                                const float pv = (sv == -INFINITY) ? 0.f : expf(sv - mnew);
+                                sacc[mt][nt][hh * 2 + e] = pv;
+                                ls += pv;
+                            }
+                        lrow[mt][hh] = lrow[mt][hh] * alpha + ls;
+#pragma unroll
+                        for (int nt = 0; nt < 16; ++nt) {
+                            o[mt][nt][hh * 2 + 0] *= alpha;
+                            o[mt][nt][hh * 2 + 1] *= alpha;
+                        }
+                    }
+                    pa[mt][0] = pack_bf16(sacc[mt][0][0], sacc[mt][0][1]);
+                    pa[mt][1] = pack_bf16(sacc[mt][0][2], sacc[mt][0][3]);
+                    pa[mt][2] = pack_bf16(sacc[mt][1][0], sacc[mt][1][1]);
+                    pa[mt][3] = pack_bf16(sacc[mt][1][2], sacc[mt][1][3]);
+                }
+                {
+                    const int qm = lane >> 3, i8 = lane & 7;
+                    const int key = ((qm & 1) ? 8 : 0) + i8;
+#pragma unroll
+                    for (int dp = 0; dp < 8; ++dp) {
+                        uint32_t b0a, b1a, b0b, b1b;
+                        ldsm_x4_t(vs_base + pswz(key, 2 * dp + (qm >> 1), hs), b0a, b1a, b0b, b1b);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt) {
+                            mma16816(o[mt][2 * dp], pa[mt], b0a, b1a);
+                            mma16816(o[mt][2 * dp + 1], pa[mt], b0b, b1b);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty_bar[st]);  // this warp is done with the stage
+        }
+        if (failed) break;
+        if (!active) continue;
+
+        // ---- finish the segment: the final output, or this CTA's partial ----
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                float l = lrow[mt][hh];
+                l += __shfl_xor_sync(0xffffffffu, l, 1);
+                l += __shfl_xor_sync(0xffffffffu, l, 2);
+                const int rho = mt * 16 + r + hh * 8;
+                if (rho >= R) continue;
+                const int j = rho / p.gsz, g = rho % p.gsz;
+                const int qrow = q0 + j, head = h * p.gsz + g;
+                if (whole) {
+                    const size_t ob = (size_t)qrow * p.nh * kHD + (size_t)head * kHD;
+#pragma unroll
+                    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int d = nt * 8 + 2 * c + e;
+                            float v = l > 0.f ? bf16_round(__fdiv_rn(o[mt][nt][hh * 2 + e], l)) : 0.f;
+                            if (p.gate) {
+                                const float gt = bf2f(p.gate[ob + d]);
+                                const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt))));
+                                v = __fmul_rn(v, sg);
+                            }
+                            p.out[ob + d] = f2bf(v);
+                        }
+                } else {
+                    float *rec = p.part + ((((size_t)cta * 2 + slot) * p.max_q + j) * p.nh + head) * (kHD + 2);
+#pragma unroll
+                    for (int nt = 0; nt < 16; ++nt) {
+                        rec[nt * 8 + 2 * c] = o[mt][nt][hh * 2 + 0];
+                        rec[nt * 8 + 2 * c + 1] = o[mt][nt][hh * 2 + 1];
+                    }
+                    if (c == 0) {
+                        rec[kHD] = mrow[mt][hh];
+                        rec[kHD + 1] = l;
+                    }
+                }
+            }
+    }
+}
+
+// grid: total_q * nh; block: 128 (one thread per dim).  Combines the per-CTA partials of
+// sequences that were cut by CTA range boundaries, in CTA order.
+__global__ void attn_merge_pages(const PageAttnParams p) {
+    const int item = blockIdx.x;
+    const int d = threadIdx.x;
+    if (item >= p.total_q * p.nh) return;
+    const int qrow = item / p.nh, head = item % p.nh;
+    int lo = 0, hi = p.B - 1;  // sequence of this row: largest b with cu_q[b] <= qrow
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.cu_q[mid] <= qrow) lo = mid; else hi = mid - 1;
+    }
+    const int b = lo, j = qrow - p.cu_q[b];
+    const long long T = p.prefix[p.B];
+    const long long P0 = p.prefix[b], P1 = p.prefix[b + 1];
+    if (P1 <= P0 || T <= 0) return;
+    const int c0 = cta_of_page(P0, T, p.G), c1 = cta_of_page(P1 - 1, T, p.G);
+    if (c0 == c1) return;  // finished by its CTA
+    // CTAs between c0 and c1 with an empty range (more CTAs than pages) wrote nothing
+    auto empty = [&](int c) { return ((long long)c * T) / p.G == ((long long)(c + 1) * T) / p.G; };
+    float M = -INFINITY;
+    for (int c = c0; c <= c1; ++c) {
+        if (empty(c)) continue;
+        const int slot = ((long long)c * T) / p.G >= P0 ? 0 : 1;
+        const float *rec = p.part + ((((size_t)c * 2 + slot) * p.max_q + j) * p.nh + head) * (kHD + 2);
+        if (rec[kHD + 1] > 0.f) M = fmaxf(M, rec[kHD]);
+    }
+    float L = 0.f, O = 0.f;
+    for (int c = c0; c <= c1; ++c) {
+        if (empty(c)) continue;
+        const int slot = ((long long)c * T) / p.G >= P0 ? 0 : 1;
+        const float *rec = p.part + ((((size_t)c * 2 + slot) * p.max_q + j) * p.nh + head) * (kHD + 2);
+        const float l = rec[kHD + 1];
+        if (!(l > 0.f)) continue;
+        const float f = expf(rec[kHD] - M);
+        L += l * f;
+        O += rec[d] * f;
+    }
+    float v = L > 0.f ? bf16_round(__fdiv_rn(O, L)) : 0.f;
+    const size_t ob = (size_t)qrow * p.nh * kHD + (size_t)head * kHD;
+    if (p.gate) {
+        const float gt = bf2f(p.gate[ob + d]);
+        const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt))));
+        v = __fmul_rn(v, sg);
+    }
+    p.out[ob + d] = f2bf(v);
+}
+
 // Clear the split partials of every (row, head) so that CTAs which exit early (no
 // rows or no visible pages in their split) leave an empty record (l = 0).
 __global__ void attn_clear_ml(float *ml, size_t n) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         ml[i] = (i & 1) ? 0.f : -INFINITY;
+}
+
+// K/V cache [num_blocks * 16 slots, n_kv, 128] bf16 as a 3-D tensor (dim, head, slot);
+// one box is 64 dims x 1 head x 16 slots (a 128-byte SWIZZLE_128B half of one head's page)
+int encode_kv_maps(const __nv_bfloat16 *kc, const __nv_bfloat16 *vc, int nkv, int num_blocks, CUtensorMap (&maps)[2],
+                   const char *what) {
+    TensorMapEncodeTiledFn enc = tensor_map_encoder();
+    PILM_REQUIRE(enc, ECPU_ERR_UNSUPPORTED, "%s: cuTensorMapEncodeTiled is unavailable", what);
+    PILM_REQUIRE((((uintptr_t)kc) & 15) == 0 && (((uintptr_t)vc) & 15) == 0, ECPU_ERR_PARAM,
+                 "%s: the K and V caches must be 16-byte aligned", what);
+    const __nv_bfloat16 *src[2] = {kc, vc};
+    for (int i = 0; i < 2; ++i) {
+        cuuint64_t dims[3] = {(cuuint64_t)kHD, (cuuint64_t)nkv, (cuuint64_t)num_blocks * 16};
+        cuuint64_t strides[2] = {(cuuint64_t)kHD * 2, (cuuint64_t)nkv * kHD * 2};
+        cuuint32_t box[3] = {64, 1, 16};
+        cuuint32_t es[3] = {1, 1, 1};
+        const CUresult r = enc(&maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void *)src[i], dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        PILM_REQUIRE(r == CUDA_SUCCESS, ECPU_ERR_PARAM, "%s: the K/V cache tensor map was rejected (error %d)", what,
+                     (int)r);
+    }
+    return ECPU_OK;
+}
+
+// K/V cache as a 3-D tensor (dim, slot, head): one box of 64 dims x 16 slots x all heads
+// is a 128-byte half of a whole page, landing as [head][slot][128 B] (each head's 16 rows
+// a 2 KB, 1024-byte aligned SWIZZLE_128B block).  Four boxes load a page's K and V.
+int encode_kv_page_maps(const __nv_bfloat16 *kc, const __nv_bfloat16 *vc, int nkv, int num_blocks,
+                        CUtensorMap (&maps)[2], const char *what) {
+    TensorMapEncodeTiledFn enc = tensor_map_encoder();
+    PILM_REQUIRE(enc, ECPU_ERR_UNSUPPORTED, "%s: cuTensorMapEncodeTiled is unavailable", what);
+    PILM_REQUIRE((((uintptr_t)kc) & 15) == 0 && (((uintptr_t)vc) & 15) == 0, ECPU_ERR_PARAM,
+                 "%s: the K and V caches must be 16-byte aligned", what);
+    const __nv_bfloat16 *src[2] = {kc, vc};
+    for (int i = 0; i < 2; ++i) {
+        cuuint64_t dims[3] = {(cuuint64_t)kHD, (cuuint64_t)num_blocks * 16, (cuuint64_t)nkv};
+        cuuint64_t strides[2] = {(cuuint64_t)nkv * kHD * 2, (cuuint64_t)kHD * 2};
+        cuuint32_t box[3] = {64, 16, (cuuint32_t)nkv};
+        cuuint32_t es[3] = {1, 1, 1};
+        const CUresult r = enc(&maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void *)src[i], dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        PILM_REQUIRE(r == CUDA_SUCCESS, ECPU_ERR_PARAM, "%s: the K/V page tensor map was rejected (error %d)", what,
+                     (int)r);
+    }
+    return ECPU_OK;
+}
+
+// The whole-page persistent kernel and its merge; ECPU_ERR_UNSUPPORTED (nothing launched)
+// for shapes it does not take: more than 8 KV heads, more than 1024 sequences, or more
+// than 16 query rows per KV head (q_len x n_heads / n_kv; more would spill registers).
+int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnParams &a, const char *what) {
+    const int max_q = (int)(desc->max_q_len ? desc->max_q_len : 1);
+    const int R = max_q * a.gsz;
+    if (a.nkv > kPMaxKv || desc->num_seqs > (size_t)kPMaxSeqs || R > 16) return ECPU_ERR_UNSUPPORTED;
+    PageAttnParams p;
+    p.q = a.q;
+    p.block_table = a.block_table;
+    p.cu_q = a.cu_q;
+    p.ctx = a.ctx;
+    p.gate = a.gate;
+    p.out = a.out;
+    p.nh = a.nh;
+    p.nkv = a.nkv;
+    p.gsz = a.gsz;
+    p.max_blocks = a.max_blocks;
+    p.num_blocks = a.num_blocks;
+    p.B = (int)desc->num_seqs;
+    p.max_q = max_q;
+    p.G = num_sms();
+    p.total_q = a.total_q;
+    p.scale = a.scale;
+    p.err = device_error_word();
+    PILM_REQUIRE(p.err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
+    const size_t part_bytes = (size_t)p.G * 2 * max_q * p.nh * (kHD + 2) * sizeof(float);
+    char *ws = (char *)scratch(kScratchAttn, part_bytes + ((size_t)p.B + 1) * sizeof(int) + 256);
+    PILM_REQUIRE(ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+    p.part = (float *)ws;
+    p.prefix = (int *)(ws + part_bytes);
+    CUtensorMap maps[2];
+    int rc = encode_kv_page_maps(a.kc, a.vc, a.nkv, a.num_blocks, maps, what);
+    if (rc != ECPU_OK) return rc;
+    const size_t smem = (size_t)kPStages * 4 * p.nkv * 2048 + 1024;  // + alignment slack
+    const unsigned threads = (unsigned)(p.nkv + 1) * 32;
+    cudaFuncSetAttribute(attn_pages<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attn_pages<1><<<p.G, threads, smem, stream()>>>(maps[0], maps[1], p);
+    rc = check_launch(what);
+    if (rc != ECPU_OK) return rc;
+    rc = check_error_word(what, "a K/V page load did not complete");
+    if (rc != ECPU_OK) return rc;
+    attn_merge_pages<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
+    return check_launch(what);
+}
+
+// Encodes the K/V tensor maps, launches attn_verify (and attn_merge when split), and in
+// synchronous mode reports a page wait that gave up.
+int launch_attention(AttnParams &p, const ekernel_paged_attn_desc_t *desc, int MT, int row_chunks, int splits,
+                     const char *what) {
+    p.err = device_error_word();
+    PILM_REQUIRE(p.err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
+    CUtensorMap maps[2];
+    int rc0 = encode_kv_maps(p.kc, p.vc, p.nkv, p.num_blocks, maps, what);
+    if (rc0 != ECPU_OK) return rc0;
+    const size_t ring = (size_t)kWarps * kStages * 2 * kPageBytes;
+    const size_t mergebuf = (size_t)kWarps * 16 * MT * (kHD + 2) * sizeof(float);
+    const size_t smem = (ring > mergebuf ? ring : mergebuf) + 1024;  // + alignment slack
+    dim3 grid(splits, p.nkv * row_chunks, (unsigned)desc->num_seqs);
+    if (MT == 1) {
+        cudaFuncSetAttribute(attn_verify<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_verify<1><<<grid, kWarps * 32, smem, stream()>>>(maps[0], maps[1], p);
+    } else {
+        cudaFuncSetAttribute(attn_verify<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_verify<2><<<grid, kWarps * 32, smem, stream()>>>(maps[0], maps[1], p);
+    }
+    int rc = check_launch(what);
+    if (rc != ECPU_OK) return rc;
+    rc = check_error_word(what, "a K/V page load did not complete");
+    if (rc != ECPU_OK || splits == 1) return rc;
+    attn_merge<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
+    return check_launch(what);
 }
 
 int check_desc(const ekernel_paged_attn_desc_t *d, const char *what) {
@@ -538,6 +1149,10 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
     // narrowed to fp32 (the bf16 kernel's opmath type)
     p.scale = (float)(1.0 / sqrt((double)kHD));
 
+    // whole pages per CTA where the shape allows it, else the per-head split kernel
+    rc = launch_attention_pages(desc, p, what);
+    if (rc != ECPU_ERR_UNSUPPORTED) return rc;
+
     const int rows = (int)(desc->max_q_len ? desc->max_q_len : 1) * p.gsz;
     const int MT = rows > 16 ? 2 : 1;
     const int row_chunks = (rows + 16 * MT - 1) / (16 * MT);
@@ -568,21 +1183,7 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
-    const size_t ring = (size_t)kWarps * kStages * 2 * kPageBytes;
-    const size_t mergebuf = (size_t)kWarps * 16 * MT * (kHD + 2) * sizeof(float);
-    const size_t smem = ring > mergebuf ? ring : mergebuf;
-    dim3 grid(splits, p.nkv * row_chunks, (unsigned)desc->num_seqs);
-    if (MT == 1) {
-        cudaFuncSetAttribute(attn_verify<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_verify<1><<<grid, kWarps * 32, smem, stream()>>>(p);
-    } else {
-        cudaFuncSetAttribute(attn_verify<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_verify<2><<<grid, kWarps * 32, smem, stream()>>>(p);
-    }
-    rc = check_launch(what);
-    if (rc != ECPU_OK || splits == 1) return rc;
-    attn_merge<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
-    return check_launch(what);
+    return launch_attention(p, desc, MT, row_chunks, splits, what);
 }
 
 }  // extern "C"
@@ -658,7 +1259,8 @@ extern "C" int ekernel_paged_attention_verify_noalloc(const ekernel_paged_attn_d
     p.total_q = (int)desc->total_q;
     p.scale = (float)(1.0 / sqrt((double)kHD));
 
-    // the same split choice as ekernel_paged_attention_verify, so both give the same result
+    // the per-head split kernel (its partials are bounded by the split count, so they fit the
+    // fixed array); results agree with ekernel_paged_attention_verify within fp32 rounding
     const int rows = (int)(desc->max_q_len ? desc->max_q_len : 1) * p.gsz;
     const int MT = rows > 16 ? 2 : 1;
     const int row_chunks = (rows + 16 * MT - 1) / (16 * MT);
@@ -696,19 +1298,5 @@ extern "C" int ekernel_paged_attention_verify_noalloc(const ekernel_paged_attn_d
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
-    const size_t ring = (size_t)kWarps * kStages * 2 * kPageBytes;
-    const size_t mergebuf = (size_t)kWarps * 16 * MT * (kHD + 2) * sizeof(float);
-    const size_t smem = ring > mergebuf ? ring : mergebuf;
-    dim3 grid(splits, p.nkv * row_chunks, (unsigned)desc->num_seqs);
-    if (MT == 1) {
-        cudaFuncSetAttribute(attn_verify<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_verify<1><<<grid, kWarps * 32, smem, stream()>>>(p);
-    } else {
-        cudaFuncSetAttribute(attn_verify<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_verify<2><<<grid, kWarps * 32, smem, stream()>>>(p);
-    }
-    rc = check_launch(what);
-    if (rc != ECPU_OK || splits == 1) return rc;
-    attn_merge<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
-    return check_launch(what);
+    return launch_attention(p, desc, MT, row_chunks, splits, what);
 }

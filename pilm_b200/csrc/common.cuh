@@ -1,6 +1,7 @@
 // Shared device/host helpers for libpilm_cuda (sm_100a only).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -36,6 +37,19 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
 // 2 = W8 per-row.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
                 const char *what);
+
+// cuTensorMapEncodeTiled, reached through the runtime's driver entry point (no link
+// against libcuda); null if the driver does not provide it.
+typedef CUresult (*TensorMapEncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                           const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                           const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                           CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+TensorMapEncodeTiledFn tensor_map_encoder();
+// Device word that pipelined kernels set when a bounded wait gave up (null if it could not
+// be allocated).  In synchronous mode check_error_word reads and clears it and turns a set
+// word into ECPU_ERR_KERNEL with the message "<what>: <msg>".
+int *device_error_word();
+int check_error_word(const char *what, const char *msg);
 
 // Post-launch check: ECPU_ERR_KERNEL on a launch error; in synchronous mode
 // (PILM_CUDA_SYNC=1) also waits for the stream and reports execution errors.

@@ -528,32 +528,6 @@ __global__ void __launch_bounds__(256) splitk_combine(const float *__restrict__ 
 }
 
 // ---- host side ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    });
-    return fn;
-}
-
-int *device_error_word() {
-    static int *err = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        if (cudaMalloc(&err, sizeof(int)) == cudaSuccess) cudaMemset(err, 0, sizeof(int));
-    });
-    return err;
-}
-
 }  // namespace
 
 namespace pilm {
@@ -563,7 +537,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     static const bool disabled = getenv("PILM_DISABLE_TC") && getenv("PILM_DISABLE_TC")[0] == '1';
     if (disabled || M < 64 || (K % 128) != 0 || N < 1) return ECPU_ERR_UNSUPPORTED;
     if ((((uintptr_t)X) & 15) || (((uintptr_t)W) & 15)) return ECPU_ERR_UNSUPPORTED;
-    EncodeTiledFn enc = encode_fn();
+    TensorMapEncodeTiledFn enc = tensor_map_encoder();
     int *err = device_error_word();
     if (!enc || !err) return ECPU_ERR_UNSUPPORTED;
 
@@ -674,16 +648,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
-    if (sync_mode()) {
-        int h = 0;
-        cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost);
-        if (h) {
-            cudaMemset(err, 0, sizeof(int));
-            set_error("%s: tensor-core GEMM pipeline timed out", what);
-            return ECPU_ERR_KERNEL;
-        }
-    }
-    return ECPU_OK;
+    return check_error_word(what, "tensor-core GEMM pipeline timed out");
 }
 
 }  // namespace pilm

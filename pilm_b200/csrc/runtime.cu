@@ -118,6 +118,41 @@ int sync_mode() {
     return g.sync;
 }
 
+TensorMapEncodeTiledFn tensor_map_encoder() {
+    static TensorMapEncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (TensorMapEncodeTiledFn)ptr;
+    });
+    return fn;
+}
+
+int *device_error_word() {
+    static int *err = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        if (cudaMalloc(&err, sizeof(int)) == cudaSuccess) cudaMemset(err, 0, sizeof(int));
+    });
+    return err;
+}
+
+int check_error_word(const char *what, const char *msg) {
+    int *err = device_error_word();
+    if (!sync_mode() || !err) return ECPU_OK;
+    int h = 0;
+    cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (h) {
+        cudaMemset(err, 0, sizeof(int));
+        set_error("%s: %s", what, msg);
+        return ECPU_ERR_KERNEL;
+    }
+    return ECPU_OK;
+}
+
 int num_sms() {
     if (g.sms == 0) {
         int dev = 0;

@@ -18,7 +18,7 @@ def _init():
     yield
 
 
-def run_case(nh, nkv, ctxs, qlens, gated=False, gemma=False, seed=0, num_blocks=None, partial=1.0):
+def run_case(nh, nkv, ctxs, qlens, gated=False, gemma=False, seed=0, num_blocks=None, partial=1.0, poison=False):
     g = torch.Generator().manual_seed(seed)
     cfg = om.Qwen3Config(n_heads=nh, n_kv_heads=nkv, gated=gated, gemma_norm=gemma, partial_rotary=partial)
     hd, bs = 128, 16
@@ -67,6 +67,11 @@ def run_case(nh, nkv, ctxs, qlens, gated=False, gemma=False, seed=0, num_blocks=
                         qkv_stride=qkv.shape[1], rope_rows=max_pos, rot_dim=int(hd * partial), eps=1e-6,
                         add_one=gemma, output_gate=gated)
     kc_d, vc_d = kc.to(d), vc.to(d)
+    if poison:  # the slots past each context in its last page hold NaN on the device
+        for b in range(B):
+            if ctxs[b] % bs:
+                kc_d[tables[b][-1], ctxs[b] % bs:] = float("nan")
+                vc_d[tables[b][-1], ctxs[b] % bs:] = float("nan")
     q_out = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d)
     gate = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d) if gated else None
     out = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d)
@@ -110,3 +115,18 @@ def test_partial_rotary():
 
 def test_qwen3_8b_head_layout():
     run_case(32, 8, ctxs=[531, 1000], qlens=[3, 3], seed=5)
+
+
+def test_many_ragged_sequences_nan_past_context():
+    """40 sequences of ragged lengths: the whole-page kernel's per-SM page ranges start and
+    end inside sequences, so many rows are combined from several CTAs' partials.  The slots
+    past each context in its last page are NaN: keys past the context never reach the output."""
+    import random
+    rnd = random.Random(7)
+    ctxs, qlens = [], []
+    for _ in range(40):
+        q = rnd.randint(1, 3)
+        st = 16 * rnd.randint(0, 40) + rnd.randint(0, 16 - q)
+        ctxs.append(st + q)
+        qlens.append(q)
+    run_case(32, 8, ctxs=ctxs, qlens=qlens, seed=8, poison=True)
