@@ -324,6 +324,95 @@ class OracleModel:
 
 
 # ---------------------------------------------------------------------------------------
+# MTP draft module (mtp.py:15-82)
+# ---------------------------------------------------------------------------------------
+
+MTP_LINEARS = ("fc", "q_proj", "k_proj", "v_proj", "o_proj", "gate", "up", "down")
+MTP_NORMS = ("pre_fc_norm_embedding", "pre_fc_norm_hidden", "input_norm", "post_norm", "q_norm", "k_norm",
+             "final_norm")
+
+
+def make_mtp_checkpoint(cfg: Qwen3Config, seed: int) -> dict[str, torch.Tensor]:
+    """Seeded synthetic Qwen3MTPDraft weights (mtp.py:15-23): fc [H, 2H] and one transformer
+    block shaped like the model's, N(0, 0.02) in bf16; norm weights as make_checkpoint.
+    Drawn from a separate stream (seed + 7919) so the model's own weights are unchanged."""
+    g = torch.Generator().manual_seed(seed + 7919)
+
+    def rnd(shape):
+        return (torch.randn(shape, generator=g, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+
+    shapes = linear_shapes(cfg)
+    ck = {"fc": rnd((cfg.hidden, 2 * cfg.hidden))}
+    for name in LINEAR_NAMES:
+        ck[name] = rnd(shapes[name])
+    norm_init = torch.zeros if cfg.gemma_norm else torch.ones
+    for name in MTP_NORMS:
+        ck[name] = norm_init(cfg.head_dim if name in ("q_norm", "k_norm") else cfg.hidden, dtype=torch.bfloat16)
+    return ck
+
+
+def quantize_mtp(ck: dict[str, torch.Tensor]) -> dict[str, dict[str, np.ndarray]]:
+    """The reference's W4A16 option for the draft module (mtp.py:85-94, PILM_MTP_QUANTIZE=
+    w4a16): every bias-free linear becomes QuantizedW4A16Linear.from_linear, per-row scales
+    (linear.py:291-296)."""
+    return {name: quantize_linear(ck[name], "w4row") for name in MTP_LINEARS}
+
+
+class OracleMTP:
+    """Qwen3MTPDraft.hidden / draft_tokens (mtp.py:25-82) with W4 per-row linears, sharing
+    the model's embedding and LM head.  The block is TransformerBlock (model.py:43-73)
+    called without a KV cache, so its attention sees only the token itself
+    (attention.py:113-116): the softmax over one key is exactly 1, the output is that
+    token's V expanded over the GQA group (attention.py:118-121, 134-136), times
+    sigmoid(gate) when the q projection is gated (attention.py:139).  Q, K, their norms and
+    RoPE cannot change it and are not computed."""
+
+    def __init__(self, cfg: Qwen3Config, ck: dict[str, torch.Tensor], model: OracleModel,
+                 q: dict | None = None):
+        self.cfg = cfg
+        self.q = q if q is not None else quantize_mtp(ck)
+        self.norms = {k: ck[k] for k in MTP_NORMS}
+        self.model = model
+
+    def hidden(self, hidden: torch.Tensor, token_embedding: torch.Tensor) -> torch.Tensor:
+        c = self.cfg
+        h = rms_norm(hidden.reshape(1, -1), self.norms["pre_fc_norm_hidden"], c.eps, c.gemma_norm)
+        e = rms_norm(token_embedding.reshape(1, -1), self.norms["pre_fc_norm_embedding"], c.eps, c.gemma_norm)
+        x = qlinear(torch.cat([e, h], dim=-1), self.q["fc"], "w4row")
+        r = x
+        a = rms_norm(x, self.norms["input_norm"], c.eps, c.gemma_norm)
+        v = qlinear(a, self.q["v_proj"], "w4row")
+        rep = c.n_heads // c.n_kv_heads
+        out = v.view(1, c.n_kv_heads, 1, c.head_dim).expand(1, c.n_kv_heads, rep, c.head_dim)
+        out = out.reshape(1, c.n_heads * c.head_dim)
+        if c.gated:
+            qg = qlinear(a, self.q["q_proj"], "w4row").view(1, c.n_heads, 2 * c.head_dim)
+            gate = qg[..., c.head_dim:].reshape(1, -1)
+            out = out * torch.sigmoid(gate)
+        x = r + qlinear(out, self.q["o_proj"], "w4row")
+        r = x
+        m = rms_norm(x, self.norms["post_norm"], c.eps, c.gemma_norm)
+        g = qlinear(m, self.q["gate"], "w4row")
+        u = qlinear(m, self.q["up"], "w4row")
+        x = r + qlinear(torch.nn.functional.silu(g) * u, self.q["down"], "w4row")
+        return rms_norm(x, self.norms["final_norm"], c.eps, c.gemma_norm)
+
+    def draft_tokens(self, hidden: torch.Tensor, first_token_id: int, num_tokens: int):
+        """k sequential drafts from the verify row's normed hidden state and the token it
+        produced; returns (drafts, the last draft step's hidden)."""
+        drafts = []
+        token_id = int(first_token_id)
+        state = hidden.reshape(1, -1)
+        last = state
+        for _ in range(max(0, int(num_tokens))):
+            last = self.hidden(state, self.model.embed[token_id])
+            token_id = int(torch.argmax(self.model.logits(last)[-1]).item())
+            drafts.append(token_id)
+            state = last
+        return drafts, last[-1]
+
+
+# ---------------------------------------------------------------------------------------
 # Speculative verify bookkeeping (engine.py)
 # ---------------------------------------------------------------------------------------
 

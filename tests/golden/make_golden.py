@@ -48,7 +48,8 @@ from runtime.scheduler import KVCacheManager, Request, Scheduler  # noqa: E402
 from runtime.kvcache import PhysicalKVCache  # noqa: E402
 from models.qwen3.model import Qwen3Model  # noqa: E402
 from models.base.layers import RMSNorm  # noqa: E402
-from models.base.linear import QuantizedW4A16Linear, QuantizedW8A32Linear  # noqa: E402
+from models.base.linear import BackendLinear, QuantizedW4A16Linear, QuantizedW8A32Linear  # noqa: E402
+from models.qwen3.mtp import Qwen3MTPDraft, _quantize_mtp_linears  # noqa: E402
 
 from oracle import model as om  # noqa: E402  (only for the seeded checkpoint recipe)
 
@@ -186,6 +187,44 @@ def build_reference_model(cfg: om.Qwen3Config, ck: dict[str, torch.Tensor]) -> Q
     return model
 
 
+def build_reference_mtp(cfg: om.Qwen3Config, mck: dict[str, torch.Tensor], mc) -> Qwen3MTPDraft:
+    """The reference draft module (mtp.py:15-23) with the seeded weights, quantized by the
+    reference's own W4A16 option (_quantize_mtp_linears, mtp.py:85-94).  Plain Qwen3 uses
+    the same harness shims as the main model (+inf gate half, RMSNorm for GemmaRMSNorm)."""
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        mtp = Qwen3MTPDraft(mc)
+    finally:
+        torch.set_default_dtype(prev)
+
+    def lin(w: torch.Tensor) -> BackendLinear:
+        m = BackendLinear(w.shape[1], w.shape[0], bias=False)
+        m.weight = nn.Parameter(w.clone(), requires_grad=False)
+        return m
+
+    blk = mtp.layers[0]
+    at = blk.self_attn
+    mtp.fc = lin(mck["fc"])
+    at.q_proj = lin(mck["q_proj"])
+    at.k_proj = lin(mck["k_proj"])
+    at.v_proj = lin(mck["v_proj"])
+    at.o_proj = lin(mck["o_proj"])
+    blk.mlp.gate = lin(mck["gate"])
+    blk.mlp.up = lin(mck["up"])
+    blk.mlp.down = lin(mck["down"])
+    mtp.quantized_linear_modules = _quantize_mtp_linears(mtp)
+    if not cfg.gated:
+        at.q_proj = _GateFreeQ(at.q_proj, cfg.n_heads, cfg.head_dim)
+    pairs = [(mtp, "pre_fc_norm_embedding", "pre_fc_norm_embedding"), (mtp, "pre_fc_norm_hidden", "pre_fc_norm_hidden"),
+             (blk, "input_layernorm", "input_norm"), (blk, "post_attention_layernorm", "post_norm"),
+             (at, "q_norm", "q_norm"), (at, "k_norm", "k_norm"), (mtp, "norm", "final_norm")]
+    for mod, attr, key in pairs:
+        _set_norm(mod, attr, mck[key], cfg)
+    mtp.eval()
+    return mtp
+
+
 def _set_norm(mod: nn.Module, attr: str, w: torch.Tensor, cfg: om.Qwen3Config) -> None:
     if not cfg.gemma_norm:
         setattr(mod, attr, RMSNorm(w.shape[0], cfg.eps))
@@ -218,6 +257,10 @@ def model_trace(name: str, kwargs: dict, seed: int) -> dict[str, np.ndarray]:
     cfg = om.Qwen3Config(**kwargs)
     ck = om.make_checkpoint(cfg, seed)
     model = build_reference_model(cfg, ck)
+    mtp = None
+    if cfg.quant == "w4g128":  # the W4A16 draft module (bf16 activations)
+        mck = om.make_mtp_checkpoint(cfg, seed)
+        mtp = build_reference_mtp(cfg, mck, model.config)
     rng = np.random.default_rng(seed)
     prompts = [list(rng.integers(0, cfg.vocab, size=n)) for n in (21, 27, 13, 31)]
     k = 3
@@ -310,6 +353,14 @@ def model_trace(name: str, kwargs: dict, seed: int) -> dict[str, np.ndarray]:
         res[f"b{bi}.logits"] = logits.numpy().copy()
         res[f"b{bi}.accept"] = np.array([acc, nxt], np.int64)
         res[f"b{bi}.num_computed_after"] = np.array([start + 1 + acc], np.int64)
+        if mtp is not None:
+            # the next cycle's drafts (engine.py:527-536 after a reject, :548-557 after a full
+            # accept): from the normed hidden of the row that produced the next token
+            with torch.no_grad():
+                d_next, h_last = mtp.draft_tokens(h[acc], nxt, start + acc + 1, model.embed_tokens, model.lm_head,
+                                                  num_tokens=3)
+            res[f"b{bi}.mtp_drafts"] = np.array(d_next, np.int64)
+            res[f"b{bi}.mtp_last_hidden"] = bits(h_last.reshape(1, -1))
         if acc < len(drafts_all[bi]):
             # reference reject path (engine.py:505-525): re-run the accepted prefix
             hp = run_forward(model, kv, ids[:1 + acc], sr.positions[:1 + acc], sr.block_ids, True)
@@ -323,6 +374,13 @@ def model_trace(name: str, kwargs: dict, seed: int) -> dict[str, np.ndarray]:
         hsh.update(q[key]["qweight"].tobytes())
         hsh.update(q[key]["scales"].tobytes())
     res["qweights_sha256"] = np.frombuffer(hsh.digest(), np.uint8).copy()
+    if mtp is not None:
+        hsh = hashlib.sha256()
+        mq = om.quantize_mtp(om.make_mtp_checkpoint(cfg, seed))
+        for key in sorted(mq):
+            hsh.update(mq[key]["qweight"].tobytes())
+            hsh.update(mq[key]["scales"].tobytes())
+        res["mtp_qweights_sha256"] = np.frombuffer(hsh.digest(), np.uint8).copy()
     return res
 
 

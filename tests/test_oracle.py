@@ -116,6 +116,29 @@ def test_oracle_model_matches_reference_trace(variant):
                 np.testing.assert_allclose(row.numpy(), z[f"b{b}.recompute_hidden_last"], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("variant", [v for v in G.MODEL_VARIANTS if "w4g128" in v])
+def test_oracle_mtp_drafts_match_reference(variant):
+    """The W4A16 MTP draft module: from each sequence's verify row that produced the next
+    token (its normed hidden state and that token), three draft steps give the reference's
+    drafts, and the last step's hidden state equals the reference's bit for bit."""
+    z = G.load(f"model_{variant}.npz")
+    cfg, seed = G.model_config(z)
+    m = om.OracleModel(cfg, om.make_checkpoint(cfg, seed))
+    mck = om.make_mtp_checkpoint(cfg, seed)
+    mtp = om.OracleMTP(cfg, mck, m)
+    h = hashlib.sha256()
+    for key in sorted(mtp.q):
+        h.update(mtp.q[key]["qweight"].tobytes())
+        h.update(mtp.q[key]["scales"].tobytes())
+    assert np.frombuffer(h.digest(), np.uint8).tolist() == z["mtp_qweights_sha256"].tolist()
+    for b in range(G.num_seqs(z)):
+        acc, nxt = G.ilist(z[f"b{b}.accept"])
+        hid = om._from_bits(z[f"b{b}.hidden"])[acc]
+        drafts, last = mtp.draft_tokens(hid, nxt, 3)
+        assert drafts == G.ilist(z[f"b{b}.mtp_drafts"])
+        assert np.array_equal(om._to_bits(last.reshape(1, -1)), z[f"b{b}.mtp_last_hidden"])
+
+
 def test_draft_limit_matches_engine_rule():
     # engine.py:399-401
     assert om.draft_limit(21, 16, 64, 3) == 3
