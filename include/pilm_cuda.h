@@ -217,6 +217,26 @@ int ekernel_add_rmsnorm_bf16(uint16_t *residual, const uint16_t *delta, const ui
  * [inter, 2*inter); out is [rows, inter]. */
 int ekernel_silu_mul_bf16(const uint16_t *gate_up, size_t rows, size_t inter, uint16_t *out);
 
+/* MTP draft step input (Qwen3MTPDraft.hidden, mtp.py:35-39): for sequence b,
+ * out[b, 0:H]  = norm(embed[tokens[b], :], w_embed_norm)        (pre_fc_norm_embedding)
+ * out[b, H:2H] = norm(hidden[src(b), :], w_hidden_norm)        (pre_fc_norm_hidden)
+ * i.e. torch.cat([e, h], -1), with the torch-module rounding of ekernel_add_rmsnorm_bf16
+ * (add_one: GemmaRMSNorm).  src(b) = row_base[b] + row_offset[b] (row_offset NULL: 0), or b
+ * when row_base is NULL; after a verify step row_base = cu_q and row_offset = the accept
+ * counts select the row that produced the next token.  Token ids outside [0, vocab) read
+ * row 0 and make the call return ECPU_ERR_KERNEL in synchronous mode. */
+int ekernel_mtp_fc_input_bf16(const uint16_t *hidden, const int32_t *row_base, const int32_t *row_offset,
+                              const uint16_t *embed, const int32_t *tokens, size_t vocab, const uint16_t *w_embed_norm,
+                              const uint16_t *w_hidden_norm, size_t num_seqs, size_t hidden_size, float eps,
+                              int add_one, uint16_t *out);
+
+/* Attention of each row over itself alone: FullAttention.forward without a KV cache
+ * (attention.py:113-139), as in the MTP draft block (mtp.py:40).  The softmax over one key
+ * is 1, so out[r, h*hd + d] = v[r, (h / (n_heads / n_kv_heads))*hd + d], multiplied by
+ * rne(sigmoid(gate[r, h*hd + d])) when gate != NULL (Qwen3.5 gated attention). */
+int ekernel_self_attention_bf16(const uint16_t *v, const uint16_t *gate, size_t rows, size_t n_heads,
+                                size_t n_kv_heads, size_t head_dim, uint16_t *out);
+
 typedef struct {
     size_t num_seqs;           /* B */
     size_t total_q;            /* rows = sum of per-sequence query lengths */

@@ -114,9 +114,10 @@ def _w4_common(x, qweight, scales, in_features, scale_ndim, groups_of):
     return x, qweight, scales, m, n, k
 
 
-def linear_w4a16_bf16(x, qweight, scales, in_features=None) -> torch.Tensor:
+def linear_w4a16_bf16(x, qweight, scales, in_features=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 1, None)
-    out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     _stream()
     _check(abi.linear_w4a16_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
            "ekernel_linear_w4a16_bf16")
@@ -226,6 +227,40 @@ def add_rmsnorm_bf16(residual: torch.Tensor, delta: Optional[torch.Tensor], weig
     _check(abi.lib().ekernel_add_rmsnorm_bf16(residual.data_ptr(), delta.data_ptr() if delta is not None else None,
                                               weight.data_ptr(), rows, n, float(eps), int(add_one), out.data_ptr()),
            "ekernel_add_rmsnorm_bf16")
+    return out
+
+
+def mtp_fc_input_bf16(hidden: torch.Tensor, row_base: Optional[torch.Tensor], row_offset: Optional[torch.Tensor],
+                      embed: torch.Tensor, tokens: torch.Tensor, w_embed_norm: torch.Tensor,
+                      w_hidden_norm: torch.Tensor, eps: float, add_one: bool,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[norm(embed[tokens]) | norm(hidden[row_base + row_offset])] per sequence: the fc
+    input of one MTP draft step (mtp.py:35-39)."""
+    hidden = _cuda("hidden", hidden, torch.bfloat16, 2)
+    embed = _cuda("embed", embed, torch.bfloat16, 2)
+    tokens = _cuda("tokens", tokens, torch.int32, 1)
+    B, H = tokens.shape[0], hidden.shape[1]
+    if out is None:
+        out = torch.empty((B, 2 * H), dtype=torch.bfloat16, device=hidden.device)
+    _stream()
+    _check(abi.lib().ekernel_mtp_fc_input_bf16(hidden.data_ptr(), _p(row_base), _p(row_offset), embed.data_ptr(),
+                                               tokens.data_ptr(), embed.shape[0], w_embed_norm.data_ptr(),
+                                               w_hidden_norm.data_ptr(), B, H, float(eps), int(add_one),
+                                               out.data_ptr()), "ekernel_mtp_fc_input_bf16")
+    return out
+
+
+def self_attention_bf16(v: torch.Tensor, gate: Optional[torch.Tensor], n_heads: int, n_kv_heads: int,
+                        head_dim: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Attention of each row over itself alone: V expanded over the GQA group (times
+    sigmoid(gate) when gated)."""
+    v = _cuda("v", v, torch.bfloat16, 2)
+    rows = v.shape[0]
+    if out is None:
+        out = torch.empty((rows, n_heads * head_dim), dtype=torch.bfloat16, device=v.device)
+    _stream()
+    _check(abi.lib().ekernel_self_attention_bf16(v.data_ptr(), _p(gate), rows, n_heads, n_kv_heads, head_dim,
+                                                 out.data_ptr()), "ekernel_self_attention_bf16")
     return out
 
 
