@@ -228,6 +228,49 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         e2e_rows_all = float(e2e_rows)
     e2e_ms_max = float(e2e_t[0].item())
     maxp = max(len(s.pages) for s in eng.sched.running)
+
+    # ---- the speculative cycle: verify + k MTP draft steps on the GPU (cycle) --------
+    # The engine drafts each sequence's next tokens with the GPU drafter inside the same
+    # captured step; verify_step() then verifies them.  Synthetic weights: the random
+    # drafter rarely agrees with the random model, so accepted tok/s sits near the
+    # 1-token-per-step floor; the timing is what a real checkpoint's cycle costs.
+    cycle = None
+    if e2e_steps and not args.no_draft:
+        from pilm_b200.mtp import MTPDrafter, MTPWeights
+        mw = MTPWeights.synthetic(shape, seed + 17, dev)
+        eng.drafter, eng.draft_k, eng.graphs, eng.pending = MTPDrafter(mw, weights, SEQS, dev), K_DRAFT, {}, {}
+        for _ in range(max(args.warmup, PAGE)):
+            eng.verify_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        c_rows = c_tokens = c_att = c_acc = 0
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(e2e_steps):
+            rows_before = eng.stats["verified_rows"]
+            for r in eng.verify_step():
+                c_tokens += 1 + r.accepted
+                c_att += len(r.drafts)
+                c_acc += r.accepted
+            c_rows += eng.stats["verified_rows"] - rows_before
+        c1.record(stream)
+        torch.cuda.synchronize()
+        c_t = torch.tensor([c0.elapsed_time(c1) / e2e_steps, c_rows, c_tokens], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(c_t[:1], op=dist.ReduceOp.MAX)
+            dist.all_reduce(c_t[1:], op=dist.ReduceOp.SUM)
+        c_ms = float(c_t[0].item())
+        cycle = {
+            "verified_tok_s": round(float(c_t[1].item()) / e2e_steps / (c_ms * 1e-3), 2),
+            "accepted_tok_s": round(float(c_t[2].item()) / e2e_steps / (c_ms * 1e-3), 2),
+            "ms_per_cycle": round(c_ms, 4),
+            "draft_k": K_DRAFT,
+            "draft_linear_bytes": mw.linear_bytes,
+            "accept_rate": round(c_acc / max(1, c_att), 4),
+            "call": "pilm_b200.engine.MTPVerifyEngine.verify_step() with the GPU MTP drafter "
+                    "(verify + k draft steps in one captured step; host accept results and drafts out)",
+        }
     h2d = 4 * (3 * rows_per_step + SEQS * maxp + 2 * SEQS + 1) + 0
     d2h = 4 * 2 * SEQS
 
@@ -283,6 +326,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "host_wall_ms_per_step": round(wall_ms, 4),
             "call": "pilm_b200.engine.MTPVerifyEngine.verify_step (host drafts -> host accept results)",
         },
+        "cycle": cycle,
         "roofline": {
             "kernel": "attn_verify (+ merge), per layer",
             "bound": "hbm",
@@ -436,6 +480,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end engine leg (profiling runs)")
+    ap.add_argument("--no-draft", action="store_true", help="skip the verify + GPU draft cycle leg")
     ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per GPU (default: the BASELINE config)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens per sequence")
     ap.add_argument("--layers", type=int, default=0, help="decoder layers (0 = all 36); profiling only")

@@ -49,6 +49,7 @@ TensorMapEncodeTiledFn tensor_map_encoder();
 // be allocated).  In synchronous mode check_error_word reads and clears it and turns a set
 // word into ECPU_ERR_KERNEL with the message "<what>: <msg>".
 int *device_error_word();
+bool capturing();  // the library stream is being captured into a CUDA graph
 int check_error_word(const char *what, const char *msg);
 
 // Post-launch check: ECPU_ERR_KERNEL on a launch error; in synchronous mode

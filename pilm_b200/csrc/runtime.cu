@@ -118,6 +118,13 @@ int sync_mode() {
     return g.sync;
 }
 
+// The library stream is being captured into a CUDA graph: synchronous mode then neither
+// synchronizes nor reads back (either would invalidate the capture).
+bool capturing() {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(g.stream, &st) == cudaSuccess && st != cudaStreamCaptureStatusNone;
+}
+
 TensorMapEncodeTiledFn tensor_map_encoder() {
     static TensorMapEncodeTiledFn fn = nullptr;
     static std::once_flag once;
@@ -142,7 +149,7 @@ int *device_error_word() {
 
 int check_error_word(const char *what, const char *msg) {
     int *err = device_error_word();
-    if (!sync_mode() || !err) return ECPU_OK;
+    if (!sync_mode() || !err || capturing()) return ECPU_OK;
     int h = 0;
     cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost);
     if (h) {
@@ -221,7 +228,7 @@ int check_launch(const char *what) {
         set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
         return ECPU_ERR_KERNEL;
     }
-    if (sync_mode()) {
+    if (sync_mode() && !capturing()) {
         e = cudaStreamSynchronize(g.stream);
         if (e != cudaSuccess) {
             set_error("%s: execution failed: %s", what, cudaGetErrorString(e));

@@ -51,11 +51,15 @@ class StepResult:
 class MTPVerifyEngine:
     def __init__(self, verifier: Qwen3Verifier, num_blocks: int, block_size: int = 16, max_model_len: int = 65536,
                  max_pages_per_seq: Optional[int] = None, pin_memory: bool = True,
-                 max_num_batched_tokens: int = 1 << 30, use_graphs: bool = True):
+                 max_num_batched_tokens: int = 1 << 30, use_graphs: bool = True, drafter=None, draft_k: int = 0):
         """max_num_batched_tokens is the scheduler's per-pass token budget; the reference
         engine uses one page (16, engine.py:218), which also fixes its page order.
         use_graphs replays each verify-step shape (sequences, rows) from a captured CUDA
-        graph instead of launching ~15 kernels per layer from Python."""
+        graph instead of launching ~15 kernels per layer from Python.
+        drafter (pilm_b200.mtp.MTPDrafter) with draft_k > 0 drafts each sequence's next
+        tokens on the GPU right after its verify step (in the same graph); verify_step()
+        without explicit drafts then uses them, as the reference's speculative loop does
+        with pending_mtp_draft_ids (engine.py:380-408, 527-557)."""
         self.v = verifier
         self.device = verifier.device
         self.block_size = block_size
@@ -75,6 +79,11 @@ class MTPVerifyEngine:
         # staging buffers reused every step
         self._page_rows: dict[int, tuple[int, np.ndarray, int]] = {}
         self._staging: dict[str, torch.Tensor] = {}
+        self.drafter = drafter if draft_k > 0 else None
+        self.draft_k = draft_k if self.drafter is not None else 0
+        if self.drafter is not None and not use_graphs:
+            raise ValueError("the GPU drafter runs inside the captured verify step (use_graphs=True)")
+        self.pending: dict[int, list[int]] = {}  # next step's drafts per sequence (from the drafter)
 
     # ---- admission -------------------------------------------------------------------
     def add_request(self, prompt: list[int], max_new_tokens: int = 256, eos_token_id: int = -1) -> int:
@@ -179,7 +188,8 @@ class MTPVerifyEngine:
         key = (b.num_seqs, b.total_q, b.max_q_len)
         g = self.graphs.get(key)
         if g is None:
-            g = VerifyGraph(self.v, b.num_seqs, b.total_q, b.max_q_len, self.max_pages, self.max_model_len)
+            g = VerifyGraph(self.v, b.num_seqs, b.total_q, b.max_q_len, self.max_pages, self.max_model_len,
+                            self.drafter, self.draft_k)
             g.load(b)
             g.capture()
             self.graphs[key] = g
@@ -218,8 +228,12 @@ class MTPVerifyEngine:
         return first
 
     # ---- the verify step --------------------------------------------------------------
-    def verify_step(self, drafts: dict[int, list[int]]) -> list[StepResult]:
-        """One MTP verify step over every running sequence in decode state."""
+    def verify_step(self, drafts: Optional[dict[int, list[int]]] = None) -> list[StepResult]:
+        """One MTP verify step over every running sequence in decode state.  Without
+        explicit drafts each sequence verifies the drafts the GPU drafter produced in its
+        previous step (none before its first step)."""
+        if drafts is None:
+            drafts = self.pending
         seqs, starts, counts, used = [], [], [], []
         for s in list(self.sched.running):
             if s.num_uncomputed != 1 or s.is_prefill:
@@ -239,18 +253,24 @@ class MTPVerifyEngine:
         if not seqs:
             return []
         B = len(seqs)
+        new_drafts = None
         if self.use_graphs:
             b = self.build_batch(seqs, starts, counts, on_device=False)
             g = self.graph_for(b)
             g.replay()
             acc, nxt = g.acc, g.next
+            if self.draft_k:
+                new_drafts = g.drafts
         else:
             b = self.build_batch(seqs, starts, counts)
             acc = torch.empty(B, dtype=torch.int32, device=self.device)
             nxt = torch.empty(B, dtype=torch.int32, device=self.device)
             ctx = b.context_lens.clone()
             self.v.verify_greedy(b, acc, nxt, ctx)
-        res = torch.stack([acc, nxt]).to("cpu", non_blocking=False).tolist()
+        parts = [acc, nxt] + ([new_drafts[j] for j in range(self.draft_k)] if new_drafts is not None else [])
+        res = torch.stack(parts).to("cpu", non_blocking=False).tolist()
+        if new_drafts is not None:
+            self.pending = {s.seq_id: [int(res[2 + j][i]) for j in range(self.draft_k)] for i, s in enumerate(seqs)}
         out = []
         for i, s in enumerate(seqs):
             a, t = int(res[0][i]), int(res[1][i])
@@ -273,4 +293,5 @@ class MTPVerifyEngine:
             self.sched.running.remove(s)
             self.pages.free(s)
             self._page_rows.pop(s.seq_id, None)
+            self.pending.pop(s.seq_id, None)
         return out

@@ -410,6 +410,7 @@ class Qwen3Verifier:
         stream; returns the logits buffer view (bf16)."""
         n0 = abi.launch_count()
         h = self.forward(b)
+        self.hidden_out = h  # normed hidden states of the rows (the MTP drafter's input)
         logits = self.lm_head(h)
         T = b.total_q
         ck.argmax_top2(logits, self.top1[:T], None, self.margin[:T])
@@ -429,10 +430,16 @@ class VerifyGraph:
     any batch whose contexts stay within it can be replayed."""
 
     def __init__(self, verifier: "Qwen3Verifier", num_seqs: int, total_q: int, max_q_len: int, max_pages: int,
-                 max_context: int):
+                 max_context: int, drafter=None, draft_k: int = 0):
+        """drafter (pilm_b200.mtp.MTPDrafter) and draft_k > 0 add the next step's MTP drafts
+        to the graph: k draft steps from the row that produced each sequence's next token,
+        written to ``drafts`` [k, num_seqs]."""
         dev = verifier.device
         i32 = dict(dtype=torch.int32, device=dev)
         self.v = verifier
+        self.drafter = drafter if draft_k > 0 else None
+        self.draft_k = draft_k if self.drafter is not None else 0
+        self.drafts = torch.zeros((max(1, self.draft_k), num_seqs), **i32)
         self.batch = VerifyBatch(ids=torch.zeros(total_q, **i32), positions=torch.zeros(total_q, **i32),
                                  slots=torch.full((total_q,), -1, **i32),
                                  block_table=torch.zeros((num_seqs, max_pages), **i32),
@@ -461,6 +468,8 @@ class VerifyGraph:
     def _body(self) -> None:
         self.ctx_out.copy_(self.batch.context_lens)
         self.v.verify_greedy(self.batch, self.acc, self.next, self.ctx_out)
+        if self.drafter is not None:
+            self.drafter.draft(self.v.hidden_out, self.batch.cu_q, self.acc, self.next, self.draft_k, self.drafts)
 
     def capture(self) -> None:
         """One eager run (sizes the library's scratch memory, which must not grow

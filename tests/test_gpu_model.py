@@ -110,6 +110,41 @@ def test_engine_prefill_and_verify_end_to_end(variant):
     assert agree >= B - 1
 
 
+@pytest.mark.parametrize("variant", BF16_VARIANTS)
+def test_engine_drafts_next_step_on_gpu(variant):
+    """The MTP drafter inside the captured verify step: after the golden verify step each
+    sequence's pending drafts equal the reference drafter's (from the row that produced
+    its next token), and the following verify_step() verifies them, capped at the page."""
+    from pilm_b200.mtp import MTPDrafter, MTPWeights
+    z, cfg, ckpt, w = build(variant)
+    _, seed = G.model_config(z)
+    mw = MTPWeights.from_checkpoint(w.shape, om.make_mtp_checkpoint(cfg, seed), dev())
+    B = G.num_seqs(z)
+    kv = PagedKVCache(w.shape, 32, dev())
+    ver = Qwen3Verifier(w, kv, max_rows=128, max_pos=256, device=dev())
+    eng = MTPVerifyEngine(ver, num_blocks=32, max_model_len=256, max_num_batched_tokens=16,
+                          drafter=MTPDrafter(mw, w, max_seqs=8, device=dev()), draft_k=3)
+    sids = [eng.add_request(G.ilist(z[f"b{b}.prompt"]), max_new_tokens=64) for b in range(B)]
+    first = eng.prefill()
+    res = eng.verify_step({sid: G.ilist(z[f"b{b}.drafts"]) for b, sid in enumerate(sids)})
+    agree = 0
+    for b, sid in enumerate(sids):
+        r = next(x for x in res if x.seq_id == sid)
+        if first[sid] != int(z[f"b{b}.first_token"][0]) or [r.accepted, r.next_token] != G.ilist(z[f"b{b}.accept"]):
+            continue  # a near tie upstream: a different verify row, different drafts
+        assert eng.pending[sid] == G.ilist(z[f"b{b}.mtp_drafts"]), f"sequence {b}"
+        agree += 1
+    assert agree >= B - 1
+    before = {sid: (eng.sched.seqs[sid].num_computed, 64 - len(eng.sched.seqs[sid].outputs), list(eng.pending[sid]))
+              for sid in sids}
+    res2 = eng.verify_step()
+    assert len(res2) == B
+    for r in res2:
+        n_comp, remaining, pend = before[r.seq_id]
+        cap = om.draft_limit(n_comp, cfg.block_size, remaining, len(pend))
+        assert r.drafts == pend[:cap]
+
+
 def test_verify_step_is_deterministic():
     z, cfg, ckpt, w = build("qwen3_w4g128")
     outs = []
