@@ -341,6 +341,35 @@ int ekernel_verify_accept_rejection(const ekernel_accept_desc_t *desc, const flo
                                     float temperature, float top_p, int32_t *accept_counts,
                                     int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
 
+/* ---- fp32-activation verify path (model dtype float32: the W8A32 configuration,
+ * QuantizedW8A32Linear, linear.py:188-233).  The bf16 operations above with every
+ * intermediate in fp32, as torch computes them for float32 tensors. ---- */
+
+/* out[r,:] = table[ids[r],:] (fp32 embedding, model.py:110); ids outside [0, vocab) read
+ * row 0 and make the call return ECPU_ERR_KERNEL in synchronous mode. */
+int ekernel_embedding_f32(const int32_t *ids, size_t rows, const float *table, size_t vocab, size_t hidden,
+                          float *out);
+
+/* residual += delta (if delta != NULL), then out = w' * (residual * rsqrt(mean(residual^2) + eps)),
+ * w' = w or 1 + w (RMSNorm / GemmaRMSNorm on fp32 tensors, layers.py:94-98, 115-119). */
+int ekernel_add_rmsnorm_f32(float *residual, const float *delta, const float *weight, size_t rows, size_t n, float eps,
+                            int add_one, float *out);
+
+/* ekernel_qk_norm_rope_kv_append with fp32 projections, norm weights, caches and outputs. */
+int ekernel_qk_norm_rope_kv_append_f32(const ekernel_paged_attn_desc_t *desc, const float *qkv, const float *q_norm_w,
+                                       const float *k_norm_w, const float *rope_cos, const float *rope_sin,
+                                       const int32_t *positions, const int32_t *slot_mapping, float *k_cache,
+                                       float *v_cache, float *q_out, float *gate_out);
+
+/* ekernel_paged_attention_verify with fp32 queries, caches, gate and output: scores
+ * q.k * (1/sqrt(128)), causal mask, softmax and P.V in fp32 (attention.py:95-139). */
+int ekernel_paged_attention_verify_f32(const ekernel_paged_attn_desc_t *desc, const float *q, const float *k_cache,
+                                       const float *v_cache, const int32_t *block_table, const int32_t *cu_q,
+                                       const int32_t *context_lens, const float *gate, float *out);
+
+/* out = silu(gate) * up in fp32 (layers.py:193); gate_up is [rows, 2*inter]. */
+int ekernel_silu_mul_f32(const float *gate_up, size_t rows, size_t inter, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -178,6 +178,11 @@ def _configure(lib) -> None:
     lib.ekernel_mtp_fc_input_bf16.argtypes = [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _sz, _sz, ctypes.c_float, _i32,
                                               _vp]
     lib.ekernel_self_attention_bf16.argtypes = [_vp, _vp, _sz, _sz, _sz, _sz, _vp]
+    lib.ekernel_embedding_f32.argtypes = [_vp, _sz, _vp, _sz, _sz, _vp]
+    lib.ekernel_add_rmsnorm_f32.argtypes = [_vp, _vp, _vp, _sz, _sz, ctypes.c_float, _i32, _vp]
+    lib.ekernel_qk_norm_rope_kv_append_f32.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 11
+    lib.ekernel_paged_attention_verify_f32.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 8
+    lib.ekernel_silu_mul_f32.argtypes = [_vp, _sz, _sz, _vp]
     lib.ekernel_qk_norm_rope_kv_append.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 11
     lib.ekernel_paged_attention_verify.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 8
     lib.ekernel_paged_attention_verify_noalloc.argtypes = [ctypes.POINTER(PagedAttnDesc)] + [_vp] * 8

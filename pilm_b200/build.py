@@ -18,7 +18,7 @@ CSRC = HERE / "csrc"
 LIB = HERE / "libpilm_cuda.so"
 INCLUDE = HERE.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["runtime.cu", "linear.cu", "linear_tc.cu", "norm.cu", "attention.cu", "accept.cu", "mtp.cu"]
+SOURCES = ["runtime.cu", "linear.cu", "linear_tc.cu", "norm.cu", "attention.cu", "accept.cu", "mtp.cu", "f32.cu"]
 
 
 def nvcc() -> str:

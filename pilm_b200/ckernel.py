@@ -56,7 +56,8 @@ def gemm_f32(a: torch.Tensor, b: torch.Tensor, transpose_b: bool = False) -> tor
     return out
 
 
-def linear_w8a32(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+def linear_w8a32(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
     x = _cuda("x", x, torch.float32, 2)
     qweight = _cuda("qweight", qweight, torch.int8, 2)
     scales = _cuda("scales", scales, torch.float32, 1)
@@ -65,7 +66,8 @@ def linear_w8a32(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor) -
     if wk != k or scales.shape[0] != n:
         raise ValueError(f"incompatible W8A32 shapes: x={tuple(x.shape)} qweight={tuple(qweight.shape)} "
                          f"scales={tuple(scales.shape)}")
-    out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
     _stream()
     _check(abi.linear_w8a32_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
            "ekernel_linear_w8a32")
@@ -301,6 +303,60 @@ def paged_attention_verify(desc, q, k_cache, v_cache, block_table, cu_q, context
     _check(abi.lib().ekernel_paged_attention_verify(ctypes.byref(desc), _p(q), _p(k_cache), _p(v_cache),
                                                     _p(block_table), _p(cu_q), _p(context_lens), _p(gate), _p(out)),
            "ekernel_paged_attention_verify")
+
+
+# ---- fp32-activation path (the W8A32 configuration) --------------------------------------
+
+def embedding_f32(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    ids = _cuda("ids", ids, torch.int32, 1)
+    table = _cuda("table", table, torch.float32, 2)
+    if out is None:
+        out = torch.empty((ids.shape[0], table.shape[1]), dtype=torch.float32, device=ids.device)
+    _stream()
+    _check(abi.lib().ekernel_embedding_f32(ids.data_ptr(), ids.shape[0], table.data_ptr(), table.shape[0],
+                                           table.shape[1], out.data_ptr()), "ekernel_embedding_f32")
+    return out
+
+
+def add_rmsnorm_f32(residual: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, eps: float,
+                    add_one: bool, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if residual.device.type != "cuda" or residual.dtype != torch.float32 or not residual.is_contiguous():
+        raise ValueError("residual must be a contiguous CUDA float32 tensor")
+    rows, n = residual.shape
+    if out is None:
+        out = torch.empty_like(residual)
+    _stream()
+    _check(abi.lib().ekernel_add_rmsnorm_f32(residual.data_ptr(), _p(delta), weight.data_ptr(), rows, n, float(eps),
+                                             int(add_one), out.data_ptr()), "ekernel_add_rmsnorm_f32")
+    return out
+
+
+def qk_norm_rope_kv_append_f32(desc, qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, positions, slot_mapping, k_cache,
+                               v_cache, q_out, gate_out=None) -> None:
+    import ctypes
+    _stream()
+    _check(abi.lib().ekernel_qk_norm_rope_kv_append_f32(ctypes.byref(desc), _p(qkv), _p(q_norm_w), _p(k_norm_w),
+                                                        _p(rope_cos), _p(rope_sin), _p(positions), _p(slot_mapping),
+                                                        _p(k_cache), _p(v_cache), _p(q_out), _p(gate_out)),
+           "ekernel_qk_norm_rope_kv_append_f32")
+
+
+def paged_attention_verify_f32(desc, q, k_cache, v_cache, block_table, cu_q, context_lens, gate, out) -> None:
+    import ctypes
+    _stream()
+    _check(abi.lib().ekernel_paged_attention_verify_f32(ctypes.byref(desc), _p(q), _p(k_cache), _p(v_cache),
+                                                        _p(block_table), _p(cu_q), _p(context_lens), _p(gate),
+                                                        _p(out)), "ekernel_paged_attention_verify_f32")
+
+
+def silu_mul_f32(gate_up: torch.Tensor, inter: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    gate_up = _cuda("gate_up", gate_up, torch.float32, 2)
+    rows = gate_up.shape[0]
+    if out is None:
+        out = torch.empty((rows, inter), dtype=torch.float32, device=gate_up.device)
+    _stream()
+    _check(abi.lib().ekernel_silu_mul_f32(gate_up.data_ptr(), rows, inter, out.data_ptr()), "ekernel_silu_mul_f32")
+    return out
 
 
 def argmax_top2(logits: torch.Tensor, top1: torch.Tensor, top1_val=None, margin=None) -> None:

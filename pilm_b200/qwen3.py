@@ -187,12 +187,20 @@ def rope_tables(shape: Qwen3Shape, max_pos: int, device) -> tuple[torch.Tensor, 
 class PagedKVCache:
     """Device-resident paged KV: per layer K and V [num_blocks, block_size, n_kv, hd] bf16."""
 
-    def __init__(self, shape: Qwen3Shape, num_blocks: int, device, fill: Optional[str] = None, seed: int = 0):
+    def __init__(self, shape: Qwen3Shape, num_blocks: int, device, fill: Optional[str] = None, seed: int = 0,
+                 dtype: torch.dtype = torch.bfloat16):
+        """dtype: bf16, or fp32 for the fp32-activation (W8A32) model (zero-filled only)."""
         self.num_blocks = num_blocks
         self.block_size = shape.block_size
+        self.dtype = dtype
         dims = (num_blocks, shape.block_size, shape.n_kv_heads, shape.head_dim)
         self.k = []
         self.v = []
+        if dtype == torch.float32:
+            for _ in range(shape.layers):
+                self.k.append(torch.zeros(dims, dtype=torch.float32, device=device))
+                self.v.append(torch.zeros(dims, dtype=torch.float32, device=device))
+            return
         g = torch.Generator(device=device).manual_seed(seed) if fill == "random" else None
         for _ in range(shape.layers):
             if fill == "random":
@@ -205,7 +213,7 @@ class PagedKVCache:
 
     @property
     def bytes_per_token(self) -> int:
-        return len(self.k) * 2 * self.k[0].shape[2] * self.k[0].shape[3] * 2
+        return len(self.k) * 2 * self.k[0].shape[2] * self.k[0].shape[3] * self.k[0].element_size()
 
 
 @dataclass
@@ -499,3 +507,109 @@ def attention_bytes(shape: Qwen3Shape, context_lens: list[int], q_lens: list[int
     qo = rows * shape.n_heads * shape.head_dim * 2 * 2
     app = rows * shape.n_kv_heads * shape.head_dim * 2 * 2
     return kv + qo + app
+
+
+# ---------------------------------------------------------------------------------------
+# fp32-activation model: the W8A32 configuration
+# ---------------------------------------------------------------------------------------
+
+class W8Linear:
+    """Device-resident W8A32 linear (QuantizedW8A32Linear, linear.py:188-233): int8
+    [N, K] with per-row fp32 scales, fp32 activations in and out."""
+
+    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor):
+        self.qweight = qweight.contiguous()
+        self.scales = scales.contiguous()
+        self.in_features = int(qweight.shape[1])
+        self.out_features = int(qweight.shape[0])
+
+    @classmethod
+    def quantize(cls, w: torch.Tensor) -> "W8Linear":
+        qw, s = ck.quantize_weight_i8_per_row(w)
+        return cls(qw, s)
+
+    @classmethod
+    def cat(cls, parts: list["W8Linear"]) -> "W8Linear":
+        return cls(torch.cat([p.qweight for p in parts]), torch.cat([p.scales for p in parts]))
+
+    @property
+    def nbytes(self) -> int:
+        return self.qweight.numel() + self.scales.numel() * 4
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return ck.linear_w8a32(x, self.qweight, self.scales, out=out)
+
+
+class Qwen3WeightsF32(Qwen3Weights):
+    """fp32 model with W8A32 linears; q/k/v and gate/up fused row-wise (rows are
+    independent, per-row scales), tied LM head."""
+
+    @classmethod
+    def from_checkpoint(cls, shape: Qwen3Shape, ck_tensors: dict[str, torch.Tensor], device) -> "Qwen3WeightsF32":
+        def q(name):
+            return W8Linear.quantize(ck_tensors[name].to(device))
+
+        def f(name):
+            return ck_tensors[name].to(device, torch.float32).contiguous()
+
+        layers = []
+        for li in range(shape.layers):
+            p = f"l{li}."
+            layers.append({
+                "qkv": W8Linear.cat([q(p + "q_proj"), q(p + "k_proj"), q(p + "v_proj")]),
+                "o": q(p + "o_proj"),
+                "gate_up": W8Linear.cat([q(p + "gate"), q(p + "up")]),
+                "down": q(p + "down"),
+                "input_norm": f(p + "input_norm"), "post_norm": f(p + "post_norm"),
+                "q_norm": f(p + "q_norm"), "k_norm": f(p + "k_norm"),
+            })
+        return cls(shape, f("embed"), layers, f("final_norm"), W8Linear.quantize(ck_tensors["embed"].to(device)))
+
+
+class Qwen3VerifierF32(Qwen3Verifier):
+    """The verify forward with fp32 activations and KV (model dtype float32, W8A32):
+    the same structure as Qwen3Verifier with the fp32 kernels; fp32 logits."""
+
+    def __init__(self, weights: Qwen3WeightsF32, kv: PagedKVCache, max_rows: int, max_pos: int, device):
+        if kv.dtype != torch.float32:
+            raise ValueError("the fp32 verifier needs an fp32 KV cache")
+        super().__init__(weights, kv, max_rows, max_pos, device)
+        s = self.shape
+        f = dict(dtype=torch.float32, device=device)
+        self.residual = torch.empty((max_rows, s.hidden), **f)
+        self.h = torch.empty((max_rows, s.hidden), **f)
+        self.qkv = torch.empty((max_rows, s.qkv_rows), **f)
+        self.q = torch.empty((max_rows, s.n_heads * s.head_dim), **f)
+        self.gate = torch.empty((max_rows, s.n_heads * s.head_dim), **f) if s.gated else None
+        self.attn = torch.empty((max_rows, s.n_heads * s.head_dim), **f)
+        self.o = torch.empty((max_rows, s.hidden), **f)
+        self.gu = torch.empty((max_rows, 2 * s.intermediate), **f)
+        self.act = torch.empty((max_rows, s.intermediate), **f)
+        self.mlp = torch.empty((max_rows, s.hidden), **f)
+        self.logits = torch.empty((max_rows, s.vocab), **f)
+
+    def forward(self, b: VerifyBatch) -> torch.Tensor:
+        s = self.shape
+        T = b.total_q
+        if T > self.max_rows:
+            raise ValueError(f"{T} rows exceed max_rows={self.max_rows}")
+        desc = self._desc(b)
+        res, h = self.residual[:T], self.h[:T]
+        ck.embedding_f32(b.ids, self.w.embed, out=res)
+        delta = None
+        gate = self.gate[:T] if s.gated else None
+        for li, L in enumerate(self.w.layers):
+            ck.add_rmsnorm_f32(res, delta, L["input_norm"], s.eps, s.gemma_norm, out=h)
+            L["qkv"](h, out=self.qkv[:T])
+            ck.qk_norm_rope_kv_append_f32(desc, self.qkv[:T], L["q_norm"], L["k_norm"], self.cos, self.sin,
+                                          b.positions, b.slots, self.kv.k[li], self.kv.v[li], self.q[:T], gate)
+            ck.paged_attention_verify_f32(desc, self.q[:T], self.kv.k[li], self.kv.v[li], b.block_table, b.cu_q,
+                                          b.context_lens, gate, self.attn[:T])
+            L["o"](self.attn[:T], out=self.o[:T])
+            ck.add_rmsnorm_f32(res, self.o[:T], L["post_norm"], s.eps, s.gemma_norm, out=h)
+            L["gate_up"](h, out=self.gu[:T])
+            ck.silu_mul_f32(self.gu[:T], s.intermediate, out=self.act[:T])
+            L["down"](self.act[:T], out=self.mlp[:T])
+            delta = self.mlp[:T]
+        ck.add_rmsnorm_f32(res, delta, self.w.final_norm, s.eps, s.gemma_norm, out=h)
+        return h

@@ -145,6 +145,79 @@ def test_engine_drafts_next_step_on_gpu(variant):
         assert r.drafts == pend[:cap]
 
 
+def _batch_from_golden(z, B):
+    ids, pos, slots, cu, tables, ctx = [], [], [], [0], [], []
+    for b in range(B):
+        ids += G.ilist(z[f"b{b}.verify_ids"])
+        p = G.ilist(z[f"b{b}.positions"])
+        pos += p
+        slots += G.ilist(z[f"b{b}.slots"])
+        cu.append(cu[-1] + len(p))
+        tables.append(G.ilist(z[f"b{b}.block_ids"]))
+        ctx.append(p[-1] + 1)
+    maxp = max(len(t) for t in tables)
+    i32 = dict(dtype=torch.int32, device=dev())
+    return VerifyBatch(torch.tensor(ids, **i32), torch.tensor(pos, **i32), torch.tensor(slots, **i32),
+                       torch.tensor([t + [0] * (maxp - len(t)) for t in tables], **i32), torch.tensor(cu, **i32),
+                       torch.tensor(ctx, **i32), max(cu[i + 1] - cu[i] for i in range(B)), max(ctx)), cu
+
+
+def test_fp32_w8a32_verify_step_from_reference_kv():
+    """The fp32-activation W8A32 model (the small CPU-runnable configuration): the verify
+    step from the reference's fp32 KV cache gives its logits within 1e-2 and, where the
+    row argmaxes agree, its accept counts, next tokens and rollback."""
+    from pilm_b200.qwen3 import Qwen3VerifierF32, Qwen3WeightsF32
+    z = G.load("model_qwen3_w8a32_f32.npz")
+    cfg, seed = G.model_config(z)
+    w = Qwen3WeightsF32.from_checkpoint(shape_of(cfg), om.make_checkpoint(cfg, seed), dev())
+    B = G.num_seqs(z)
+    kv = PagedKVCache(w.shape, 32, dev(), dtype=torch.float32)
+    for li in range(cfg.layers):
+        kv.k[li].copy_(torch.from_numpy(z[f"kv.k{li}"]))
+        kv.v[li].copy_(torch.from_numpy(z[f"kv.v{li}"]))
+    ver = Qwen3VerifierF32(w, kv, max_rows=64, max_pos=256, device=dev())
+    batch, cu = _batch_from_golden(z, B)
+    i32 = dict(dtype=torch.int32, device=dev())
+    acc, nxt = torch.empty(B, **i32), torch.empty(B, **i32)
+    ctx_out = batch.context_lens.clone()
+    logits = ver.verify_greedy(batch, acc, nxt, ctx_out).cpu()
+    top1 = ver.top1[:batch.total_q].cpu()
+    for b in range(B):
+        ref = z[f"b{b}.logits"]
+        assert rel_err(logits[cu[b]:cu[b + 1]].numpy(), ref) <= REL_TOL
+        rows = top1[cu[b]:cu[b + 1]].tolist()
+        assert argmax_agrees(rows, ref)
+        if rows == torch.as_tensor(ref).argmax(-1).tolist():
+            assert [int(acc[b]), int(nxt[b])] == G.ilist(z[f"b{b}.accept"])
+        assert int(ctx_out[b]) == int(z[f"b{b}.num_computed_after"][0])
+        hid = ver.hidden_out[cu[b]:cu[b + 1]].cpu().numpy()
+        assert rel_err(hid, z[f"b{b}.hidden"]) <= REL_TOL
+
+
+def test_fp32_w8a32_engine_end_to_end():
+    """The fp32 model through the engine: prefill in the reference's chunk order, then the
+    captured verify step with the golden drafts; first tokens and accept results match."""
+    from pilm_b200.qwen3 import Qwen3VerifierF32, Qwen3WeightsF32
+    z = G.load("model_qwen3_w8a32_f32.npz")
+    cfg, seed = G.model_config(z)
+    w = Qwen3WeightsF32.from_checkpoint(shape_of(cfg), om.make_checkpoint(cfg, seed), dev())
+    B = G.num_seqs(z)
+    kv = PagedKVCache(w.shape, 32, dev(), dtype=torch.float32)
+    ver = Qwen3VerifierF32(w, kv, max_rows=128, max_pos=256, device=dev())
+    eng = MTPVerifyEngine(ver, num_blocks=32, max_model_len=256, max_num_batched_tokens=16)
+    sids = [eng.add_request(G.ilist(z[f"b{b}.prompt"]), max_new_tokens=64) for b in range(B)]
+    first = eng.prefill()
+    res = eng.verify_step({sid: G.ilist(z[f"b{b}.drafts"]) for b, sid in enumerate(sids)})
+    agree = 0
+    for b, sid in enumerate(sids):
+        assert eng.sched.seqs[sid].pages == G.ilist(z[f"b{b}.block_ids"])
+        if first[sid] != int(z[f"b{b}.first_token"][0]):
+            continue
+        r = next(x for x in res if x.seq_id == sid)
+        agree += int([r.accepted, r.next_token] == G.ilist(z[f"b{b}.accept"]))
+    assert agree >= B - 1
+
+
 def test_verify_step_is_deterministic():
     z, cfg, ckpt, w = build("qwen3_w4g128")
     outs = []
