@@ -38,9 +38,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "verified tok/s/GPU, Qwen3-8B W4A16 MTP verify; quant-GEMM HBM GB/s vs peak"
 SEQS, PROMPT, K_DRAFT, PAGE = 32, 8192, 2, 16
-# ncu capture of one attn_verify launch: 16 sequences x 8195 keys, 8 KV heads x 128 bf16,
+# ncu capture of one attn_pages launch: 16 sequences x 8195 keys, 8 KV heads x 128 bf16,
 # DRAM read + write bytes, and the K/V bytes of that launch
-ATTN_TRAFFIC_CAPTURE = (537.568256e6 + 5.998336e6, 16 * 8195 * 8 * 128 * 2 * 2)
+ATTN_TRAFFIC_CAPTURE = (538.756096e6 + 4.719872e6, 16 * 8195 * 8 * 128 * 2 * 2)
 GEN_HEADROOM = 512
 
 
@@ -53,7 +53,8 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons, every 20 ms, from the start of
+    the first timed region to the end of the last (the device step, e2e and cycle legs)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -66,12 +67,17 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start; the timed region begins once it is sampling
+        t0 = time.perf_counter()
+        while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 5.0:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -181,7 +187,6 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
     ms = e0.elapsed_time(e1) / args.steps
     rows_per_step = batch.total_q
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -271,6 +276,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "call": "pilm_b200.engine.MTPVerifyEngine.verify_step() with the GPU MTP drafter "
                     "(verify + k draft steps in one captured step; host accept results and drafts out)",
         }
+    clocks = sampler.stop()
     h2d = 4 * (3 * rows_per_step + SEQS * maxp + 2 * SEQS + 1) + 0
     d2h = 4 * 2 * SEQS
 
@@ -287,7 +293,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     lin_ms = op_ms.get("linear_total")
     lin_gbs = lin_bytes / (lin_ms * 1e-3) / 1e9 if lin_ms else None
     step_bytes = att_bytes * shape.layers + lin_bytes + 2 * rows_per_step * shape.hidden * 2
-    # DRAM traffic of one attn_verify launch: an ncu capture of the same kernel on a
+    # DRAM traffic of one attn_pages launch: an ncu capture of the same kernel on a
     # 16-sequence case (dram__bytes_read.sum + dram__bytes_write.sum), scaled by this
     # launch's K/V bytes, with which the kernel's traffic grows (it reads each K/V byte once)
     kv_bytes = sum(ctx) * shape.n_kv_heads * shape.head_dim * 2 * 2
@@ -328,7 +334,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         },
         "cycle": cycle,
         "roofline": {
-            "kernel": "attn_verify (+ merge), per layer",
+            "kernel": "attn_pages (+ attn_merge_pages), per layer",
             "bound": "hbm",
             "achieved": round(att_gbs, 1) if att_gbs else None,
             "peak": pk["hbm_gbs"],

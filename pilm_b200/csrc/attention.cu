@@ -595,6 +595,9 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
     __shared__ __align__(8) uint64_t full_bar[kPStages], empty_bar[kPStages];
     __shared__ int s_blk_ok[kPStages];  // the stage's block id was valid (else zero its tiles)
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // the merge kernel may be scheduled now: it waits for this grid's completion before it
+    // reads anything (programmatic dependent launch)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkv = p.nkv;
     const int cta = blockIdx.x;
@@ -904,48 +907,65 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
     }
 }
 
-// grid: total_q * nh; block: 128 (one thread per dim).  Combines the per-CTA partials of
-// sequences that were cut by CTA range boundaries, in CTA order.
+// grid: (nh, max_q, B); block: 128 (one thread per dim).  Combines, in CTA order, the
+// per-CTA partials of a sequence that CTA range boundaries cut; a sequence one CTA holds
+// whole was written by that CTA.  Launched as a programmatic dependent of attn_pages: every
+// CTA waits for that grid first.  The loads of each step are independent of one another,
+// so a CTA waits on three rounds of memory: the metadata, then the pieces' (m, l, O).
 __global__ void attn_merge_pages(const PageAttnParams p) {
-    const int item = blockIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int head = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
     const int d = threadIdx.x;
-    if (item >= p.total_q * p.nh) return;
-    const int qrow = item / p.nh, head = item % p.nh;
-    int lo = 0, hi = p.B - 1;  // sequence of this row: largest b with cu_q[b] <= qrow
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (p.cu_q[mid] <= qrow) lo = mid; else hi = mid - 1;
-    }
-    const int b = lo, j = qrow - p.cu_q[b];
-    const long long T = p.prefix[p.B];
-    const long long P0 = p.prefix[b], P1 = p.prefix[b + 1];
-    if (P1 <= P0 || T <= 0) return;
+    const int q0 = p.cu_q[b], q1 = p.cu_q[b + 1];
+    const long long P0 = p.prefix[b], P1 = p.prefix[b + 1], T = p.prefix[p.B];
+    if (j >= q1 - q0 || P1 <= P0 || T <= 0) return;
     const int c0 = cta_of_page(P0, T, p.G), c1 = cta_of_page(P1 - 1, T, p.G);
     if (c0 == c1) return;  // finished by its CTA
-    // CTAs between c0 and c1 with an empty range (more CTAs than pages) wrote nothing
-    auto empty = [&](int c) { return ((long long)c * T) / p.G == ((long long)(c + 1) * T) / p.G; };
-    float M = -INFINITY;
-    for (int c = c0; c <= c1; ++c) {
-        if (empty(c)) continue;
-        const int slot = ((long long)c * T) / p.G >= P0 ? 0 : 1;
-        const float *rec = p.part + ((((size_t)c * 2 + slot) * p.max_q + j) * p.nh + head) * (kHD + 2);
-        if (rec[kHD + 1] > 0.f) M = fmaxf(M, rec[kHD]);
-    }
-    float L = 0.f, O = 0.f;
-    for (int c = c0; c <= c1; ++c) {
-        if (empty(c)) continue;
-        const int slot = ((long long)c * T) / p.G >= P0 ? 0 : 1;
-        const float *rec = p.part + ((((size_t)c * 2 + slot) * p.max_q + j) * p.nh + head) * (kHD + 2);
-        const float l = rec[kHD + 1];
-        if (!(l > 0.f)) continue;
-        const float f = expf(rec[kHD] - M);
-        L += l * f;
-        O += rec[d] * f;
+    const size_t ob = (size_t)(q0 + j) * p.nh * kHD + (size_t)head * kHD;
+    const float gt = p.gate ? bf2f(p.gate[ob + d]) : 0.f;
+    // CTA c's record for this sequence: slot 0 if the sequence starts inside c's range,
+    // slot 1 if it runs on from before; CTAs with an empty range (more CTAs than pages)
+    // wrote nothing and are skipped
+    constexpr int U = 8;
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int cb = c0; cb <= c1; cb += U) {
+        float m[U], l[U], o[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            m[u] = -INFINITY;
+            l[u] = 0.f;
+            o[u] = 0.f;
+            const int c = cb + u;
+            const long long lo = ((long long)c * T) / p.G, hi = ((long long)(c + 1) * T) / p.G;
+            if (c <= c1 && lo < hi) {
+                const float *rec =
+                    p.part + ((((size_t)c * 2 + (lo >= P0 ? 0 : 1)) * p.max_q + j) * p.nh + head) * (kHD + 2);
+                m[u] = rec[kHD];
+                l[u] = rec[kHD + 1];
+                o[u] = rec[d];
+            }
+        }
+        float mc = M;
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (l[u] > 0.f) mc = fmaxf(mc, m[u]);
+        if (mc == -INFINITY) continue;
+        if (mc > M && L > 0.f) {  // only when the pieces exceed one chunk of U
+            const float f = expf(M - mc);
+            L *= f;
+            O *= f;
+        }
+        M = mc;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (!(l[u] > 0.f)) continue;
+            const float f = expf(m[u] - M);
+            L += l[u] * f;
+            O += o[u] * f;
+        }
     }
     float v = L > 0.f ? bf16_round(__fdiv_rn(O, L)) : 0.f;
-    const size_t ob = (size_t)qrow * p.nh * kHD + (size_t)head * kHD;
     if (p.gate) {
-        const float gt = bf2f(p.gate[ob + d]);
         const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt))));
         v = __fmul_rn(v, sg);
     }
@@ -1048,7 +1068,18 @@ int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnPara
     if (rc != ECPU_OK) return rc;
     rc = check_error_word(what, "a K/V page load did not complete");
     if (rc != ECPU_OK) return rc;
-    attn_merge_pages<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p.nh, (unsigned)p.max_q, (unsigned)p.B);
+    cfg.blockDim = dim3(kHD);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_merge_pages, p);
+    PILM_REQUIRE(e == cudaSuccess, ECPU_ERR_KERNEL, "%s: merge launch failed: %s", what, cudaGetErrorString(e));
     return check_launch(what);
 }
 

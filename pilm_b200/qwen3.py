@@ -355,23 +355,36 @@ class Qwen3Verifier:
         return h
 
     def time_attention(self, b: VerifyBatch, reps: int = 2) -> float:
-        """Average ms per paged-attention launch: every layer's attention over the batch,
-        launched back to back (reps x layers launches) between two CUDA events."""
+        """Average ms per paged-attention call (kernel + merge): every layer's attention over
+        the batch, captured once as a graph and replayed reps times between two CUDA events,
+        so the figure is device time, free of host launch overhead."""
         s = self.shape
         T = b.total_q
         desc = self._desc(b)
         gate = self.gate[:T] if s.gated else None
-        run = lambda li: ck.paged_attention_verify(desc, self.q[:T], self.kv.k[li], self.kv.v[li], b.block_table,
-                                                   b.cu_q, b.context_lens, gate, self.attn[:T])
-        run(0)
+
+        def body():
+            for li in range(s.layers):
+                ck.paged_attention_verify(desc, self.q[:T], self.kv.k[li], self.kv.v[li], b.block_table, b.cu_q,
+                                          b.context_lens, gate, self.attn[:T])
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            body()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            body()
+        g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            for li in range(s.layers):
-                run(li)
+            g.replay()
         e1.record()
         torch.cuda.synchronize()
+        del g
         return e0.elapsed_time(e1) / (reps * s.layers)
 
     def time_linears(self, T: int, reps: int = 5) -> dict:
