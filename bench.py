@@ -478,6 +478,154 @@ def run_reference(args, rank: int) -> dict | None:
     }
 
 
+# ---------------------------------------------------------------------------------------
+# op sweep: each hot-path kernel alone, over the shapes the configurations use
+# ---------------------------------------------------------------------------------------
+
+SWEEP_M = (1, 2, 3, 4, 8, 16, 32, 64, 128, 256)
+SWEEP_KN = ((4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096), (4096, 151936))
+L2_BYTES = 126 * 2 ** 20
+
+
+def _graph_ms(body, calls: int, iters: int = 5) -> float:
+    """ms per call: body() issues `calls` launches; it is captured once as a CUDA graph and
+    replayed `iters` times between two CUDA events after a warm-up replay."""
+    import torch
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        body()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        body()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / (iters * calls)
+
+
+def run_sweep(args) -> None:
+    """One JSON line per case.  Linears: W4A16 g128 and W8A32 at every M of SWEEP_M on the
+    Qwen3-8B projection shapes (K, N); enough weight copies are cycled that each call reads
+    its weights from HBM (copies x bytes > 2 x L2).  Paged attention: q_len 2-5 at 1K, 8K
+    and 32K keys, 32 Q / 8 KV heads, batch sized to about 1 GB of K/V per call.  Accept:
+    row top-2 + greedy accept over 256 sequences x 5 rows x 151936 bf16 logits."""
+    import torch
+
+    from pilm_b200 import bindings
+    from pilm_b200 import ckernel as ck
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    bindings.init()
+    pk = peaks()
+    peak = pk["hbm_gbs"]
+    g = torch.Generator(device=dev).manual_seed(7)
+
+    def emit(d):
+        d["peak_gbs"], d["peak_source"] = peak, pk["source"]
+        print(json.dumps(d), flush=True)
+
+    only = set(args.sweep.split(",")) if args.sweep != "all" else {"linear", "attention", "accept"}
+    if "linear" in only:
+        for K, N in SWEEP_KN:
+            for fmt in ("w4a16g128", "w8a32"):
+                if fmt == "w4a16g128":
+                    wbytes = N * K // 2 + 4 * N * (K // 128)
+                    mk = lambda: (torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g),
+                                  torch.rand((N, K // 128), device=dev, generator=g) * 0.01 + 1e-4)
+                else:
+                    wbytes = N * K + 4 * N
+                    mk = lambda: (torch.randint(-127, 128, (N, K), dtype=torch.int8, device=dev, generator=g),
+                                  torch.rand((N,), device=dev, generator=g) * 0.01 + 1e-4)
+                copies = max(1, -(-2 * L2_BYTES // wbytes))
+                ws = [mk() for _ in range(copies)]
+                calls = max(copies, 8)
+                for M in SWEEP_M:
+                    if fmt == "w4a16g128":
+                        x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+                        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                        io = 2 * M * K + 2 * M * N
+                        fn = lambda i: ck.linear_w4a16g128_bf16(x, ws[i % copies][0], ws[i % copies][1], out=y)
+                    else:
+                        x = torch.randn((M, K), device=dev, generator=g)
+                        y = torch.empty((M, N), dtype=torch.float32, device=dev)
+                        io = 4 * M * K + 4 * M * N
+                        fn = lambda i: ck.linear_w8a32(x, ws[i % copies][0], ws[i % copies][1], out=y)
+
+                    def body():
+                        for i in range(calls):
+                            fn(i)
+                    ms = _graph_ms(body, calls)
+                    gbs = (wbytes + io) / (ms * 1e-3) / 1e9
+                    emit({"sweep": "linear", "format": fmt, "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
+                          "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                          "tflops": round(2 * M * N * K / (ms * 1e-3) / 1e12, 2)})
+                del ws
+                torch.cuda.empty_cache()
+    if "attention" in only:
+        from pilm_b200.qwen3 import QWEN3_8B, attention_bytes
+        s = QWEN3_8B
+        for ctx in (1024, 8192, 32768):
+            B = max(1, (2 ** 30) // (ctx * s.n_kv_heads * s.head_dim * 4))
+            pages = -(-(ctx + 8) // 16)
+            nb = B * pages + 1
+            kc = torch.randn((nb, 16, s.n_kv_heads, s.head_dim), device=dev, generator=g).to(torch.bfloat16)
+            vc = torch.randn((nb, 16, s.n_kv_heads, s.head_dim), device=dev, generator=g).to(torch.bfloat16)
+            perm = (torch.randperm(nb - 1, device=dev, generator=g) + 1).to(torch.int32)
+            table = perm[:B * pages].view(B, pages).contiguous()
+            for q_len in (2, 3, 4, 5):
+                T = B * q_len
+                i32 = dict(dtype=torch.int32, device=dev)
+                cu = torch.arange(0, T + 1, q_len, **i32)
+                ctxs = torch.full((B,), ctx, **i32)
+                q = torch.randn((T, s.n_heads * s.head_dim), device=dev, generator=g).to(torch.bfloat16)
+                out = torch.empty_like(q)
+                desc = ck.attn_desc(num_seqs=B, total_q=T, max_q_len=q_len, n_heads=s.n_heads,
+                                    n_kv_heads=s.n_kv_heads, head_dim=s.head_dim, block_size=16, num_blocks=nb,
+                                    max_blocks_per_seq=pages, max_context=ctx, qkv_stride=s.qkv_rows,
+                                    rope_rows=0, rot_dim=s.rot_dim, eps=s.eps, add_one=0, output_gate=0)
+
+                def body():
+                    for _ in range(4):
+                        ck.paged_attention_verify(desc, q, kc, vc, table, cu, ctxs, None, out)
+                ms = _graph_ms(body, 4)
+                nbytes = attention_bytes(s, [ctx] * B, [q_len] * B)
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                emit({"sweep": "attention", "q_len": q_len, "ctx": ctx, "seqs": B, "heads": [s.n_heads, s.n_kv_heads],
+                      "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+            del kc, vc
+            torch.cuda.empty_cache()
+    if "accept" in only:
+        B, k, V = 256, 4, 151936
+        T = B * (k + 1)
+        i32 = dict(dtype=torch.int32, device=dev)
+        logits = torch.randn((T, V), device=dev, generator=g).to(torch.bfloat16)
+        ids = torch.randint(0, V, (T,), device=dev, generator=g).to(torch.int32)
+        cu = torch.arange(0, T + 1, k + 1, **i32)
+        top1, acc, nxt = torch.empty(T, **i32), torch.empty(B, **i32), torch.empty(B, **i32)
+        ctx0 = torch.full((B,), 4096, **i32)
+        ctxs = ctx0.clone()
+
+        def body():
+            for _ in range(4):
+                ctxs.copy_(ctx0)
+                ck.argmax_top2(logits, top1)
+                ck.verify_accept_greedy(B, ids, top1, cu, acc, nxt, ctxs)
+        ms = _graph_ms(body, 4)
+        nbytes = T * V * 2
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        emit({"sweep": "accept", "seqs": B, "k": k, "vocab": V, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+              "frac": round(gbs / peak, 4)})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -490,7 +638,12 @@ def main():
     ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per GPU (default: the BASELINE config)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens per sequence")
     ap.add_argument("--layers", type=int, default=0, help="decoder layers (0 = all 36); profiling only")
+    ap.add_argument("--sweep", default=None,
+                    help="per-kernel op sweep instead of the bench line: all, or any of linear,attention,accept")
     args = ap.parse_args()
+    if args.sweep:
+        run_sweep(args)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -47,17 +47,60 @@ __device__ __forceinline__ float ld_logit<float>(const float *p, size_t i) { ret
 template <>
 __device__ __forceinline__ float ld_logit<__nv_bfloat16>(const __nv_bfloat16 *p, size_t i) { return bf2f(p[i]); }
 
-// one CTA (512 threads) per row
+// the e-th logit held in a 16-byte vector
 template <typename T>
-__global__ void __launch_bounds__(512) row_top2(const T *__restrict__ logits, int rows, int V,
-                                                int32_t *__restrict__ top1, float *__restrict__ top1_val,
-                                                float *__restrict__ margin) {
-    __shared__ Top2 sh[16];
+__device__ __forceinline__ float vec_logit(const uint4 &r, int e);
+template <>
+__device__ __forceinline__ float vec_logit<float>(const uint4 &r, int e) {
+    const uint32_t w = e == 0 ? r.x : (e == 1 ? r.y : (e == 2 ? r.z : r.w));
+    return __uint_as_float(w);
+}
+template <>
+__device__ __forceinline__ float vec_logit<__nv_bfloat16>(const uint4 &r, int e) {
+    const int k = e >> 1;
+    const uint32_t w = k == 0 ? r.x : (k == 1 ? r.y : (k == 2 ? r.z : r.w));
+    return __uint_as_float((e & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+
+constexpr int kTop2Threads = 1024;
+constexpr int kTop2Unroll = 4;
+
+// One CTA per row.  The row's 16-byte-aligned middle is read with 16-byte loads, four in
+// flight per thread (64 KB per CTA), so a single CTA streams its row near an SM's share
+// of HBM bandwidth; the unaligned head and tail are read element by element.  The result
+// does not depend on the visiting order: ties keep the smallest index, like torch.argmax.
+template <typename T>
+__global__ void __launch_bounds__(kTop2Threads) row_top2(const T *__restrict__ logits, int rows, int V,
+                                                         int32_t *__restrict__ top1, float *__restrict__ top1_val,
+                                                         float *__restrict__ margin) {
+    __shared__ Top2 sh[kTop2Threads / 32];
     const int row = blockIdx.x;
     if (row >= rows) return;
     const T *x = logits + (size_t)row * V;
+    constexpr int E = 16 / sizeof(T);
+    const int head = min(V, (int)(((16 - ((uintptr_t)x & 15)) & 15) / sizeof(T)));
+    const int nvec = (V - head) / E;
+    const int tail0 = head + nvec * E;
     Top2 t{-INFINITY, 0x7fffffff, -INFINITY};
-    for (int i = threadIdx.x; i < V; i += blockDim.x) top2_push(t, ld_logit<T>(x, i), i);
+    for (int i = threadIdx.x; i < head; i += blockDim.x) top2_push(t, ld_logit<T>(x, i), i);
+    const uint4 *xv = reinterpret_cast<const uint4 *>(x + head);
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += kTop2Unroll * blockDim.x) {
+        uint4 r[kTop2Unroll];
+#pragma unroll
+        for (int u = 0; u < kTop2Unroll; ++u) {
+            const int v = v0 + u * blockDim.x;
+            r[u] = v < nvec ? ldg_nc_v4(xv + v) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kTop2Unroll; ++u) {
+            const int v = v0 + u * blockDim.x;
+            if (v < nvec) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) top2_push(t, vec_logit<T>(r[u], e), head + v * E + e);
+            }
+        }
+    }
+    for (int i = tail0 + threadIdx.x; i < V; i += blockDim.x) top2_push(t, ld_logit<T>(x, i), i);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         Top2 u;
@@ -302,7 +345,7 @@ int ekernel_argmax_top2_f32(const ekernel_accept_desc_t *desc, const float *logi
     PILM_REQUIRE(desc && logits, ECPU_ERR_PARAM, "ekernel_argmax_top2_f32: null argument");
     PILM_REQUIRE(desc->vocab > 0 && desc->vocab <= 0x7fffffff, ECPU_ERR_PARAM, "ekernel_argmax_top2_f32: bad vocab");
     if (desc->total_q == 0) return ECPU_OK;
-    row_top2<float><<<(unsigned)desc->total_q, 512, 0, stream()>>>(logits, (int)desc->total_q, (int)desc->vocab, top1,
+    row_top2<float><<<(unsigned)desc->total_q, kTop2Threads, 0, stream()>>>(logits, (int)desc->total_q, (int)desc->vocab, top1,
                                                                    top1_val, margin);
     return check_launch("ekernel_argmax_top2_f32");
 }
@@ -312,7 +355,7 @@ int ekernel_argmax_top2_bf16(const ekernel_accept_desc_t *desc, const uint16_t *
     PILM_REQUIRE(desc && logits, ECPU_ERR_PARAM, "ekernel_argmax_top2_bf16: null argument");
     PILM_REQUIRE(desc->vocab > 0 && desc->vocab <= 0x7fffffff, ECPU_ERR_PARAM, "ekernel_argmax_top2_bf16: bad vocab");
     if (desc->total_q == 0) return ECPU_OK;
-    row_top2<__nv_bfloat16><<<(unsigned)desc->total_q, 512, 0, stream()>>>(
+    row_top2<__nv_bfloat16><<<(unsigned)desc->total_q, kTop2Threads, 0, stream()>>>(
         (const __nv_bfloat16 *)logits, (int)desc->total_q, (int)desc->vocab, top1, top1_val, margin);
     return check_launch("ekernel_argmax_top2_bf16");
 }

@@ -7,7 +7,7 @@
 //   W8A32 (:437-467):                            C = s[n] * sum_k A q     (fp32)
 // q is the signed int4 nibble (even k in the low nibble, :43-46) or int8.
 //
-// Small M (the verify regime, M = batch*(k+1) < 64) is HBM-bound: the packed
+// Small M (M <= 16; larger M goes to the tensor-core GEMM) is HBM-bound: the packed
 // weights are streamed once with 128-bit loads and dequantised in registers straight
 // into tensor-core A fragments (mma.sync m16n8k16, bf16 x bf16 -> fp32); the
 // activations form the B fragments.  The k order inside each 128-wide group is
@@ -263,47 +263,89 @@ __global__ void __launch_bounds__(256) linear_generic(const __nv_bfloat16 *__res
     }
 }
 
-// W8A32: fp32 activations, int8 weights, per-row scale, fp32 out.  One warp per row;
-// 16 int8 weights per lane per step when K % 16 == 0 (coalesced 16-byte loads).
+// W8A32: fp32 activations, int8 weights, per-row scale, fp32 out.  A warp owns kW8Rows
+// weight rows and streams them once per chunk of four activation rows: each lane keeps
+// kW8Rows x kW8Unroll 16-byte weight loads in flight, and every activation value it
+// loads serves all of the warp's rows.  Each lane sums its k positions in increasing
+// order (16 per 512-wide step), then the warp sums its lanes.  Ragged K or unaligned
+// pointers take the scalar loop.
+constexpr int kW8Rows = 4, kW8Unroll = 2;
+
 __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, int M, int K,
                                                   const int8_t *__restrict__ W, const float *__restrict__ S, int N,
                                                   float *__restrict__ Y) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = blockIdx.x * 8 + warp;
-    if (n >= N) return;
-    const int8_t *w = W + (size_t)n * K;
+    const int n0 = (blockIdx.x * 8 + warp) * kW8Rows;
+    if (n0 >= N) return;
     const bool vec = ((K & 15) == 0) && ((((uintptr_t)W) & 15) == 0) && ((((uintptr_t)X) & 15) == 0);
+    const int8_t *w[kW8Rows];
+    bool rv[kW8Rows];
+#pragma unroll
+    for (int r = 0; r < kW8Rows; ++r) {
+        rv[r] = n0 + r < N;
+        w[r] = W + (size_t)(rv[r] ? n0 + r : n0) * K;
+    }
     for (int m0 = 0; m0 < M; m0 += 4) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int mc = min(4, M - m0);
+        float acc[4][kW8Rows];
+#pragma unroll
+        for (int mm = 0; mm < 4; ++mm)
+#pragma unroll
+            for (int r = 0; r < kW8Rows; ++r) acc[mm][r] = 0.f;
         if (vec) {
-            for (int k = lane * 16; k < K; k += 512) {
-                uint4 q4 = ldg_nc_v4(w + k);
-                const int8_t *q = reinterpret_cast<const int8_t *>(&q4);
+            for (int kb = lane * 16; kb < K; kb += 512 * kW8Unroll) {
+                uint4 q[kW8Unroll][kW8Rows];
 #pragma unroll
-                for (int mm = 0; mm < 4; ++mm) {
-                    if (m0 + mm >= M) break;
-                    const float4 *xr = reinterpret_cast<const float4 *>(X + (size_t)(m0 + mm) * K + k);
+                for (int u = 0; u < kW8Unroll; ++u) {
+                    const int k = kb + u * 512;
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        float4 xv = __ldg(xr + v);
-                        acc[mm] = fmaf(xv.x, (float)q[4 * v + 0], acc[mm]);
-                        acc[mm] = fmaf(xv.y, (float)q[4 * v + 1], acc[mm]);
-                        acc[mm] = fmaf(xv.z, (float)q[4 * v + 2], acc[mm]);
-                        acc[mm] = fmaf(xv.w, (float)q[4 * v + 3], acc[mm]);
+                    for (int r = 0; r < kW8Rows; ++r) q[u][r] = k < K ? ldg_nc_v4(w[r] + k) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < kW8Unroll; ++u) {
+                    const int k = kb + u * 512;
+                    if (k >= K) continue;
+#pragma unroll
+                    for (int mm = 0; mm < 4; ++mm) {
+                        if (mm >= mc) continue;
+                        const float4 *xr = reinterpret_cast<const float4 *>(X + (size_t)(m0 + mm) * K + k);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            const float4 xv = __ldg(xr + v);
+#pragma unroll
+                            for (int r = 0; r < kW8Rows; ++r) {
+                                const int8_t *qq = reinterpret_cast<const int8_t *>(&q[u][r]);
+                                acc[mm][r] = fmaf(xv.x, (float)qq[4 * v + 0], acc[mm][r]);
+                                acc[mm][r] = fmaf(xv.y, (float)qq[4 * v + 1], acc[mm][r]);
+                                acc[mm][r] = fmaf(xv.z, (float)qq[4 * v + 2], acc[mm][r]);
+                                acc[mm][r] = fmaf(xv.w, (float)qq[4 * v + 3], acc[mm][r]);
+                            }
+                        }
                     }
                 }
             }
         } else {
             for (int k = lane; k < K; k += 32) {
-                float q = (float)w[k];
-                for (int mm = 0; mm < 4 && m0 + mm < M; ++mm) acc[mm] = fmaf(X[(size_t)(m0 + mm) * K + k], q, acc[mm]);
+                float qf[kW8Rows];
+#pragma unroll
+                for (int r = 0; r < kW8Rows; ++r) qf[r] = (float)w[r][k];
+#pragma unroll
+                for (int mm = 0; mm < 4; ++mm) {
+                    if (mm >= mc) continue;
+                    const float xk = X[(size_t)(m0 + mm) * K + k];
+#pragma unroll
+                    for (int r = 0; r < kW8Rows; ++r) acc[mm][r] = fmaf(xk, qf[r], acc[mm][r]);
+                }
             }
         }
-        const float s = __ldg(S + n);
 #pragma unroll
-        for (int mm = 0; mm < 4; ++mm) {
-            float v = warp_sum(acc[mm]);
-            if (lane == 0 && m0 + mm < M) Y[(size_t)(m0 + mm) * N + n] = v * s;
+        for (int r = 0; r < kW8Rows; ++r) {
+            const float sc = rv[r] ? __ldg(S + n0 + r) : 0.f;
+#pragma unroll
+            for (int mm = 0; mm < 4; ++mm) {
+                const float v = warp_sum(acc[mm][r]);
+                if (lane == 0 && mm < mc && rv[r]) Y[(size_t)(m0 + mm) * N + n0 + r] = v * sc;
+            }
         }
     }
 }
@@ -405,7 +447,9 @@ int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, cons
     if (M == 0 || N == 0) return ECPU_OK;
     const bool mma_ok = (qf == 1 || (qf == 0 && gs == 128)) && (K % 128 == 0) && aligned16(A) && aligned16(W);
     if (mma_ok) {
-        if (M >= 64) {
+        // above 16 rows the register-dequant GEMV re-reads each activation tile per 16
+        // weight rows; the tensor-core GEMM stages it once per 128 (N = 32, 48, ... rows)
+        if (M > 16) {
             int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, what);
             if (rc != ECPU_ERR_UNSUPPORTED) return rc;
         }
@@ -456,8 +500,8 @@ int ekernel_linear_w8a32(const ekernel_linear_w8a32_desc_t *desc, const float *A
     (void)isa;
     LINEAR_ARGS_OK("ekernel_linear_w8a32");
     if (desc->M == 0 || desc->N == 0) return ECPU_OK;
-    w8a32_gemv<<<(unsigned)((desc->N + 7) / 8), 256, 0, pilm::stream()>>>(A, (int)desc->M, (int)desc->K, W, scales,
-                                                                        (int)desc->N, C);
+    w8a32_gemv<<<(unsigned)((desc->N + 8 * kW8Rows - 1) / (8 * kW8Rows)), 256, 0, pilm::stream()>>>(
+        A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C);
     return pilm::check_launch("ekernel_linear_w8a32");
 }
 

@@ -1,4 +1,4 @@
-// W4A16 group-128 GEMM for M >= 64 on 5th-generation tensor cores (tcgen05 + TMEM).
+// W4A16 group-128 GEMM for M > 16 on 5th-generation tensor cores (tcgen05 + TMEM).
 //
 // Reference semantics (src/ecpu/src/kernel/kernels.c:1089-1139):
 //     C[m,n] = rne_bf16( sum_g s[n,g] * sum_{k in g} A[m,k] * q[n,k] )
@@ -535,7 +535,7 @@ namespace pilm {
 int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
                  bool grouped, const char *what) {
     static const bool disabled = getenv("PILM_DISABLE_TC") && getenv("PILM_DISABLE_TC")[0] == '1';
-    if (disabled || M < 64 || (K % 128) != 0 || N < 1) return ECPU_ERR_UNSUPPORTED;
+    if (disabled || M <= 16 || (K % 128) != 0 || N < 1) return ECPU_ERR_UNSUPPORTED;
     if ((((uintptr_t)X) & 15) || (((uintptr_t)W) & 15)) return ECPU_ERR_UNSUPPORTED;
     TensorMapEncodeTiledFn enc = tensor_map_encoder();
     int *err = device_error_word();

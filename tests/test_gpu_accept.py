@@ -33,6 +33,28 @@ def test_top2_matches_torch_first_max():
     assert top1.cpu().tolist() == torch.argmax(xb.float(), -1).tolist()
 
 
+@pytest.mark.parametrize("V", [1, 3, 7, 9, 1001, 32003])
+def test_top2_ragged_vocab_unaligned_rows(V):
+    """Vocabularies that leave rows off 16-byte boundaries: the scalar head and tail and
+    the vector middle agree with torch's first-max argmax, ties across the three included."""
+    g = torch.Generator().manual_seed(V)
+    x = torch.randn((6, V), generator=g)
+    if V >= 3:
+        x[1, 0] = x[1, V - 1] = 40.0       # head vs tail
+        x[2, V // 2] = x[2, V - 1] = 41.0  # middle vs tail
+        x[3, 1] = x[3, V // 2] = 42.0      # head vs middle
+    x[4, V - 1] = 43.0
+    t = torch.topk(x, min(2, V), -1).values
+    for dt in (torch.float32, torch.bfloat16):
+        xd = x.to(dt)
+        top1 = torch.empty(6, dtype=torch.int32, device=dev())
+        margin = torch.empty(6, dtype=torch.float32, device=dev())
+        ck.argmax_top2(xd.to(dev()), top1, None, margin)
+        assert top1.cpu().tolist() == torch.argmax(xd.float(), -1).tolist()
+        if dt == torch.float32 and V >= 2:
+            assert torch.allclose(margin.cpu(), t[:, 0] - t[:, 1])
+
+
 def test_greedy_accept_and_rollback():
     # 4 sequences: full accept, partial, immediate reject, no drafts
     cu = [0, 4, 8, 11, 12]

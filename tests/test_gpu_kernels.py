@@ -50,8 +50,9 @@ def test_linears_vs_reference_golden(kz):
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 12, 16, 24, 32, 48, 63, 64, 96, 100, 128, 130, 256])
 @pytest.mark.parametrize("NK", [(256, 512), (384, 1024), (200, 4096), (136, 1152), (100, 2048)])
 def test_w4g128_vs_oracle_all_regimes(M, NK):
-    """Every GEMV tile configuration (M <= 8, 16, 32, 64) and the M >= 64 path,
-    including split-K (K=4096), ragged N, an N that is not a multiple of 8 (no split-K
+    """Both GEMV tile configurations (M <= 8, 16) and the tensor-core path above 16 rows
+    (N = 32, 48, 64, ... activation rows per MMA), including split-K (K=4096), ragged N,
+    an N that is not a multiple of 8 (no split-K
     combine pass), and a group count that is not a multiple of 4 (K=1152: the tensor-core
     path loads group scales directly instead of by TMA)."""
     N, K = NK
