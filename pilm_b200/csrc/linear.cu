@@ -264,13 +264,23 @@ __global__ void __launch_bounds__(256) linear_generic(const __nv_bfloat16 *__res
 }
 
 // W8A32: fp32 activations, int8 weights, per-row scale, fp32 out.  A warp owns kW8Rows
-// weight rows and streams them once per chunk of four activation rows: each lane keeps
+// weight rows and streams them once per chunk of MC activation rows: each lane keeps
 // kW8Rows x kW8Unroll 16-byte weight loads in flight, and every activation value it
 // loads serves all of the warp's rows.  Each lane sums its k positions in increasing
 // order (16 per 512-wide step), then the warp sums its lanes.  Ragged K or unaligned
 // pointers take the scalar loop.
 constexpr int kW8Rows = 4, kW8Unroll = 2;
 
+// Signed byte e of w as an exact fp32: with the sign bit flipped, the byte u = q + 128 is
+// placed in the low mantissa bits of 2^23 (exponent byte 0x4B), giving 2^23 + u exactly,
+// and subtracting 2^23 + 128 leaves q.  One byte permute and one add instead of an
+// integer-to-float conversion.
+__device__ __forceinline__ float i8_to_f32(uint32_t w, int e) {
+    const uint32_t t = __byte_perm(w ^ 0x80808080u, 0x4B000000u, (uint32_t)e | 0x7440u);
+    return __uint_as_float(t) - 8388736.0f;
+}
+
+template <int MC>
 __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, int M, int K,
                                                   const int8_t *__restrict__ W, const float *__restrict__ S, int N,
                                                   float *__restrict__ Y) {
@@ -285,11 +295,11 @@ __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, i
         rv[r] = n0 + r < N;
         w[r] = W + (size_t)(rv[r] ? n0 + r : n0) * K;
     }
-    for (int m0 = 0; m0 < M; m0 += 4) {
-        const int mc = min(4, M - m0);
-        float acc[4][kW8Rows];
+    for (int m0 = 0; m0 < M; m0 += MC) {
+        const int mc = min(MC, M - m0);
+        float acc[MC][kW8Rows];
 #pragma unroll
-        for (int mm = 0; mm < 4; ++mm)
+        for (int mm = 0; mm < MC; ++mm)
 #pragma unroll
             for (int r = 0; r < kW8Rows; ++r) acc[mm][r] = 0.f;
         if (vec) {
@@ -305,20 +315,28 @@ __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, i
                 for (int u = 0; u < kW8Unroll; ++u) {
                     const int k = kb + u * 512;
                     if (k >= K) continue;
+                    float4 xv[MC][4];  // activation rows x 16 k
 #pragma unroll
-                    for (int mm = 0; mm < 4; ++mm) {
-                        if (mm >= mc) continue;
-                        const float4 *xr = reinterpret_cast<const float4 *>(X + (size_t)(m0 + mm) * K + k);
+                    for (int mm = 0; mm < MC; ++mm) {
+                        const float4 *xr = reinterpret_cast<const float4 *>(X + (size_t)(m0 + (mm < mc ? mm : 0)) * K + k);
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) xv[mm][v] = mm < mc ? __ldg(xr + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int r = 0; r < kW8Rows; ++r) {
 #pragma unroll
                         for (int v = 0; v < 4; ++v) {
-                            const float4 xv = __ldg(xr + v);
+                            const uint32_t w4 = word_of(q[u][r], v);
+                            float f[4];
 #pragma unroll
-                            for (int r = 0; r < kW8Rows; ++r) {
-                                const int8_t *qq = reinterpret_cast<const int8_t *>(&q[u][r]);
-                                acc[mm][r] = fmaf(xv.x, (float)qq[4 * v + 0], acc[mm][r]);
-                                acc[mm][r] = fmaf(xv.y, (float)qq[4 * v + 1], acc[mm][r]);
-                                acc[mm][r] = fmaf(xv.z, (float)qq[4 * v + 2], acc[mm][r]);
-                                acc[mm][r] = fmaf(xv.w, (float)qq[4 * v + 3], acc[mm][r]);
+                            for (int e = 0; e < 4; ++e) f[e] = i8_to_f32(w4, e);
+#pragma unroll
+                            for (int mm = 0; mm < MC; ++mm) {
+                                if (mm >= mc) continue;
+                                acc[mm][r] = fmaf(xv[mm][v].x, f[0], acc[mm][r]);
+                                acc[mm][r] = fmaf(xv[mm][v].y, f[1], acc[mm][r]);
+                                acc[mm][r] = fmaf(xv[mm][v].z, f[2], acc[mm][r]);
+                                acc[mm][r] = fmaf(xv[mm][v].w, f[3], acc[mm][r]);
                             }
                         }
                     }
@@ -330,7 +348,7 @@ __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, i
 #pragma unroll
                 for (int r = 0; r < kW8Rows; ++r) qf[r] = (float)w[r][k];
 #pragma unroll
-                for (int mm = 0; mm < 4; ++mm) {
+                for (int mm = 0; mm < MC; ++mm) {
                     if (mm >= mc) continue;
                     const float xk = X[(size_t)(m0 + mm) * K + k];
 #pragma unroll
@@ -342,7 +360,7 @@ __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, i
         for (int r = 0; r < kW8Rows; ++r) {
             const float sc = rv[r] ? __ldg(S + n0 + r) : 0.f;
 #pragma unroll
-            for (int mm = 0; mm < 4; ++mm) {
+            for (int mm = 0; mm < MC; ++mm) {
                 const float v = warp_sum(acc[mm][r]);
                 if (lane == 0 && mm < mc && rv[r]) Y[(size_t)(m0 + mm) * N + n0 + r] = v * sc;
             }
@@ -500,8 +518,14 @@ int ekernel_linear_w8a32(const ekernel_linear_w8a32_desc_t *desc, const float *A
     (void)isa;
     LINEAR_ARGS_OK("ekernel_linear_w8a32");
     if (desc->M == 0 || desc->N == 0) return ECPU_OK;
-    w8a32_gemv<<<(unsigned)((desc->N + 8 * kW8Rows - 1) / (8 * kW8Rows)), 256, 0, pilm::stream()>>>(
-        A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C);
+    const unsigned grid = (unsigned)((desc->N + 8 * kW8Rows - 1) / (8 * kW8Rows));
+    const int M = (int)desc->M, K = (int)desc->K, N = (int)desc->N;
+    if (M == 1)
+        w8a32_gemv<1><<<grid, 256, 0, pilm::stream()>>>(A, M, K, W, scales, N, C);
+    else if (M == 2)
+        w8a32_gemv<2><<<grid, 256, 0, pilm::stream()>>>(A, M, K, W, scales, N, C);
+    else
+        w8a32_gemv<4><<<grid, 256, 0, pilm::stream()>>>(A, M, K, W, scales, N, C);
     return pilm::check_launch("ekernel_linear_w8a32");
 }
 

@@ -9,22 +9,25 @@
 //
 // CTA tile: 128 weight rows (the MMA M dimension, TMEM lanes) x up to 128 activation
 // rows (the MMA N dimension), over a range of quant groups (split-K).  Warp roles
-// (640 threads):
-//   warp 0      TMA: packed weight tile [128 rows x 64 B] per group -> raw ring
-//   warp 1      TMA: activation tile [Nm rows x 128 k] (two SWIZZLE_128B boxes) -> X ring
-//   warp 2      TMEM owner + MMA issuer: 8 x tcgen05.mma (M=128, N=Nm, K=16) per group,
-//               A from TMEM, B from shared memory, into one of three TMEM partials
-//   warp 3      TMA: group scales, [128 rows x 16 groups] fp32 tiles
-//   warps 4-19  compute: warp w owns TMEM lane quadrant w%4 and quarter q = (w-4)/4 of the
-//               work there.  Step i of a compute warp: wait for the MMAs of group i-2,
-//               dequantize its quarter-row of group i (16 packed bytes -> 32 bf16, k in
-//               [32q, 32q+32)) into the A stage those MMAs released (tcgen05.st), signal
-//               the MMA issuer, then fold group i-2's partial into its accumulators
-//               (tcgen05.ld, acc + rn(part * s[n,g]) for activation-row chunk q).  Four
-//               compute warps share each SM sub-partition: the work of one step is a
-//               short dependent chain, and the other warps' arithmetic hides its TMEM,
-//               shared-memory and barrier latencies.  Keeping A in TMEM (not shared memory) halves
-//               the shared-memory traffic per group.
+// (704 threads); a warp reaches TMEM lanes 32 * (warp % 4) .. + 31 only:
+//   warp 0      TMA, one thread: per group the packed weight tile [128 rows x 64 B] (raw
+//               ring) and the activation tile [Nm rows x 128 k] (two SWIZZLE_128B boxes,
+//               X ring) on one barrier; every 16th group a [128 rows x 16 groups] fp32
+//               tile of group scales
+//   warp 1      TMEM owner + MMA issuer: 8 x tcgen05.mma (M=128, N=Nm, K=16) per group,
+//               A from TMEM, B from shared memory, into one of two TMEM partials
+//   warps 2-5   dequant: warp w owns TMEM lane quadrant w % 4 and dequantizes its 32 rows
+//               of every group (64 packed bytes -> 128 bf16 per row) into one of four A
+//               stages (tcgen05.st).  Four stages let it run up to four groups ahead of the
+//               tensor pipe, so a stage is nearly always free when it gets there.
+//   warps 6-21  fold: four per lane quadrant, each a quarter of the activation columns.
+//               For every group in order: wait for its MMAs, tcgen05.ld the partial,
+//               hand the partial buffer back to the issuer at once, then
+//               acc = acc + rn(part * s[n,g]).
+// The roles work on different groups at the same time: while the tensor pipe runs the
+// MMAs of group i, the fold warps drain group i - 1 and the dequant warps fill group
+// i + 1 .. i + 3.  Keeping A in TMEM (not shared memory) halves the shared-memory traffic
+// per group.
 // The MMA issuer pays for one barrier wait and one commit per group: the issuing thread
 // is held while its MMAs execute, so every extra wait there leaves the tensor pipe idle.
 // Every mbarrier wait is bounded: on timeout the CTA records an error, drains, frees
@@ -43,34 +46,37 @@ constexpr int kTileRows = 128;   // weight rows per CTA
 constexpr int kMaxNm = 128;      // activation rows per CTA
 constexpr int kRawStages = 8;
 constexpr int kXStages = 4;
-constexpr int kAStages = 2;                          // A buffers in TMEM (64 columns each)
+constexpr int kAStages = 4;                          // A buffers in TMEM (64 columns each)
 constexpr int kRawBytes = kTileRows * 64;            // one group of packed weights
 constexpr int kXSubBytes = kMaxNm * 128;             // Nm rows x 64 k bf16 (max)
 constexpr int kXBytes = 2 * kXSubBytes;
-constexpr int kThreads = 640;
-constexpr int kComputeWarps = 16;
-constexpr int kTBufs = 3;                            // TMEM partial buffers (MMA runs 2 groups ahead)
+constexpr int kDqWarps = 4;                          // warps 2-5
+constexpr int kFoldWarps = 16;                       // warps 6-21
+constexpr int kThreads = (2 + kDqWarps + kFoldWarps) * 32;
+constexpr int kTBufs = 2;                            // TMEM partial buffers (kMaxNm columns each)
 constexpr int kTmemCols = 512;
-constexpr int kAColBase = 0;                         // TMEM columns [0, 128): A stages
-constexpr int kAccColBase = 128;                     // TMEM columns [128, 512): partials
+constexpr int kAColBase = 0;                         // TMEM columns [0, 256): A stages
+constexpr int kAccColBase = kAStages * 64;           // TMEM columns [256, 512): partials
 constexpr uint32_t kWaitLimit = 1u << 20;            // polls before a wait gives up (bounded wait)
 constexpr uint32_t kSleepHintNs = 2000;              // longest sleep of one poll
 
 // Every mbarrier operation costs a few hundred cycles inside this kernel, so each group
 // has exactly three, all on rings indexed by slot i % kSlots:
-//   in_full[q]   both TMA copies of group i (packed weights and activations) complete
-//                here: the compute warps' one wait for their inputs
-//   op_full[q]   the MMA issuer's one wait: one arrival per compute warp once its part of
-//                A is in TMEM.  Partial buffer i % kTBufs is free by then (the same warps
-//                folded group i - 3 out of it one step earlier).  The weight producer
-//                also waits here before reusing raw slot i % kRawStages (group i - 8).
-//   mma_done[q]  the issuer's one commit: the compute warps wait for group i - 2 (partial
-//                ready, A stage i % 2 free), the activation producer for group i - 4
+//   in_full[q]   the TMA copies of group i (packed weights and activations) complete
+//                here: the dequant warps' wait for their inputs
+//   op_full[q]   the MMA issuer's one wait.  One arrival per dequant warp once its rows of
+//                A(i) are in TMEM, and one per fold warp once it has loaded group i - 2's
+//                partial (the buffer group i writes; groups 0 and 1 get theirs up front).
+//                The producer also waits here before reusing raw slot i % 8.
+//   mma_done[q]  the issuer's one commit: the fold warps wait for group i's partial, the
+//                dequant warps for A stage i % 4 (group i + 4), the producer for X
+//                stage i % 4 (group i + 4)
 // A waiter's parity is (j / kSlots) & 1 for the group j it needs.  No waiter can fall
 // kSlots or more completions behind: every later phase of its slot needs work that the
 // waiter itself has not released yet, so parities never alias.
 constexpr int kSlots = 8;
-static_assert(kSlots == kRawStages && kXStages == 4 && kAStages == 2 && kTBufs == 3, "pipeline depths");
+static_assert(kSlots == kRawStages && kXStages == 4 && kAStages == 4 && kTBufs == 2, "pipeline depths");
+static_assert(kAccColBase + kTBufs * kMaxNm <= kTmemCols, "TMEM budget");
 
 struct __align__(8) Barriers {
     uint64_t in_full[kSlots];
@@ -88,6 +94,7 @@ constexpr int kScaleBytes = kTileRows * kScaleChunk * 4;
 constexpr size_t kSmemScale = kSmemX + (size_t)kXStages * kXBytes;     // +128 KB
 constexpr size_t kSmemBar = kSmemScale + 2 * (size_t)kScaleBytes;      // +16 KB (two scale tiles)
 constexpr size_t kSmemTotal = kSmemBar + sizeof(Barriers) + 1024;      // + alignment slack
+static_assert(kSmemTotal <= 227 * 1024, "shared memory budget");
 
 // ---- PTX wrappers ---------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -268,79 +275,75 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     if (threadIdx.x == 0) {
         // consumer-side barriers take one arrival per warp (lane 0 after __syncwarp)
         for (int i = 0; i < kSlots; ++i) {
-            mbar_init(&bar->in_full[i], 2);  // the two producers' arrive.expect_tx
-            mbar_init(&bar->op_full[i], kComputeWarps);
+            mbar_init(&bar->in_full[i], 1);  // the producer's arrive.expect_tx
+            mbar_init(&bar->op_full[i], kDqWarps + kFoldWarps);
             mbar_init(&bar->mma_done[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bar->s_full[i], 1);
-            mbar_init(&bar->s_empty[i], kComputeWarps);
+            mbar_init(&bar->s_empty[i], kFoldWarps);
         }
         mbar_init(&bar->drain, 1);
         bar->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 2) tmem_alloc(&bar->tmem_base, kTmemCols);
+    if (warp == 1) tmem_alloc(&bar->tmem_base, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
 
-    float2 acc[16];  // one 32-column chunk as fp32 pairs: one packed multiply and add per pair
+
     const int x_bytes = 2 * p.Nm * 128;
 
     if (warp == 0) {
-        // ---- packed weights: TMA into the raw ring ----
+        // ---- TMA: packed weights into the raw ring, activations into the X ring, and
+        // group scales into a two-slot ring (a slot is refilled once every fold warp has
+        // finished the tile's last group) ----
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
-            int issued = 0;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+            if (nchunks > 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
+            int issued = 0, s_issued = 0;
             for (int i = 0; i < ng; ++i) {
-                const int s = i % kRawStages;
-                // raw slot s held group i - kRawStages, read by every compute warp before it
-                // arrived on that group's op_full
+                if (nchunks > 0 && i % kScaleChunk == 0) {
+                    const int c = i / kScaleChunk, slot = c & 1;
+                    if (c >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((c - 2) >> 1) & 1u, abort_flag)) break;
+                    mbar_expect_tx(&bar->s_full[slot], kScaleBytes);
+                    tma_load_2d(smem + kSmemScale + (size_t)slot * kScaleBytes, &smap, &bar->s_full[slot],
+                                g0 + kScaleChunk * c, row0);
+                    ++s_issued;
+                }
+                // raw slot i % 8 held group i - 8, read by the dequant warps before they
+                // arrived on that group's op_full; X stage i % 4 held group i - 4, read by
+                // its MMAs
                 if (i >= kRawStages && !mbar_wait(&bar->op_full[(i - kRawStages) % kSlots],
                                                   (uint32_t)((i - kRawStages) / kSlots) & 1u, abort_flag))
                     break;
-                mbar_expect_tx(&bar->in_full[i % kSlots], kRawBytes);
-                tma_load_2d(smem + kSmemRaw + (size_t)s * kRawBytes, &wmap, &bar->in_full[i % kSlots], (g0 + i) * 64,
-                            row0);
-                ++issued;
-            }
-            // drain: every issued copy has landed before the CTA may exit (after an abort a
-            // phase may lack the other producer's arrival: the bounded drain then just waits
-            // out its limit, far longer than any copy takes)
-            for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
-                mbar_drain(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        // ---- activations: TMA (SWIZZLE_128B) into the X ring ----
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
-            int issued = 0;
-            for (int i = 0; i < ng; ++i) {
-                const int s = i % kXStages;
-                // X stage s is free once the MMAs of group i - kXStages have completed
                 if (i >= kXStages && !mbar_wait(&bar->mma_done[(i - kXStages) % kSlots],
                                                 (uint32_t)((i - kXStages) / kSlots) & 1u, abort_flag))
                     break;
                 uint64_t *full = &bar->in_full[i % kSlots];
-                mbar_expect_tx(full, (uint32_t)x_bytes);
-                uint8_t *dst = smem + kSmemX + (size_t)s * kXBytes;
+                mbar_expect_tx(full, (uint32_t)(kRawBytes + x_bytes));
+                tma_load_2d(smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes, &wmap, full, (g0 + i) * 64, row0);
+                uint8_t *dst = smem + kSmemX + (size_t)(i % kXStages) * kXBytes;
                 tma_load_2d(dst, &xmap, full, (g0 + i) * 128, m0);
                 tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, full, (g0 + i) * 128 + 64, m0);
                 ++issued;
             }
-            for (int i = issued > kXStages ? issued - kXStages : 0; i < issued; ++i)
+            // drain: every issued copy has landed before the CTA may exit
+            for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
                 mbar_drain(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
+            for (int c = s_issued > 2 ? s_issued - 2 : 0; c < s_issued; ++c)
+                mbar_drain(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u);
         }
         __syncwarp();
-    } else if (warp == 2) {
+    } else if (warp == 1) {
         // ---- MMA issuer ----
         if (lane == 0) {
             for (int i = 0; i < ng; ++i) {
                 const int q = i % kSlots, sa = i % kAStages, sx = i % kXStages, b = i % kTBufs;
-                if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag, false)) break;
+                if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * 64);
                 const uint32_t x_base = smem_u32(smem + kSmemX + (size_t)sx * kXBytes);
@@ -360,58 +363,28 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             mbar_drain(&bar->drain, 0);
         }
         __syncwarp();
-    } else if (warp == 3) {
-        // ---- group scales: TMA, [128 rows x 16 groups] tiles into a two-slot ring.  A slot
-        // is refilled once every compute warp has finished the tile's last group. ----
-        if (lane == 0 && nchunks > 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
-            int issued = 0;
-            for (int c = 0; c < nchunks; ++c) {
-                const int slot = c & 1;
-                if (c >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((c - 2) >> 1) & 1u, abort_flag)) break;
-                mbar_expect_tx(&bar->s_full[slot], kScaleBytes);
-                tma_load_2d(smem + kSmemScale + (size_t)slot * kScaleBytes, &smap, &bar->s_full[slot],
-                            g0 + kScaleChunk * c, row0);
-                ++issued;
-            }
-            for (int c = issued > 2 ? issued - 2 : 0; c < issued; ++c)
-                mbar_drain(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u);
-        }
-        __syncwarp();
-    } else {
-        // ---- compute warps ----
+    } else if (warp < 2 + kDqWarps) {
+        // ---- dequant: rows 32 * quad .. + 31 of every group into A stage i % 4 ----
         const int quad = warp & 3;
-        const int part = (warp - 4) >> 2;  // k quarter of the dequant, activation-row chunk of the fold
         const int rloc = 32 * quad + lane;  // this thread's weight row in the tile = TMEM lane
-        const int row = row0 + rloc;
-        const bool row_ok = row < p.N;
         const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
-        const float *srow = p.S + (size_t)(row_ok ? row : 0) * p.G + g0;
-        const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.f, 0.f);
-        // per-row scales (no group scales) or the fallback path: one group ahead by __ldg
-        float sc_next = (p.grouped && !p.scale_tma) ? __ldg(srow) : 1.0f;
-        float4 sc4 = make_float4(1.f, 1.f, 1.f, 1.f);  // four groups' scales of this row
-
-        for (int i = 0; i < ng + 2; ++i) {
-            const int j = i - 2;  // the group folded in this step
-            const int c = j / kScaleChunk, ci = j % kScaleChunk;
-            // the MMAs of group j have completed: their partial is ready and A stage i % 2 is free
-            if (i >= 2 && !mbar_wait_warp(&bar->mma_done[j % kSlots], (uint32_t)(j / kSlots) & 1u, abort_flag)) break;
+        const int sw = (rloc >> 1) & 3;
+        for (int i = 0; i < ng; ++i) {
+            const int sa = i % kAStages;
+            // A stage sa held group i - 4: its MMAs have completed
+            if (i >= kAStages && !mbar_wait_warp(&bar->mma_done[(i - kAStages) % kSlots],
+                                                 (uint32_t)((i - kAStages) / kSlots) & 1u, abort_flag))
+                break;
+            if (!mbar_wait_warp(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
             tc_fence_after();
-            // -- dequantize this warp's quarter of group i into A stage i % 2, then release the
-            // group to the MMA issuer before folding: the fold is off the MMA's critical path --
-            if (i < ng) {
-                const int s = i % kRawStages, sa = i % kAStages;
-                if (!mbar_wait_warp(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
-                // raw tile written with SWIZZLE_64B: 16-byte chunk c of row r sits at chunk
-                // c ^ ((r >> 1) & 3), so 8 consecutive rows hit 8 distinct bank groups
-                const uint8_t *rowp = smem + kSmemRaw + (size_t)s * kRawBytes + rloc * 64;
-                const int sw = (rloc >> 1) & 3;
-                const uint4 v0 = *reinterpret_cast<const uint4 *>(rowp + ((part ^ sw) << 4));
+            // raw tile written with SWIZZLE_64B: 16-byte chunk c of row r sits at chunk
+            // c ^ ((r >> 1) & 3), so 8 consecutive rows hit 8 distinct bank groups
+            const uint8_t *rowp = smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes + rloc * 64;
+#pragma unroll 2
+            for (int c = 0; c < 4; ++c) {  // 16 bytes = 32 k values -> 16 columns
+                const uint4 v = *reinterpret_cast<const uint4 *>(rowp + ((c ^ sw) << 4));
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
                 uint32_t cols[16];
-                const uint32_t words[4] = {v0.x, v0.y, v0.z, v0.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {  // 8 k values per word -> 4 columns
                     const uint4 o = dq_word(words[q]);
@@ -420,45 +393,70 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     cols[4 * q + 2] = o.z;
                     cols[4 * q + 3] = o.w;
                 }
-                tmem_st16(tmem + lane_addr + (uint32_t)(kAColBase + sa * 64 + 16 * part), cols);
-                tmem_st_wait();
-                // partial buffer i % 3 is free: group i - 3 was folded last step
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar->op_full[i % kSlots]);
+                tmem_st16(tmem + lane_addr + (uint32_t)(kAColBase + sa * 64 + 16 * c), cols);
             }
-            // -- fold group j into the accumulators --
-            if (i >= 2) {
-                float sc = sc_next;
-                if (p.scale_tma) {
-                    if (ci == 0 && !mbar_wait_warp(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u, abort_flag)) break;
-                    if ((ci & 3) == 0)
-                        sc4 = *reinterpret_cast<const float4 *>(
-                            &sring[(size_t)(c & 1) * (kTileRows * kScaleChunk) + rloc * kScaleChunk + ci]);
-                    const int k4 = ci & 3;
-                    sc = k4 == 0 ? sc4.x : k4 == 1 ? sc4.y : k4 == 2 ? sc4.z : sc4.w;
-                } else if (p.grouped && j + 1 < ng) {
-                    sc_next = __ldg(srow + j + 1);
-                }
-                const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (j % kTBufs) * kMaxNm);
-                const float2 sc2 = make_float2(sc, sc);
-                if (part * 32 < p.Nm) {
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar->op_full[i % kSlots]);
+        }
+    } else {
+        // ---- fold: activation-column quarter fq of lane quadrant quad, every group in order ----
+        const int quad = warp & 3;
+        const int fq = (warp - 2 - kDqWarps) >> 2;
+        const int rloc = 32 * quad + lane;
+        const int row = row0 + rloc;
+        const bool row_ok = row < p.N;
+        const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
+        const int nc = p.Nm / 16;            // 16-column chunks of the partial (<= 8)
+        const int per = (nc + 3) / 4;        // chunks per quarter (<= 2)
+        const int c_lo = fq * per, c_hi = min(nc, c_lo + per);
+        const float *srow = p.S + (size_t)(row_ok ? row : 0) * p.G + g0;
+        const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
+        float2 acc[16];  // two 16-column chunks as fp32 pairs: one packed multiply and add per pair
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        uint32_t r[16];
-                        tmem_ld16(taddr + part * 32 + u * 16, r);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
-                            const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-                            acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
-                        }
-                    }
-                }
-                tc_fence_before();  // the loads are complete before the buffer is handed back
-                if (p.scale_tma && (ci == kScaleChunk - 1 || j == ng - 1)) {
+        for (int e = 0; e < 16; ++e) acc[e] = make_float2(0.f, 0.f);
+        // partial buffers 0 and 1 start free
+        __syncwarp();
+        if (lane == 0)
+            for (int i = 0; i < kTBufs && i < ng; ++i) mbar_arrive(&bar->op_full[i]);
+        float sc_next = (p.grouped && !p.scale_tma) ? __ldg(srow) : 1.0f;
+        for (int j = 0; j < ng; ++j) {
+            const int c = j / kScaleChunk, ci = j % kScaleChunk;
+            // group j's scale first: the tile arrives long before the MMAs complete
+            float sc = sc_next;
+            if (p.scale_tma) {
+                if (ci == 0 && !mbar_wait_warp(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u, abort_flag)) break;
+                sc = sring[(size_t)(c & 1) * (kTileRows * kScaleChunk) + rloc * kScaleChunk + ci];
+                if (ci == kScaleChunk - 1 || j == ng - 1) {
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&bar->s_empty[c & 1]);  // done with scale tile c
+                }
+            } else if (p.grouped && j + 1 < ng) {
+                sc_next = __ldg(srow + j + 1);
+            }
+            const float2 sc2 = make_float2(sc, sc);
+            if (!mbar_wait_warp(&bar->mma_done[j % kSlots], (uint32_t)(j / kSlots) & 1u, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (j % kTBufs) * kMaxNm);
+            // one 16-column chunk at a time (register budget); the buffer goes back to the
+            // issuer for group j + 2 as soon as the last chunk is in registers
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                uint32_t r[16];
+                const bool have = c_lo + u < c_hi;
+                if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
+                tmem_ld_wait();
+                if (u == 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0 && j + kTBufs < ng) mbar_arrive(&bar->op_full[(j + kTBufs) % kSlots]);
+                }
+                if (!have) continue;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
+                    const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                    acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
                 }
             }
         }
@@ -467,15 +465,19 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             const float sr = p.grouped ? 1.0f : __ldg(p.S + row);
             const int mlim = min(p.Nm, p.M - m0);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int ml = part * 32 + j;  // activation row in the tile
-                const float a = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
-                if (ml < mlim) {
-                    const int m = m0 + ml;
-                    if (p.splits == 1)
-                        p.Y[(size_t)m * p.N + row] = f2bf(a * sr);
-                    else
-                        p.ws[((size_t)split * p.M + m) * p.N + row] = a;
+            for (int u = 0; u < 2; ++u) {
+                if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    const int ml = 16 * (c_lo + u) + t;  // activation row in the tile
+                    const float a = (t & 1) ? acc[u * 8 + (t >> 1)].y : acc[u * 8 + (t >> 1)].x;
+                    if (ml < mlim) {
+                        const int m = m0 + ml;
+                        if (p.splits == 1)
+                            p.Y[(size_t)m * p.N + row] = f2bf(a * sr);
+                        else
+                            p.ws[((size_t)split * p.M + m) * p.N + row] = a;
+                    }
                 }
             }
         }
@@ -487,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     if (*abort_flag) {
         if (threadIdx.x == 0) atomicExch(p.err, 1);
     }
-    if (warp == 2) {
+    if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
