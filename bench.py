@@ -513,7 +513,8 @@ def _graph_ms(body, calls: int, iters: int = 5) -> float:
 
 
 def run_sweep(args) -> None:
-    """One JSON line per case.  Linears: W4A16 g128 and W8A32 at every M of SWEEP_M on the
+    """One JSON line per case.  Linears: W4A16 g128 (reference packing, and the k-pair
+    layout the model keeps its weights in) and W8A32 at every M of SWEEP_M on the
     Qwen3-8B projection shapes (K, N); enough weight copies are cycled that each call reads
     its weights from HBM (copies x bytes > 2 x L2).  Paged attention: q_len 2-5 at 1K, 8K
     and 32K keys, 32 Q / 8 KV heads, batch sized to about 1 GB of K/V per call.  Accept:
@@ -536,8 +537,8 @@ def run_sweep(args) -> None:
     only = set(args.sweep.split(",")) if args.sweep != "all" else {"linear", "attention", "accept"}
     if "linear" in only:
         for K, N in SWEEP_KN:
-            for fmt in ("w4a16g128", "w8a32"):
-                if fmt == "w4a16g128":
+            for fmt in ("w4a16g128", "w4a16g128_kpairs", "w8a32"):
+                if fmt.startswith("w4a16g128"):
                     wbytes = N * K // 2 + 4 * N * (K // 128)
                     mk = lambda: (torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g),
                                   torch.rand((N, K // 128), device=dev, generator=g) * 0.01 + 1e-4)
@@ -547,13 +548,15 @@ def run_sweep(args) -> None:
                                   torch.rand((N,), device=dev, generator=g) * 0.01 + 1e-4)
                 copies = max(1, -(-2 * L2_BYTES // wbytes))
                 ws = [mk() for _ in range(copies)]
+                kp = fmt.endswith("_kpairs")  # the model's load-time layout (a nibble permutation)
                 calls = max(copies, 8)
                 for M in SWEEP_M:
-                    if fmt == "w4a16g128":
+                    if fmt.startswith("w4a16g128"):
                         x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
                         y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
                         io = 2 * M * K + 2 * M * N
-                        fn = lambda i: ck.linear_w4a16g128_bf16(x, ws[i % copies][0], ws[i % copies][1], out=y)
+                        fn = lambda i: ck.linear_w4a16g128_bf16(x, ws[i % copies][0], ws[i % copies][1], out=y,
+                                                                kpairs=kp)
                     else:
                         x = torch.randn((M, K), device=dev, generator=g)
                         y = torch.empty((M, N), dtype=torch.float32, device=dev)

@@ -169,10 +169,24 @@ int ekernel_linear_w4a16g32_bf16(const ekernel_linear_w8a32_desc_t *desc, const 
                                  const float *scales, uint16_t *C, ekernel_isa_t isa);
 
 /* kernel/api.h:121-126 (kernels.c:1150-1157): group-128 scales[N, ceil(K/128)];
- * C = rne(sum_g s[n,g] * dot_g).  M < 64 runs the register-dequant tensor-core GEMV;
- * larger M runs the tiled GEMM. */
+ * C = rne(sum_g s[n,g] * dot_g).  M <= 16 runs the register-dequant tensor-core GEMV;
+ * larger M runs the tcgen05 GEMM. */
 int ekernel_linear_w4a16g128_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
                                   const float *scales, uint16_t *C, ekernel_isa_t isa);
+
+/* Load-time repack of reference-packed int4 weights (uint8 [N, K/2], even k in the low
+ * nibble; ckernel.py:70-161) into the k-pair nibble order: within every 32-bit word
+ * (k = 8i .. 8i+7 of a row) nibble p holds k = 8i + 2p for p < 4 and 8i + 2(p-4) + 1 for
+ * p >= 4.  The kernels then dequantize a word into consecutive-k bf16 pairs without byte
+ * permutes.  K % 8 == 0; buffers 4-byte aligned; out may equal qweight. */
+int ekernel_repack_w4_kpairs(const uint8_t *qweight, size_t N, size_t K, uint8_t *out);
+
+/* ekernel_linear_w4a16g128_bf16 and ekernel_linear_w4a16_bf16 on k-pair repacked weights
+ * (same scales, same results); K % 128 == 0 and 16-byte aligned A and W. */
+int ekernel_linear_w4a16g128_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                         const uint8_t *W, const float *scales, uint16_t *C, ekernel_isa_t isa);
+int ekernel_linear_w4a16_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                                     const float *scales, uint16_t *C, ekernel_isa_t isa);
 
 /* kernel/api.h:180-186 (kernels.c:1485-1526): rne(x * rsqrt(mean(x^2)+eps) * (w [+1])). */
 int ekernel_rmsnorm_bf16(const uint16_t *x, uint16_t *out, const uint16_t *weight, size_t rows, size_t n,

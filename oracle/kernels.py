@@ -130,6 +130,24 @@ def unpack_i4(qw: np.ndarray, K: int) -> np.ndarray:
 # Kernel restatements (bit-identical to the reference library; see oracle_kernels.c)
 # ---------------------------------------------------------------------------------
 
+KPAIRS_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)  # nibble position p of a word holds k = 8i + KPAIRS_ORDER[p]
+
+
+def repack_w4_kpairs(qw: np.ndarray) -> np.ndarray:
+    """Checker for the GPU library's own load-time layout (ekernel_repack_w4_kpairs), not a
+    reference format: reference-packed int4 rows (nibble j of a row = k j, even k in the low
+    nibble) rewritten so that within every 32-bit word (k = 8i .. 8i+7) nibble position p
+    holds k = 8i + 2p for p < 4 and 8i + 2(p - 4) + 1 for p >= 4."""
+    n, kb = qw.shape
+    if kb % 4:
+        raise ValueError("rows must hold whole 32-bit words (K % 8 == 0)")
+    nib = np.empty((n, 2 * kb), np.uint8)
+    nib[:, 0::2] = qw & 15
+    nib[:, 1::2] = qw >> 4
+    out = nib.reshape(n, -1, 8)[:, :, list(KPAIRS_ORDER)].reshape(n, -1)
+    return (out[:, 0::2] | (out[:, 1::2] << 4)).astype(np.uint8)
+
+
 def gemm_f32(a: np.ndarray, b: np.ndarray, transpose_b: bool = False) -> np.ndarray:
     """ekernel_gemm (kernels.c:396-435)."""
     a = np.ascontiguousarray(a, np.float32)

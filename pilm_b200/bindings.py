@@ -50,6 +50,16 @@ KERNEL_SYMBOLS = [
     "ekernel_argmax_top2_bf16",
     "ekernel_verify_accept_greedy",
     "ekernel_verify_accept_rejection",
+    "ekernel_repack_w4_kpairs",
+    "ekernel_linear_w4a16g128_bf16_kpairs",
+    "ekernel_linear_w4a16_bf16_kpairs",
+    "ekernel_mtp_fc_input_bf16",
+    "ekernel_self_attention_bf16",
+    "ekernel_embedding_f32",
+    "ekernel_add_rmsnorm_f32",
+    "ekernel_qk_norm_rope_kv_append_f32",
+    "ekernel_paged_attention_verify_f32",
+    "ekernel_silu_mul_f32",
 ]
 
 
@@ -159,12 +169,15 @@ def _configure(lib) -> None:
     lib.edevice_get.restype = ctypes.POINTER(EdeviceVtable)
     lib.ekernel_gemm.argtypes = [ctypes.POINTER(EkernelGemmDesc), _vp, _vp, _vp, _i32]
     for name in ("ekernel_linear_w8a32", "ekernel_linear_w8a16_bf16", "ekernel_linear_w4a16_bf16",
-                 "ekernel_linear_w4a16g32_bf16", "ekernel_linear_w4a16g128_bf16"):
+                 "ekernel_linear_w4a16g32_bf16", "ekernel_linear_w4a16g128_bf16",
+                 "ekernel_linear_w4a16g128_bf16_kpairs", "ekernel_linear_w4a16_bf16_kpairs"):
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp, _vp, _vp, _i32]
         fn.restype = _i32
     lib.ekernel_linear_w8a16_bf16_argmax.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp, _vp,
                                                      ctypes.POINTER(_sz), ctypes.POINTER(ctypes.c_float), _i32]
+    lib.ekernel_repack_w4_kpairs.argtypes = [_vp, _sz, _sz, _vp]
+    lib.ekernel_repack_w4_kpairs.restype = _i32
     lib.ekernel_swiglu_bf16.argtypes = [_vp, _vp, _vp, _sz]
     lib.ekernel_swiglu_w4a16_bf16.argtypes = [ctypes.POINTER(EkernelW4A16SwiGLUDesc), _vp, _vp, _vp, _vp, _vp, _vp,
                                               _i32]
@@ -321,6 +334,18 @@ def linear_w4a16g32_bf16_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa=None)
 
 def linear_w4a16g128_bf16_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa=None) -> int:
     return _linear("ekernel_linear_w4a16g128_bf16", a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa)
+
+
+def linear_w4a16g128_bf16_kpairs_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa=None) -> int:
+    return _linear("ekernel_linear_w4a16g128_bf16_kpairs", a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa)
+
+
+def linear_w4a16_bf16_kpairs_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa=None) -> int:
+    return _linear("ekernel_linear_w4a16_bf16_kpairs", a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa)
+
+
+def repack_w4_kpairs_ptr(qweight_ptr, n, k, out_ptr) -> int:
+    return int(_load_lib().ekernel_repack_w4_kpairs(qweight_ptr, n, k, out_ptr))
 
 
 def swiglu_bf16_ptr(gate_ptr, up_ptr, out_ptr, n) -> int:

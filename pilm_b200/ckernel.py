@@ -116,13 +116,28 @@ def _w4_common(x, qweight, scales, in_features, scale_ndim, groups_of):
     return x, qweight, scales, m, n, k
 
 
-def linear_w4a16_bf16(x, qweight, scales, in_features=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def linear_w4a16_bf16(x, qweight, scales, in_features=None, out: Optional[torch.Tensor] = None,
+                      kpairs: bool = False) -> torch.Tensor:
+    """kpairs: qweight is in the k-pair nibble order (repack_w4_kpairs)."""
     x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 1, None)
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     _stream()
-    _check(abi.linear_w4a16_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
-           "ekernel_linear_w4a16_bf16")
+    fn = abi.linear_w4a16_bf16_kpairs_ptr if kpairs else abi.linear_w4a16_bf16_ptr
+    _check(fn(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
+           "ekernel_linear_w4a16_bf16" + ("_kpairs" if kpairs else ""))
+    return out
+
+
+def repack_w4_kpairs(qweight: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Reference-packed int4 weights [N, K/2] -> the k-pair nibble order the kernels
+    dequantize without byte permutes (ekernel_repack_w4_kpairs); out may be qweight."""
+    qweight = _cuda("qweight", qweight, torch.uint8, 2)
+    n, kb = qweight.shape
+    if out is None:
+        out = torch.empty_like(qweight)
+    _stream()
+    _check(abi.repack_w4_kpairs_ptr(qweight.data_ptr(), n, 2 * kb, out.data_ptr()), "ekernel_repack_w4_kpairs")
     return out
 
 
@@ -135,13 +150,16 @@ def linear_w4a16g32_bf16(x, qweight, scales, in_features=None) -> torch.Tensor:
     return out
 
 
-def linear_w4a16g128_bf16(x, qweight, scales, in_features=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+def linear_w4a16g128_bf16(x, qweight, scales, in_features=None, out: Optional[torch.Tensor] = None,
+                          kpairs: bool = False) -> torch.Tensor:
+    """kpairs: qweight is in the k-pair nibble order (repack_w4_kpairs)."""
     x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 2, 128)
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
     _stream()
-    _check(abi.linear_w4a16g128_bf16_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n,
-                                         k), "ekernel_linear_w4a16g128_bf16")
+    fn = abi.linear_w4a16g128_bf16_kpairs_ptr if kpairs else abi.linear_w4a16g128_bf16_ptr
+    _check(fn(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
+           "ekernel_linear_w4a16g128_bf16" + ("_kpairs" if kpairs else ""))
     return out
 
 

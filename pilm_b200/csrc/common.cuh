@@ -29,14 +29,15 @@ void *scratch(int slot, size_t bytes);
 inline void *workspace(size_t bytes) { return scratch(kScratchSplitK, bytes); }
 int *counters(size_t n);  // zero-initialised, self-resetting arrival counters
 
-// W4 GEMM for M >= 64 (tcgen05 path, linear_tc.cu); returns ECPU_ERR_UNSUPPORTED
+// W4 GEMM for M > 16 (tcgen05 path, linear_tc.cu); returns ECPU_ERR_UNSUPPORTED
 // when the shape is not handled there, in which case the caller uses the GEMV.
+// kpairs: the packed weights are in the k-pair nibble order (ekernel_repack_w4_kpairs).
 int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N,
-                 __nv_bfloat16 *Y, bool grouped, const char *what);
+                 __nv_bfloat16 *Y, bool grouped, bool kpairs, const char *what);
 // Quantized bf16 linear (linear.cu).  qf: 0 = W4 grouped (gs 32/128), 1 = W4 per-row,
-// 2 = W8 per-row.
+// 2 = W8 per-row.  kpairs (W4 only): weights in the k-pair nibble order.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
-                const char *what);
+                const char *what, bool kpairs = false);
 
 // cuTensorMapEncodeTiled, reached through the runtime's driver entry point (no link
 // against libcuda); null if the driver does not provide it.

@@ -63,7 +63,7 @@ __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
 // the B fragment of the same thread carries A[m, k] for exactly those k (gathered
 // with byte permutes from one 16-byte load), so every MMA slot pairs W[n,k] with
 // A[m,k] for the same k and the 8 steps of a group sum the whole group.
-template <int RT, int NT, bool GROUPED>
+template <int RT, int NT, bool GROUPED, bool KP>
 __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
     const __nv_bfloat16 *__restrict__ X, int M, int K, const uint8_t *__restrict__ W,
     const float *__restrict__ S, int N, __nv_bfloat16 *__restrict__ Y, float *__restrict__ ws,
@@ -143,10 +143,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
                 uint32_t b0[NT], b1[NT];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    uint32_t lo = hh ? xw[nt].y : xw[nt].x;
-                    uint32_t hi = hh ? xw[nt].w : xw[nt].z;
-                    b0[nt] = __byte_perm(lo, hi, 0x5410);
-                    b1[nt] = __byte_perm(lo, hi, 0x7632);
+                    if (KP) {  // nibble pairs (2hh, 2hh+4) and (2hh+1, 2hh+5) are k (4hh, 4hh+1), (4hh+2, 4hh+3)
+                        b0[nt] = hh ? xw[nt].z : xw[nt].x;
+                        b1[nt] = hh ? xw[nt].w : xw[nt].y;
+                    } else {
+                        uint32_t lo = hh ? xw[nt].y : xw[nt].x;
+                        uint32_t hi = hh ? xw[nt].w : xw[nt].z;
+                        b0[nt] = __byte_perm(lo, hi, 0x5410);
+                        b1[nt] = __byte_perm(lo, hi, 0x7632);
+                    }
                 }
 #pragma unroll
                 for (int rt = 0; rt < RT; ++rt) {
@@ -413,7 +418,7 @@ __global__ void argmax_bf16_row(const __nv_bfloat16 *__restrict__ v, int n, int 
     }
 }
 
-template <int RT, int NT, bool GROUPED>
+template <int RT, int NT, bool GROUPED, bool KP>
 int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
                const char *what) {
     const int tiles = (N + 16 * RT - 1) / (16 * RT);
@@ -436,18 +441,34 @@ int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const flo
         PILM_REQUIRE(ws && ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
     dim3 grid(tiles, splits);
-    w4_gemv_mma<RT, NT, GROUPED><<<grid, kGemvWarps * 32, 0, pilm::stream()>>>(X, M, K, W, S, N, Y, ws, ctr, splits,
-                                                                                 gps);
+    w4_gemv_mma<RT, NT, GROUPED, KP><<<grid, kGemvWarps * 32, 0, pilm::stream()>>>(X, M, K, W, S, N, Y, ws, ctr,
+                                                                                     splits, gps);
     return pilm::check_launch(what);
 }
 
-template <bool GROUPED>
+template <bool GROUPED, bool KP>
 int dispatch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
                  const char *what) {
-    if (M <= 8) return launch_mma<2, 1, GROUPED>(X, M, K, W, S, N, Y, what);
-    if (M <= 16) return launch_mma<2, 2, GROUPED>(X, M, K, W, S, N, Y, what);
-    if (M <= 32) return launch_mma<1, 4, GROUPED>(X, M, K, W, S, N, Y, what);
-    return launch_mma<1, 8, GROUPED>(X, M, K, W, S, N, Y, what);
+    if (M <= 8) return launch_mma<2, 1, GROUPED, KP>(X, M, K, W, S, N, Y, what);
+    if (M <= 16) return launch_mma<2, 2, GROUPED, KP>(X, M, K, W, S, N, Y, what);
+    if (M <= 32) return launch_mma<1, 4, GROUPED, KP>(X, M, K, W, S, N, Y, what);
+    return launch_mma<1, 8, GROUPED, KP>(X, M, K, W, S, N, Y, what);
+}
+
+// k-pair nibble order: within every 32-bit word (k = 8i .. 8i + 7 of a row, k at nibble
+// k - 8i in the reference packing), nibble p holds k = 8i + 2p for p < 4 and
+// 8i + 2(p - 4) + 1 for p >= 4.  One thread per word; in place is allowed.
+__global__ void repack_w4_kpairs(const uint32_t *__restrict__ in, uint32_t *out, size_t words) {
+    for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < words; t += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t w = in[t];
+        uint32_t r = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int pos = (j & 1) ? 4 + (j >> 1) : (j >> 1);
+            r |= ((w >> (4 * j)) & 15u) << (4 * pos);
+        }
+        out[t] = r;
+    }
 }
 
 bool aligned16(const void *p) { return (((uintptr_t)p) & 15) == 0; }
@@ -459,16 +480,18 @@ namespace pilm {
 // Shared entry used by the ABI wrappers and by the fused SwiGLU path.
 // qf: 0 = W4 grouped (gs = 32 or 128), 1 = W4 per-row, 2 = W8 per-row.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
-                const char *what) {
+                const char *what, bool kpairs) {
     const __nv_bfloat16 *X = (const __nv_bfloat16 *)A;
     __nv_bfloat16 *Y = (__nv_bfloat16 *)C;
     if (M == 0 || N == 0) return ECPU_OK;
     const bool mma_ok = (qf == 1 || (qf == 0 && gs == 128)) && (K % 128 == 0) && aligned16(A) && aligned16(W);
+    PILM_REQUIRE(!kpairs || mma_ok, ECPU_ERR_UNSUPPORTED,
+                 "%s: k-pair weights need K %% 128 == 0 and 16-byte aligned activations and weights", what);
     if (mma_ok) {
         // above 16 rows the register-dequant GEMV re-reads each activation tile per 16
         // weight rows; the tensor-core GEMM stages it once per 128 (N = 32, 48, ... rows)
         if (M > 16) {
-            int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, what);
+            int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, kpairs, what);
             if (rc != ECPU_ERR_UNSUPPORTED) return rc;
         }
         // register-dequant GEMV, in slabs of at most 64 activation rows
@@ -476,8 +499,11 @@ int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, cons
             const int mm = M - m0 < 64 ? M - m0 : 64;
             const __nv_bfloat16 *Xs = X + (size_t)m0 * K;
             __nv_bfloat16 *Ys = Y + (size_t)m0 * N;
-            int rc = qf == 0 ? dispatch_mma<true>(Xs, mm, K, (const uint8_t *)W, S, N, Ys, what)
-                             : dispatch_mma<false>(Xs, mm, K, (const uint8_t *)W, S, N, Ys, what);
+            const uint8_t *Wq = (const uint8_t *)W;
+            int rc = qf == 0 ? (kpairs ? dispatch_mma<true, true>(Xs, mm, K, Wq, S, N, Ys, what)
+                                       : dispatch_mma<true, false>(Xs, mm, K, Wq, S, N, Ys, what))
+                             : (kpairs ? dispatch_mma<false, true>(Xs, mm, K, Wq, S, N, Ys, what)
+                                       : dispatch_mma<false, false>(Xs, mm, K, Wq, S, N, Ys, what));
             if (rc != ECPU_OK) return rc;
         }
         return ECPU_OK;
@@ -590,6 +616,35 @@ int ekernel_linear_w4a16g128_bf16(const ekernel_linear_w8a32_desc_t *desc, const
     LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16");
     return pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
                              "ekernel_linear_w4a16g128_bf16");
+}
+
+int ekernel_repack_w4_kpairs(const uint8_t *qweight, size_t N, size_t K, uint8_t *out) {
+    PILM_REQUIRE(qweight && out, ECPU_ERR_PARAM, "ekernel_repack_w4_kpairs: null argument");
+    PILM_REQUIRE(K % 8 == 0, ECPU_ERR_PARAM, "ekernel_repack_w4_kpairs: K must be a multiple of 8");
+    PILM_REQUIRE((((uintptr_t)qweight) & 3) == 0 && (((uintptr_t)out) & 3) == 0, ECPU_ERR_PARAM,
+                 "ekernel_repack_w4_kpairs: buffers must be 4-byte aligned");
+    const size_t words = N * (K / 8);
+    if (words == 0) return ECPU_OK;
+    const size_t blocks = (words + 255) / 256;
+    repack_w4_kpairs<<<(unsigned)(blocks < 8192 ? blocks : 8192), 256, 0, pilm::stream()>>>(
+        (const uint32_t *)qweight, (uint32_t *)out, words);
+    return pilm::check_launch("ekernel_repack_w4_kpairs");
+}
+
+int ekernel_linear_w4a16g128_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                         const uint8_t *W, const float *scales, uint16_t *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16_kpairs");
+    return pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                             "ekernel_linear_w4a16g128_bf16_kpairs", true);
+}
+
+int ekernel_linear_w4a16_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
+                                     const float *scales, uint16_t *C, ekernel_isa_t isa) {
+    (void)isa;
+    LINEAR_ARGS_OK("ekernel_linear_w4a16_bf16_kpairs");
+    return pilm::linear_bf16(1, 0, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                             "ekernel_linear_w4a16_bf16_kpairs", true);
 }
 
 }  // extern "C"

@@ -244,6 +244,18 @@ __device__ __forceinline__ uint4 dq_word(uint32_t w) {
     return o;
 }
 
+// The same 8 values from a word in the k-pair nibble order (nibble p holds k = 2p for
+// p < 4 and 2(p - 4) + 1 above): each nibble pair (p, p + 4) is already (k_2j, k_2j+1),
+// so no byte permute is needed.
+__device__ __forceinline__ uint4 dq_word_kpairs(uint32_t w) {
+    uint4 o;
+    o.x = dq_pair(w);        // k0,k1
+    o.y = dq_pair(w >> 4);   // k2,k3
+    o.z = dq_pair(w >> 8);   // k4,k5
+    o.w = dq_pair(w >> 12);  // k6,k7
+    return o;
+}
+
 struct TcParams {
     const float *S;     // scales [N, G]
     __nv_bfloat16 *Y;   // [M, N]
@@ -257,6 +269,7 @@ struct TcParams {
     int scale_tma;      // group scales arrive by TMA (G % 4 == 0, group offsets 16-byte aligned)
 };
 
+template <bool KP>
 __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant__ CUtensorMap wmap,
                                                          const __grid_constant__ CUtensorMap xmap,
                                                          const __grid_constant__ CUtensorMap smap,
@@ -387,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 uint32_t cols[16];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {  // 8 k values per word -> 4 columns
-                    const uint4 o = dq_word(words[q]);
+                    const uint4 o = KP ? dq_word_kpairs(words[q]) : dq_word(words[q]);
                     cols[4 * q + 0] = o.x;
                     cols[4 * q + 1] = o.y;
                     cols[4 * q + 2] = o.z;
@@ -535,7 +548,7 @@ __global__ void __launch_bounds__(256) splitk_combine(const float *__restrict__ 
 namespace pilm {
 
 int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
-                 bool grouped, const char *what) {
+                 bool grouped, bool kpairs, const char *what) {
     static const bool disabled = getenv("PILM_DISABLE_TC") && getenv("PILM_DISABLE_TC")[0] == '1';
     if (disabled || M <= 16 || (K % 128) != 0 || N < 1) return ECPU_ERR_UNSUPPORTED;
     if ((((uintptr_t)X) & 15) || (((uintptr_t)W) & 15)) return ECPU_ERR_UNSUPPORTED;
@@ -636,11 +649,15 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     }
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(w4_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
         attr_set = true;
     }
     dim3 grid(tiles_n, tiles_m, splits);
-    w4_gemm_tc<<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
+    if (kpairs)
+        w4_gemm_tc<true><<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
+    else
+        w4_gemm_tc<false><<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     if (splits > 1) {

@@ -34,11 +34,14 @@ NORMS = ("pre_fc_norm_embedding", "pre_fc_norm_hidden", "input_norm", "post_norm
 
 
 class W4RowLinear:
-    """Device-resident W4A16 linear with per-row scales (qweight uint8 [N, ceil(K/2)],
-    scales fp32 [N])."""
+    """Device-resident W4A16 linear with per-row scales (scales fp32 [N]); the packed
+    weights (uint8 [N, ceil(K/2)]) are held in the k-pair nibble order
+    (ekernel_repack_w4_kpairs).  Rows are independent: repacked rows concatenate and
+    select like reference-packed ones."""
 
-    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, in_features: int):
-        self.qweight = qweight.contiguous()
+    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, in_features: int, kpairs: bool = False):
+        qweight = qweight.contiguous()
+        self.qweight = qweight if kpairs else ck.repack_w4_kpairs(qweight)
         self.scales = scales.contiguous()
         self.in_features = int(in_features)
         self.out_features = int(qweight.shape[0])
@@ -50,18 +53,20 @@ class W4RowLinear:
 
     @classmethod
     def cat(cls, parts: list["W4RowLinear"]) -> "W4RowLinear":
-        return cls(torch.cat([p.qweight for p in parts]), torch.cat([p.scales for p in parts]), parts[0].in_features)
+        return cls(torch.cat([p.qweight for p in parts]), torch.cat([p.scales for p in parts]), parts[0].in_features,
+                   kpairs=True)
 
     def rows(self, index: torch.Tensor) -> "W4RowLinear":
         """The linear restricted to some output rows (rows are independent)."""
-        return W4RowLinear(self.qweight.index_select(0, index), self.scales.index_select(0, index), self.in_features)
+        return W4RowLinear(self.qweight.index_select(0, index), self.scales.index_select(0, index), self.in_features,
+                           kpairs=True)
 
     @property
     def nbytes(self) -> int:
         return self.qweight.numel() + self.scales.numel() * 4
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        return ck.linear_w4a16_bf16(x, self.qweight, self.scales, out=out)
+        return ck.linear_w4a16_bf16(x, self.qweight, self.scales, out=out, kpairs=True)
 
 
 class MTPWeights:

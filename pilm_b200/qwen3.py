@@ -69,18 +69,22 @@ QWEN3_0_6B = Qwen3Shape(hidden=1024, layers=28, n_heads=16, n_kv_heads=8, head_d
 
 
 class W4Linear:
-    """Device-resident W4A16 group-128 linear in the reference packing
-    (qweight uint8 [N, ceil(K/2)], scales fp32 [N, ceil(K/128)])."""
+    """Device-resident W4A16 group-128 linear: the reference's scales (fp32 [N, ceil(K/128)])
+    and packed weights (uint8 [N, ceil(K/2)]), the latter held in the k-pair nibble order
+    (ekernel_repack_w4_kpairs) that the kernels dequantize without byte permutes.  Rows are
+    independent, so repacked linears concatenate like reference-packed ones."""
 
-    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, in_features: int):
-        self.qweight = qweight.contiguous()
+    def __init__(self, qweight: torch.Tensor, scales: torch.Tensor, in_features: int, kpairs: bool = False):
+        qweight = qweight.contiguous()
+        self.qweight = qweight if kpairs else ck.repack_w4_kpairs(qweight)
         self.scales = scales.contiguous()
         self.in_features = int(in_features)
         self.out_features = int(qweight.shape[0])
 
     @classmethod
     def cat(cls, parts: list["W4Linear"]) -> "W4Linear":
-        return cls(torch.cat([p.qweight for p in parts]), torch.cat([p.scales for p in parts]), parts[0].in_features)
+        return cls(torch.cat([p.qweight for p in parts]), torch.cat([p.scales for p in parts]), parts[0].in_features,
+                   kpairs=True)
 
     @property
     def nbytes(self) -> int:
@@ -91,10 +95,10 @@ class W4Linear:
         if out is None:
             out = torch.empty((m, self.out_features), dtype=torch.bfloat16, device=x.device)
         ck._stream()  # launch on the caller's current stream (graph capture included)
-        rc = abi.linear_w4a16g128_bf16_ptr(x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(),
-                                           out.data_ptr(), m, self.out_features, self.in_features)
+        rc = abi.linear_w4a16g128_bf16_kpairs_ptr(x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(),
+                                                  out.data_ptr(), m, self.out_features, self.in_features)
         if rc != 0:
-            raise RuntimeError(f"ekernel_linear_w4a16g128_bf16 failed: rc={rc}: {abi.last_error()}")
+            raise RuntimeError(f"ekernel_linear_w4a16g128_bf16_kpairs failed: rc={rc}: {abi.last_error()}")
         return out
 
 

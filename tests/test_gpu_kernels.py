@@ -88,6 +88,41 @@ def test_large_m_qwen3_8b_shapes(M):
             assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
 
 
+def test_kpairs_repack_and_linears():
+    """The k-pair repack is the oracle's nibble permutation bit for bit (in place too), and
+    both W4 linears on repacked weights match the oracle on the reference packing: the
+    GEMV tiles (M <= 8, 16) and the tensor-core path, with and without split-K."""
+    rng = np.random.default_rng(11)
+    for (N, K) in [(384, 1024), (200, 4096)]:
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        qw, s = ok.quantize_i4_grouped(w, 128)
+        qr, sr = ok.quantize_i4_per_row(w)
+        want = ok.repack_w4_kpairs(qw)
+        qd = _t(qw)
+        got = ck.repack_w4_kpairs(qd)
+        assert np.array_equal(got.cpu().numpy(), want)
+        inplace = qd.clone()
+        ck.repack_w4_kpairs(inplace, out=inplace)
+        assert np.array_equal(inplace.cpu().numpy(), want)
+        qrd = ck.repack_w4_kpairs(_t(qr))
+        for M in (1, 5, 16, 24, 96, 200):
+            x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+            xd = bf16_from_bits(x)
+            y = ck.linear_w4a16g128_bf16(xd, got, _t(s), kpairs=True)
+            assert_bf16_close(bits_of(y), ok.linear_w4a16g_bf16(x, qw, s, 128), ulp_frac=0.99)
+            y = ck.linear_w4a16_bf16(xd, qrd, _t(sr), kpairs=True)
+            assert_bf16_close(bits_of(y), ok.linear_w4a16_bf16(x, qr, sr), ulp_frac=0.99)
+
+
+def test_kpairs_refuses_ragged_k():
+    rng = np.random.default_rng(12)
+    w = (rng.standard_normal((16, 200)) * 0.02).astype(np.float32)
+    qw, s = ok.quantize_i4_grouped(w, 128)
+    x = bf16_from_bits(ok.f32_to_bf16(rng.standard_normal((3, 200)).astype(np.float32)))
+    with pytest.raises(RuntimeError, match="kpairs"):
+        ck.linear_w4a16g128_bf16(x, ck.repack_w4_kpairs(_t(qw)), _t(s), kpairs=True)
+
+
 def test_ragged_k_falls_back_and_matches():
     rng = np.random.default_rng(3)
     for (M, N, K) in [(3, 17, 130), (1, 5, 77), (6, 33, 200)]:

@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import kernels as ok
 from oracle import model as om
 from pilm_b200 import bindings as abi
 from pilm_b200 import ckernel as ck
@@ -41,7 +42,8 @@ def build(variant):
 def test_device_quantizer_matches_reference_format():
     z, cfg, ckpt, w = build("qwen3_w4g128")
     ref = om.quantize_linear(ckpt["l0.down"], "w4g128")
-    assert np.array_equal(w.layers[0]["down"].qweight.cpu().numpy(), ref["qweight"])
+    # the model keeps its weights in the k-pair nibble order (a pure permutation of nibbles)
+    assert np.array_equal(w.layers[0]["down"].qweight.cpu().numpy(), ok.repack_w4_kpairs(ref["qweight"]))
     assert np.array_equal(w.layers[0]["down"].scales.cpu().numpy(), ref["scales"])
 
 

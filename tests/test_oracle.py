@@ -159,3 +159,21 @@ def test_rejection_sampling_restatement_properties():
     assert acc == 1
     acc, nxt = om.rejection_accept(logits, [d], [float(p[d]) + 1e-6], [0.5, 0.5], 0.8, 0.95)
     assert acc == 0 and nxt != d
+
+
+def test_kpairs_repack_is_a_nibble_permutation():
+    """The checker for the GPU library's k-pair layout only moves nibbles within 32-bit
+    words: unpacking it and undoing the permutation gives the reference packing back."""
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((7, 256)) * 0.02).astype(np.float32)
+    qw, _ = ok.quantize_i4_grouped(w, 128)
+    kp = ok.repack_w4_kpairs(qw)
+    nib = np.empty((7, 256), np.uint8)
+    nib[:, 0::2] = kp & 15
+    nib[:, 1::2] = kp >> 4
+    words = nib.reshape(7, -1, 8)
+    back = np.empty_like(words)
+    back[:, :, list(ok.KPAIRS_ORDER)] = words
+    back = back.reshape(7, -1)
+    assert np.array_equal((back[:, 0::2] | (back[:, 1::2] << 4)).astype(np.uint8), qw)
+    assert not np.array_equal(kp, qw)
