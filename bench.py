@@ -234,22 +234,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     e2e_ms_max = float(e2e_t[0].item())
     maxp = max(len(s.pages) for s in eng.sched.running)
 
-    # ---- the speculative cycle: verify + k MTP draft steps on the GPU (cycle) --------
-    # The engine drafts each sequence's next tokens with the GPU drafter inside the same
-    # captured step; verify_step() then verifies them.  Synthetic weights: the random
-    # drafter rarely agrees with the random model, so accepted tok/s sits near the
-    # 1-token-per-step floor; the timing is what a real checkpoint's cycle costs.
-    cycle = None
-    if e2e_steps and not args.no_draft:
+    def run_cycle(linears: str) -> dict:
         from pilm_b200.mtp import MTPDrafter, MTPWeights
-        mw = MTPWeights.synthetic(shape, seed + 17, dev)
+        mw = MTPWeights.synthetic(shape, seed + 17, dev, linears=linears)
         eng.drafter, eng.draft_k, eng.graphs, eng.pending = MTPDrafter(mw, weights, SEQS, dev), K_DRAFT, {}, {}
         for _ in range(max(args.warmup, PAGE)):
             eng.verify_step()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        c_rows = c_tokens = c_att = c_acc = 0
+        c_tokens = c_att = c_acc = 0
+        c_rows = 0
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record(stream)
         for _ in range(e2e_steps):
@@ -266,16 +261,29 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             dist.all_reduce(c_t[:1], op=dist.ReduceOp.MAX)
             dist.all_reduce(c_t[1:], op=dist.ReduceOp.SUM)
         c_ms = float(c_t[0].item())
-        cycle = {
+        eng.graphs = {}
+        return {
             "verified_tok_s": round(float(c_t[1].item()) / e2e_steps / (c_ms * 1e-3), 2),
             "accepted_tok_s": round(float(c_t[2].item()) / e2e_steps / (c_ms * 1e-3), 2),
             "ms_per_cycle": round(c_ms, 4),
             "draft_k": K_DRAFT,
+            "draft_linears": linears,
             "draft_linear_bytes": mw.linear_bytes,
             "accept_rate": round(c_acc / max(1, c_att), 4),
             "call": "pilm_b200.engine.MTPVerifyEngine.verify_step() with the GPU MTP drafter "
                     "(verify + k draft steps in one captured step; host accept results and drafts out)",
         }
+
+    # ---- the speculative cycle: verify + k MTP draft steps on the GPU (cycle) --------
+    # The engine drafts each sequence's next tokens with the GPU drafter inside the same
+    # captured step; verify_step() then verifies them.  Synthetic weights: the random
+    # drafter rarely agrees with the random model, so accepted tok/s sits near the
+    # 1-token-per-step floor; the timing is what a real checkpoint's cycle costs.  Both
+    # draft-module options: the W4A16 one (cycle) and the reference's default bf16 one.
+    cycle = cycle_bf16 = None
+    if e2e_steps and not args.no_draft:
+        cycle = run_cycle("w4a16")
+        cycle_bf16 = run_cycle("bf16")
     clocks = sampler.stop()
     h2d = 4 * (3 * rows_per_step + SEQS * maxp + 2 * SEQS + 1) + 0
     d2h = 4 * 2 * SEQS
@@ -333,6 +341,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "call": "pilm_b200.engine.MTPVerifyEngine.verify_step (host drafts -> host accept results)",
         },
         "cycle": cycle,
+        "cycle_bf16_drafter": cycle_bf16,
         "roofline": {
             "kernel": "attn_pages (+ attn_merge_pages), per layer",
             "bound": "hbm",

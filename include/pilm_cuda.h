@@ -174,6 +174,11 @@ int ekernel_linear_w4a16g32_bf16(const ekernel_linear_w8a32_desc_t *desc, const 
 int ekernel_linear_w4a16g128_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
                                   const float *scales, uint16_t *C, ekernel_isa_t isa);
 
+/* C[M, N] = rne_bf16(A[M, K] . W[N, K]^T), fp32 accumulation: F.linear on bf16 tensors,
+ * the reference's default BackendLinear (models/base/linear.py:170-183) as the MTP draft
+ * module uses it (mtp.py:21, 137).  K % 8 == 0; A and W 16-byte aligned. */
+int ekernel_linear_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint16_t *W, uint16_t *C);
+
 /* Load-time repack of reference-packed int4 weights (uint8 [N, K/2], even k in the low
  * nibble; ckernel.py:70-161) into the k-pair nibble order: within every 32-bit word
  * (k = 8i .. 8i+7 of a row) nibble p holds k = 8i + 2p for p < 4 and 8i + 2(p-4) + 1 for

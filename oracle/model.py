@@ -368,33 +368,46 @@ class OracleMTP:
     RoPE cannot change it and are not computed."""
 
     def __init__(self, cfg: Qwen3Config, ck: dict[str, torch.Tensor], model: OracleModel,
-                 q: dict | None = None):
+                 q: dict | None = None, linears: str = "w4row"):
+        """linears: "w4row" (the PILM_MTP_QUANTIZE=w4a16 option) or "bf16" (the reference's
+        default: BackendLinear, i.e. F.linear on the bf16 weights, linear.py:170-183)."""
         self.cfg = cfg
-        self.q = q if q is not None else quantize_mtp(ck)
+        self.linears = linears
+        if linears == "w4row":
+            self.q = q if q is not None else quantize_mtp(ck)
+        elif linears == "bf16":
+            self.w = {name: ck[name].to(torch.bfloat16) for name in MTP_LINEARS}
+        else:
+            raise ValueError(f"unknown draft-module linears {linears!r}")
         self.norms = {k: ck[k] for k in MTP_NORMS}
         self.model = model
+
+    def _lin(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        if self.linears == "bf16":
+            return torch.nn.functional.linear(x, self.w[name])
+        return qlinear(x, self.q[name], "w4row")
 
     def hidden(self, hidden: torch.Tensor, token_embedding: torch.Tensor) -> torch.Tensor:
         c = self.cfg
         h = rms_norm(hidden.reshape(1, -1), self.norms["pre_fc_norm_hidden"], c.eps, c.gemma_norm)
         e = rms_norm(token_embedding.reshape(1, -1), self.norms["pre_fc_norm_embedding"], c.eps, c.gemma_norm)
-        x = qlinear(torch.cat([e, h], dim=-1), self.q["fc"], "w4row")
+        x = self._lin(torch.cat([e, h], dim=-1), "fc")
         r = x
         a = rms_norm(x, self.norms["input_norm"], c.eps, c.gemma_norm)
-        v = qlinear(a, self.q["v_proj"], "w4row")
+        v = self._lin(a, "v_proj")
         rep = c.n_heads // c.n_kv_heads
         out = v.view(1, c.n_kv_heads, 1, c.head_dim).expand(1, c.n_kv_heads, rep, c.head_dim)
         out = out.reshape(1, c.n_heads * c.head_dim)
         if c.gated:
-            qg = qlinear(a, self.q["q_proj"], "w4row").view(1, c.n_heads, 2 * c.head_dim)
+            qg = self._lin(a, "q_proj").view(1, c.n_heads, 2 * c.head_dim)
             gate = qg[..., c.head_dim:].reshape(1, -1)
             out = out * torch.sigmoid(gate)
-        x = r + qlinear(out, self.q["o_proj"], "w4row")
+        x = r + self._lin(out, "o_proj")
         r = x
         m = rms_norm(x, self.norms["post_norm"], c.eps, c.gemma_norm)
-        g = qlinear(m, self.q["gate"], "w4row")
-        u = qlinear(m, self.q["up"], "w4row")
-        x = r + qlinear(torch.nn.functional.silu(g) * u, self.q["down"], "w4row")
+        g = self._lin(m, "gate")
+        u = self._lin(m, "up")
+        x = r + self._lin(torch.nn.functional.silu(g) * u, "down")
         return rms_norm(x, self.norms["final_norm"], c.eps, c.gemma_norm)
 
     def draft_tokens(self, hidden: torch.Tensor, first_token_id: int, num_tokens: int):

@@ -50,6 +50,7 @@ KERNEL_SYMBOLS = [
     "ekernel_argmax_top2_bf16",
     "ekernel_verify_accept_greedy",
     "ekernel_verify_accept_rejection",
+    "ekernel_linear_bf16",
     "ekernel_repack_w4_kpairs",
     "ekernel_linear_w4a16g128_bf16_kpairs",
     "ekernel_linear_w4a16_bf16_kpairs",
@@ -176,6 +177,8 @@ def _configure(lib) -> None:
         fn.restype = _i32
     lib.ekernel_linear_w8a16_bf16_argmax.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp, _vp,
                                                      ctypes.POINTER(_sz), ctypes.POINTER(ctypes.c_float), _i32]
+    lib.ekernel_linear_bf16.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp, _vp]
+    lib.ekernel_linear_bf16.restype = _i32
     lib.ekernel_repack_w4_kpairs.argtypes = [_vp, _sz, _sz, _vp]
     lib.ekernel_repack_w4_kpairs.restype = _i32
     lib.ekernel_swiglu_bf16.argtypes = [_vp, _vp, _vp, _sz]
@@ -342,6 +345,11 @@ def linear_w4a16g128_bf16_kpairs_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, i
 
 def linear_w4a16_bf16_kpairs_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa=None) -> int:
     return _linear("ekernel_linear_w4a16_bf16_kpairs", a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa)
+
+
+def linear_bf16_ptr(a_ptr, w_ptr, c_ptr, m, n, k) -> int:
+    d = EkernelLinearW8A32Desc(m, n, k)
+    return int(_load_lib().ekernel_linear_bf16(ctypes.byref(d), a_ptr, w_ptr, c_ptr))
 
 
 def repack_w4_kpairs_ptr(qweight_ptr, n, k, out_ptr) -> int:

@@ -129,6 +129,22 @@ def linear_w4a16_bf16(x, qweight, scales, in_features=None, out: Optional[torch.
     return out
 
 
+def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """F.linear(x, weight) on bf16 tensors (BackendLinear, linear.py:170-183) through
+    ekernel_linear_bf16: fp32 accumulation, one rounding to bf16."""
+    x = _cuda("x", x, torch.bfloat16, 2)
+    weight = _cuda("weight", weight, torch.bfloat16, 2)
+    m, k = x.shape
+    n, wk = weight.shape
+    if wk != k:
+        raise ValueError(f"incompatible bf16 linear shapes: x={tuple(x.shape)} weight={tuple(weight.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _stream()
+    _check(abi.linear_bf16_ptr(x.data_ptr(), weight.data_ptr(), out.data_ptr(), m, n, k), "ekernel_linear_bf16")
+    return out
+
+
 def repack_w4_kpairs(qweight: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Reference-packed int4 weights [N, K/2] -> the k-pair nibble order the kernels
     dequantize without byte permutes (ekernel_repack_w4_kpairs); out may be qweight."""

@@ -226,6 +226,153 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
     if (threadIdx.x == 0) ctr[blockIdx.x] = 0;  // self-reset for the next launch / graph replay
 }
 
+// bf16-weight GEMV on tensor cores: C[m, n] = rne_bf16(sum_k A[m, k] * W[n, k]), fp32
+// accumulation (F.linear on bf16 tensors: the reference's default BackendLinear,
+// src/models/base/linear.py:170-183, which the MTP draft module uses unless
+// PILM_MTP_QUANTIZE=w4a16).
+//
+// Tile: a warp owns RT row tiles of 16 weight rows and NT tiles of 8 activation rows; the
+// CTA's 8 warps split K into 32-wide blocks.  In block b, lane 4r + c loads the 16 bytes
+// W[row][32b + 8c .. + 7] (rows r and r + 8 of each row tile) and A[m][32b + 8c .. + 7]:
+// words x, y feed MMA step 0 (k slots {2c, 2c+1} and {2c+8, 2c+9}), words z, w step 1, for
+// A and B alike, so the loaded words are the fragments with no permutes.  Split-K partials
+// are reduced in a fixed order by the last CTA of each row tile, as in w4_gemv_mma.
+template <int RT, int NT>
+__global__ void __launch_bounds__(kGemvWarps * 32) bf16w_gemv_mma(
+    const __nv_bfloat16 *__restrict__ X, int M, int K, const __nv_bfloat16 *__restrict__ W, int N,
+    __nv_bfloat16 *__restrict__ Y, float *__restrict__ ws, int *__restrict__ ctr, int splits, int blocks_per_split) {
+    constexpr int ROWS = 16 * RT;
+    constexpr int NACC = RT * NT * 4;
+    __shared__ float red[kGemvWarps][NACC][32];
+    __shared__ int s_last;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane >> 2, c = lane & 3;
+    const int row_base = blockIdx.x * ROWS;
+    const int nb = (K + 31) >> 5;
+    const int b0 = blockIdx.y * blocks_per_split;
+    const int b1 = min(nb, b0 + blocks_per_split);
+
+    const __nv_bfloat16 *wp[RT][2];
+    bool rv[RT][2];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = row_base + rt * 16 + h * 8 + r;
+            rv[rt][h] = row < N;
+            wp[rt][h] = W + (size_t)(row < N ? row : 0) * K + c * 8;
+        }
+    const __nv_bfloat16 *xp[NT];
+    bool xv[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + r;
+        xv[nt] = m < M;
+        xp[nt] = X + (size_t)(m < M ? m : 0) * K + c * 8;
+    }
+
+    float acc[RT][NT][4];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[rt][nt][j] = 0.f;
+
+    for (int b = b0 + warp; b < b1; b += kGemvWarps) {
+        const int k = b * 32 + c * 8;  // this lane's 8 k values (K % 8 == 0: all or none)
+        const bool kin = k < K;
+        uint4 wq[RT][2];
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                wq[rt][h] = (rv[rt][h] && kin) ? ldg_nc_v4(wp[rt][h] + (size_t)b * 32) : make_uint4(0, 0, 0, 0);
+        uint4 xw[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            xw[nt] = (xv[nt] && kin) ? ldg_v4(xp[nt] + (size_t)b * 32) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int st = 0; st < 2; ++st)
+#pragma unroll
+            for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    mma16816(acc[rt][nt], st ? wq[rt][0].z : wq[rt][0].x, st ? wq[rt][1].z : wq[rt][1].x,
+                             st ? wq[rt][0].w : wq[rt][0].y, st ? wq[rt][1].w : wq[rt][1].y,
+                             st ? xw[nt].z : xw[nt].x, st ? xw[nt].w : xw[nt].y);
+    }
+
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) red[warp][(rt * NT + nt) * 4 + j][lane] = acc[rt][nt][j];
+    __syncthreads();
+    for (int e = threadIdx.x; e < NACC * 32; e += blockDim.x) {
+        const int idx = e >> 5, ln = e & 31;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w) v += red[w][idx][ln];
+        const int rt = idx / (NT * 4), nt = (idx / 4) % NT, j = idx & 3;
+        const int row = row_base + rt * 16 + (ln >> 2) + ((j & 2) ? 8 : 0);
+        const int m = nt * 8 + 2 * (ln & 3) + (j & 1);
+        if (row < N && m < M) {
+            if (splits == 1)
+                Y[(size_t)m * N + row] = f2bf(v);
+            else
+                ws[((size_t)blockIdx.y * M + m) * N + row] = v;
+        }
+    }
+    if (splits == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(ctr + blockIdx.x, 1);
+        s_last = (prev == splits - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int e = threadIdx.x; e < ROWS * M; e += blockDim.x) {
+        const int m = e / ROWS, row = row_base + e % ROWS;
+        if (row >= N) continue;
+        float v = 0.f;
+        for (int sp = 0; sp < splits; ++sp) v += __ldcg(ws + ((size_t)sp * M + m) * N + row);
+        Y[(size_t)m * N + row] = f2bf(v);
+    }
+    if (threadIdx.x == 0) ctr[blockIdx.x] = 0;  // self-reset for the next launch / graph replay
+}
+
+template <int RT, int NT>
+int launch_bf16w(const __nv_bfloat16 *X, int M, int K, const __nv_bfloat16 *W, int N, __nv_bfloat16 *Y,
+                 const char *what) {
+    const int tiles = (N + 16 * RT - 1) / (16 * RT);
+    const int nb = (K + 31) / 32;
+    const int target = 2 * pilm::num_sms();
+    int splits = 1;
+    if (tiles < target) {
+        splits = (target + tiles - 1) / tiles;
+        int max_splits = nb / kGemvWarps;  // keep every warp busy
+        if (max_splits < 1) max_splits = 1;
+        if (splits > max_splits) splits = max_splits;
+    }
+    const int bps = (nb + splits - 1) / splits;
+    splits = (nb + bps - 1) / bps;
+    float *ws = nullptr;
+    int *ctr = nullptr;
+    if (splits > 1) {
+        ws = (float *)pilm::workspace((size_t)splits * M * N * sizeof(float));
+        ctr = pilm::counters((size_t)tiles);
+        PILM_REQUIRE(ws && ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+    }
+    bf16w_gemv_mma<RT, NT><<<dim3(tiles, splits), kGemvWarps * 32, 0, pilm::stream()>>>(X, M, K, W, N, Y, ws, ctr,
+                                                                                          splits, bps);
+    return pilm::check_launch(what);
+}
+
 // Generic fallback (any K, any alignment): one warp per output row; lanes stride
 // over k; per scale group the lanes' partial dots are summed, then
 // acc = acc + dot_g * s[n,g] (QF 0), or the row dot is scaled once (QF 1: W4 per-row,
@@ -616,6 +763,34 @@ int ekernel_linear_w4a16g128_bf16(const ekernel_linear_w8a32_desc_t *desc, const
     LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16");
     return pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
                              "ekernel_linear_w4a16g128_bf16");
+}
+
+int ekernel_linear_bf16(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint16_t *W, uint16_t *C) {
+    PILM_REQUIRE(desc && A && W && C, ECPU_ERR_PARAM, "ekernel_linear_bf16: null argument");
+    PILM_REQUIRE(desc->M <= 0x7fffffff && desc->N <= 0x7fffffff && desc->K <= 0x7fffffff, ECPU_ERR_PARAM,
+                 "ekernel_linear_bf16: dimension too large");
+    const int M = (int)desc->M, N = (int)desc->N, K = (int)desc->K;
+    if (M == 0 || N == 0) return ECPU_OK;
+    PILM_REQUIRE(K % 8 == 0 && aligned16(A) && aligned16(W), ECPU_ERR_UNSUPPORTED,
+                 "ekernel_linear_bf16: needs K %% 8 == 0 and 16-byte aligned A and W");
+    const __nv_bfloat16 *X = (const __nv_bfloat16 *)A, *Wb = (const __nv_bfloat16 *)W;
+    __nv_bfloat16 *Y = (__nv_bfloat16 *)C;
+    for (int m0 = 0; m0 < M; m0 += 64) {  // slabs of at most 64 activation rows
+        const int mm = M - m0 < 64 ? M - m0 : 64;
+        const __nv_bfloat16 *Xs = X + (size_t)m0 * K;
+        __nv_bfloat16 *Ys = Y + (size_t)m0 * N;
+        int rc;
+        if (mm <= 8)
+            rc = launch_bf16w<2, 1>(Xs, mm, K, Wb, N, Ys, "ekernel_linear_bf16");
+        else if (mm <= 16)
+            rc = launch_bf16w<2, 2>(Xs, mm, K, Wb, N, Ys, "ekernel_linear_bf16");
+        else if (mm <= 32)
+            rc = launch_bf16w<2, 4>(Xs, mm, K, Wb, N, Ys, "ekernel_linear_bf16");
+        else
+            rc = launch_bf16w<1, 8>(Xs, mm, K, Wb, N, Ys, "ekernel_linear_bf16");
+        if (rc != ECPU_OK) return rc;
+    }
+    return ECPU_OK;
 }
 
 int ekernel_repack_w4_kpairs(const uint8_t *qweight, size_t N, size_t K, uint8_t *out) {

@@ -3,7 +3,7 @@
 One draft step, batched over B sequences, everything on the device:
 
     f   = [norm_e(embed[token]) | norm_h(state)]        ekernel_mtp_fc_input_bf16  (mtp.py:35-39)
-    x   = fc(f)                                         W4 per-row linear, 2H -> H
+    x   = fc(f)                                         bf16 or W4 per-row linear, 2H -> H
     a   = input_norm(x)                                 ekernel_add_rmsnorm_bf16 (no add)
     att = expand(v_proj(a)) [* sigmoid(gate_proj(a))]   ekernel_self_attention_bf16
     x   = x + o_proj(att); m = post_norm(x)             ekernel_add_rmsnorm_bf16
@@ -14,8 +14,9 @@ One draft step, batched over B sequences, everything on the device:
 The block is TransformerBlock called without a KV cache, so attention sees the token alone
 and reduces to V expanded over the GQA group (times the output gate when gated): no Q, K,
 norms or RoPE are computed.  The linears use the reference's W4A16 option for the draft
-module (PILM_MTP_QUANTIZE=w4a16: per-row int4, mtp.py:85-94, linear.py:291-296), so each is
-ekernel_linear_w4a16_bf16.  The first step reads the verify row that produced the next
+module (PILM_MTP_QUANTIZE=w4a16: per-row int4, mtp.py:85-94, linear.py:291-296), each
+ekernel_linear_w4a16_bf16_kpairs, or the reference's default bf16 layers (F.linear), each
+ekernel_linear_bf16.  The first step reads the verify row that produced the next
 token directly from the verify output (row cu_q[b] + accepted[b]), as the reference engine
 passes that row's hidden state (engine.py:527-557); later steps read the previous step's
 output.  Buffers are preallocated, so draft() allocates nothing and can be captured in a
@@ -69,9 +70,41 @@ class W4RowLinear:
         return ck.linear_w4a16_bf16(x, self.qweight, self.scales, out=out, kpairs=True)
 
 
+class BF16Linear:
+    """Device-resident bf16 linear (weight [N, K]): the reference's default BackendLinear
+    (F.linear, linear.py:170-183), through ekernel_linear_bf16."""
+
+    def __init__(self, weight: torch.Tensor):
+        self.weight = weight.to(torch.bfloat16).contiguous()
+        self.in_features = int(weight.shape[1])
+        self.out_features = int(weight.shape[0])
+
+    @classmethod
+    def cat(cls, parts: list["BF16Linear"]) -> "BF16Linear":
+        return cls(torch.cat([p.weight for p in parts]))
+
+    def rows(self, index: torch.Tensor) -> "BF16Linear":
+        return BF16Linear(self.weight.index_select(0, index))
+
+    @property
+    def nbytes(self) -> int:
+        return self.weight.numel() * 2
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        return ck.linear_bf16(x, self.weight, out=out)
+
+
+LINEAR_MODES = {"bf16": lambda w: BF16Linear(w), "w4a16": lambda w: W4RowLinear.quantize(w)}
+
+
 class MTPWeights:
-    def __init__(self, shape: Qwen3Shape, fc: W4RowLinear, gate_proj: Optional[W4RowLinear], v_proj: W4RowLinear,
-                 o_proj: W4RowLinear, gate_up: W4RowLinear, down: W4RowLinear, norms: dict[str, torch.Tensor]):
+    """The draft module's weights.  linears: "bf16" is the reference's default (plain bf16
+    BackendLinear layers, mtp.py:21 and 137); "w4a16" is its PILM_MTP_QUANTIZE=w4a16 option
+    (per-row int4, mtp.py:85-94, linear.py:291-296)."""
+
+    def __init__(self, shape: Qwen3Shape, fc, gate_proj, v_proj, o_proj, gate_up, down,
+                 norms: dict[str, torch.Tensor], linears: str = "bf16"):
+        self.linears = linears
         self.shape = shape
         self.fc, self.gate_proj, self.v_proj, self.o_proj = fc, gate_proj, v_proj, o_proj
         self.gate_up, self.down = gate_up, down
@@ -85,12 +118,16 @@ class MTPWeights:
         return sum(l.nbytes for l in lins)
 
     @classmethod
-    def from_checkpoint(cls, shape: Qwen3Shape, ck_tensors: dict[str, torch.Tensor], device) -> "MTPWeights":
-        """Quantize a bf16 draft-module checkpoint (oracle.model.make_mtp_checkpoint naming)
-        on the device with the reference's per-row int4 quantizer.  Of the (gated) q_proj
-        only the gate half of each head is kept: [q_h | gate_h] per head (attention.py:81-83)."""
+    def from_checkpoint(cls, shape: Qwen3Shape, ck_tensors: dict[str, torch.Tensor], device,
+                        linears: str = "bf16") -> "MTPWeights":
+        """A bf16 draft-module checkpoint (oracle.model.make_mtp_checkpoint naming) on the
+        device, its linears kept in bf16 or quantized with the reference's per-row int4
+        quantizer (linears="w4a16").  Of the (gated) q_proj only the gate half of each head
+        is kept: [q_h | gate_h] per head (attention.py:81-83)."""
+        make = LINEAR_MODES[linears]
+
         def q(name):
-            return W4RowLinear.quantize(ck_tensors[name].to(device))
+            return make(ck_tensors[name].to(device))
 
         gate_proj = None
         if shape.gated:
@@ -98,25 +135,28 @@ class MTPWeights:
             idx = torch.cat([torch.arange(h * 2 * hd + hd, h * 2 * hd + 2 * hd) for h in range(shape.n_heads)])
             gate_proj = q("q_proj").rows(idx.to(device))
         norms = {n: ck_tensors[n].to(device, torch.bfloat16).contiguous() for n in NORMS}
-        return cls(shape, q("fc"), gate_proj, q("v_proj"), q("o_proj"), W4RowLinear.cat([q("gate"), q("up")]),
-                   q("down"), norms)
+        gu = q("gate"), q("up")
+        return cls(shape, q("fc"), gate_proj, q("v_proj"), q("o_proj"), type(gu[0]).cat(list(gu)), q("down"), norms,
+                   linears)
 
     @classmethod
-    def synthetic(cls, shape: Qwen3Shape, seed: int, device) -> "MTPWeights":
-        """Seeded random-init draft module generated and quantized on the device: N(0, 0.02)
-        weights rounded to bf16, per-row int4; norm weights ones (plain) or zeros (Gemma)."""
+    def synthetic(cls, shape: Qwen3Shape, seed: int, device, linears: str = "bf16") -> "MTPWeights":
+        """Seeded random-init draft module generated on the device: N(0, 0.02) weights
+        rounded to bf16, kept in bf16 or quantized per row to int4 (linears="w4a16"); norm
+        weights ones (plain) or zeros (Gemma)."""
         g = torch.Generator(device=device).manual_seed(seed)
         H, I, hd = shape.hidden, shape.intermediate, shape.head_dim
+        make = LINEAR_MODES[linears]
 
         def q(n, k):
             w = (torch.randn((n, k), generator=g, device=device) * 0.02).to(torch.bfloat16)
-            return W4RowLinear.quantize(w)
+            return make(w)
 
         mk = torch.zeros if shape.gemma_norm else torch.ones
         norms = {n: mk(H, dtype=torch.bfloat16, device=device) for n in NORMS}
         gate_proj = q(shape.n_heads * hd, H) if shape.gated else None
         return cls(shape, q(H, 2 * H), gate_proj, q(shape.n_kv_heads * hd, H), q(H, shape.n_heads * hd),
-                   q(2 * I, H), q(H, I), norms)
+                   q(2 * I, H), q(H, I), norms, linears)
 
 
 class MTPDrafter:

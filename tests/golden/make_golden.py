@@ -187,10 +187,12 @@ def build_reference_model(cfg: om.Qwen3Config, ck: dict[str, torch.Tensor]) -> Q
     return model
 
 
-def build_reference_mtp(cfg: om.Qwen3Config, mck: dict[str, torch.Tensor], mc) -> Qwen3MTPDraft:
-    """The reference draft module (mtp.py:15-23) with the seeded weights, quantized by the
-    reference's own W4A16 option (_quantize_mtp_linears, mtp.py:85-94).  Plain Qwen3 uses
-    the same harness shims as the main model (+inf gate half, RMSNorm for GemmaRMSNorm)."""
+def build_reference_mtp(cfg: om.Qwen3Config, mck: dict[str, torch.Tensor], mc, quantize: bool = True) -> Qwen3MTPDraft:
+    """The reference draft module (mtp.py:15-23) with the seeded weights: quantized by the
+    reference's own W4A16 option (_quantize_mtp_linears, mtp.py:85-94, PILM_MTP_QUANTIZE=
+    w4a16), or with its default bf16 BackendLinear layers (quantize=False, mtp.py:137).
+    Plain Qwen3 uses the same harness shims as the main model (+inf gate half, RMSNorm for
+    GemmaRMSNorm)."""
     prev = torch.get_default_dtype()
     torch.set_default_dtype(torch.bfloat16)
     try:
@@ -213,7 +215,8 @@ def build_reference_mtp(cfg: om.Qwen3Config, mck: dict[str, torch.Tensor], mc) -
     blk.mlp.gate = lin(mck["gate"])
     blk.mlp.up = lin(mck["up"])
     blk.mlp.down = lin(mck["down"])
-    mtp.quantized_linear_modules = _quantize_mtp_linears(mtp)
+    if quantize:
+        mtp.quantized_linear_modules = _quantize_mtp_linears(mtp)
     if not cfg.gated:
         at.q_proj = _GateFreeQ(at.q_proj, cfg.n_heads, cfg.head_dim)
     pairs = [(mtp, "pre_fc_norm_embedding", "pre_fc_norm_embedding"), (mtp, "pre_fc_norm_hidden", "pre_fc_norm_hidden"),
@@ -257,10 +260,11 @@ def model_trace(name: str, kwargs: dict, seed: int) -> dict[str, np.ndarray]:
     cfg = om.Qwen3Config(**kwargs)
     ck = om.make_checkpoint(cfg, seed)
     model = build_reference_model(cfg, ck)
-    mtp = None
-    if cfg.quant == "w4g128":  # the W4A16 draft module (bf16 activations)
+    mtp = mtp_bf16 = None
+    if cfg.quant == "w4g128":  # the draft module (bf16 activations): W4A16 option and bf16 default
         mck = om.make_mtp_checkpoint(cfg, seed)
         mtp = build_reference_mtp(cfg, mck, model.config)
+        mtp_bf16 = build_reference_mtp(cfg, mck, model.config, quantize=False)
     rng = np.random.default_rng(seed)
     prompts = [list(rng.integers(0, cfg.vocab, size=n)) for n in (21, 27, 13, 31)]
     k = 3
@@ -361,6 +365,11 @@ def model_trace(name: str, kwargs: dict, seed: int) -> dict[str, np.ndarray]:
                                                   num_tokens=3)
             res[f"b{bi}.mtp_drafts"] = np.array(d_next, np.int64)
             res[f"b{bi}.mtp_last_hidden"] = bits(h_last.reshape(1, -1))
+            with torch.no_grad():
+                d_next, h_last = mtp_bf16.draft_tokens(h[acc], nxt, start + acc + 1, model.embed_tokens,
+                                                       model.lm_head, num_tokens=3)
+            res[f"b{bi}.mtp_drafts_bf16"] = np.array(d_next, np.int64)
+            res[f"b{bi}.mtp_last_hidden_bf16"] = bits(h_last.reshape(1, -1))
         if acc < len(drafts_all[bi]):
             # reference reject path (engine.py:505-525): re-run the accepted prefix
             hp = run_forward(model, kv, ids[:1 + acc], sr.positions[:1 + acc], sr.block_ids, True)

@@ -120,7 +120,7 @@ def test_engine_drafts_next_step_on_gpu(variant):
     from pilm_b200.mtp import MTPDrafter, MTPWeights
     z, cfg, ckpt, w = build(variant)
     _, seed = G.model_config(z)
-    mw = MTPWeights.from_checkpoint(w.shape, om.make_mtp_checkpoint(cfg, seed), dev())
+    mw = MTPWeights.from_checkpoint(w.shape, om.make_mtp_checkpoint(cfg, seed), dev(), linears="w4a16")
     B = G.num_seqs(z)
     kv = PagedKVCache(w.shape, 32, dev())
     ver = Qwen3Verifier(w, kv, max_rows=128, max_pos=256, device=dev())

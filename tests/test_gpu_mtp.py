@@ -30,13 +30,17 @@ def shape_of(cfg: om.Qwen3Config) -> Qwen3Shape:
                       gemma_norm=cfg.gemma_norm, block_size=cfg.block_size)
 
 
+@pytest.mark.parametrize("linears", ["w4a16", "bf16"])
 @pytest.mark.parametrize("variant", VARIANTS)
-def test_drafts_match_reference(variant):
+def test_drafts_match_reference(variant, linears):
+    """Both draft-module options: the PILM_MTP_QUANTIZE=w4a16 linears and the reference's
+    default bf16 linears, against the reference drafts of that option."""
     z = G.load(f"model_{variant}.npz")
     cfg, seed = G.model_config(z)
     shape = shape_of(cfg)
     w = Qwen3Weights.from_checkpoint(shape, om.make_checkpoint(cfg, seed), dev())
-    mw = MTPWeights.from_checkpoint(shape, om.make_mtp_checkpoint(cfg, seed), dev())
+    mw = MTPWeights.from_checkpoint(shape, om.make_mtp_checkpoint(cfg, seed), dev(), linears=linears)
+    sfx = "_bf16" if linears == "bf16" else ""
     drafter = MTPDrafter(mw, w, max_seqs=8, device=dev())
     B = G.num_seqs(z)
     rows, cu, acc, nxt = [], [0], [], []
@@ -54,9 +58,23 @@ def test_drafts_match_reference(variant):
     torch.cuda.synchronize()
     got = out.cpu().numpy()
     for b in range(B):
-        assert got[:, b].tolist() == G.ilist(z[f"b{b}.mtp_drafts"]), f"sequence {b}"
-        ref = f32_of_bits(z[f"b{b}.mtp_last_hidden"])[0]
+        assert got[:, b].tolist() == G.ilist(z[f"b{b}.mtp_drafts{sfx}"]), f"sequence {b}"
+        ref = f32_of_bits(z[f"b{b}.mtp_last_hidden{sfx}"])[0]
         assert rel_err(f32_of_bits(bits_of(last[b])), ref) <= REL_TOL
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 24, 32, 40, 64, 70])
+def test_bf16_linear_vs_fp32_reference(M):
+    """ekernel_linear_bf16 against torch's fp32 product of the same bf16 tensors, rounded
+    once: every GEMV tile (M <= 8, 16, 32, 64), slabs above 64 rows, split-K and a ragged N."""
+    g = torch.Generator().manual_seed(M)
+    for (N, K) in [(300, 512), (1000, 4096)]:
+        x = torch.randn((M, K), generator=g).to(torch.bfloat16)
+        w = (torch.randn((N, K), generator=g) * 0.02).to(torch.bfloat16)
+        ref = (x.float() @ w.float().t()).to(torch.bfloat16)
+        got = ck.linear_bf16(x.to(dev()), w.to(dev())).cpu()
+        assert rel_err(got.float().numpy(), ref.float().numpy()) <= REL_TOL
+        assert (got == ref).float().mean().item() >= 0.99
 
 
 def test_fc_input_and_self_attention_kernels():

@@ -139,6 +139,22 @@ def test_oracle_mtp_drafts_match_reference(variant):
         assert np.array_equal(om._to_bits(last.reshape(1, -1)), z[f"b{b}.mtp_last_hidden"])
 
 
+@pytest.mark.parametrize("variant", [v for v in G.MODEL_VARIANTS if "w4g128" in v])
+def test_oracle_mtp_bf16_drafts_match_reference(variant):
+    """The draft module with the reference's default bf16 linears: the same three draft
+    steps give the reference's drafts and its last hidden state bit for bit."""
+    z = G.load(f"model_{variant}.npz")
+    cfg, seed = G.model_config(z)
+    m = om.OracleModel(cfg, om.make_checkpoint(cfg, seed))
+    mtp = om.OracleMTP(cfg, om.make_mtp_checkpoint(cfg, seed), m, linears="bf16")
+    for b in range(G.num_seqs(z)):
+        acc, nxt = G.ilist(z[f"b{b}.accept"])
+        hid = om._from_bits(z[f"b{b}.hidden"])[acc]
+        drafts, last = mtp.draft_tokens(hid, nxt, 3)
+        assert drafts == G.ilist(z[f"b{b}.mtp_drafts_bf16"])
+        assert np.array_equal(om._to_bits(last.reshape(1, -1)), z[f"b{b}.mtp_last_hidden_bf16"])
+
+
 def test_draft_limit_matches_engine_rule():
     # engine.py:399-401
     assert om.draft_limit(21, 16, 64, 3) == 3
