@@ -522,9 +522,10 @@ def _graph_ms(body, calls: int, iters: int = 5) -> float:
 
 
 def run_sweep(args) -> None:
-    """One JSON line per case.  Linears: W4A16 g128 (reference packing, and the k-pair
-    layout the model keeps its weights in) and W8A32 at every M of SWEEP_M on the
-    Qwen3-8B projection shapes (K, N); enough weight copies are cycled that each call reads
+    """One JSON line per case.  Linears on the Qwen3-8B projection shapes (K, N): W4A16 g128
+    (reference packing, and the k-pair layout the model keeps its weights in) and W8A32 at
+    every M of SWEEP_M, bf16 weights (the draft module's default) at M <= 64; enough
+    weight copies are cycled that each call reads
     its weights from HBM (copies x bytes > 2 x L2).  Paged attention: q_len 2-5 at 1K, 8K
     and 32K keys, 32 Q / 8 KV heads, batch sized to about 1 GB of K/V per call.  Accept:
     row top-2 + greedy accept over 256 sequences x 5 rows x 151936 bf16 logits."""
@@ -544,10 +545,17 @@ def run_sweep(args) -> None:
         print(json.dumps(d), flush=True)
 
     only = set(args.sweep.split(",")) if args.sweep != "all" else {"linear", "attention", "accept"}
+    m_list = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else SWEEP_M
+    kns = [tuple(int(t) for t in v.split("x")) for v in args.sweep_kn.split(",")] if args.sweep_kn else SWEEP_KN
+    fmts = (args.sweep_formats.split(",") if args.sweep_formats
+            else ("w4a16g128", "w4a16g128_kpairs", "w8a32", "bf16"))
     if "linear" in only:
-        for K, N in SWEEP_KN:
-            for fmt in ("w4a16g128", "w4a16g128_kpairs", "w8a32"):
-                if fmt.startswith("w4a16g128"):
+        for K, N in kns:
+            for fmt in fmts:
+                if fmt == "bf16":
+                    wbytes = 2 * N * K
+                    mk = lambda: ((torch.randn((N, K), device=dev, generator=g) * 0.02).to(torch.bfloat16), None)
+                elif fmt.startswith("w4a16g128"):
                     wbytes = N * K // 2 + 4 * N * (K // 128)
                     mk = lambda: (torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g),
                                   torch.rand((N, K // 128), device=dev, generator=g) * 0.01 + 1e-4)
@@ -559,8 +567,15 @@ def run_sweep(args) -> None:
                 ws = [mk() for _ in range(copies)]
                 kp = fmt.endswith("_kpairs")  # the model's load-time layout (a nibble permutation)
                 calls = max(copies, 8)
-                for M in SWEEP_M:
-                    if fmt.startswith("w4a16g128"):
+                for M in m_list:
+                    if fmt == "bf16" and M > 64:
+                        continue  # the draft module's shapes: M = sequences per step
+                    if fmt == "bf16":
+                        x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+                        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                        io = 2 * M * K + 2 * M * N
+                        fn = lambda i: ck.linear_bf16(x, ws[i % copies][0], out=y)
+                    elif fmt.startswith("w4a16g128"):
                         x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
                         y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
                         io = 2 * M * K + 2 * M * N
@@ -652,6 +667,10 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="decoder layers (0 = all 36); profiling only")
     ap.add_argument("--sweep", default=None,
                     help="per-kernel op sweep instead of the bench line: all, or any of linear,attention,accept")
+    ap.add_argument("--sweep-m", default=None, help="linear sweep: comma-separated M values (default: all)")
+    ap.add_argument("--sweep-kn", default=None, help="linear sweep: comma-separated KxN shapes (default: Qwen3-8B)")
+    ap.add_argument("--sweep-formats", default=None,
+                    help="linear sweep: comma-separated formats of w4a16g128,w4a16g128_kpairs,w8a32,bf16")
     args = ap.parse_args()
     if args.sweep:
         run_sweep(args)
