@@ -8,7 +8,8 @@
 // the product rounded before the add, as the reference does.
 //
 // CTA tile: 128 weight rows (the MMA M dimension, TMEM lanes) x up to 128 activation
-// rows (the MMA N dimension), over a range of quant groups (split-K).  Warp roles
+// rows (the MMA N dimension), over a range of quant groups: the CTA's contiguous range of
+// (tile, group) units under a stream-K or split schedule (below).  Warp roles
 // (704 threads); a warp reaches TMEM lanes 32 * (warp % 4) .. + 31 only:
 //   warp 0      TMA, one thread: per group the packed weight tile [128 rows x 64 B] (raw
 //               ring) and the activation tile [Nm rows x 128 k] (two SWIZZLE_128B boxes,
@@ -257,17 +258,47 @@ __device__ __forceinline__ uint4 dq_word_kpairs(uint32_t w) {
 }
 
 struct TcParams {
-    const float *S;     // scales [N, G]
+    const float *S;     // scales [N, G] (grouped) or [N] (per-row)
     __nv_bfloat16 *Y;   // [M, N]
-    float *ws;          // split-K partials [splits, M, N]
+    float *part;        // pieces of cut tiles: [P][2][kMaxNm columns][128 rows] fp32
+    int *cnt;           // arrivals per (tile, fold warp): zero-initialised, self-resetting
+    float *ws;          // split schedule: fp32 partials [splits, M, N] for splitk_combine
+    int split_mode;     // 1: CTA c runs split c % splits of tile c / splits (gps groups)
+    int splits, gps;
     int *err;           // device error word
     int M, N, K, G;
-    int Nm;             // activation rows per CTA (multiple of 16, <= 128)
-    int splits, gps;    // number of K splits, groups per split
+    int Nm;             // activation rows per tile (multiple of 16, <= 128)
+    int tiles_n;        // 128-row weight tiles; tile t = tile_n + tiles_n * tile_m
+    int U;              // work units: tiles x G (unit w = t * G + group); U * P < 2^31
+    int P;              // CTAs, one per SM
     uint32_t idesc;
     int grouped;
     int scale_tma;      // group scales arrive by TMA (G % 4 == 0, group offsets 16-byte aligned)
 };
+
+// Two schedules over the units w = t * G + group, each CTA running one contiguous range:
+//  * stream-K (at least one tile per SM): CTA c takes [c U / P, (c+1) U / P), walking
+//    through tiles and their groups in order, so every SM gets the same number of groups
+//    and the rings stream straight across tile boundaries.  A tile cut by a range boundary
+//    is reduced in the kernel (the last piece to arrive adds them up).
+//  * split (fewer tiles than SMs): CTA c runs groups [s gps, (s+1) gps) of tile c / splits,
+//    s = c % splits, and writes fp32 partials that splitk_combine sums in split order.  With
+//    few tiles, stream-K would cut each into many pieces and put their reduction on the
+//    critical path.
+__device__ __forceinline__ int unit_begin(int c, const TcParams &p) { return (int)(((unsigned)c * (unsigned)p.U) / (unsigned)p.P); }
+// the CTA whose range holds unit w
+__device__ __forceinline__ int cta_of_unit(int w, const TcParams &p) {
+    int c = (int)(((unsigned)w * (unsigned)p.P) / (unsigned)p.U);
+    if (c >= p.P) c = p.P - 1;
+    while (c + 1 < p.P && unit_begin(c + 1, p) <= w) ++c;
+    while (c > 0 && unit_begin(c, p) > w) --c;
+    return c;
+}
+// a CTA keeps a cut tile's piece in slot 0 for its first tile, slot 1 for its last
+__device__ __forceinline__ float *piece_of(const TcParams &p, int c, int t) {
+    const int slot = t == unit_begin(c, p) / p.G ? 0 : 1;
+    return p.part + (size_t)(c * 2 + slot) * kMaxNm * kTileRows;
+}
 
 template <bool KP>
 __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant__ CUtensorMap wmap,
@@ -279,11 +310,18 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     Barriers *bar = reinterpret_cast<Barriers *>(smem + kSmemBar);
     volatile int *abort_flag = &bar->abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
-    const int row0 = tile_n * kTileRows, m0 = tile_m * kMaxNm;
-    const int g0 = split * p.gps, g1 = min(p.G, g0 + p.gps);
-    const int ng = g1 - g0;
-    const int nchunks = p.scale_tma ? (ng + kScaleChunk - 1) / kScaleChunk : 0;
+    const int cta = blockIdx.x;
+    const int G = p.G;
+    int W0, ng, split = 0;  // this CTA's first unit and group count (>= 1)
+    if (p.split_mode) {
+        split = cta % p.splits;
+        const int gs = split * p.gps;
+        W0 = (cta / p.splits) * G + gs;
+        ng = min(G, gs + p.gps) - gs;
+    } else {
+        W0 = unit_begin(cta, p);
+        ng = unit_begin(cta + 1, p) - W0;
+    }
 
     if (threadIdx.x == 0) {
         // consumer-side barriers take one arrival per warp (lane 0 after __syncwarp)
@@ -306,25 +344,35 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
 
-
     const int x_bytes = 2 * p.Nm * 128;
 
     if (warp == 0) {
         // ---- TMA: packed weights into the raw ring, activations into the X ring, and
-        // group scales into a two-slot ring (a slot is refilled once every fold warp has
-        // finished the tile's last group) ----
+        // group scales into a two-slot ring: a [128 rows x 16 groups] tile whenever a
+        // group starts one (a slot is refilled once every fold warp has finished with it) ----
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
-            if (nchunks > 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
+            if (p.scale_tma) asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
             int issued = 0, s_issued = 0;
+            int t = W0 / G, g = W0 % G - 1;
+            int row0 = (t % p.tiles_n) * kTileRows, m0 = (t / p.tiles_n) * kMaxNm;
             for (int i = 0; i < ng; ++i) {
-                if (nchunks > 0 && i % kScaleChunk == 0) {
-                    const int c = i / kScaleChunk, slot = c & 1;
-                    if (c >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((c - 2) >> 1) & 1u, abort_flag)) break;
+                if (++g == G) {  // next tile: next 128 weight rows, or the next activation tile
+                    g = 0;
+                    ++t;
+                    row0 += kTileRows;
+                    if (row0 >= p.tiles_n * kTileRows) {
+                        row0 = 0;
+                        m0 += kMaxNm;
+                    }
+                }
+                if (p.scale_tma && (i == 0 || g % kScaleChunk == 0)) {
+                    const int sq = s_issued, slot = sq & 1;
+                    if (sq >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((sq - 2) >> 1) & 1u, abort_flag)) break;
                     mbar_expect_tx(&bar->s_full[slot], kScaleBytes);
                     tma_load_2d(smem + kSmemScale + (size_t)slot * kScaleBytes, &smap, &bar->s_full[slot],
-                                g0 + kScaleChunk * c, row0);
+                                kScaleChunk * (g / kScaleChunk), row0);
                     ++s_issued;
                 }
                 // raw slot i % 8 held group i - 8, read by the dequant warps before they
@@ -338,10 +386,10 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     break;
                 uint64_t *full = &bar->in_full[i % kSlots];
                 mbar_expect_tx(full, (uint32_t)(kRawBytes + x_bytes));
-                tma_load_2d(smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes, &wmap, full, (g0 + i) * 64, row0);
+                tma_load_2d(smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes, &wmap, full, g * 64, row0);
                 uint8_t *dst = smem + kSmemX + (size_t)(i % kXStages) * kXBytes;
-                tma_load_2d(dst, &xmap, full, (g0 + i) * 128, m0);
-                tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, full, (g0 + i) * 128 + 64, m0);
+                tma_load_2d(dst, &xmap, full, g * 128, m0);
+                tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, full, g * 128 + 64, m0);
                 ++issued;
             }
             // drain: every issued copy has landed before the CTA may exit
@@ -416,15 +464,13 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     } else {
         // ---- fold: activation-column quarter fq of lane quadrant quad, every group in order ----
         const int quad = warp & 3;
-        const int fq = (warp - 2 - kDqWarps) >> 2;
+        const int fw = warp - 2 - kDqWarps;  // 0..15
+        const int fq = fw >> 2;
         const int rloc = 32 * quad + lane;
-        const int row = row0 + rloc;
-        const bool row_ok = row < p.N;
         const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
         const int nc = p.Nm / 16;            // 16-column chunks of the partial (<= 8)
         const int per = (nc + 3) / 4;        // chunks per quarter (<= 2)
         const int c_lo = fq * per, c_hi = min(nc, c_lo + per);
-        const float *srow = p.S + (size_t)(row_ok ? row : 0) * p.G + g0;
         const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
         float2 acc[16];  // two 16-column chunks as fp32 pairs: one packed multiply and add per pair
 #pragma unroll
@@ -433,66 +479,159 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         __syncwarp();
         if (lane == 0)
             for (int i = 0; i < kTBufs && i < ng; ++i) mbar_arrive(&bar->op_full[i]);
-        float sc_next = (p.grouped && !p.scale_tma) ? __ldg(srow) : 1.0f;
-        for (int j = 0; j < ng; ++j) {
-            const int c = j / kScaleChunk, ci = j % kScaleChunk;
-            // group j's scale first: the tile arrives long before the MMAs complete
-            float sc = sc_next;
-            if (p.scale_tma) {
-                if (ci == 0 && !mbar_wait_warp(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u, abort_flag)) break;
-                sc = sring[(size_t)(c & 1) * (kTileRows * kScaleChunk) + rloc * kScaleChunk + ci];
-                if (ci == kScaleChunk - 1 || j == ng - 1) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&bar->s_empty[c & 1]);  // done with scale tile c
+        int s_seen = 0;   // scale tiles started so far (the producer's sequence)
+        int t = W0 / G, g = W0 % G;
+        int row = (t % p.tiles_n) * kTileRows + rloc;
+        // one pass per tile segment: the groups of tile t this CTA runs, then the write-out
+        // (kept out of the per-group loop, whose registers the accumulators fill)
+        for (int i = 0; i < ng;) {
+            const int seg_g0 = g;
+            const int seg_end = min(ng, i + (G - g));  // exclusive
+            const bool row_ok = row < p.N;
+            bool aborted = false;
+            for (; i < seg_end; ++i, ++g) {
+                // group g's scale first: the tile arrives long before the MMAs complete
+                float sc = 1.0f;
+                if (p.grouped) {
+                    if (p.scale_tma) {
+                        if (i == 0 || g % kScaleChunk == 0) {
+                            const int sq = s_seen++;
+                            if (!mbar_wait_warp(&bar->s_full[sq & 1], (uint32_t)(sq >> 1) & 1u, abort_flag)) {
+                                aborted = true;
+                                break;
+                            }
+                        }
+                        const int slot = (s_seen - 1) & 1;
+                        sc = sring[(size_t)slot * (kTileRows * kScaleChunk) + rloc * kScaleChunk + g % kScaleChunk];
+                        if (i == ng - 1 || g == G - 1 || (g + 1) % kScaleChunk == 0) {
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&bar->s_empty[slot]);  // done with this scale tile
+                        }
+                    } else {
+                        sc = row_ok ? __ldg(p.S + (size_t)row * G + g) : 0.f;
+                    }
                 }
-            } else if (p.grouped && j + 1 < ng) {
-                sc_next = __ldg(srow + j + 1);
-            }
-            const float2 sc2 = make_float2(sc, sc);
-            if (!mbar_wait_warp(&bar->mma_done[j % kSlots], (uint32_t)(j / kSlots) & 1u, abort_flag)) break;
-            tc_fence_after();
-            const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (j % kTBufs) * kMaxNm);
-            // one 16-column chunk at a time (register budget); the buffer goes back to the
-            // issuer for group j + 2 as soon as the last chunk is in registers
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                uint32_t r[16];
-                const bool have = c_lo + u < c_hi;
-                if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
-                tmem_ld_wait();
-                if (u == 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0 && j + kTBufs < ng) mbar_arrive(&bar->op_full[(j + kTBufs) % kSlots]);
+                const float2 sc2 = make_float2(sc, sc);
+                if (!mbar_wait_warp(&bar->mma_done[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) {
+                    aborted = true;
+                    break;
                 }
-                if (!have) continue;
+                tc_fence_after();
+                const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (i % kTBufs) * kMaxNm);
+                // one 16-column chunk at a time (register budget); the buffer goes back to the
+                // issuer for group i + 2 as soon as the last chunk is in registers
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
-                    const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-                    acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
-                }
-            }
-        }
-        // ---- write out: direct (no split) or fp32 partial for the split-K reduction ----
-        if (!*abort_flag && row_ok) {
-            const float sr = p.grouped ? 1.0f : __ldg(p.S + row);
-            const int mlim = min(p.Nm, p.M - m0);
+                for (int u = 0; u < 2; ++u) {
+                    uint32_t r[16];
+                    const bool have = c_lo + u < c_hi;
+                    if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
+                    tmem_ld_wait();
+                    if (u == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0 && i + kTBufs < ng) mbar_arrive(&bar->op_full[(i + kTBufs) % kSlots]);
+                    }
+                    if (!have) continue;
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                if (c_lo + u >= c_hi) continue;
-#pragma unroll
-                for (int t = 0; t < 16; ++t) {
-                    const int ml = 16 * (c_lo + u) + t;  // activation row in the tile
-                    const float a = (t & 1) ? acc[u * 8 + (t >> 1)].y : acc[u * 8 + (t >> 1)].x;
-                    if (ml < mlim) {
-                        const int m = m0 + ml;
-                        if (p.splits == 1)
-                            p.Y[(size_t)m * p.N + row] = f2bf(a * sr);
-                        else
-                            p.ws[((size_t)split * p.M + m) * p.N + row] = a;
+                    for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
+                        const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                        acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
                     }
                 }
             }
+            if (aborted) break;
+            // ---- end of this CTA's segment of tile t: write the tile, or its piece ----
+            const int last_g = g - 1;
+            const float sr = (p.grouped || !row_ok) ? 1.0f : __ldg(p.S + row);
+            const int m0 = (t / p.tiles_n) * kMaxNm;
+            const int mlim = min(p.Nm, p.M - m0);
+            if (seg_g0 == 0 && last_g == G - 1) {
+                if (row_ok) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int ml = 16 * (c_lo + u) + k;  // activation row in the tile
+                            const float a = (k & 1) ? acc[u * 8 + (k >> 1)].y : acc[u * 8 + (k >> 1)].x;
+                            if (ml < mlim) p.Y[(size_t)(m0 + ml) * p.N + row] = f2bf(a * sr);
+                        }
+                    }
+                }
+            } else if (p.split_mode) {
+                // split partial for splitk_combine
+                if (row_ok) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int ml = 16 * (c_lo + u) + k;
+                            const float a = (k & 1) ? acc[u * 8 + (k >> 1)].y : acc[u * 8 + (k >> 1)].x;
+                            if (ml < mlim) p.ws[((size_t)split * p.M + m0 + ml) * p.N + row] = a;
+                        }
+                    }
+                }
+            } else {
+                // cut tile: publish this piece; the last of the tile's CTAs to arrive (per fold
+                // warp region) sums the pieces in CTA order and writes the tile
+                float *pc = piece_of(p, cta, t) + rloc;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int ml = 16 * (c_lo + u) + 2 * e;
+                        pc[(size_t)ml * kTileRows] = acc[u * 8 + e].x;
+                        pc[(size_t)(ml + 1) * kTileRows] = acc[u * 8 + e].y;
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                const int k0 = cta_of_unit(t * G, p), k1 = cta_of_unit(t * G + G - 1, p);
+                int last = 0;
+                if (lane == 0) last = atomicAdd(p.cnt + (size_t)t * kFoldWarps + fw, 1) == k1 - k0;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    // sum = 0 + piece(k0) + piece(k0 + 1) + ... in CTA order (deterministic)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) acc[e] = make_float2(0.f, 0.f);
+                    for (int cc = k0; cc <= k1; ++cc) {
+                        const float *pq = piece_of(p, cc, t) + rloc;
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const int ml = 16 * (c_lo + u) + 2 * e;
+                                acc[u * 8 + e].x += __ldcg(pq + (size_t)ml * kTileRows);
+                                acc[u * 8 + e].y += __ldcg(pq + (size_t)(ml + 1) * kTileRows);
+                            }
+                        }
+                    }
+                    if (row_ok) {
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) {
+                                const int ml = 16 * (c_lo + u) + k;
+                                const float a = (k & 1) ? acc[u * 8 + (k >> 1)].y : acc[u * 8 + (k >> 1)].x;
+                                if (ml < mlim) p.Y[(size_t)(m0 + ml) * p.N + row] = f2bf(a * sr);
+                            }
+                        }
+                    }
+                    if (lane == 0) p.cnt[(size_t)t * kFoldWarps + fw] = 0;  // self-reset for the next launch
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[e] = make_float2(0.f, 0.f);
+            // next tile: the next 128 weight rows, or the first of the next activation tile
+            g = 0;
+            ++t;
+            row += kTileRows;
+            if (row >= p.tiles_n * kTileRows) row = rloc;
         }
     }
 
@@ -558,10 +697,8 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
 
     const int G = K / 128;
     const int tiles_m = (M + kMaxNm - 1) / kMaxNm;
-    const int rows_last = M - (tiles_m - 1) * kMaxNm;
     // activation rows per CTA: all tiles use the same N (multiple of 16)
     int Nm = tiles_m == 1 ? ((M + 15) / 16) * 16 : kMaxNm;
-    (void)rows_last;
     const int tiles_n = (N + kTileRows - 1) / kTileRows;
 
     CUtensorMap wmap, xmap;
@@ -586,25 +723,29 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
             return ECPU_ERR_UNSUPPORTED;
     }
 
-    // Split K by a cost model in units of one group's pipeline time: every wave of CTAs pays
-    // its groups per CTA plus a fixed prologue and pipeline fill (about 2 groups), and a
-    // split adds one combine pass (about 3).  Group scales by TMA need every split's first
-    // group (the scale tile's x coordinate) at a multiple of 4; the combine pass wants
-    // N % 8 == 0 and 16-byte aligned output rows.
+    // Group scales by TMA: [128 rows x 16 groups] tiles at 16-group-aligned x (16-byte
+    // aligned), which needs a 16-byte row pitch (G % 4 == 0) and base.
     const bool scale_tma = grouped && (G % 4) == 0 && ((uintptr_t)S & 15) == 0;
-    const int base = tiles_n * tiles_m;
+    const int tiles = tiles_n * tiles_m;
     const int sms = num_sms();
-    int splits = 1, gps = G;
-    {
+    const long long U = (long long)tiles * G;
+    const bool stream_k = tiles >= sms;
+    int P = sms, splits = 1, gps = G;
+    if (stream_k) {
+        if (U * P >= (1ll << 31)) return ECPU_ERR_UNSUPPORTED;  // unit arithmetic is 32-bit
+    } else {
+        // Split K by a cost model in units of one group's pipeline time: every wave of CTAs
+        // pays its groups per CTA plus a fixed prologue and pipeline fill (about 2 groups),
+        // and a split adds one combine pass (about 3).  The combine pass wants N % 8 == 0 and
+        // 16-byte aligned output rows.
         double best = 1e30;
         const bool can_split = (N % 8) == 0 && (((uintptr_t)Y) & 15) == 0;
         const int max_splits = can_split ? (G < 16 ? G : 16) : 1;
         for (int s = 1; s <= max_splits; ++s) {
-            int g = (G + s - 1) / s;
-            if (scale_tma) g = (g + 3) & ~3;
+            const int g = (G + s - 1) / s;
             const int se = (G + g - 1) / g;
             if (se != s) continue;
-            const int waves = (base * se + sms - 1) / sms;
+            const int waves = (tiles * se + sms - 1) / sms;
             const double est = waves * (g + 2.0) + (se > 1 ? 3.0 : 0.0);
             if (est < best - 1e-9) {
                 best = est;
@@ -612,6 +753,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
                 gps = g;
             }
         }
+        P = tiles * splits;
     }
 
     CUtensorMap smap;
@@ -630,20 +772,30 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     TcParams p;
     p.S = S;
     p.Y = Y;
-    p.ws = nullptr;
     p.err = err;
     p.M = M;
     p.N = N;
     p.K = K;
     p.G = G;
     p.Nm = Nm;
+    p.tiles_n = tiles_n;
+    p.U = stream_k ? (int)U : 0;
+    p.P = P;
+    p.split_mode = stream_k ? 0 : 1;
     p.splits = splits;
     p.gps = gps;
+    p.ws = nullptr;
     p.grouped = grouped ? 1 : 0;
     p.scale_tma = smap_ok ? 1 : 0;
     // kind::f16 instruction descriptor: D fp32, A/B bf16, K-major both, N = Nm, M = 128
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Nm >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-    if (splits > 1) {
+    p.part = nullptr;
+    p.cnt = nullptr;
+    if (stream_k) {
+        p.part = (float *)workspace((size_t)P * 2 * kMaxNm * kTileRows * sizeof(float));
+        p.cnt = counters((size_t)tiles * kFoldWarps);
+        PILM_REQUIRE(p.part && p.cnt, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+    } else if (splits > 1) {
         p.ws = (float *)workspace((size_t)splits * M * N * sizeof(float));
         PILM_REQUIRE(p.ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
@@ -653,11 +805,10 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         cudaFuncSetAttribute(w4_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
         attr_set = true;
     }
-    dim3 grid(tiles_n, tiles_m, splits);
     if (kpairs)
-        w4_gemm_tc<true><<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
+        w4_gemm_tc<true><<<P, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
     else
-        w4_gemm_tc<false><<<grid, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
+        w4_gemm_tc<false><<<P, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     if (splits > 1) {
