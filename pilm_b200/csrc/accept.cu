@@ -73,6 +73,7 @@ template <typename T>
 __global__ void __launch_bounds__(kTop2Threads) row_top2(const T *__restrict__ logits, int rows, int V,
                                                          int32_t *__restrict__ top1, float *__restrict__ top1_val,
                                                          float *__restrict__ margin) {
+    pdl_entry();
     __shared__ Top2 sh[kTop2Threads / 32];
     const int row = blockIdx.x;
     if (row >= rows) return;
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(kTop2Threads) row_top2(const T *__restrict__ l
 __global__ void greedy_accept(int B, const int32_t *__restrict__ ids, const int32_t *__restrict__ top1,
                               const int32_t *__restrict__ cu_q, int32_t *__restrict__ acc_out,
                               int32_t *__restrict__ next_out, int32_t *__restrict__ ctx, int32_t *__restrict__ slots) {
+    pdl_entry();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const int q0 = cu_q[b], q_len = cu_q[b + 1] - q0;
@@ -345,7 +347,7 @@ int ekernel_argmax_top2_f32(const ekernel_accept_desc_t *desc, const float *logi
     PILM_REQUIRE(desc && logits, ECPU_ERR_PARAM, "ekernel_argmax_top2_f32: null argument");
     PILM_REQUIRE(desc->vocab > 0 && desc->vocab <= 0x7fffffff, ECPU_ERR_PARAM, "ekernel_argmax_top2_f32: bad vocab");
     if (desc->total_q == 0) return ECPU_OK;
-    row_top2<float><<<(unsigned)desc->total_q, kTop2Threads, 0, stream()>>>(logits, (int)desc->total_q, (int)desc->vocab, top1,
+    launch_pdl(row_top2<float>, dim3((unsigned)desc->total_q), dim3(kTop2Threads), 0, logits, (int)desc->total_q, (int)desc->vocab, top1,
                                                                    top1_val, margin);
     return check_launch("ekernel_argmax_top2_f32");
 }
@@ -355,7 +357,7 @@ int ekernel_argmax_top2_bf16(const ekernel_accept_desc_t *desc, const uint16_t *
     PILM_REQUIRE(desc && logits, ECPU_ERR_PARAM, "ekernel_argmax_top2_bf16: null argument");
     PILM_REQUIRE(desc->vocab > 0 && desc->vocab <= 0x7fffffff, ECPU_ERR_PARAM, "ekernel_argmax_top2_bf16: bad vocab");
     if (desc->total_q == 0) return ECPU_OK;
-    row_top2<__nv_bfloat16><<<(unsigned)desc->total_q, kTop2Threads, 0, stream()>>>(
+    launch_pdl(row_top2<__nv_bfloat16>, dim3((unsigned)desc->total_q), dim3(kTop2Threads), 0, 
         (const __nv_bfloat16 *)logits, (int)desc->total_q, (int)desc->vocab, top1, top1_val, margin);
     return check_launch("ekernel_argmax_top2_bf16");
 }
@@ -366,7 +368,7 @@ int ekernel_verify_accept_greedy(const ekernel_accept_desc_t *desc, const int32_
     PILM_REQUIRE(desc && verify_ids && top1 && cu_q && accept_counts && next_tokens && context_lens, ECPU_ERR_PARAM,
                  "ekernel_verify_accept_greedy: null argument");
     if (desc->num_seqs == 0) return ECPU_OK;
-    greedy_accept<<<(unsigned)((desc->num_seqs + 127) / 128), 128, 0, stream()>>>(
+    launch_pdl(greedy_accept, dim3((unsigned)((desc->num_seqs + 127) / 128)), dim3(128), 0, 
         (int)desc->num_seqs, verify_ids, top1, cu_q, accept_counts, next_tokens, context_lens, slot_mapping);
     return check_launch("ekernel_verify_accept_greedy");
 }

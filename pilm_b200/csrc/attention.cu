@@ -48,6 +48,7 @@ __global__ void qk_prologue(const __nv_bfloat16 *__restrict__ qkv, int total_q, 
                             const int32_t *__restrict__ slots, long long num_slots, __nv_bfloat16 *__restrict__ kc,
                             __nv_bfloat16 *__restrict__ vc, __nv_bfloat16 *__restrict__ q_out,
                             __nv_bfloat16 *__restrict__ gate_out) {
+    pdl_entry();
     __shared__ float buf[8][kHD];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int item = blockIdx.x * 8 + warp;
@@ -223,6 +224,7 @@ template <int MT>
 __global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const __grid_constant__ CUtensorMap kmap,
                                                              const __grid_constant__ CUtensorMap vmap,
                                                              const AttnParams p) {
+    pdl_entry();
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[kWarps][kStages];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -510,6 +512,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const __grid_const
 
 // grid: (total_q * nh); block: 128 (one thread per dim)
 __global__ void attn_merge(const AttnParams p) {
+    pdl_entry();
     const int item = blockIdx.x;
     const int d = threadIdx.x;
     if (item >= p.total_q * p.nh) return;
@@ -596,8 +599,8 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
     __shared__ int s_blk_ok[kPStages];  // the stage's block id was valid (else zero its tiles)
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     // the merge kernel may be scheduled now: it waits for this grid's completion before it
-    // reads anything (programmatic dependent launch)
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // reads anything; this grid waits for its own predecessor (programmatic dependent launch)
+    pdl_entry();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkv = p.nkv;
     const int cta = blockIdx.x;
@@ -913,7 +916,7 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
 // CTA waits for that grid first.  The loads of each step are independent of one another,
 // so a CTA waits on three rounds of memory: the metadata, then the pieces' (m, l, O).
 __global__ void attn_merge_pages(const PageAttnParams p) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    pdl_entry();
     const int head = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
     const int d = threadIdx.x;
     const int q0 = p.cu_q[b], q1 = p.cu_q[b + 1];
@@ -975,6 +978,7 @@ __global__ void attn_merge_pages(const PageAttnParams p) {
 // Clear the split partials of every (row, head) so that CTAs which exit early (no
 // rows or no visible pages in their split) leave an empty record (l = 0).
 __global__ void attn_clear_ml(float *ml, size_t n) {
+    pdl_entry();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         ml[i] = (i & 1) ? 0.f : -INFINITY;
 }
@@ -1063,7 +1067,7 @@ int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnPara
     const size_t smem = (size_t)kPStages * 4 * p.nkv * 2048 + 1024;  // + alignment slack
     const unsigned threads = (unsigned)(p.nkv + 1) * 32;
     cudaFuncSetAttribute(attn_pages<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attn_pages<1><<<p.G, threads, smem, stream()>>>(maps[0], maps[1], p);
+    launch_pdl(attn_pages<1>, dim3(p.G), dim3(threads), smem, maps[0], maps[1], p);
     rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     rc = check_error_word(what, "a K/V page load did not complete");
@@ -1098,16 +1102,16 @@ int launch_attention(AttnParams &p, const ekernel_paged_attn_desc_t *desc, int M
     dim3 grid(splits, p.nkv * row_chunks, (unsigned)desc->num_seqs);
     if (MT == 1) {
         cudaFuncSetAttribute(attn_verify<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_verify<1><<<grid, kWarps * 32, smem, stream()>>>(maps[0], maps[1], p);
+        launch_pdl(attn_verify<1>, dim3(grid), dim3(kWarps * 32), smem, maps[0], maps[1], p);
     } else {
         cudaFuncSetAttribute(attn_verify<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_verify<2><<<grid, kWarps * 32, smem, stream()>>>(maps[0], maps[1], p);
+        launch_pdl(attn_verify<2>, dim3(grid), dim3(kWarps * 32), smem, maps[0], maps[1], p);
     }
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     rc = check_error_word(what, "a K/V page load did not complete");
     if (rc != ECPU_OK || splits == 1) return rc;
-    attn_merge<<<(unsigned)(desc->total_q * desc->n_heads), kHD, 0, stream()>>>(p);
+    launch_pdl(attn_merge, dim3((unsigned)(desc->total_q * desc->n_heads)), dim3(kHD), 0, p);
     return check_launch(what);
 }
 
@@ -1140,7 +1144,7 @@ int ekernel_qk_norm_rope_kv_append(const ekernel_paged_attn_desc_t *desc, const 
     PILM_REQUIRE(!desc->output_gate || gate_out, ECPU_ERR_PARAM, "%s: gate_out required when output_gate", what);
     if (desc->total_q == 0) return ECPU_OK;
     const int items = (int)(desc->total_q * (desc->n_heads + desc->n_kv_heads));
-    qk_prologue<<<(items + 7) / 8, 256, 0, stream()>>>(
+    launch_pdl(qk_prologue, dim3((items + 7) / 8), dim3(256), 0, 
         (const __nv_bfloat16 *)qkv, (int)desc->total_q, (int)desc->n_heads, (int)desc->n_kv_heads,
         (int)desc->qkv_stride, desc->output_gate, (const __nv_bfloat16 *)q_norm_w, (const __nv_bfloat16 *)k_norm_w,
         desc->eps, desc->add_one, rope_cos, rope_sin, (int)desc->rope_rows, (int)desc->rot_dim, positions,
@@ -1209,8 +1213,7 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
         PILM_REQUIRE(ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
         p.part_o = (float *)ws;
         p.part_ml = p.part_o + n_rec * kHD;
-        attn_clear_ml<<<(int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096), 256, 0,
-                        stream()>>>(p.part_ml, n_rec * 2);
+        launch_pdl(attn_clear_ml, dim3((int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096)), dim3(256), 0, p.part_ml, n_rec * 2);
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
@@ -1324,8 +1327,7 @@ extern "C" int ekernel_paged_attention_verify_noalloc(const ekernel_paged_attn_d
         p.part_o = (float *)base_ptr;
         p.part_ml = p.part_o + n_rec * kHD;
         // the array keeps the previous call's contents: reset every (m, l) record
-        attn_clear_ml<<<(int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096), 256, 0,
-                        stream()>>>(p.part_ml, n_rec * 2);
+        launch_pdl(attn_clear_ml, dim3((int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096)), dim3(256), 0, p.part_ml, n_rec * 2);
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }

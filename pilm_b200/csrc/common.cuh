@@ -58,6 +58,36 @@ int check_error_word(const char *what, const char *msg);
 int check_launch(const char *what);
 
 // ---------------------------------------------------------------------------------
+// Programmatic dependent launch.  The verify path's kernels are launched with
+// launch_pdl and start with pdl_entry(): the next kernel in the stream may then launch
+// while this one runs (its CTAs become resident and wait in their own pdl_entry), and
+// this one touches no global memory before the previous kernel has completed.  Only the
+// launch and CTA setup of consecutive kernels overlap.  The next kernel can launch only
+// once every CTA of this one has run the trigger, so all of them are already resident.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+    pdl_trigger();
+    pdl_wait();
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------------
 // bf16 helpers.  The reference rounds fp32 -> bf16 to nearest-even
 // (kernels.c:19-25); __float2bfloat16_rn is the same rounding for finite values.
 // ---------------------------------------------------------------------------------

@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
     const __nv_bfloat16 *__restrict__ X, int M, int K, const uint8_t *__restrict__ W,
     const float *__restrict__ S, int N, __nv_bfloat16 *__restrict__ Y, float *__restrict__ ws,
     int *__restrict__ ctr, int splits, int groups_per_split) {
+    pdl_entry();
     constexpr int ROWS = 16 * RT;
     constexpr int NACC = RT * NT * 4;
     __shared__ float red[kGemvWarps][NACC][32];
@@ -241,6 +242,7 @@ template <int RT, int NT>
 __global__ void __launch_bounds__(kGemvWarps * 32) bf16w_gemv_mma(
     const __nv_bfloat16 *__restrict__ X, int M, int K, const __nv_bfloat16 *__restrict__ W, int N,
     __nv_bfloat16 *__restrict__ Y, float *__restrict__ ws, int *__restrict__ ctr, int splits, int blocks_per_split) {
+    pdl_entry();
     constexpr int ROWS = 16 * RT;
     constexpr int NACC = RT * NT * 4;
     __shared__ float red[kGemvWarps][NACC][32];
@@ -368,7 +370,7 @@ int launch_bf16w(const __nv_bfloat16 *X, int M, int K, const __nv_bfloat16 *W, i
         ctr = pilm::counters((size_t)tiles);
         PILM_REQUIRE(ws && ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
-    bf16w_gemv_mma<RT, NT><<<dim3(tiles, splits), kGemvWarps * 32, 0, pilm::stream()>>>(X, M, K, W, N, Y, ws, ctr,
+    launch_pdl(bf16w_gemv_mma<RT, NT>, dim3(dim3(tiles, splits)), dim3(kGemvWarps * 32), 0, X, M, K, W, N, Y, ws, ctr,
                                                                                           splits, bps);
     return pilm::check_launch(what);
 }
@@ -588,7 +590,7 @@ int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const flo
         PILM_REQUIRE(ws && ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
     dim3 grid(tiles, splits);
-    w4_gemv_mma<RT, NT, GROUPED, KP><<<grid, kGemvWarps * 32, 0, pilm::stream()>>>(X, M, K, W, S, N, Y, ws, ctr,
+    launch_pdl(w4_gemv_mma<RT, NT, GROUPED, KP>, dim3(grid), dim3(kGemvWarps * 32), 0, X, M, K, W, S, N, Y, ws, ctr,
                                                                                      splits, gps);
     return pilm::check_launch(what);
 }

@@ -323,6 +323,24 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         ng = unit_begin(cta + 1, p) - W0;
     }
 
+    // programmatic dependent launch: the next kernel may launch now; this CTA's setup and
+    // an L2 prefetch of its first weight tiles (never written by another kernel) overlap
+    // the previous kernel, and nothing else touches global memory before it completes
+    pdl_trigger();
+    if (threadIdx.x == 32 * 2) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+        int t = W0 / G, g = W0 % G;
+        int row0 = (t % p.tiles_n) * kTileRows;
+        for (int i = 0; i < ng && i < kRawStages; ++i) {
+            asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(&wmap), "r"(g * 64),
+                         "r"(row0)
+                         : "memory");
+            if (++g == G) {
+                g = 0;
+                row0 = row0 + kTileRows >= p.tiles_n * kTileRows ? 0 : row0 + kTileRows;
+            }
+        }
+    }
     if (threadIdx.x == 0) {
         // consumer-side barriers take one arrival per warp (lane 0 after __syncwarp)
         for (int i = 0; i < kSlots; ++i) {
@@ -343,6 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
+    pdl_wait();
 
     const int x_bytes = 2 * p.Nm * 128;
 
@@ -652,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
 // sr is the per-row scale of the ungrouped format (nullptr: grouped, already applied).
 __global__ void __launch_bounds__(256) splitk_combine(const float *__restrict__ ws, int splits, int M, int N,
                                                       const float *__restrict__ sr, __nv_bfloat16 *__restrict__ Y) {
+    pdl_entry();
     const size_t total8 = (size_t)M * N / 8;
     const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= total8) return;
@@ -806,14 +826,14 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         attr_set = true;
     }
     if (kpairs)
-        w4_gemm_tc<true><<<P, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
+        launch_pdl(w4_gemm_tc<true>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
     else
-        w4_gemm_tc<false><<<P, kThreads, kSmemTotal, stream()>>>(wmap, xmap, smap, p);
+        launch_pdl(w4_gemm_tc<false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     if (splits > 1) {
         const size_t total8 = (size_t)M * N / 8;
-        splitk_combine<<<(unsigned)((total8 + 255) / 256), 256, 0, stream()>>>(p.ws, splits, M, N,
+        launch_pdl(splitk_combine, dim3((unsigned)((total8 + 255) / 256)), dim3(256), 0, p.ws, splits, M, N,
                                                                             grouped ? nullptr : S, Y);
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;

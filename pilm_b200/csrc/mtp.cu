@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256) mtp_fc_input_kernel(const __nv_bfloat16 *
                                                            const __nv_bfloat16 *__restrict__ w_hidden, int H,
                                                            float eps, int add_one, __nv_bfloat16 *__restrict__ out,
                                                            int *__restrict__ err) {
+    pdl_entry();
     __shared__ float red[8];
     const int b = blockIdx.x;
     const bool is_hidden = blockIdx.y == 1;
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(256) mtp_fc_input_kernel(const __nv_bfloat16 *
 // gate is given (the attention kernels' gate rounding); one thread per output element.
 __global__ void self_attention_kernel(const __nv_bfloat16 *__restrict__ v, const __nv_bfloat16 *__restrict__ gate,
                                       size_t total, int nh, int nkv, int hd, __nv_bfloat16 *__restrict__ out) {
+    pdl_entry();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= total) return;
     const int width = nh * hd;
@@ -114,7 +116,7 @@ int ekernel_mtp_fc_input_bf16(const uint16_t *hidden, const int32_t *row_base, c
     if (num_seqs == 0) return ECPU_OK;
     int *err = device_error_word();
     PILM_REQUIRE(err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
-    mtp_fc_input_kernel<<<dim3((unsigned)num_seqs, 2), 256, 0, stream()>>>(
+    launch_pdl(mtp_fc_input_kernel, dim3(dim3((unsigned)num_seqs, 2)), dim3(256), 0, 
         (const __nv_bfloat16 *)hidden, row_base, row_offset, (const __nv_bfloat16 *)embed, tokens, (int)vocab,
         (const __nv_bfloat16 *)w_embed_norm, (const __nv_bfloat16 *)w_hidden_norm, (int)hidden_size, eps, add_one,
         (__nv_bfloat16 *)out, err);
@@ -131,7 +133,7 @@ int ekernel_self_attention_bf16(const uint16_t *v, const uint16_t *gate, size_t 
                  ECPU_ERR_PARAM, "%s: n_heads must be a multiple of n_kv_heads", what);
     const size_t total = rows * n_heads * head_dim;
     if (total == 0) return ECPU_OK;
-    self_attention_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream()>>>(
+    launch_pdl(self_attention_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, 
         (const __nv_bfloat16 *)v, (const __nv_bfloat16 *)gate, total, (int)n_heads, (int)n_kv_heads, (int)head_dim,
         (__nv_bfloat16 *)out);
     return check_launch(what);

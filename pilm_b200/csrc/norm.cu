@@ -53,6 +53,7 @@ __global__ void rmsnorm_c_kernel(const __nv_bfloat16 *__restrict__ x, __nv_bfloa
 __global__ void add_rmsnorm_kernel(__nv_bfloat16 *__restrict__ res, const __nv_bfloat16 *__restrict__ delta,
                                    const __nv_bfloat16 *__restrict__ w, int rows, int n, float eps, int add_one,
                                    __nv_bfloat16 *__restrict__ out) {
+    pdl_entry();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + warp;
     if (row >= rows) return;
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__r
                                                               const __nv_bfloat16 *__restrict__ delta,
                                                               const __nv_bfloat16 *__restrict__ w, int n, float eps,
                                                               int add_one, __nv_bfloat16 *__restrict__ out) {
+    pdl_entry();
     __shared__ float red[8];
     const int row = blockIdx.x;
     __nv_bfloat16 *r = res + (size_t)row * n;
@@ -164,6 +166,7 @@ __global__ void swiglu_c_rows_kernel(const __nv_bfloat16 *__restrict__ gu, int r
 // torch semantics (layers.py:193): h = rne(rne(silu(g)) * u).
 __global__ void silu_mul_module_kernel(const __nv_bfloat16 *__restrict__ gu, int rows, int inter,
                                        __nv_bfloat16 *__restrict__ out) {
+    pdl_entry();
     const size_t n = (size_t)rows * inter;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const size_t r = i / inter, c = i % inter;
@@ -175,6 +178,7 @@ __global__ void silu_mul_module_kernel(const __nv_bfloat16 *__restrict__ gu, int
 
 __global__ void embedding_kernel(const int32_t *__restrict__ ids, int rows, const __nv_bfloat16 *__restrict__ table,
                                  int vocab, int hidden, __nv_bfloat16 *__restrict__ out) {
+    pdl_entry();
     const int row = blockIdx.x;
     if (row >= rows) return;
     const int id = ids[row];
@@ -221,14 +225,14 @@ int ekernel_add_rmsnorm_bf16(uint16_t *residual, const uint16_t *delta, const ui
     if (vec) {
         const __nv_bfloat16 *dl = (const __nv_bfloat16 *)delta;
         if (n <= 256 * 8 * 2)
-            add_rmsnorm_row_kernel<2><<<(unsigned)rows, 256, 0, stream()>>>(
+            launch_pdl(add_rmsnorm_row_kernel<2>, dim3((unsigned)rows), dim3(256), 0, 
                 (__nv_bfloat16 *)residual, dl, (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out);
         else
-            add_rmsnorm_row_kernel<4><<<(unsigned)rows, 256, 0, stream()>>>(
+            launch_pdl(add_rmsnorm_row_kernel<4>, dim3((unsigned)rows), dim3(256), 0, 
                 (__nv_bfloat16 *)residual, dl, (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out);
         return check_launch("ekernel_add_rmsnorm_bf16");
     }
-    add_rmsnorm_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, stream()>>>(
+    launch_pdl(add_rmsnorm_kernel, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, 
         (__nv_bfloat16 *)residual, (const __nv_bfloat16 *)delta, (const __nv_bfloat16 *)weight, (int)rows, (int)n,
         eps, add_one, (__nv_bfloat16 *)out);
     return check_launch("ekernel_add_rmsnorm_bf16");
@@ -245,7 +249,7 @@ int ekernel_swiglu_bf16(const uint16_t *gate, const uint16_t *up, uint16_t *out,
 int ekernel_silu_mul_bf16(const uint16_t *gate_up, size_t rows, size_t inter, uint16_t *out) {
     PILM_REQUIRE(gate_up && out, ECPU_ERR_PARAM, "ekernel_silu_mul_bf16: null argument");
     if (rows == 0 || inter == 0) return ECPU_OK;
-    silu_mul_module_kernel<<<grid_for(rows * inter, 256), 256, 0, stream()>>>(
+    launch_pdl(silu_mul_module_kernel, dim3(grid_for(rows * inter, 256)), dim3(256), 0, 
         (const __nv_bfloat16 *)gate_up, (int)rows, (int)inter, (__nv_bfloat16 *)out);
     return check_launch("ekernel_silu_mul_bf16");
 }
@@ -254,7 +258,7 @@ int ekernel_embedding_bf16(const int32_t *ids, size_t rows, const uint16_t *tabl
                            uint16_t *out) {
     PILM_REQUIRE(ids && table && out, ECPU_ERR_PARAM, "ekernel_embedding_bf16: null argument");
     if (rows == 0) return ECPU_OK;
-    embedding_kernel<<<(unsigned)rows, 128, 0, stream()>>>(ids, (int)rows, (const __nv_bfloat16 *)table, (int)vocab,
+    launch_pdl(embedding_kernel, dim3((unsigned)rows), dim3(128), 0, ids, (int)rows, (const __nv_bfloat16 *)table, (int)vocab,
                                                            (int)hidden, (__nv_bfloat16 *)out);
     return check_launch("ekernel_embedding_bf16");
 }
