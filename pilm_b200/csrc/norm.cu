@@ -176,6 +176,29 @@ __global__ void silu_mul_module_kernel(const __nv_bfloat16 *__restrict__ gu, int
     }
 }
 
+// The same with 8 consecutive outputs per thread (inter % 8 == 0, 16-byte aligned rows):
+// one 16-byte load each of gate and up, one 16-byte store; grid (chunks of 2048, rows).
+__global__ void __launch_bounds__(256) silu_mul_module_v8_kernel(const __nv_bfloat16 *__restrict__ gu, int inter,
+                                                                 __nv_bfloat16 *__restrict__ out) {
+    pdl_entry();
+    const int r = blockIdx.y;
+    const int c = (blockIdx.x * 256 + threadIdx.x) * 8;
+    if (c >= inter) return;
+    const __nv_bfloat16 *row = gu + (size_t)r * 2 * inter;
+    const uint4 gv = *reinterpret_cast<const uint4 *>(row + c);
+    const uint4 uv = *reinterpret_cast<const uint4 *>(row + inter + c);
+    const __nv_bfloat16 *ge = reinterpret_cast<const __nv_bfloat16 *>(&gv);
+    const __nv_bfloat16 *ue = reinterpret_cast<const __nv_bfloat16 *>(&uv);
+    uint4 o;
+    __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float s = bf16_round(silu_f(bf2f(ge[j])));
+        oe[j] = f2bf(__fmul_rn(s, bf2f(ue[j])));
+    }
+    *reinterpret_cast<uint4 *>(out + (size_t)r * inter + c) = o;
+}
+
 __global__ void embedding_kernel(const int32_t *__restrict__ ids, int rows, const __nv_bfloat16 *__restrict__ table,
                                  int vocab, int hidden, __nv_bfloat16 *__restrict__ out) {
     pdl_entry();
@@ -249,8 +272,12 @@ int ekernel_swiglu_bf16(const uint16_t *gate, const uint16_t *up, uint16_t *out,
 int ekernel_silu_mul_bf16(const uint16_t *gate_up, size_t rows, size_t inter, uint16_t *out) {
     PILM_REQUIRE(gate_up && out, ECPU_ERR_PARAM, "ekernel_silu_mul_bf16: null argument");
     if (rows == 0 || inter == 0) return ECPU_OK;
-    launch_pdl(silu_mul_module_kernel, dim3(grid_for(rows * inter, 256)), dim3(256), 0, 
-        (const __nv_bfloat16 *)gate_up, (int)rows, (int)inter, (__nv_bfloat16 *)out);
+    if (inter % 8 == 0 && (((uintptr_t)gate_up) & 15) == 0 && (((uintptr_t)out) & 15) == 0 && rows <= 65535)
+        launch_pdl(silu_mul_module_v8_kernel, dim3((unsigned)((inter / 8 + 255) / 256), (unsigned)rows), dim3(256), 0,
+                   (const __nv_bfloat16 *)gate_up, (int)inter, (__nv_bfloat16 *)out);
+    else
+        launch_pdl(silu_mul_module_kernel, dim3(grid_for(rows * inter, 256)), dim3(256), 0,
+                   (const __nv_bfloat16 *)gate_up, (int)rows, (int)inter, (__nv_bfloat16 *)out);
     return check_launch("ekernel_silu_mul_bf16");
 }
 

@@ -88,6 +88,22 @@ def test_large_m_qwen3_8b_shapes(M):
             assert_bf16_close(bits_of(y), ref, ulp_frac=0.99)
 
 
+@pytest.mark.parametrize("inter", [512, 12288, 100])
+def test_silu_mul_vector_path_matches_scalar(inter):
+    """silu(gate) * up with torch-module rounding: the 8-wide kernel (aligned rows, inter %
+    8 == 0) gives the scalar kernel's bits (an output offset by one element takes the
+    scalar kernel), and both stay within 1e-2 of the fp32 formula."""
+    g = torch.Generator().manual_seed(inter)
+    gu = (torch.randn((7, 2 * inter), generator=g) * 3).to(torch.bfloat16).to(dev())
+    fast = ck.silu_mul_bf16(gu, inter)
+    buf = torch.empty(7 * inter + 1, dtype=torch.bfloat16, device=dev())
+    slow = ck.silu_mul_bf16(gu, inter, out=buf[1:].view(7, inter))
+    assert torch.equal(fast.cpu(), slow.cpu())
+    gf, uf = gu[:, :inter].float().cpu(), gu[:, inter:].float().cpu()
+    ref = (gf / (1 + torch.exp(-gf))) * uf
+    assert rel_err(fast.float().cpu().numpy(), ref.numpy()) <= REL_TOL
+
+
 def test_kpairs_repack_and_linears():
     """The k-pair repack is the oracle's nibble permutation bit for bit (in place too), and
     both W4 linears on repacked weights match the oracle on the reference packing: the
