@@ -23,6 +23,7 @@ skipped for synthetic benchmarks whose KV pages are filled directly.
 """
 from __future__ import annotations
 
+import itertools
 from dataclasses import dataclass
 from typing import Optional
 
@@ -166,18 +167,20 @@ class MTPVerifyEngine:
         table = self._stage("table", (B, maxp))
         ids_n, pos_n, slots_n = ids.numpy(), pos.numpy(), slots.numpy()
         cu_n, ctx_n, table_n = cu.numpy(), ctx.numpy(), table.numpy()
-        o = 0
+        cnt = np.asarray(counts, dtype=np.int32)
+        st = np.asarray(starts, dtype=np.int32)
         cu_n[0] = 0
-        for i, (s, st, n) in enumerate(zip(seqs, starts, counts)):
-            row = self._page_row(s)
-            table_n[i] = row[:maxp]
-            ids_n[o:o + n] = s.tokens[st:st + n]
-            p = np.arange(st, st + n, dtype=np.int32)
-            pos_n[o:o + n] = p
-            slots_n[o:o + n] = row[p // bs] * bs + p % bs
-            o += n
-            cu_n[i + 1] = o
-            ctx_n[i] = st + n
+        np.cumsum(cnt, out=cu_n[1:])
+        np.add(st, cnt, out=ctx_n)
+        for i, s in enumerate(seqs):
+            table_n[i] = self._page_row(s)[:maxp]
+        ids_n[:] = np.fromiter(itertools.chain.from_iterable(s.tokens[a:a + n] for s, a, n in zip(seqs, starts, counts)),
+                               dtype=np.int32, count=T)
+        # row r of sequence b sits at position starts[b] + (r - cu[b])
+        seq_of_row = np.repeat(np.arange(B), cnt)
+        p = np.arange(T, dtype=np.int32) + np.repeat(st - cu_n[:-1], cnt)
+        pos_n[:] = p
+        slots_n[:] = table_n[seq_of_row, p // bs] * bs + p % bs
         return VerifyBatch(ids=ids, positions=pos, slots=slots, block_table=table, cu_q=cu, context_lens=ctx,
                            max_q_len=max(counts), max_context=int(ctx_n.max()))
 
@@ -258,17 +261,15 @@ class MTPVerifyEngine:
             b = self.build_batch(seqs, starts, counts, on_device=False)
             g = self.graph_for(b)
             g.replay()
-            acc, nxt = g.acc, g.next
-            if self.draft_k:
-                new_drafts = g.drafts
+            new_drafts = g.drafts if self.draft_k else None
+            res = g.results.to("cpu").tolist()  # accept counts, next tokens, drafts: one copy
         else:
             b = self.build_batch(seqs, starts, counts)
             acc = torch.empty(B, dtype=torch.int32, device=self.device)
             nxt = torch.empty(B, dtype=torch.int32, device=self.device)
             ctx = b.context_lens.clone()
             self.v.verify_greedy(b, acc, nxt, ctx)
-        parts = [acc, nxt] + ([new_drafts[j] for j in range(self.draft_k)] if new_drafts is not None else [])
-        res = torch.stack(parts).to("cpu", non_blocking=False).tolist()
+            res = torch.stack([acc, nxt]).to("cpu").tolist()
         if new_drafts is not None:
             self.pending = {s.seq_id: [int(res[2 + j][i]) for j in range(self.draft_k)] for i, s in enumerate(seqs)}
         out = []

@@ -464,14 +464,16 @@ class VerifyGraph:
         self.v = verifier
         self.drafter = drafter if draft_k > 0 else None
         self.draft_k = draft_k if self.drafter is not None else 0
-        self.drafts = torch.zeros((max(1, self.draft_k), num_seqs), **i32)
+        # the step's results as rows of one tensor, read back with a single copy:
+        # accept counts, next tokens, then the k drafts
+        self.results = torch.zeros((2 + self.draft_k, num_seqs), **i32)
+        self.acc, self.next = self.results[0], self.results[1]
+        self.drafts = self.results[2:] if self.draft_k else torch.zeros((1, num_seqs), **i32)
         self.batch = VerifyBatch(ids=torch.zeros(total_q, **i32), positions=torch.zeros(total_q, **i32),
                                  slots=torch.full((total_q,), -1, **i32),
                                  block_table=torch.zeros((num_seqs, max_pages), **i32),
                                  cu_q=torch.zeros(num_seqs + 1, **i32), context_lens=torch.zeros(num_seqs, **i32),
                                  max_q_len=max_q_len, max_context=max_context)
-        self.acc = torch.zeros(num_seqs, **i32)
-        self.next = torch.zeros(num_seqs, **i32)
         self.ctx_out = torch.zeros(num_seqs, **i32)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches = 0
