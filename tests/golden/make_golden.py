@@ -427,11 +427,102 @@ def paging_trace() -> dict[str, np.ndarray]:
             "lens": np.array(lens, np.int64)}
 
 
+# ------------------------------------------------------------------------------------------
+# 4. a quant bundle in the reference's export format (scripts/export_pilm_quant_bundle.py)
+# ------------------------------------------------------------------------------------------
+
+BUNDLE_VARIANT = "qwen35_w4g128"
+
+
+def quant_bundle(name: str, kwargs: dict, seed: int, out_dir: Path) -> None:
+    """The seeded checkpoint of a model variant as a pilm-quant-bundle-v1 directory: every
+    linear (LM head included: the w4a16-all policy) quantized by the reference's group-128
+    quantizer and written by the reference's own cache writer under its cache file name
+    (models/qwen3/weights.py:59-62, 252-266); the embedding and norms as bf16 residual
+    tensors; the HF source names of weights.py:20-44; a config.json the reference's
+    config parser reads (runtime/loader/config_parser.py:81-125)."""
+    import json
+    import shutil
+
+    from safetensors.torch import save_file
+
+    from models.qwen3.weights import _quant_cache_path, _save_quantized_linear_cache
+
+    cfg = om.Qwen3Config(**kwargs)
+    ck = om.make_checkpoint(cfg, seed)
+    if out_dir.exists():
+        shutil.rmtree(out_dir)
+    (out_dir / "linear_w4a16").mkdir(parents=True)
+    (out_dir / "residual_bf16").mkdir()
+    pre = "model.language_model."
+    hf_lin = {"q_proj": "self_attn.q_proj", "k_proj": "self_attn.k_proj", "v_proj": "self_attn.v_proj",
+              "o_proj": "self_attn.o_proj", "gate": "mlp.gate_proj", "up": "mlp.up_proj", "down": "mlp.down_proj"}
+    hf_norm = {"input_norm": "input_layernorm", "post_norm": "post_attention_layernorm",
+               "q_norm": "self_attn.q_norm", "k_norm": "self_attn.k_norm"}
+    quantized = {}
+    for li in range(cfg.layers):
+        for k, v in hf_lin.items():
+            quantized[f"{pre}layers.{li}.{v}.weight"] = ck[f"l{li}.{k}"]
+    quantized["lm_head.weight"] = ck["embed"]  # tied LM head, quantized like any linear
+    for src, w in sorted(quantized.items()):
+        qw, s = ref_ck.quantize_weight_i4_grouped_chunked(w.to(torch.float32), group_size=128)
+        _save_quantized_linear_cache(_quant_cache_path(out_dir / "linear_w4a16", src), qw, s, w.shape[1])
+    residual = {f"{pre}embed_tokens.weight": ck["embed"], f"{pre}norm.weight": ck["final_norm"]}
+    for li in range(cfg.layers):
+        for k, v in hf_norm.items():
+            residual[f"{pre}layers.{li}.{v}.weight"] = ck[f"l{li}.{k}"]
+    rel = "residual_bf16/residual-0001.safetensors"
+    save_file({k: v.contiguous() for k, v in residual.items()}, str(out_dir / rel))
+    text = {"hidden_size": cfg.hidden, "num_hidden_layers": cfg.layers, "num_attention_heads": cfg.n_heads,
+            "num_key_value_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
+            "intermediate_size": cfg.intermediate, "vocab_size": cfg.vocab, "rms_norm_eps": cfg.eps,
+            "layer_types": ["full_attention"] * cfg.layers, "tie_word_embeddings": True,
+            "rope_parameters": {"rope_type": "default", "rope_theta": cfg.rope_theta,
+                                "partial_rotary_factor": cfg.partial_rotary}}
+    (out_dir / "config.json").write_text(json.dumps({"model_type": "qwen3_5", "text_config": text,
+                                                     "tie_word_embeddings": True}, indent=2))
+    manifest = {"format": "pilm-quant-bundle-v1", "quantize": "w4a16-all", "small_files": ["config.json"],
+                "quantized_linear_tensors": len(quantized), "residual_bf16_tensors": len(residual),
+                "mtp_bf16_tensors": 0, "quantized_linear_sources": sorted(quantized),
+                "residual_sources": sorted(residual), "mtp_sources": [], "missing_linear_cache": [],
+                "residual_exports": [{"file": rel, "tensors": len(residual)}], "mtp_exports": []}
+    (out_dir / "pilm_quant_manifest.json").write_text(json.dumps(manifest, indent=2))
+    _check_bundle_with_reference(out_dir, cfg, quantized)
+
+
+def _check_bundle_with_reference(out_dir: Path, cfg: om.Qwen3Config, quantized: dict) -> None:
+    """Read the bundle back through the reference's own loader code: its config parser,
+    manifest reader and bundle weight map, and every linear cache file by name with the
+    shapes and dtypes its cache loader accepts (weights.py:200-249)."""
+    from safetensors.torch import load_file
+
+    from models.qwen3.weights import _bundle_weight_map, _load_quant_bundle_manifest, _quant_cache_path
+    from runtime.loader.config_parser import parse_config
+
+    mc = parse_config(str(out_dir))
+    tc = mc.text_config
+    assert (tc.hidden_size, tc.num_hidden_layers, tc.num_attention_heads, tc.num_key_value_heads, tc.head_dim,
+            tc.intermediate_size, tc.vocab_size) == (cfg.hidden, cfg.layers, cfg.n_heads, cfg.n_kv_heads,
+                                                     cfg.head_dim, cfg.intermediate, cfg.vocab)
+    manifest = _load_quant_bundle_manifest(out_dir)
+    wmap = _bundle_weight_map(out_dir, manifest)
+    assert all(wmap[k] == "__pilm_linear_cache__" for k in quantized)
+    for src, w in quantized.items():
+        payload = load_file(str(_quant_cache_path(out_dir / "linear_w4a16", src)))
+        n, k = w.shape
+        assert tuple(payload["qweight"].shape) == (n, (k + 1) // 2) and payload["qweight"].dtype == torch.uint8
+        assert tuple(payload["scales"].shape) == (n, (k + 127) // 128) and payload["scales"].dtype == torch.float32
+        assert int(payload["in_features"].reshape(-1)[0]) == k
+
+
 def main() -> None:
     np.savez_compressed(OUT / "kernels.npz", **kernel_goldens())
     for i, (name, kw) in enumerate(VARIANTS.items()):
         np.savez_compressed(OUT / f"model_{name}.npz", **model_trace(name, kw, seed=100 + i))
     np.savez_compressed(OUT / "paging.npz", **paging_trace())
+    names = list(VARIANTS)
+    quant_bundle(BUNDLE_VARIANT, VARIANTS[BUNDLE_VARIANT], 100 + names.index(BUNDLE_VARIANT),
+                 OUT / f"bundle_{BUNDLE_VARIANT}")
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

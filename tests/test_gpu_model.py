@@ -9,6 +9,7 @@ from oracle import kernels as ok
 from oracle import model as om
 from pilm_b200 import bindings as abi
 from pilm_b200 import ckernel as ck
+from pilm_b200.bundle import load_quant_bundle
 from pilm_b200.engine import MTPVerifyEngine
 from pilm_b200.qwen3 import PagedKVCache, Qwen3Shape, Qwen3Verifier, Qwen3Weights, VerifyBatch
 from tests import _golden as G
@@ -32,10 +33,17 @@ def shape_of(cfg: om.Qwen3Config) -> Qwen3Shape:
 
 
 def build(variant):
-    z = G.load(f"model_{variant}.npz")
+    """Golden trace and device weights of a variant; "<variant>:bundle" loads the weights from
+    the variant's reference-format quant bundle instead of quantizing the checkpoint."""
+    base, _, source = variant.partition(":")
+    z = G.load(f"model_{base}.npz")
     cfg, seed = G.model_config(z)
     ckpt = om.make_checkpoint(cfg, seed)
-    w = Qwen3Weights.from_checkpoint(shape_of(cfg), ckpt, dev())
+    if source == "bundle":
+        w = load_quant_bundle(G.GOLDEN / f"bundle_{base}", dev())
+        assert w.shape == shape_of(cfg)
+    else:
+        w = Qwen3Weights.from_checkpoint(shape_of(cfg), ckpt, dev())
     return z, cfg, ckpt, w
 
 
@@ -47,7 +55,7 @@ def test_device_quantizer_matches_reference_format():
     assert np.array_equal(w.layers[0]["down"].scales.cpu().numpy(), ref["scales"])
 
 
-@pytest.mark.parametrize("variant", BF16_VARIANTS)
+@pytest.mark.parametrize("variant", BF16_VARIANTS + ["qwen35_w4g128:bundle"])
 def test_verify_step_from_reference_kv(variant):
     z, cfg, ckpt, w = build(variant)
     B = G.num_seqs(z)
