@@ -52,9 +52,13 @@ class StepResult:
 class MTPVerifyEngine:
     def __init__(self, verifier: Qwen3Verifier, num_blocks: int, block_size: int = 16, max_model_len: int = 65536,
                  max_pages_per_seq: Optional[int] = None, pin_memory: bool = True,
-                 max_num_batched_tokens: int = 1 << 30, use_graphs: bool = True, drafter=None, draft_k: int = 0):
+                 max_num_batched_tokens: int = 1 << 30, use_graphs: bool = True, drafter=None, draft_k: int = 0,
+                 page_aligned_chunks: bool = True):
         """max_num_batched_tokens is the scheduler's per-pass token budget; the reference
         engine uses one page (16, engine.py:218), which also fixes its page order.
+        page_aligned_chunks=False lets a prefill pass run past page boundaries (a long
+        prompt in budget-sized passes; the verifier's max_rows must cover the budget);
+        the default keeps the reference's one-page chunks and page order.
         use_graphs replays each verify-step shape (sequences, rows) from a captured CUDA
         graph instead of launching ~15 kernels per layer from Python.
         drafter (pilm_b200.mtp.MTPDrafter) with draft_k > 0 drafts each sequence's next
@@ -68,7 +72,8 @@ class MTPVerifyEngine:
         mp = max_pages_per_seq or (max_model_len + block_size - 1) // block_size
         self.max_pages = mp
         self.sched = VerifyScheduler(self.pages, max_num_batched_tokens=max_num_batched_tokens, max_num_seqs=1 << 20,
-                                     max_model_len=max_model_len, max_pages_per_seq=mp)
+                                     max_model_len=max_model_len, max_pages_per_seq=mp,
+                                     page_aligned_chunks=page_aligned_chunks)
         self._next_id = 0
         self.max_model_len = max_model_len
         self.use_graphs = use_graphs

@@ -159,10 +159,18 @@ class ScheduleResult:
 
 
 class VerifyScheduler:
-    """FCFS continuous batching with page-aligned chunks (scheduler.py:70-235)."""
+    """FCFS continuous batching with page-aligned chunks (scheduler.py:70-235).
+
+    page_aligned_chunks=False lifts the reference's rule that a pass ends each sequence's
+    chunk at its current page boundary (the reference's attention writes a pass's K/V
+    inside one page); chunks then take the whole token budget, so a long prompt runs in a
+    few large passes instead of one per page.  Page ids stay in allocation order per
+    sequence, but with several sequences they interleave differently from the
+    reference's."""
 
     def __init__(self, pages: PageTableManager, max_num_batched_tokens: int = 2048, max_num_seqs: int = 128,
-                 max_model_len: int = 8192, max_pages_per_seq: int = 512):
+                 max_model_len: int = 8192, max_pages_per_seq: int = 512, page_aligned_chunks: bool = True):
+        self.page_aligned_chunks = page_aligned_chunks
         self.pages = pages
         self.block_size = pages.block_size
         self.max_num_batched_tokens = max_num_batched_tokens
@@ -180,6 +188,8 @@ class VerifyScheduler:
 
     def _cap(self, seq: Sequence, num_new: int, budget: int, computed: int) -> int:
         num_new = min(num_new, budget, self.max_model_len - computed - 1)
+        if not self.page_aligned_chunks:
+            return num_new
         return min(num_new, self.block_size - (computed % self.block_size))
 
     def schedule(self) -> ScheduleResult:

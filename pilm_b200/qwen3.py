@@ -25,6 +25,7 @@ import math
 from dataclasses import dataclass
 from typing import Optional
 
+import numpy as np
 import torch
 
 from . import bindings as abi
@@ -316,6 +317,37 @@ class Qwen3Verifier:
                             max_context=b.max_context, qkv_stride=s.qkv_rows, rope_rows=self.max_pos,
                             rot_dim=s.rot_dim, eps=s.eps, add_one=s.gemma_norm, output_gate=s.gated)
 
+    def _attention_view(self, b: VerifyBatch):
+        """Attention metadata for passes with more than 16 query rows per KV head (prefill
+        chunks).  The whole-page kernel takes at most 16 rows (q_len x group) per sequence,
+        so each sequence's rows are cut into slices of 16 / group positions, each a
+        sequence of its own: same page-table row, context ending at the slice's last row
+        (the kernel's causal rule for the rows at the end of a context), rows in place.
+        Consecutive slices read overlapping pages, mostly from L2.  None when the pass fits
+        the kernel as it is, or when the slices would exceed its 1024 sequences."""
+        s = self.shape
+        gsz = s.n_heads // s.n_kv_heads
+        if b.max_q_len * gsz <= 16 or gsz > 16:
+            return None
+        span = 16 // gsz
+        cu = b.cu_q.cpu().numpy().astype(np.int64)
+        ctx = b.context_lens.cpu().numpy().astype(np.int64)
+        ql = cu[1:] - cu[:-1]
+        ns = (ql + span - 1) // span
+        if int(ns.sum()) > 1024:
+            return None
+        seq = np.repeat(np.arange(len(ql)), ns)
+        k = np.arange(int(ns.sum())) - np.repeat(np.cumsum(ns) - ns, ns)  # slice index within its sequence
+        n = np.minimum(span, ql[seq] - k * span)                            # rows in the slice
+        ends = ctx[seq] - ql[seq] + k * span + n                            # context through its last row
+        i32 = dict(dtype=torch.int32, device=self.device)
+        cu_v = torch.tensor(np.concatenate([[0], np.cumsum(n)]), **i32)
+        ctx_v = torch.tensor(ends, **i32)
+        table_v = b.block_table.index_select(0, torch.tensor(seq, dtype=torch.int64, device=self.device)).contiguous()
+        vb = VerifyBatch(ids=b.ids, positions=b.positions, slots=b.slots, block_table=table_v, cu_q=cu_v,
+                         context_lens=ctx_v, max_q_len=span, max_context=int(ends.max()))
+        return self._desc(vb), vb
+
     def forward(self, b: VerifyBatch) -> torch.Tensor:
         """Post-final-norm hidden states [T, H] (Qwen3Model.forward, return_last_hidden)."""
         s = self.shape
@@ -323,6 +355,8 @@ class Qwen3Verifier:
         if T > self.max_rows:
             raise ValueError(f"{T} rows exceed max_rows={self.max_rows}")
         desc = self._desc(b)
+        view = self._attention_view(b)
+        adesc, ab = view if view is not None else (desc, b)
         res, h = self.residual[:T], self.h[:T]
         ck.embedding_bf16(b.ids, self.w.embed, out=res)
         delta = None
@@ -336,8 +370,8 @@ class Qwen3Verifier:
                                       b.slots, self.kv.k[li], self.kv.v[li], self.q[:T],
                                       self.gate[:T] if s.gated else None)
             e = self._ev("attention")
-            ck.paged_attention_verify(desc, self.q[:T], self.kv.k[li], self.kv.v[li], b.block_table, b.cu_q,
-                                      b.context_lens, self.gate[:T] if s.gated else None, self.attn[:T])
+            ck.paged_attention_verify(adesc, self.q[:T], self.kv.k[li], self.kv.v[li], ab.block_table, ab.cu_q,
+                                      ab.context_lens, self.gate[:T] if s.gated else None, self.attn[:T])
             if e is not None:
                 e.record()
             e = self._ev("linear_o")

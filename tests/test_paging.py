@@ -139,3 +139,28 @@ def test_host_verify_batch_matches_list_build_across_growth_preemption_and_finis
         if step == 20:  # a finished sequence leaves the batch
             eng.pages.free(seqs[4])
             seqs.pop(4)
+
+
+def test_cross_page_chunks_take_the_whole_budget():
+    """page_aligned_chunks=False: a 300-token prompt under a 128-token budget runs in
+    chunks of 128, 128 and 44 tokens; each chunk's page table covers its last token, and
+    the pages are the same ones the page-aligned schedule allocates for one sequence."""
+    def run(aligned):
+        mgr = PageTableManager(64, 16)
+        sch = VerifyScheduler(mgr, max_num_batched_tokens=128, max_num_seqs=4, max_model_len=1024,
+                              page_aligned_chunks=aligned)
+        s = Sequence(0, list(range(300)), 8)
+        sch.add(s)
+        chunks = []
+        while sch.waiting or any(q.is_prefill for q in sch.running):
+            for c in sch.schedule().scheduled:
+                assert len(c.pages) * 16 >= c.positions[-1] + 1
+                assert c.positions == list(range(c.positions[0], c.positions[0] + c.num_tokens))
+                chunks.append((c.positions[0], c.num_tokens, c.is_prefill_chunk))
+        return chunks, list(s.pages)
+
+    chunks, pages = run(False)
+    assert chunks == [(0, 128, True), (128, 128, True), (256, 44, False)]
+    aligned_chunks, aligned_pages = run(True)
+    assert all(n <= 16 - p % 16 for p, n, _ in aligned_chunks)
+    assert pages == aligned_pages and len(pages) == 19
