@@ -498,6 +498,55 @@ SWEEP_KN = ((4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096), (4096, 151
 L2_BYTES = 126 * 2 ** 20
 
 
+def run_prefill(args) -> None:
+    """Prefill of one long prompt through MTPVerifyEngine.prefill (not the verify metric):
+    chunks of --prefill-chunk tokens crossing page boundaries, against the reference's
+    page-aligned chunks (engine.py:218).  One JSON line per schedule: wall time of the
+    whole prefill (host scheduling included), prompt tokens/s, the first token, and a
+    per-op split from a third run with the verifier's CUDA events on."""
+    import torch
+
+    from pilm_b200 import bindings
+    from pilm_b200.engine import MTPVerifyEngine
+    from pilm_b200.qwen3 import QWEN3_8B, PagedKVCache, Qwen3Verifier, Qwen3Weights
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bindings.init()
+    shape = QWEN3_8B
+    P = args.prefill
+    weights = Qwen3Weights.synthetic(shape, 1234, dev)
+    prompt = torch.randint(0, shape.vocab, (P,), generator=torch.Generator().manual_seed(5)).tolist()
+    nb = (P + GEN_HEADROOM) // PAGE + 2
+    schedules = [(args.prefill_chunk, False)] + ([(PAGE * 32, True)] if args.prefill_aligned else [])
+    for chunk, aligned in schedules:
+        kv = PagedKVCache(shape, nb, dev)
+        ver = Qwen3Verifier(weights, kv, max_rows=chunk, max_pos=P + GEN_HEADROOM, device=dev)
+
+        def once():
+            eng = MTPVerifyEngine(ver, num_blocks=nb, max_model_len=P + GEN_HEADROOM,
+                                  max_num_batched_tokens=chunk, page_aligned_chunks=aligned)
+            sid = eng.add_request(prompt, max_new_tokens=8)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            first = eng.prefill()[sid]
+            torch.cuda.synchronize()
+            return time.perf_counter() - t0, first, len(eng.sched.seqs[sid].pages)
+
+        cold, _, _ = once()  # scratch buffers, kernel attributes
+        t, first, npages = once()
+        ver.op_timing, ver.op_events = True, []
+        once()
+        ops = {k: round(v, 2) for k, v in ver.collect_op_times().items() if k != "attention"}
+        ver.op_timing = False
+        print(json.dumps({"prefill_tokens": P, "chunk": chunk, "page_aligned": aligned, "ms": round(t * 1e3, 1),
+                          "cold_ms": round(cold * 1e3, 1), "tok_s": round(P / t, 1), "first_token": first,
+                          "pages": npages, "op_ms": ops, "model": "Qwen3-8B W4A16 g128 (synthetic weights)"}),
+              flush=True)
+        del ver, kv
+        torch.cuda.empty_cache()
+
+
 def _graph_ms(body, calls: int, iters: int = 5) -> float:
     """ms per call: body() issues `calls` launches; it is captured once as a CUDA graph and
     replayed `iters` times between two CUDA events after a warm-up replay."""
@@ -600,7 +649,7 @@ def run_sweep(args) -> None:
                 del ws
                 torch.cuda.empty_cache()
     if "attention" in only:
-        from pilm_b200.qwen3 import QWEN3_8B, attention_bytes
+        from pilm_b200.qwen3 import QWEN3_8B, attention_bytes, attention_slices
         s = QWEN3_8B
         for ctx in (1024, 8192, 32768):
             B = max(1, (2 ** 30) // (ctx * s.n_kv_heads * s.head_dim * 4))
@@ -610,7 +659,7 @@ def run_sweep(args) -> None:
             vc = torch.randn((nb, 16, s.n_kv_heads, s.head_dim), device=dev, generator=g).to(torch.bfloat16)
             perm = (torch.randperm(nb - 1, device=dev, generator=g) + 1).to(torch.int32)
             table = perm[:B * pages].view(B, pages).contiguous()
-            for q_len in (2, 3, 4, 5):
+            for q_len in (2, 3, 4, 5, 16):
                 T = B * q_len
                 i32 = dict(dtype=torch.int32, device=dev)
                 cu = torch.arange(0, T + 1, q_len, **i32)
@@ -630,6 +679,25 @@ def run_sweep(args) -> None:
                 gbs = nbytes / (ms * 1e-3) / 1e9
                 emit({"sweep": "attention", "q_len": q_len, "ctx": ctx, "seqs": B, "heads": [s.n_heads, s.n_kv_heads],
                       "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+                cut = attention_slices(cu.cpu().numpy(), ctxs.cpu().numpy(), s.n_heads // s.n_kv_heads)
+                if q_len * s.n_heads // s.n_kv_heads > 16 and cut is not None:
+                    # the same pass cut into 16-row slices for the whole-page kernel
+                    seq, cu_v, ctx_v, span = cut
+                    table_v = table.index_select(0, torch.tensor(seq, dtype=torch.int64, device=dev)).contiguous()
+                    cu_v, ctx_v = torch.tensor(cu_v, **i32), torch.tensor(ctx_v, **i32)
+                    desc_v = ck.attn_desc(num_seqs=len(seq), total_q=T, max_q_len=span, n_heads=s.n_heads,
+                                          n_kv_heads=s.n_kv_heads, head_dim=s.head_dim, block_size=16, num_blocks=nb,
+                                          max_blocks_per_seq=pages, max_context=ctx, qkv_stride=s.qkv_rows,
+                                          rope_rows=0, rot_dim=s.rot_dim, eps=s.eps, add_one=0, output_gate=0)
+
+                    def body_v():
+                        for _ in range(4):
+                            ck.paged_attention_verify(desc_v, q, kc, vc, table_v, cu_v, ctx_v, None, out)
+                    ms = _graph_ms(body_v, 4)
+                    gbs = nbytes / (ms * 1e-3) / 1e9
+                    emit({"sweep": "attention_sliced", "q_len": q_len, "ctx": ctx, "seqs": B, "slices": len(seq),
+                          "heads": [s.n_heads, s.n_kv_heads], "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4)})
             del kc, vc
             torch.cuda.empty_cache()
     if "accept" in only:
@@ -673,7 +741,15 @@ def main():
     ap.add_argument("--sweep-kn", default=None, help="linear sweep: comma-separated KxN shapes (default: Qwen3-8B)")
     ap.add_argument("--sweep-formats", default=None,
                     help="linear sweep: comma-separated formats of w4a16g128,w4a16g128_kpairs,w8a32,bf16")
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="time the prefill of one prompt of this many tokens instead of the bench line")
+    ap.add_argument("--prefill-chunk", type=int, default=2048, help="prefill: tokens per pass (cross-page chunks)")
+    ap.add_argument("--prefill-aligned", action="store_true",
+                    help="prefill: also time the reference's page-aligned chunk schedule")
     args = ap.parse_args()
+    if args.prefill:
+        run_prefill(args)
+        return
     if args.sweep:
         run_sweep(args)
         return

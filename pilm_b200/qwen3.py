@@ -242,6 +242,29 @@ class VerifyBatch:
         return self.ids.shape[0]
 
 
+def attention_slices(cu_q, context_lens, group: int, max_slices: int = 1024):
+    """Cut a pass's query rows into sequences the whole-page attention kernel takes (at
+    most 16 rows, q_len x group, per KV head): each sequence's rows become slices of
+    16 // group positions, each a sequence of its own with the same page-table row, its
+    rows in place, and a context ending at the slice's last row (the kernel's causal rule
+    for rows at the end of a context, which is the reference's triangular mask).
+    Returns (sequence of each slice, cu_q of the slices, their contexts, positions per
+    slice) as numpy arrays, or None when the slices would exceed max_slices."""
+    span = 16 // group
+    cu = np.asarray(cu_q, np.int64)
+    ctx = np.asarray(context_lens, np.int64)
+    ql = cu[1:] - cu[:-1]
+    ns = (ql + span - 1) // span
+    total = int(ns.sum())
+    if total > max_slices:
+        return None
+    seq = np.repeat(np.arange(len(ql)), ns)
+    k = np.arange(total) - np.repeat(np.cumsum(ns) - ns, ns)  # slice index within its sequence
+    n = np.minimum(span, ql[seq] - k * span)                  # rows in the slice
+    ends = ctx[seq] - ql[seq] + k * span + n                  # context through the slice's last row
+    return seq, np.concatenate([[0], np.cumsum(n)]), ends, span
+
+
 class Qwen3Verifier:
     """Runs the batched verify forward, the LM head and the acceptance kernels."""
 
@@ -271,6 +294,11 @@ class Qwen3Verifier:
         self.margin = torch.empty((max_rows,), dtype=torch.float32, device=device)
         # optional CUDA-event timing of the attention and linear launches (bench.py)
         self.op_timing = False
+        # passes of more than 16 query rows per KV head: run on the per-head kernel (False),
+        # or cut into 16-row slices for the whole-page kernel (True).  The slices re-read
+        # their sequence's pages once per slice; on B200 that is slower at 1K-8K contexts
+        # (q_len 5, GQA 4: 415 vs 320 us at 1K) and a few percent faster at 32K.
+        self.slice_attention = False
         self.op_events: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
         self._launches_before = None
         self._last_step_launches = None
@@ -318,34 +346,25 @@ class Qwen3Verifier:
                             rot_dim=s.rot_dim, eps=s.eps, add_one=s.gemma_norm, output_gate=s.gated)
 
     def _attention_view(self, b: VerifyBatch):
-        """Attention metadata for passes with more than 16 query rows per KV head (prefill
-        chunks).  The whole-page kernel takes at most 16 rows (q_len x group) per sequence,
-        so each sequence's rows are cut into slices of 16 / group positions, each a
-        sequence of its own: same page-table row, context ending at the slice's last row
-        (the kernel's causal rule for the rows at the end of a context), rows in place.
-        Consecutive slices read overlapping pages, mostly from L2.  None when the pass fits
-        the kernel as it is, or when the slices would exceed its 1024 sequences."""
+        """Attention metadata for passes with more than 16 query rows per KV head, cut by
+        attention_slices() for the whole-page kernel.  None (the per-head kernel takes the
+        pass as it is) when the pass fits the page kernel already, when slicing is off, or
+        while a CUDA graph is being captured: the slices are cut from the host copy of
+        cu_q, which a replay with other row counts would not update."""
         s = self.shape
         gsz = s.n_heads // s.n_kv_heads
-        if b.max_q_len * gsz <= 16 or gsz > 16:
+        if (not self.slice_attention or b.max_q_len * gsz <= 16 or gsz > 16
+                or torch.cuda.is_current_stream_capturing()):
             return None
-        span = 16 // gsz
-        cu = b.cu_q.cpu().numpy().astype(np.int64)
-        ctx = b.context_lens.cpu().numpy().astype(np.int64)
-        ql = cu[1:] - cu[:-1]
-        ns = (ql + span - 1) // span
-        if int(ns.sum()) > 1024:
+        cut = attention_slices(b.cu_q.cpu().numpy(), b.context_lens.cpu().numpy(), gsz)
+        if cut is None:
             return None
-        seq = np.repeat(np.arange(len(ql)), ns)
-        k = np.arange(int(ns.sum())) - np.repeat(np.cumsum(ns) - ns, ns)  # slice index within its sequence
-        n = np.minimum(span, ql[seq] - k * span)                            # rows in the slice
-        ends = ctx[seq] - ql[seq] + k * span + n                            # context through its last row
+        seq, cu_v, ctx_v, span = cut
         i32 = dict(dtype=torch.int32, device=self.device)
-        cu_v = torch.tensor(np.concatenate([[0], np.cumsum(n)]), **i32)
-        ctx_v = torch.tensor(ends, **i32)
         table_v = b.block_table.index_select(0, torch.tensor(seq, dtype=torch.int64, device=self.device)).contiguous()
-        vb = VerifyBatch(ids=b.ids, positions=b.positions, slots=b.slots, block_table=table_v, cu_q=cu_v,
-                         context_lens=ctx_v, max_q_len=span, max_context=int(ends.max()))
+        vb = VerifyBatch(ids=b.ids, positions=b.positions, slots=b.slots, block_table=table_v,
+                         cu_q=torch.tensor(cu_v, **i32), context_lens=torch.tensor(ctx_v, **i32), max_q_len=span,
+                         max_context=int(ctx_v.max()))
         return self._desc(vb), vb
 
     def forward(self, b: VerifyBatch) -> torch.Tensor:

@@ -95,10 +95,12 @@ def test_verify_step_from_reference_kv(variant):
         assert int(ctx_out[b]) == int(z[f"b{b}.num_computed_after"][0])
 
 
+@pytest.mark.parametrize("sliced", [False, True])
 @pytest.mark.parametrize("variant", ["qwen3_w4g128", "qwen3_w4g128_gqa4"])
-def test_long_prefill_chunks_match_oracle(variant):
+def test_long_prefill_chunks_match_oracle(variant, sliced):
     """Prefill chunks of 128 tokens crossing pages (more than 16 query rows per KV head:
-    the attention runs as 16-row slices on the whole-page kernel) against the oracle model
+    the attention runs on the per-head kernel, or as 16-row slices on the whole-page
+    kernel) against the oracle model
     run over the same pages.  Layer 0's K/V (no attention upstream) comes from passes of
     more than 16 rows, whose QKV projection runs on the tensor-core GEMM (fp32 sums in MMA
     order against the reference's sequential sums): 99% of elements within one bf16 ulp,
@@ -109,6 +111,7 @@ def test_long_prefill_chunks_match_oracle(variant):
     z, cfg, ckpt, w = build(variant)
     kv = PagedKVCache(w.shape, 32, dev())
     ver = Qwen3Verifier(w, kv, max_rows=128, max_pos=512, device=dev())
+    ver.slice_attention = sliced
     eng = MTPVerifyEngine(ver, num_blocks=32, max_model_len=512, max_num_batched_tokens=128,
                           page_aligned_chunks=False)
     rng = np.random.default_rng(3)
@@ -136,6 +139,33 @@ def test_long_prefill_chunks_match_oracle(variant):
             else:
                 assert rel_err(g, r) <= 2 * REL_TOL, f"layer {li}"
     assert first == ref_first
+
+
+def test_verify_rows_beyond_the_page_kernel_graph_and_eager_agree():
+    """Five verify rows per sequence with GQA 4 (20 query rows per KV head): the eager step
+    with slicing on cuts them into 16-row slices for the whole-page kernel, the captured
+    step runs the per-head kernel.  Both give the same accept counts and next tokens, and
+    logits within 1e-2 of each other."""
+    z, cfg, ckpt, w = build("qwen3_w4g128_gqa4")
+    rng = np.random.default_rng(9)
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab, n)] for n in (32, 48, 37)]
+    drafts = [[int(t) for t in rng.integers(0, cfg.vocab, 4)] for _ in prompts]
+    out = []
+    for graphs in (False, True):
+        kv = PagedKVCache(w.shape, 32, dev())
+        ver = Qwen3Verifier(w, kv, max_rows=128, max_pos=256, device=dev())
+        ver.slice_attention = True  # ignored while the graph is captured
+        eng = MTPVerifyEngine(ver, num_blocks=32, max_model_len=256, max_num_batched_tokens=128,
+                              use_graphs=graphs, page_aligned_chunks=False)
+        sids = [eng.add_request(p, max_new_tokens=16) for p in prompts]
+        eng.prefill()
+        res = eng.verify_step({sid: d for sid, d in zip(sids, drafts)})
+        got = sorted((r.seq_id, r.accepted, r.next_token, tuple(r.drafts)) for r in res)
+        out.append((got, ver.logits[:sum(1 + len(r.drafts) for r in res)].float().cpu().numpy()))
+    (eager, le), (graph, lg) = out
+    assert all(len(r[3]) == 4 for r in eager)
+    assert eager == graph
+    assert rel_err(lg, le) <= REL_TOL
 
 
 @pytest.mark.parametrize("variant", ["qwen3_w4g128", "qwen35_w4g128"])

@@ -164,3 +164,26 @@ def test_cross_page_chunks_take_the_whole_budget():
     aligned_chunks, aligned_pages = run(True)
     assert all(n <= 16 - p % 16 for p, n, _ in aligned_chunks)
     assert pages == aligned_pages and len(pages) == 19
+
+
+def test_attention_slices_cover_every_row_once_with_its_causal_context():
+    """attention_slices: every query row of the pass lands in exactly one slice, in place
+    and in order; a slice has at most 16 // group rows, all of one sequence; and the
+    slice's context ends at its last row, so row r of a sequence with context c and q_len
+    rows sees the keys up to position c - q_len + r, as under the reference's mask."""
+    from pilm_b200.qwen3 import attention_slices
+    rng = np.random.default_rng(4)
+    for group in (1, 2, 4, 8, 16):
+        ql = rng.integers(1, 70, 9)
+        ctx = ql + rng.integers(0, 300, 9)
+        cu = np.concatenate([[0], np.cumsum(ql)])
+        seq, cu_v, ctx_v, span = attention_slices(cu, ctx, group)
+        assert span == 16 // group and cu_v[0] == 0 and cu_v[-1] == cu[-1]
+        n = np.diff(cu_v)
+        assert (n >= 1).all() and (n <= span).all() and (np.diff(seq) >= 0).all()
+        for i, b in enumerate(seq):
+            rows = np.arange(cu_v[i], cu_v[i + 1])
+            assert (rows >= cu[b]).all() and (rows < cu[b + 1]).all()
+            # the slice's last row is row (rows[-1] - cu[b]) of its sequence
+            assert ctx_v[i] == ctx[b] - ql[b] + (rows[-1] - cu[b]) + 1
+    assert attention_slices(np.arange(0, 2049 * 4, 4), np.full(2049, 100), 4) is None
