@@ -651,7 +651,9 @@ def run_sweep(args) -> None:
     if "attention" in only:
         from pilm_b200.qwen3 import QWEN3_8B, attention_bytes, attention_slices
         s = QWEN3_8B
-        for ctx in (1024, 8192, 32768):
+        ctx_list = [int(v) for v in args.sweep_ctx.split(",")] if args.sweep_ctx else [1024, 8192, 32768]
+        q_list = [int(v) for v in args.sweep_q.split(",")] if args.sweep_q else [2, 3, 4, 5, 16]
+        for ctx in ctx_list:
             B = max(1, (2 ** 30) // (ctx * s.n_kv_heads * s.head_dim * 4))
             pages = -(-(ctx + 8) // 16)
             nb = B * pages + 1
@@ -659,7 +661,7 @@ def run_sweep(args) -> None:
             vc = torch.randn((nb, 16, s.n_kv_heads, s.head_dim), device=dev, generator=g).to(torch.bfloat16)
             perm = (torch.randperm(nb - 1, device=dev, generator=g) + 1).to(torch.int32)
             table = perm[:B * pages].view(B, pages).contiguous()
-            for q_len in (2, 3, 4, 5, 16):
+            for q_len in q_list:
                 T = B * q_len
                 i32 = dict(dtype=torch.int32, device=dev)
                 cu = torch.arange(0, T + 1, q_len, **i32)
@@ -741,6 +743,8 @@ def main():
     ap.add_argument("--sweep-kn", default=None, help="linear sweep: comma-separated KxN shapes (default: Qwen3-8B)")
     ap.add_argument("--sweep-formats", default=None,
                     help="linear sweep: comma-separated formats of w4a16g128,w4a16g128_kpairs,w8a32,bf16")
+    ap.add_argument("--sweep-ctx", default=None, help="attention sweep: comma-separated context lengths")
+    ap.add_argument("--sweep-q", default=None, help="attention sweep: comma-separated rows per sequence")
     ap.add_argument("--prefill", type=int, default=0,
                     help="time the prefill of one prompt of this many tokens instead of the bench line")
     ap.add_argument("--prefill-chunk", type=int, default=2048, help="prefill: tokens per pass (cross-page chunks)")

@@ -222,7 +222,17 @@ def attention_from_proj(c: Qwen3Config, qp: torch.Tensor, kp: torch.Tensor, vp: 
     slot = start % bs
     kv_k[block_id, slot:slot + seq] = ks
     kv_v[block_id, slot:slot + seq] = vs
-    cache_len = int(positions[-1]) + 1
+    return attend(c, qs, gate, kv_k, kv_v, block_ids, int(positions[-1]) + 1, not is_decode or seq > 1)
+
+
+def attend(c: Qwen3Config, qs: torch.Tensor, gate, kv_k: torch.Tensor, kv_v: torch.Tensor, block_ids: list[int],
+           cache_len: int, masked: bool) -> torch.Tensor:
+    """The attention of FullAttention.forward once K/V are in the cache (attention.py:
+    99-139): the sequence's pages gathered up to cache_len, GQA expansion, bf16 scores
+    times the scale, the triangular mask over the last rows when masked, fp32 softmax,
+    bf16 P V, times sigmoid(gate).  qs: post-RoPE queries [seq, n_heads, hd]."""
+    seq = qs.shape[0]
+    bs = c.block_size
     needed = (cache_len + bs - 1) // bs
     full_k = torch.cat([kv_k[b] for b in block_ids[:needed]], dim=0)[:cache_len]
     full_v = torch.cat([kv_v[b] for b in block_ids[:needed]], dim=0)[:cache_len]
@@ -233,7 +243,7 @@ def attention_from_proj(c: Qwen3Config, qp: torch.Tensor, kp: torch.Tensor, vp: 
         full_v = full_v.unsqueeze(2).expand(-1, -1, rep, -1).reshape(full_v.shape[0], c.n_heads, c.head_dim)
     qt, kt, vt = qs.transpose(0, 1), full_k.transpose(0, 1), full_v.transpose(0, 1)
     scores = torch.bmm(qt, kt.transpose(1, 2)) * (1.0 / math.sqrt(c.head_dim))
-    if not is_decode or seq > 1:
+    if masked:
         kv_len = full_k.shape[0]
         mask = torch.triu(torch.ones(seq, kv_len, dtype=torch.bool), diagonal=kv_len - seq + 1)
         scores = scores.masked_fill(mask.unsqueeze(0), float("-inf"))

@@ -130,3 +130,67 @@ def test_many_ragged_sequences_nan_past_context():
         ctxs.append(st + q)
         qlens.append(q)
     run_case(32, 8, ctxs=ctxs, qlens=qlens, seed=8, poison=True)
+
+
+def prefill_case(nh, nkv, qlens, prefixes, gated=False, seed=0):
+    """Prompt chunks (q_len positions after a cached prefix) straight into the attention
+    entry point: post-RoPE queries against paged caches whose slots past each context
+    hold NaN, against the oracle's attention (attention.py:99-139) per sequence."""
+    g = torch.Generator().manual_seed(seed)
+    cfg = om.Qwen3Config(n_heads=nh, n_kv_heads=nkv, gated=gated)
+    hd, bs = 128, 16
+    ctxs = [q + p for q, p in zip(qlens, prefixes)]
+    B = len(ctxs)
+    pages = [(c + bs - 1) // bs for c in ctxs]
+    nb = sum(pages) + 4
+    perm = torch.randperm(nb - 1, generator=g)[: sum(pages)] + 1
+    tables, off = [], 0
+    for p in pages:
+        tables.append([int(x) for x in perm[off:off + p]])
+        off += p
+    maxp = max(pages)
+    kc = torch.randn((nb, bs, nkv, hd), generator=g).to(torch.bfloat16)
+    vc = (torch.randn((nb, bs, nkv, hd), generator=g) * 0.5).to(torch.bfloat16)
+    T = sum(qlens)
+    q = torch.randn((T, nh, hd), generator=g).to(torch.bfloat16)
+    gate = torch.randn((T, nh * hd), generator=g).to(torch.bfloat16) if gated else None
+    cu = [0]
+    for n in qlens:
+        cu.append(cu[-1] + n)
+    ref = torch.cat([om.attend(cfg, q[cu[b]:cu[b + 1]], gate[cu[b]:cu[b + 1]] if gated else None, kc, vc,
+                               tables[b], ctxs[b], True) for b in range(B)])
+    d = dev()
+    kc_d, vc_d = kc.to(d), vc.to(d)
+    for b in range(B):
+        if ctxs[b] % bs:
+            kc_d[tables[b][-1], ctxs[b] % bs:] = float("nan")
+            vc_d[tables[b][-1], ctxs[b] % bs:] = float("nan")
+    i32 = dict(dtype=torch.int32, device=d)
+    bt = torch.tensor([t + [0] * (maxp - len(t)) for t in tables], **i32)
+    desc = ck.attn_desc(num_seqs=B, total_q=T, max_q_len=max(qlens), n_heads=nh, n_kv_heads=nkv, head_dim=hd,
+                        block_size=bs, num_blocks=nb, max_blocks_per_seq=maxp, max_context=max(ctxs),
+                        qkv_stride=nh * hd, rope_rows=0, rot_dim=hd, eps=1e-6, add_one=0, output_gate=gated)
+    out = torch.empty((T, nh * hd), dtype=torch.bfloat16, device=d)
+    ck.paged_attention_verify(desc, q.view(T, nh * hd).to(d), kc_d, vc_d, bt, torch.tensor(cu, **i32),
+                              torch.tensor(ctxs, **i32), gate.to(d) if gated else None, out)
+    torch.cuda.synchronize()
+    e = rel_err(out.float().cpu().numpy(), ref.float().numpy())
+    assert e <= REL_TOL, e
+    return e
+
+
+def test_prefill_chunks_qwen3_8b_heads():
+    """Six chunks of up to 512 positions with GQA 4 (up to 2048 rows per KV head, 64
+    row chunks of the per-head kernel); ragged chunk ends and prefixes put the last page
+    of most sequences part-full (NaN past the context)."""
+    prefill_case(32, 8, qlens=[300, 257, 130, 512, 96, 200], prefixes=[0, 37, 1000, 5, 0, 16], seed=11)
+
+
+def test_prefill_chunks_gated_gqa2():
+    prefill_case(16, 8, qlens=[512, 301, 450, 128], prefixes=[64, 0, 211, 3], gated=True, seed=12)
+
+
+def test_prefill_single_chunk_long_prefix():
+    """One 200-position chunk after a 700-token prefix: few row chunks, so the keys are
+    split across CTAs and merged."""
+    prefill_case(32, 8, qlens=[200], prefixes=[700], seed=13)
