@@ -113,6 +113,22 @@ class ClockSampler:
 # our arm
 # ---------------------------------------------------------------------------------------
 
+def reduce_over_ranks(maxes: list[float], sums: list[float], device=None) -> tuple[list[float], list[float]]:
+    """Job-level figures of a replicated run: every rank's times reduced by MAX (the job
+    lasts as long as its slowest replica) and its counts by SUM.  Every rank makes the
+    same two collective calls; a single process returns its inputs unchanged."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(maxes), list(sums)
+    t_max = torch.tensor(list(maxes) or [0.0], dtype=torch.float64, device=device)
+    t_sum = torch.tensor(list(sums) or [0.0], dtype=torch.float64, device=device)
+    dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t_sum, op=dist.ReduceOp.SUM)
+    return t_max.tolist()[:len(maxes)], t_sum.tolist()[:len(sums)]
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -189,10 +205,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.barrier()
     ms = e0.elapsed_time(e1) / args.steps
     rows_per_step = batch.total_q
-    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
+    (ms_max,), _ = reduce_over_ranks([ms], [], dev)
     # per-kernel timings for the rooflines (CUDA events, same stream, back-to-back launches)
     op_ms = {"attention": ver.time_attention(graph.batch)}
     op_ms["attention_total"] = op_ms["attention"] * shape.layers
@@ -225,15 +238,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_end) / max(1, e2e_steps)
     wall_ms = (time.perf_counter() - t0) * 1e3 / max(1, e2e_steps)
-    e2e_t = torch.tensor([e2e_ms, e2e_rows], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_t[:1], op=dist.ReduceOp.MAX)
-        rows_all = torch.tensor([float(e2e_rows)], dtype=torch.float64, device=dev)
-        dist.all_reduce(rows_all, op=dist.ReduceOp.SUM)
-        e2e_rows_all = float(rows_all.item())
-    else:
-        e2e_rows_all = float(e2e_rows)
-    e2e_ms_max = float(e2e_t[0].item())
+    (e2e_ms_max,), (e2e_rows_all,) = reduce_over_ranks([e2e_ms], [float(e2e_rows)], dev)
     maxp = max(len(s.pages) for s in eng.sched.running)
 
     def run_cycle(linears: str) -> dict:
@@ -258,15 +263,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             c_rows += eng.stats["verified_rows"] - rows_before
         c1.record(stream)
         torch.cuda.synchronize()
-        c_t = torch.tensor([c0.elapsed_time(c1) / e2e_steps, c_rows, c_tokens], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(c_t[:1], op=dist.ReduceOp.MAX)
-            dist.all_reduce(c_t[1:], op=dist.ReduceOp.SUM)
-        c_ms = float(c_t[0].item())
+        (c_ms,), (c_rows_all, c_tokens_all) = reduce_over_ranks([c0.elapsed_time(c1) / e2e_steps],
+                                                                [float(c_rows), float(c_tokens)], dev)
         eng.graphs = {}
         return {
-            "verified_tok_s": round(float(c_t[1].item()) / e2e_steps / (c_ms * 1e-3), 2),
-            "accepted_tok_s": round(float(c_t[2].item()) / e2e_steps / (c_ms * 1e-3), 2),
+            "verified_tok_s": round(c_rows_all / e2e_steps / (c_ms * 1e-3), 2),
+            "accepted_tok_s": round(c_tokens_all / e2e_steps / (c_ms * 1e-3), 2),
             "ms_per_cycle": round(c_ms, 4),
             "draft_k": K_DRAFT,
             "draft_linears": linears,
