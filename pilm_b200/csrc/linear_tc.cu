@@ -10,7 +10,7 @@
 // CTA tile: 128 weight rows (the MMA M dimension, TMEM lanes) x up to 128 activation
 // rows (the MMA N dimension), over a range of quant groups: the CTA's contiguous range of
 // (tile, group) units under a stream-K or split schedule (below).  Warp roles
-// (704 threads); a warp reaches TMEM lanes 32 * (warp % 4) .. + 31 only:
+// (448 threads); a warp reaches TMEM lanes 32 * (warp % 4) .. + 31 only:
 //   warp 0      TMA, one thread: per group the packed weight tile [128 rows x 64 B] (raw
 //               ring) and the activation tile [Nm rows x 128 k] (two SWIZZLE_128B boxes,
 //               X ring) on one barrier; every 16th group a [128 rows x 16 groups] fp32
@@ -21,7 +21,9 @@
 //               of every group (64 packed bytes -> 128 bf16 per row) into one of four A
 //               stages (tcgen05.st).  Four stages let it run up to four groups ahead of the
 //               tensor pipe, so a stage is nearly always free when it gets there.
-//   warps 6-21  fold: four per lane quadrant, each a quarter of the activation columns.
+//   warps 6-13  fold: two per lane quadrant, each half of the activation columns (up to
+//               64 fp32 accumulators a thread in 128 registers; four warps a quadrant, each
+//               a quarter, spilled at their 80-register cap and ran 2-3% slower).
 //               For every group in order: wait for its MMAs, tcgen05.ld the partial,
 //               hand the partial buffer back to the issuer at once, then
 //               acc = acc + rn(part * s[n,g]).
@@ -52,7 +54,9 @@ constexpr int kRawBytes = kTileRows * 64;            // one group of packed weig
 constexpr int kXSubBytes = kMaxNm * 128;             // Nm rows x 64 k bf16 (max)
 constexpr int kXBytes = 2 * kXSubBytes;
 constexpr int kDqWarps = 4;                          // warps 2-5
-constexpr int kFoldWarps = 16;                       // warps 6-21
+constexpr int kFoldWarps = 8;                        // warps 6-13
+constexpr int kFoldSets = kFoldWarps / 4;            // fold warps per lane quadrant, each a column set
+constexpr int kChunksPer = (kMaxNm / 16) / kFoldSets; // 16-column chunks a fold warp holds (at most 4)
 constexpr int kThreads = (2 + kDqWarps + kFoldWarps) * 32;
 constexpr int kTBufs = 2;                            // TMEM partial buffers (kMaxNm columns each)
 constexpr int kTmemCols = 512;
@@ -481,19 +485,19 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             if (lane == 0) mbar_arrive(&bar->op_full[i % kSlots]);
         }
     } else {
-        // ---- fold: activation-column quarter fq of lane quadrant quad, every group in order ----
+        // ---- fold: activation-column set fq of lane quadrant quad, every group in order ----
         const int quad = warp & 3;
-        const int fw = warp - 2 - kDqWarps;  // 0..15
-        const int fq = fw >> 2;
+        const int fw = warp - 2 - kDqWarps;  // 0 .. kFoldWarps - 1
+        const int fq = fw >> 2;              // column set 0 .. kFoldSets - 1
         const int rloc = 32 * quad + lane;
         const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
         const int nc = p.Nm / 16;            // 16-column chunks of the partial (<= 8)
-        const int per = (nc + 3) / 4;        // chunks per quarter (<= 2)
+        const int per = (nc + kFoldSets - 1) / kFoldSets;  // chunks per set (<= kChunksPer)
         const int c_lo = fq * per, c_hi = min(nc, c_lo + per);
         const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
-        float2 acc[16];  // two 16-column chunks as fp32 pairs: one packed multiply and add per pair
+        float2 acc[8 * kChunksPer];  // 16-column chunks as fp32 pairs: one packed multiply and add per pair
 #pragma unroll
-        for (int e = 0; e < 16; ++e) acc[e] = make_float2(0.f, 0.f);
+        for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
         // partial buffers 0 and 1 start free
         __syncwarp();
         if (lane == 0)
@@ -540,12 +544,12 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // one 16-column chunk at a time (register budget); the buffer goes back to the
                 // issuer for group i + 2 as soon as the last chunk is in registers
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
+                for (int u = 0; u < kChunksPer; ++u) {
                     uint32_t r[16];
                     const bool have = c_lo + u < c_hi;
                     if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
                     tmem_ld_wait();
-                    if (u == 1) {
+                    if (u == kChunksPer - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0 && i + kTBufs < ng) mbar_arrive(&bar->op_full[(i + kTBufs) % kSlots]);
@@ -567,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             if (seg_g0 == 0 && last_g == G - 1) {
                 if (row_ok) {
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
+                    for (int u = 0; u < kChunksPer; ++u) {
                         if (c_lo + u >= c_hi) continue;
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
@@ -581,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // split partial for splitk_combine
                 if (row_ok) {
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
+                    for (int u = 0; u < kChunksPer; ++u) {
                         if (c_lo + u >= c_hi) continue;
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
@@ -596,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // warp region) sums the pieces in CTA order and writes the tile
                 float *pc = piece_of(p, cta, t) + rloc;
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
+                for (int u = 0; u < kChunksPer; ++u) {
                     if (c_lo + u >= c_hi) continue;
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -615,11 +619,11 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     __threadfence();
                     // sum = 0 + piece(k0) + piece(k0 + 1) + ... in CTA order (deterministic)
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) acc[e] = make_float2(0.f, 0.f);
+                    for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
                     for (int cc = k0; cc <= k1; ++cc) {
                         const float *pq = piece_of(p, cc, t) + rloc;
 #pragma unroll
-                        for (int u = 0; u < 2; ++u) {
+                        for (int u = 0; u < kChunksPer; ++u) {
                             if (c_lo + u >= c_hi) continue;
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
@@ -631,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     }
                     if (row_ok) {
 #pragma unroll
-                        for (int u = 0; u < 2; ++u) {
+                        for (int u = 0; u < kChunksPer; ++u) {
                             if (c_lo + u >= c_hi) continue;
 #pragma unroll
                             for (int k = 0; k < 16; ++k) {
@@ -645,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
             }
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc[e] = make_float2(0.f, 0.f);
+            for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
             // next tile: the next 128 weight rows, or the first of the next activation tile
             g = 0;
             ++t;

@@ -130,6 +130,28 @@ def test_kpairs_repack_and_linears():
             assert_bf16_close(bits_of(y), ok.linear_w4a16_bf16(x, qr, sr), ulp_frac=0.99)
 
 
+@pytest.mark.parametrize("M", [24, 96])
+@pytest.mark.parametrize("K", [512, 1152])
+def test_stream_k_schedule_vs_oracle(M, K):
+    """At least one 128-row tile per SM selects the stream-K schedule: every CTA runs an equal
+    range of (tile, group) units, so range boundaries cut tiles and the cut pieces are
+    summed in the kernel by the last CTA to arrive.  149 tiles with a ragged last one
+    (N = 19000) over 4 or 9 groups cut nearly every tile; K = 1152 also takes the group
+    scales without TMA.  Both weight layouts, twice in a row (the per-tile arrival counters
+    reset themselves)."""
+    N = 19000
+    rng = np.random.default_rng(M + K)
+    x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    qw, s = ok.quantize_i4_grouped(w, 128)
+    ref = ok.linear_w4a16g_bf16(x, qw, s, 128)
+    xd, qd, sd = bf16_from_bits(x), _t(qw), _t(s)
+    qk = ck.repack_w4_kpairs(qd)
+    for _ in range(2):
+        assert_bf16_close(bits_of(ck.linear_w4a16g128_bf16(xd, qd, sd)), ref, ulp_frac=0.99)
+        assert_bf16_close(bits_of(ck.linear_w4a16g128_bf16(xd, qk, sd, kpairs=True)), ref, ulp_frac=0.99)
+
+
 def test_kpairs_refuses_ragged_k():
     rng = np.random.default_rng(12)
     w = (rng.standard_normal((16, 200)) * 0.02).astype(np.float32)
