@@ -10,6 +10,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -28,6 +29,9 @@ struct State {
     size_t ws_bytes[pilm::kScratchSlots] = {0, 0, 0};
     int *ctr = nullptr;
     size_t ctr_n = 0;
+    // Outgrown scratch and counter buffers.  CUDA graphs captured earlier still hold
+    // their addresses, so they stay allocated until ecpu_shutdown.
+    std::vector<void *> retired;
 };
 
 State g;
@@ -180,6 +184,9 @@ void set_error(const char *fmt, ...) {
 // Scratch memory.  Each slot grows only when a request exceeds its current size;
 // growing inside stream capture is refused (the caller sees NULL and returns
 // ECPU_ERR_MEM), so graph capture must follow one eager call of the same shapes.
+// An outgrown buffer is retired, not freed: a graph captured while it was current
+// replays into it.  Each growth at least doubles the slot, so the retired buffers
+// together stay smaller than the live one.
 void *scratch(int slot, size_t bytes) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (slot < 0 || slot >= kScratchSlots) return nullptr;
@@ -187,36 +194,37 @@ void *scratch(int slot, size_t bytes) {
     cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(g.stream, &st);
     if (st != cudaStreamCaptureStatusNone) return nullptr;
-    cudaStreamSynchronize(g.stream);
-    if (g.ws[slot]) cudaFree(g.ws[slot]);
-    size_t want = bytes < (size_t)(16u << 20) ? (size_t)(16u << 20) : bytes + bytes / 4;
-    if (cudaMalloc(&g.ws[slot], want) != cudaSuccess) {
-        g.ws[slot] = nullptr;
-        g.ws_bytes[slot] = 0;
-        return nullptr;
-    }
+    size_t want = bytes + bytes / 4;
+    if (want < 2 * g.ws_bytes[slot]) want = 2 * g.ws_bytes[slot];
+    if (want < (size_t)(16u << 20)) want = (size_t)(16u << 20);
+    void *p = nullptr;
+    if (cudaMalloc(&p, want) != cudaSuccess) return nullptr;  // the current buffer stays
+    if (g.ws[slot]) g.retired.push_back(g.ws[slot]);
+    g.ws[slot] = p;
     g.ws_bytes[slot] = want;
-    return g.ws[slot];
+    return p;
 }
 
+// Zero-initialised arrival counters of the stream-K GEMM (self-resetting after each
+// launch).  Grown like scratch(): outgrown arrays are retired, not freed.
 int *counters(size_t n) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (n <= g.ctr_n) return g.ctr;
     cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(g.stream, &st);
     if (st != cudaStreamCaptureStatusNone) return nullptr;
-    cudaStreamSynchronize(g.stream);
-    if (g.ctr) cudaFree(g.ctr);
     size_t want = n < 65536 ? 65536 : n;
-    if (cudaMalloc(&g.ctr, want * sizeof(int)) != cudaSuccess) {
-        g.ctr = nullptr;
-        g.ctr_n = 0;
+    if (want < 2 * g.ctr_n) want = 2 * g.ctr_n;
+    int *p = nullptr;
+    if (cudaMalloc(&p, want * sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, want * sizeof(int)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p);
         return nullptr;
     }
-    cudaMemset(g.ctr, 0, want * sizeof(int));
-    cudaDeviceSynchronize();
+    if (g.ctr) g.retired.push_back(g.ctr);
+    g.ctr = p;
     g.ctr_n = want;
-    return g.ctr;
+    return p;
 }
 
 static unsigned long long g_launches = 0;
@@ -336,6 +344,9 @@ void ecpu_shutdown(void) {
     if (g.ctr) cudaFree(g.ctr);
     g.ctr = nullptr;
     g.ctr_n = 0;
+    cudaDeviceSynchronize();
+    for (void *p : g.retired) cudaFree(p);
+    g.retired.clear();
     edevice_shutdown_all();
     g.initialized = 0;
     g.err[0] = 0;
