@@ -34,6 +34,23 @@ def _cuda(name: str, t: torch.Tensor, dtype: torch.dtype, ndim: Optional[int] = 
     return t.contiguous()
 
 
+def _out(out: Optional[torch.Tensor], shape, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """The output buffer: a new one, or the caller's.  A caller's buffer must be a contiguous
+    tensor of the given dtype and element count on the inputs' device: the kernels write
+    through its raw pointer, so a smaller or strided buffer would be overrun."""
+    shape = tuple(int(d) for d in shape)
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    numel = 1
+    for d in shape:
+        numel *= d
+    if out.device != device or out.dtype != dtype or out.numel() != numel or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {dtype} tensor of {numel} elements {shape} on {device}, "
+                         f"got {out.dtype} {tuple(out.shape)} on {out.device}"
+                         + ("" if out.is_contiguous() else " (not contiguous)"))
+    return out
+
+
 def _check(rc: int, what: str) -> None:
     if rc != 0:
         raise RuntimeError(f"{what} failed: rc={rc}: {abi.last_error()}")
@@ -66,8 +83,7 @@ def linear_w8a32(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor,
     if wk != k or scales.shape[0] != n:
         raise ValueError(f"incompatible W8A32 shapes: x={tuple(x.shape)} qweight={tuple(qweight.shape)} "
                          f"scales={tuple(scales.shape)}")
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    out = _out(out, (m, n), torch.float32, x.device)
     _stream()
     _check(abi.linear_w8a32_ptr(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
            "ekernel_linear_w8a32")
@@ -120,8 +136,7 @@ def linear_w4a16_bf16(x, qweight, scales, in_features=None, out: Optional[torch.
                       kpairs: bool = False) -> torch.Tensor:
     """kpairs: qweight is in the k-pair nibble order (repack_w4_kpairs)."""
     x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 1, None)
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    out = _out(out, (m, n), torch.bfloat16, x.device)
     _stream()
     fn = abi.linear_w4a16_bf16_kpairs_ptr if kpairs else abi.linear_w4a16_bf16_ptr
     _check(fn(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
@@ -138,8 +153,7 @@ def linear_bf16(x: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tenso
     n, wk = weight.shape
     if wk != k:
         raise ValueError(f"incompatible bf16 linear shapes: x={tuple(x.shape)} weight={tuple(weight.shape)}")
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    out = _out(out, (m, n), torch.bfloat16, x.device)
     _stream()
     _check(abi.linear_bf16_ptr(x.data_ptr(), weight.data_ptr(), out.data_ptr(), m, n, k), "ekernel_linear_bf16")
     return out
@@ -150,8 +164,7 @@ def repack_w4_kpairs(qweight: torch.Tensor, out: Optional[torch.Tensor] = None) 
     dequantize without byte permutes (ekernel_repack_w4_kpairs); out may be qweight."""
     qweight = _cuda("qweight", qweight, torch.uint8, 2)
     n, kb = qweight.shape
-    if out is None:
-        out = torch.empty_like(qweight)
+    out = _out(out, qweight.shape, qweight.dtype, qweight.device)
     _stream()
     _check(abi.repack_w4_kpairs_ptr(qweight.data_ptr(), n, 2 * kb, out.data_ptr()), "ekernel_repack_w4_kpairs")
     return out
@@ -170,8 +183,7 @@ def linear_w4a16g128_bf16(x, qweight, scales, in_features=None, out: Optional[to
                           kpairs: bool = False) -> torch.Tensor:
     """kpairs: qweight is in the k-pair nibble order (repack_w4_kpairs)."""
     x, qweight, scales, m, n, k = _w4_common(x, qweight, scales, in_features, 2, 128)
-    if out is None:
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    out = _out(out, (m, n), torch.bfloat16, x.device)
     _stream()
     fn = abi.linear_w4a16g128_bf16_kpairs_ptr if kpairs else abi.linear_w4a16g128_bf16_ptr
     _check(fn(x.data_ptr(), qweight.data_ptr(), scales.data_ptr(), out.data_ptr(), m, n, k),
@@ -243,8 +255,7 @@ def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor, eps: float, add_one: boo
 def embedding_bf16(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     ids = _cuda("ids", ids, torch.int32, 1)
     table = _cuda("table", table, torch.bfloat16, 2)
-    if out is None:
-        out = torch.empty((ids.shape[0], table.shape[1]), dtype=torch.bfloat16, device=ids.device)
+    out = _out(out, (ids.shape[0], table.shape[1]), torch.bfloat16, ids.device)
     _stream()
     _check(abi.lib().ekernel_embedding_bf16(ids.data_ptr(), ids.shape[0], table.data_ptr(), table.shape[0],
                                             table.shape[1], out.data_ptr()), "ekernel_embedding_bf16")
@@ -257,8 +268,7 @@ def add_rmsnorm_bf16(residual: torch.Tensor, delta: Optional[torch.Tensor], weig
     if residual.device.type != "cuda" or residual.dtype != torch.bfloat16 or not residual.is_contiguous():
         raise ValueError("residual must be a contiguous CUDA bfloat16 tensor")
     rows, n = residual.shape
-    if out is None:
-        out = torch.empty_like(residual)
+    out = _out(out, residual.shape, residual.dtype, residual.device)
     _stream()
     _check(abi.lib().ekernel_add_rmsnorm_bf16(residual.data_ptr(), delta.data_ptr() if delta is not None else None,
                                               weight.data_ptr(), rows, n, float(eps), int(add_one), out.data_ptr()),
@@ -276,8 +286,7 @@ def mtp_fc_input_bf16(hidden: torch.Tensor, row_base: Optional[torch.Tensor], ro
     embed = _cuda("embed", embed, torch.bfloat16, 2)
     tokens = _cuda("tokens", tokens, torch.int32, 1)
     B, H = tokens.shape[0], hidden.shape[1]
-    if out is None:
-        out = torch.empty((B, 2 * H), dtype=torch.bfloat16, device=hidden.device)
+    out = _out(out, (B, 2 * H), torch.bfloat16, hidden.device)
     _stream()
     _check(abi.lib().ekernel_mtp_fc_input_bf16(hidden.data_ptr(), _p(row_base), _p(row_offset), embed.data_ptr(),
                                                tokens.data_ptr(), embed.shape[0], w_embed_norm.data_ptr(),
@@ -292,8 +301,7 @@ def self_attention_bf16(v: torch.Tensor, gate: Optional[torch.Tensor], n_heads: 
     sigmoid(gate) when gated)."""
     v = _cuda("v", v, torch.bfloat16, 2)
     rows = v.shape[0]
-    if out is None:
-        out = torch.empty((rows, n_heads * head_dim), dtype=torch.bfloat16, device=v.device)
+    out = _out(out, (rows, n_heads * head_dim), torch.bfloat16, v.device)
     _stream()
     _check(abi.lib().ekernel_self_attention_bf16(v.data_ptr(), _p(gate), rows, n_heads, n_kv_heads, head_dim,
                                                  out.data_ptr()), "ekernel_self_attention_bf16")
@@ -303,8 +311,7 @@ def self_attention_bf16(v: torch.Tensor, gate: Optional[torch.Tensor], n_heads: 
 def silu_mul_bf16(gate_up: torch.Tensor, inter: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     gate_up = _cuda("gate_up", gate_up, torch.bfloat16, 2)
     rows = gate_up.shape[0]
-    if out is None:
-        out = torch.empty((rows, inter), dtype=torch.bfloat16, device=gate_up.device)
+    out = _out(out, (rows, inter), torch.bfloat16, gate_up.device)
     _stream()
     _check(abi.lib().ekernel_silu_mul_bf16(gate_up.data_ptr(), rows, inter, out.data_ptr()), "ekernel_silu_mul_bf16")
     return out
@@ -344,8 +351,7 @@ def paged_attention_verify(desc, q, k_cache, v_cache, block_table, cu_q, context
 def embedding_f32(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     ids = _cuda("ids", ids, torch.int32, 1)
     table = _cuda("table", table, torch.float32, 2)
-    if out is None:
-        out = torch.empty((ids.shape[0], table.shape[1]), dtype=torch.float32, device=ids.device)
+    out = _out(out, (ids.shape[0], table.shape[1]), torch.float32, ids.device)
     _stream()
     _check(abi.lib().ekernel_embedding_f32(ids.data_ptr(), ids.shape[0], table.data_ptr(), table.shape[0],
                                            table.shape[1], out.data_ptr()), "ekernel_embedding_f32")
@@ -357,8 +363,7 @@ def add_rmsnorm_f32(residual: torch.Tensor, delta: Optional[torch.Tensor], weigh
     if residual.device.type != "cuda" or residual.dtype != torch.float32 or not residual.is_contiguous():
         raise ValueError("residual must be a contiguous CUDA float32 tensor")
     rows, n = residual.shape
-    if out is None:
-        out = torch.empty_like(residual)
+    out = _out(out, residual.shape, residual.dtype, residual.device)
     _stream()
     _check(abi.lib().ekernel_add_rmsnorm_f32(residual.data_ptr(), _p(delta), weight.data_ptr(), rows, n, float(eps),
                                              int(add_one), out.data_ptr()), "ekernel_add_rmsnorm_f32")
@@ -386,8 +391,7 @@ def paged_attention_verify_f32(desc, q, k_cache, v_cache, block_table, cu_q, con
 def silu_mul_f32(gate_up: torch.Tensor, inter: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     gate_up = _cuda("gate_up", gate_up, torch.float32, 2)
     rows = gate_up.shape[0]
-    if out is None:
-        out = torch.empty((rows, inter), dtype=torch.float32, device=gate_up.device)
+    out = _out(out, (rows, inter), torch.float32, gate_up.device)
     _stream()
     _check(abi.lib().ekernel_silu_mul_f32(gate_up.data_ptr(), rows, inter, out.data_ptr()), "ekernel_silu_mul_f32")
     return out

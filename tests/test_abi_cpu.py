@@ -74,3 +74,27 @@ def test_isa_name_table():
     lib = abi.lib()
     assert lib.ekernel_isa_name(16) == b"sm_100a"
     assert lib.ekernel_isa_name(1) == b"avx2"
+
+
+def test_wrapper_output_buffers_are_checked_before_any_launch():
+    """A caller-supplied output buffer is written through its raw pointer, so the wrappers
+    accept only a contiguous tensor of the exact element count, dtype and device; anything
+    else is refused on the host."""
+    import torch
+
+    from pilm_b200 import ckernel as ck
+
+    cpu = torch.device("cpu")
+    made = ck._out(None, (3, 4), torch.bfloat16, cpu)
+    assert made.shape == (3, 4) and made.dtype == torch.bfloat16
+    buf = torch.empty((5, 4), dtype=torch.bfloat16)
+    assert ck._out(buf[1:4], (3, 4), torch.bfloat16, cpu).data_ptr() == buf[1].data_ptr()
+    assert ck._out(buf[:3].view(12), (3, 4), torch.bfloat16, cpu).numel() == 12  # same bytes, other shape
+    with pytest.raises(ValueError, match="12 elements"):
+        ck._out(buf[:2], (3, 4), torch.bfloat16, cpu)                           # too small: would be overrun
+    with pytest.raises(ValueError):
+        ck._out(torch.empty((3, 4), dtype=torch.float32), (3, 4), torch.bfloat16, cpu)
+    with pytest.raises(ValueError, match="not contiguous"):
+        ck._out(torch.empty((4, 3), dtype=torch.bfloat16).t(), (3, 4), torch.bfloat16, cpu)
+    with pytest.raises(ValueError):
+        ck._out(torch.empty((3, 4), dtype=torch.bfloat16), (3, 4), torch.bfloat16, torch.device("meta"))
