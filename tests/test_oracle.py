@@ -77,6 +77,36 @@ def test_oracle_vs_reference_library_random_shapes():
         assert np.array_equal(ok.linear_w8a32(xf, q8, s8).view(np.uint32), reflib.linear("w8a32", xf, q8, s8).view(np.uint32))
 
 
+@pytest.mark.skipif(not reflib.available(), reason="reference library not built here")
+def test_oracle_vs_reference_library_other_kernels_random_shapes():
+    """The rest of the restated C kernels against the reference library, bit for bit, on
+    random shapes: ragged K (AVX2 tails of 1-7 values), odd K (a half-filled last byte of
+    packed int4), rows of any width for the norm, and scaled activations."""
+    rng = np.random.default_rng(23)
+    for _ in range(20):
+        M, N, K = int(rng.integers(1, 12)), int(rng.integers(1, 200)), int(rng.integers(1, 600))
+        x = ok.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32) * np.float32(rng.uniform(0.1, 5)))
+        w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        qr, sr = ok.quantize_i4_per_row(w)
+        assert np.array_equal(ok.linear_w4a16_bf16(x, qr, sr), reflib.linear("w4a16_bf16", x, qr, sr))
+        q8, s8 = ok.quantize_i8_per_row(w)
+        assert np.array_equal(ok.linear_w8a16_bf16(x, q8, s8), reflib.linear("w8a16_bf16", x, q8, s8))
+        n = int(rng.integers(1, 700))
+        xr = ok.f32_to_bf16(rng.standard_normal((M, n)).astype(np.float32) * np.float32(rng.uniform(0.01, 30)))
+        wn = ok.f32_to_bf16((1 + 0.1 * rng.standard_normal(n)).astype(np.float32))
+        for add_one in (False, True):
+            assert np.array_equal(ok.rmsnorm_bf16(xr, wn, 1e-6, add_one), reflib.rmsnorm_bf16(xr, wn, 1e-6, add_one))
+        g = ok.f32_to_bf16(rng.standard_normal(n).astype(np.float32) * 4)
+        u = ok.f32_to_bf16(rng.standard_normal(n).astype(np.float32))
+        assert np.array_equal(ok.swiglu_bf16(g, u), reflib.swiglu_bf16(g, u))
+    for H, inter in ((64, 96), (40, 136), (128, 256)):
+        x1 = ok.f32_to_bf16(rng.standard_normal((1, H)).astype(np.float32))
+        gu, gus = ok.quantize_i4_grouped((rng.standard_normal((2 * inter, H)) * 0.02).astype(np.float32), 128)
+        dq, ds = ok.quantize_i4_grouped((rng.standard_normal((H, inter)) * 0.02).astype(np.float32), 128)
+        assert np.array_equal(ok.swiglu_w4a16_bf16(x1, gu, gus, dq, ds, inter),
+                              reflib.swiglu_w4a16_bf16(x1, gu, gus, dq, ds, inter))
+
+
 @pytest.mark.parametrize("variant", G.MODEL_VARIANTS)
 def test_oracle_model_matches_reference_trace(variant):
     """Replays the reference's prefill chunk schedule, then the verify step: hidden,
