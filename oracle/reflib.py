@@ -46,6 +46,10 @@ def lib() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.argtypes = [ctypes.POINTER(LinearDesc), vp, vp, vp, vp, ctypes.c_int]
             fn.restype = ctypes.c_int
+        L.ekernel_linear_w8a16_bf16_argmax.argtypes = [ctypes.POINTER(LinearDesc), vp, vp, vp,
+                                                       ctypes.POINTER(ctypes.c_size_t),
+                                                       ctypes.POINTER(ctypes.c_float), ctypes.c_int]
+        L.ekernel_linear_w8a16_bf16_argmax.restype = ctypes.c_int
         L.ekernel_rmsnorm_bf16.argtypes = [vp, vp, vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_float, ctypes.c_int]
         L.ekernel_swiglu_bf16.argtypes = [vp, vp, vp, ctypes.c_size_t]
         L.ekernel_swiglu_w4a16_bf16.argtypes = [ctypes.POINTER(SwiGLUDesc), vp, vp, vp, vp, vp, vp, ctypes.c_int]
@@ -81,6 +85,19 @@ def linear(kind: str, x: np.ndarray, qw: np.ndarray, s: np.ndarray) -> np.ndarra
     if rc != 0:
         raise RuntimeError(f"ekernel_linear_{kind} failed: rc={rc}")
     return out
+
+
+def linear_w8a16_bf16_argmax(x: np.ndarray, qw: np.ndarray, s: np.ndarray) -> tuple[int, float]:
+    """ekernel_linear_w8a16_bf16_argmax (api.h:66-72) for one activation row: the index
+    and value of the largest output."""
+    x = np.ascontiguousarray(x, np.uint16).reshape(1, -1)
+    idx, val = ctypes.c_size_t(0), ctypes.c_float(0.0)
+    d = LinearDesc(1, qw.shape[0], x.shape[1])
+    rc = lib().ekernel_linear_w8a16_bf16_argmax(ctypes.byref(d), _p(x), _p(np.ascontiguousarray(qw)),
+                                                _p(np.ascontiguousarray(s)), ctypes.byref(idx), ctypes.byref(val), 1)
+    if rc != 0:
+        raise RuntimeError(f"ekernel_linear_w8a16_bf16_argmax failed: rc={rc}")
+    return int(idx.value), float(val.value)
 
 
 def rmsnorm_bf16(x: np.ndarray, w: np.ndarray, eps: float, add_one: bool) -> np.ndarray:

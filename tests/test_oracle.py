@@ -79,8 +79,8 @@ def test_oracle_vs_reference_library_random_shapes():
 
 @pytest.mark.skipif(not reflib.available(), reason="reference library not built here")
 def test_oracle_vs_reference_library_other_kernels_random_shapes():
-    """The rest of the restated C kernels against the reference library, bit for bit, on
-    random shapes: ragged K (AVX2 tails of 1-7 values), odd K (a half-filled last byte of
+    """The rest of the restated C kernels (the W8A16 LM-head argmax included) against the
+    reference library, bit for bit, on random shapes: ragged K (AVX2 tails of 1-7 values), odd K (a half-filled last byte of
     packed int4), rows of any width for the norm, and scaled activations."""
     rng = np.random.default_rng(23)
     for _ in range(20):
@@ -91,6 +91,8 @@ def test_oracle_vs_reference_library_other_kernels_random_shapes():
         assert np.array_equal(ok.linear_w4a16_bf16(x, qr, sr), reflib.linear("w4a16_bf16", x, qr, sr))
         q8, s8 = ok.quantize_i8_per_row(w)
         assert np.array_equal(ok.linear_w8a16_bf16(x, q8, s8), reflib.linear("w8a16_bf16", x, q8, s8))
+        got, want = ok.linear_w8a16_bf16_argmax(x[:1], q8, s8), reflib.linear_w8a16_bf16_argmax(x[:1], q8, s8)
+        assert got[0] == want[0] and np.float32(got[1]).view(np.uint32) == np.float32(want[1]).view(np.uint32)
         n = int(rng.integers(1, 700))
         xr = ok.f32_to_bf16(rng.standard_normal((M, n)).astype(np.float32) * np.float32(rng.uniform(0.01, 30)))
         wn = ok.f32_to_bf16((1 + 0.1 * rng.standard_normal(n)).astype(np.float32))
