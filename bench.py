@@ -390,18 +390,21 @@ def _ref_linear_ms(lib, M, N, K, threads_note) -> float:
     x = rng.integers(0, 65535, (M, K), dtype=np.uint16) & 0x3FFF | 0x3C00  # finite bf16 values
     qw = rng.integers(0, 256, (N, (K + 1) // 2), dtype=np.uint8)
     s = (rng.random((N, (K + 127) // 128), dtype=np.float32) * 0.01).astype(np.float32)
-    out = np.empty((M, N), np.uint16)
+    out = np.zeros((M, N), np.uint16)  # pages touched before the timed call
     d = reflib.LinearDesc(M, N, K)
+    args = (ctypes.byref(d), x.ctypes.data, qw.ctypes.data, s.ctypes.data, out.ctypes.data, 1)
+    assert lib.ekernel_linear_w4a16g128_bf16(*args) == 0  # untimed warm-up: thread pool, caches
     t0 = time.perf_counter()
-    rc = lib.ekernel_linear_w4a16g128_bf16(ctypes.byref(d), x.ctypes.data, qw.ctypes.data, s.ctypes.data,
-                                           out.ctypes.data, 1)
+    rc = lib.ekernel_linear_w4a16g128_bf16(*args)
     assert rc == 0
     return (time.perf_counter() - t0) * 1e3
 
 
 def cpu_baseline_sample(args) -> dict | None:
-    """Bounded sample: one Qwen3-8B decoder layer's five W4 g128 linears and the LM head
-    at M = 96 verify rows through the reference's ekernel_linear_w4a16g128_bf16
+    """Bounded sample: one Qwen3-8B decoder layer's seven W4 g128 linears (q, k, v, o,
+    gate, up, down) and the LM head at M = 96 verify rows, each timed on its second call
+    (the first warms the thread pool and caches), through the reference's
+    ekernel_linear_w4a16g128_bf16
     (oracle/_ref/libecpu.so, OpenMP over all host threads), plus one layer of the
     reference attention arithmetic (torch, oracle restatement) for the 32 sequences;
     extrapolated to 36 layers + head."""
@@ -463,6 +466,8 @@ def run_reference(args, rank: int) -> dict | None:
     from oracle import reflib
     if not reflib.available():
         return {"impl": "reference", "unavailable": "oracle/_ref/libecpu.so was not built (reference sources absent)"}
+    for _ in range(max(0, args.warmup)):  # untimed warm-up samples
+        cpu_baseline_sample(args)
     samples = []
     cpu = None
     for _ in range(max(1, args.steps)):
@@ -476,7 +481,7 @@ def run_reference(args, rank: int) -> dict | None:
         "unit": "verified tok/s",
         "n_gpus": 0,
         "steps": args.steps,
-        "warmup": 0,
+        "warmup": max(0, args.warmup),
         "ms_per_step": round((SEQS * (K_DRAFT + 1)) / value * 1e3, 1),
         "higher_is_better": True,
         "scaling": "weak",
