@@ -219,6 +219,12 @@ int ekernel_synchronize(void);
  * one per launch; used to report how many of the library's kernels ran in a region). */
 unsigned long long ekernel_launch_count(void);
 
+/* Number of device allocations the library has made for its own use since it was loaded
+ * (scratch buffers, stream-K counters, per-device error words; memory handed out by the
+ * device vtable's alloc is not counted).  A diagnostic: a caller can check that a region
+ * of its program made the library allocate nothing. */
+unsigned long long ekernel_alloc_count(void);
+
 /* Token embedding gather: out[r,:] = table[ids[r],:] (bf16).  Takes over
  * nn.Embedding in Qwen3Model.forward (model.py:110). */
 int ekernel_embedding_bf16(const int32_t *ids, size_t rows, const uint16_t *table, size_t vocab, size_t hidden,
@@ -311,8 +317,12 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
  * instead of library-allocated scratch, and no allocator is called.
  *  - A call whose partials would exceed 8 MiB (splits x total_q x n_heads x 520 bytes)
  *    is rejected with ECPU_ERR_PARAM and a message naming the needed size.
- *  - The first call on each device looks up the array's device address with that
- *    device current; make that first call before any stream capture.
+ *  - A page wait that gives up is recorded in a fixed device word inside the library
+ *    too (not the library's allocated error word), so no call of this entry point
+ *    allocates, including the first one in a process.
+ *  - The first call on each device looks up the device addresses of the array and of
+ *    that word with that device current; make that first call before any stream
+ *    capture.
  *  - All calls share the one array and it keeps the previous call's contents (each
  *    call resets the records it reads): calls that overlap on the GPU race, so issue
  *    them on one stream or otherwise ordered. */

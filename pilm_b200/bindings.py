@@ -40,6 +40,7 @@ KERNEL_SYMBOLS = [
     "ekernel_get_stream",
     "ekernel_synchronize",
     "ekernel_launch_count",
+    "ekernel_alloc_count",
     "ekernel_embedding_bf16",
     "ekernel_add_rmsnorm_bf16",
     "ekernel_silu_mul_bf16",
@@ -188,6 +189,7 @@ def _configure(lib) -> None:
     lib.ekernel_set_stream.argtypes = [_vp]
     lib.ekernel_get_stream.restype = _vp
     lib.ekernel_launch_count.restype = ctypes.c_ulonglong
+    lib.ekernel_alloc_count.restype = ctypes.c_ulonglong
     lib.ekernel_embedding_bf16.argtypes = [_vp, _sz, _vp, _sz, _sz, _vp]
     lib.ekernel_add_rmsnorm_bf16.argtypes = [_vp, _vp, _vp, _sz, _sz, ctypes.c_float, _i32, _vp]
     lib.ekernel_silu_mul_bf16.argtypes = [_vp, _sz, _sz, _vp]
@@ -291,6 +293,11 @@ def set_stream(stream_ptr: int) -> None:
 
 def launch_count() -> int:
     return int(_load_lib().ekernel_launch_count())
+
+
+def alloc_count() -> int:
+    """Device allocations the library has made for its own use since it was loaded."""
+    return int(_load_lib().ekernel_alloc_count())
 
 
 def synchronize() -> None:

@@ -29,6 +29,9 @@ using namespace pilm;
 // GPU that loads this library holds these bytes until the process exits.
 constexpr size_t kNoAllocAttnScratchBytes = (size_t)8 << 20;  // 8 MiB
 static __device__ __align__(256) unsigned char g_noalloc_attn_scratch[kNoAllocAttnScratchBytes];
+// The allocation-free entry point's own error word (a page wait that gave up), so that
+// it never needs the library's allocated one.
+static __device__ int g_noalloc_err_word;
 
 namespace {
 
@@ -1090,9 +1093,9 @@ int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnPara
 // Encodes the K/V tensor maps, launches attn_verify (and attn_merge when split), and in
 // synchronous mode reports a page wait that gave up.
 int launch_attention(AttnParams &p, const ekernel_paged_attn_desc_t *desc, int MT, int row_chunks, int splits,
-                     const char *what) {
-    p.err = device_error_word();
-    PILM_REQUIRE(p.err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
+                     int *err, const char *what) {
+    p.err = err;
+    PILM_REQUIRE(p.err, ECPU_ERR_MEM, "%s: no device error word", what);
     CUtensorMap maps[2];
     int rc0 = encode_kv_maps(p.kc, p.vc, p.nkv, p.num_blocks, maps, what);
     if (rc0 != ECPU_OK) return rc0;
@@ -1109,10 +1112,40 @@ int launch_attention(AttnParams &p, const ekernel_paged_attn_desc_t *desc, int M
     }
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
-    rc = check_error_word(what, "a K/V page load did not complete");
+    rc = check_error_word_at(p.err, what, "a K/V page load did not complete");
     if (rc != ECPU_OK || splits == 1) return rc;
     launch_pdl(attn_merge, dim3((unsigned)(desc->total_q * desc->n_heads)), dim3(kHD), 0, p);
     return check_launch(what);
+}
+
+// Split-KV plan of the per-head kernel: query-row tiles per KV head, KV splits and the
+// (O, m, l) records the splits leave behind.  Both attention entry points plan through
+// here, so the allocation-free variant's size check always matches what the kernel indexes.
+struct SplitPlan {
+    int MT, row_chunks, splits, pages_per_split;
+    size_t n_rec;  // split records (0 when the call is not split)
+};
+
+SplitPlan plan_splits(const ekernel_paged_attn_desc_t *desc, int gsz, int nkv) {
+    SplitPlan s;
+    const int rows = (int)(desc->max_q_len ? desc->max_q_len : 1) * gsz;
+    s.MT = rows > 16 ? 2 : 1;
+    s.row_chunks = (rows + 16 * s.MT - 1) / (16 * s.MT);
+    const int max_pages = (int)((desc->max_context + 15) / 16);
+    const int base = (int)desc->num_seqs * nkv * s.row_chunks;
+    const int target = 2 * num_sms() * 2;  // 2 resident CTAs per SM, two waves
+    int splits = (target + base - 1) / base;
+    int max_splits = max_pages / (2 * kWarps);  // at least 2 pages per warp
+    if (max_splits < 1) max_splits = 1;
+    if (splits > max_splits) splits = max_splits;
+    if (splits < 1) splits = 1;
+    s.pages_per_split = (max_pages + splits - 1) / splits;
+    if (s.pages_per_split < 1) s.pages_per_split = 1;
+    splits = (max_pages + s.pages_per_split - 1) / s.pages_per_split;
+    if (splits < 1) splits = 1;
+    s.splits = splits;
+    s.n_rec = splits > 1 ? (size_t)splits * desc->total_q * desc->n_heads : 0;
+    return s;
 }
 
 int check_desc(const ekernel_paged_attn_desc_t *d, const char *what) {
@@ -1188,36 +1221,23 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
     rc = launch_attention_pages(desc, p, what);
     if (rc != ECPU_ERR_UNSUPPORTED) return rc;
 
-    const int rows = (int)(desc->max_q_len ? desc->max_q_len : 1) * p.gsz;
-    const int MT = rows > 16 ? 2 : 1;
-    const int row_chunks = (rows + 16 * MT - 1) / (16 * MT);
-    const int max_pages = (int)((desc->max_context + 15) / 16);
-    const int base = (int)desc->num_seqs * p.nkv * row_chunks;
-    const int target = 2 * num_sms() * 2;  // 2 resident CTAs per SM, two waves
-    int splits = (target + base - 1) / base;
-    int max_splits = max_pages / (2 * kWarps);  // at least 2 pages per warp
-    if (max_splits < 1) max_splits = 1;
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-    p.pages_per_split = (max_pages + splits - 1) / splits;
-    if (p.pages_per_split < 1) p.pages_per_split = 1;
-    splits = (max_pages + p.pages_per_split - 1) / p.pages_per_split;
-    if (splits < 1) splits = 1;
-    p.splits = splits;
-    p.row_chunk = 16 * MT;
+    const SplitPlan sp = plan_splits(desc, p.gsz, p.nkv);
+    p.pages_per_split = sp.pages_per_split;
+    p.splits = sp.splits;
+    p.row_chunk = 16 * sp.MT;
     p.part_o = nullptr;
     p.part_ml = nullptr;
-    if (splits > 1) {
-        const size_t n_rec = (size_t)splits * desc->total_q * desc->n_heads;
-        char *ws = (char *)scratch(kScratchAttn, n_rec * (kHD + 2) * sizeof(float) + 256);
+    if (sp.splits > 1) {
+        char *ws = (char *)scratch(kScratchAttn, sp.n_rec * (kHD + 2) * sizeof(float) + 256);
         PILM_REQUIRE(ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
         p.part_o = (float *)ws;
-        p.part_ml = p.part_o + n_rec * kHD;
-        launch_pdl(attn_clear_ml, dim3((int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096)), dim3(256), 0, p.part_ml, n_rec * 2);
+        p.part_ml = p.part_o + sp.n_rec * kHD;
+        launch_pdl(attn_clear_ml, dim3((int)((sp.n_rec * 2 + 255) / 256 < 4096 ? (sp.n_rec * 2 + 255) / 256 : 4096)),
+                   dim3(256), 0, p.part_ml, sp.n_rec * 2);
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
-    return launch_attention(p, desc, MT, row_chunks, splits, what);
+    return launch_attention(p, desc, sp.MT, sp.row_chunks, sp.splits, device_error_word(), what);
 }
 
 }  // extern "C"
@@ -1231,33 +1251,43 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
 // or a host written in another language that only hands over buffers it already
 // owns.  For them ekernel_paged_attention_verify_noalloc takes the same inputs and
 // outputs as ekernel_paged_attention_verify but keeps its split-KV partials in
-// g_noalloc_attn_scratch, a fixed 8 MiB array compiled into the library, and calls
-// no allocator at all.  The host cannot pass g_noalloc_attn_scratch itself to a
-// kernel (in host code that name is only a host-side stand-in), so the device address
-// is looked up once per device with cudaGetSymbolAddress and cached here.
+// g_noalloc_attn_scratch, a fixed 8 MiB array compiled into the library, records a
+// page wait that gave up in g_noalloc_err_word, and calls no allocator at all.  The host
+// cannot pass either symbol itself to a kernel (in host code those names are only
+// host-side stand-ins), so their device addresses are looked up once per device with
+// cudaGetSymbolAddress and cached here.
 // ---------------------------------------------------------------------------------
 namespace {
 
 constexpr int kNoAllocMaxDevices = 64;
-void *g_noalloc_addr[kNoAllocMaxDevices];
+struct NoAllocAddrs {
+    void *scratch = nullptr;  // g_noalloc_attn_scratch on this device
+    int *err = nullptr;       // g_noalloc_err_word on this device
+};
+NoAllocAddrs g_noalloc_addr[kNoAllocMaxDevices];
 std::mutex g_noalloc_mu;
 
-// Device address of g_noalloc_attn_scratch on the current device (looked up on the
-// first call for that device, with that device current).
-int noalloc_scratch_address(void **out, const char *what) {
+// Device addresses of g_noalloc_attn_scratch and g_noalloc_err_word on the current device
+// (looked up on the first call for that device, with that device current).
+int noalloc_addresses(NoAllocAddrs *out, const char *what) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     PILM_REQUIRE(e == cudaSuccess && dev >= 0 && dev < kNoAllocMaxDevices, ECPU_ERR_DEVICE,
                  "%s: no usable current device (%s)", what, cudaGetErrorString(e));
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
-        void *ptr = nullptr;
+    NoAllocAddrs &a = g_noalloc_addr[dev];
+    if (!a.scratch || !a.err) {
+        void *ptr = nullptr, *eptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_noalloc_attn_scratch);
         PILM_REQUIRE(e == cudaSuccess && ptr, ECPU_ERR_DEVICE, "%s: cudaGetSymbolAddress failed: %s", what,
                      cudaGetErrorString(e));
-        g_noalloc_addr[dev] = ptr;
+        e = cudaGetSymbolAddress(&eptr, g_noalloc_err_word);
+        PILM_REQUIRE(e == cudaSuccess && eptr, ECPU_ERR_DEVICE, "%s: cudaGetSymbolAddress failed: %s", what,
+                     cudaGetErrorString(e));
+        a.scratch = ptr;
+        a.err = (int *)eptr;
     }
-    *out = g_noalloc_addr[dev];
+    *out = a;
     return ECPU_OK;
 }
 
@@ -1295,41 +1325,28 @@ extern "C" int ekernel_paged_attention_verify_noalloc(const ekernel_paged_attn_d
 
     // the per-head split kernel (its partials are bounded by the split count, so they fit the
     // fixed array); results agree with ekernel_paged_attention_verify within fp32 rounding
-    const int rows = (int)(desc->max_q_len ? desc->max_q_len : 1) * p.gsz;
-    const int MT = rows > 16 ? 2 : 1;
-    const int row_chunks = (rows + 16 * MT - 1) / (16 * MT);
-    const int max_pages = (int)((desc->max_context + 15) / 16);
-    const int base = (int)desc->num_seqs * p.nkv * row_chunks;
-    const int target = 2 * num_sms() * 2;
-    int splits = (target + base - 1) / base;
-    int max_splits = max_pages / (2 * kWarps);
-    if (max_splits < 1) max_splits = 1;
-    if (splits > max_splits) splits = max_splits;
-    if (splits < 1) splits = 1;
-    p.pages_per_split = (max_pages + splits - 1) / splits;
-    if (p.pages_per_split < 1) p.pages_per_split = 1;
-    splits = (max_pages + p.pages_per_split - 1) / p.pages_per_split;
-    if (splits < 1) splits = 1;
-    p.splits = splits;
-    p.row_chunk = 16 * MT;
+    const SplitPlan sp = plan_splits(desc, p.gsz, p.nkv);
+    p.pages_per_split = sp.pages_per_split;
+    p.splits = sp.splits;
+    p.row_chunk = 16 * sp.MT;
     p.part_o = nullptr;
     p.part_ml = nullptr;
-    if (splits > 1) {
-        const size_t n_rec = (size_t)splits * desc->total_q * desc->n_heads;
-        const size_t need = n_rec * (kHD + 2) * sizeof(float);
-        PILM_REQUIRE(need <= kNoAllocAttnScratchBytes, ECPU_ERR_PARAM,
-                     "%s: this call needs %zu bytes of split-KV scratch (%d splits x %zu rows x %zu heads) but the "
-                     "allocation-free variant holds at most %zu bytes; use ekernel_paged_attention_verify",
-                     what, need, splits, desc->total_q, desc->n_heads, kNoAllocAttnScratchBytes);
-        void *base_ptr = nullptr;
-        rc = noalloc_scratch_address(&base_ptr, what);
-        if (rc != ECPU_OK) return rc;
-        p.part_o = (float *)base_ptr;
-        p.part_ml = p.part_o + n_rec * kHD;
+    const size_t need = sp.n_rec * (kHD + 2) * sizeof(float);
+    PILM_REQUIRE(need <= kNoAllocAttnScratchBytes, ECPU_ERR_PARAM,
+                 "%s: this call needs %zu bytes of split-KV scratch (%d splits x %zu rows x %zu heads) but the "
+                 "allocation-free variant holds at most %zu bytes; use ekernel_paged_attention_verify",
+                 what, need, sp.splits, desc->total_q, desc->n_heads, kNoAllocAttnScratchBytes);
+    NoAllocAddrs a;
+    rc = noalloc_addresses(&a, what);
+    if (rc != ECPU_OK) return rc;
+    if (sp.splits > 1) {
+        p.part_o = (float *)a.scratch;
+        p.part_ml = p.part_o + sp.n_rec * kHD;
         // the array keeps the previous call's contents: reset every (m, l) record
-        launch_pdl(attn_clear_ml, dim3((int)((n_rec * 2 + 255) / 256 < 4096 ? (n_rec * 2 + 255) / 256 : 4096)), dim3(256), 0, p.part_ml, n_rec * 2);
+        launch_pdl(attn_clear_ml, dim3((int)((sp.n_rec * 2 + 255) / 256 < 4096 ? (sp.n_rec * 2 + 255) / 256 : 4096)),
+                   dim3(256), 0, p.part_ml, sp.n_rec * 2);
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
-    return launch_attention(p, desc, MT, row_chunks, splits, what);
+    return launch_attention(p, desc, sp.MT, sp.row_chunks, sp.splits, a.err, what);
 }

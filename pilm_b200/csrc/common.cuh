@@ -46,12 +46,14 @@ typedef CUresult (*TensorMapEncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, c
                                            const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
                                            CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 TensorMapEncodeTiledFn tensor_map_encoder();
-// Device word that pipelined kernels set when a bounded wait gave up (null if it could not
-// be allocated).  In synchronous mode check_error_word reads and clears it and turns a set
+// Device word that pipelined kernels set when a bounded wait gave up, one per device,
+// allocated on first use there (null if it could not be allocated).  In synchronous mode check_error_word reads and clears it and turns a set
 // word into ECPU_ERR_KERNEL with the message "<what>: <msg>".
 int *device_error_word();
 bool capturing();  // the library stream is being captured into a CUDA graph
 int check_error_word(const char *what, const char *msg);
+// The same check on a given error word (the allocation-free entry point's own word).
+int check_error_word_at(int *err, const char *what, const char *msg);
 
 // Post-launch check: ECPU_ERR_KERNEL on a launch error; in synchronous mode
 // (PILM_CUDA_SYNC=1) also waits for the stream and reports execution errors.

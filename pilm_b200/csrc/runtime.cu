@@ -24,7 +24,6 @@ struct State {
     char err[512] = {0};
     cudaStream_t stream = nullptr;
     int sync = -1;
-    int sms = 0;
     void *ws[pilm::kScratchSlots] = {nullptr, nullptr, nullptr};
     size_t ws_bytes[pilm::kScratchSlots] = {0, 0, 0};
     int *ctr = nullptr;
@@ -68,7 +67,6 @@ int cuda_init() {
     cudaDeviceProp p;
     if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return -1;
     if (p.major < 10) return -1;  // sm_100a kernels only
-    g.sms = p.multiProcessorCount;
     return 0;
 }
 int cuda_shutdown() { return 0; }
@@ -142,17 +140,43 @@ TensorMapEncodeTiledFn tensor_map_encoder() {
     return fn;
 }
 
+// Device allocations the library made for itself (scratch, counters, error words); the
+// vtable's alloc, which the caller asks for, is not counted.
+static unsigned long long g_lib_allocs = 0;
+
+namespace {
+constexpr int kMaxDevices = 64;
+int *g_err_word[kMaxDevices];
+int g_sms_of[kMaxDevices];
+std::mutex g_dev_mu;
+
+int current_device() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    return dev;
+}
+}  // namespace
+
+// One error word per device, allocated on that device the first time a kernel there needs
+// it (a kernel must not write another device's word).
 int *device_error_word() {
-    static int *err = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        if (cudaMalloc(&err, sizeof(int)) == cudaSuccess) cudaMemset(err, 0, sizeof(int));
-    });
-    return err;
+    const int dev = current_device();
+    if (dev < 0) return nullptr;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!g_err_word[dev]) {
+        int *w = nullptr;
+        if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) return nullptr;
+        ++g_lib_allocs;
+        if (cudaMemset(w, 0, sizeof(int)) != cudaSuccess) {
+            cudaFree(w);
+            return nullptr;
+        }
+        g_err_word[dev] = w;
+    }
+    return g_err_word[dev];
 }
 
-int check_error_word(const char *what, const char *msg) {
-    int *err = device_error_word();
+int check_error_word_at(int *err, const char *what, const char *msg) {
     if (!sync_mode() || !err || capturing()) return ECPU_OK;
     int h = 0;
     cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost);
@@ -164,14 +188,21 @@ int check_error_word(const char *what, const char *msg) {
     return ECPU_OK;
 }
 
+int check_error_word(const char *what, const char *msg) {
+    return check_error_word_at(device_error_word(), what, msg);
+}
+
+// SM count of the current device (cached per device).
 int num_sms() {
-    if (g.sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g.sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g.sms <= 0) g.sms = 148;
+    const int dev = current_device();
+    if (dev < 0) return 148;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (g_sms_of[dev] <= 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        g_sms_of[dev] = n > 0 ? n : 148;
     }
-    return g.sms;
+    return g_sms_of[dev];
 }
 
 void set_error(const char *fmt, ...) {
@@ -199,6 +230,7 @@ void *scratch(int slot, size_t bytes) {
     if (want < (size_t)(16u << 20)) want = (size_t)(16u << 20);
     void *p = nullptr;
     if (cudaMalloc(&p, want) != cudaSuccess) return nullptr;  // the current buffer stays
+    ++g_lib_allocs;
     if (g.ws[slot]) g.retired.push_back(g.ws[slot]);
     g.ws[slot] = p;
     g.ws_bytes[slot] = want;
@@ -217,6 +249,7 @@ int *counters(size_t n) {
     if (want < 2 * g.ctr_n) want = 2 * g.ctr_n;
     int *p = nullptr;
     if (cudaMalloc(&p, want * sizeof(int)) != cudaSuccess) return nullptr;
+    ++g_lib_allocs;
     if (cudaMemset(p, 0, want * sizeof(int)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(p);
         return nullptr;
@@ -383,6 +416,8 @@ int ekernel_set_stream(void *s) {
 void *ekernel_get_stream(void) { return (void *)g.stream; }
 
 unsigned long long ekernel_launch_count(void) { return pilm::g_launches; }
+
+unsigned long long ekernel_alloc_count(void) { return pilm::g_lib_allocs; }
 
 int ekernel_synchronize(void) {
     cudaError_t e = cudaStreamSynchronize(g.stream);
