@@ -38,10 +38,47 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "verified tok/s/GPU, Qwen3-8B W4A16 MTP verify; quant-GEMM HBM GB/s vs peak"
 SEQS, PROMPT, K_DRAFT, PAGE = 32, 8192, 2, 16
-# ncu capture of one attn_pages launch: 16 sequences x 8195 keys, 8 KV heads x 128 bf16,
-# DRAM read + write bytes, and the K/V bytes of that launch
-ATTN_TRAFFIC_CAPTURE = (538.756096e6 + 4.719872e6, 16 * 8195 * 8 * 128 * 2 * 2)
 GEN_HEADROOM = 512
+# the committed ncu summary of one attn_pages launch whose DRAM traffic the bench line scales
+ATTN_PROFILE = ROOT / "profiles" / "attn_pages_qwen3_8b_16seq_8k.md"
+
+
+def attn_traffic_capture() -> dict | None:
+    """DRAM read + write bytes of the attn_pages launch in ATTN_PROFILE (dram__bytes_read.sum +
+    dram__bytes_write.sum, as written there) and the K/V bytes of that launch (its title
+    line's "<seqs> seqs x <keys> keys", 8 KV heads x 128 bf16, K and V)."""
+    import re
+    try:
+        text = ATTN_PROFILE.read_text()
+    except OSError:
+        return None
+    unit = {"KB": 1e3, "MB": 1e6, "GB": 1e9}
+    got = {}
+    for name in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+        m = re.search(re.escape(name) + r"\s+([0-9.]+)\s+(KB|MB|GB)", text)
+        if not m:
+            return None
+        got[name] = float(m.group(1)) * unit[m.group(2)]
+    m = re.search(r"(\d+) seqs x (\d+) keys", text)
+    if not m:
+        return None
+    kv = int(m.group(1)) * int(m.group(2)) * 8 * 128 * 2 * 2
+    return {"bytes": got["dram__bytes_read.sum"] + got["dram__bytes_write.sum"], "kv_bytes": kv,
+            "source": f"{ATTN_PROFILE.relative_to(ROOT)} ({m.group(1)} seqs x {m.group(2)} keys), "
+                      "scaled to this launch by its K/V bytes"}
+
+
+def bench_config(layers: int, world: int, seqs: int = SEQS, prompt: int = PROMPT) -> dict:
+    """The workload both arms report (BASELINE configs[3] unless a reduced case is asked for)."""
+    full = (seqs, prompt, layers) == (32, 8192, 36)
+    return {
+        "workload": ("Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])" if full else
+                     f"reduced profiling case: {layers} layers, {seqs} seqs x {prompt} tokens"),
+        "seqs_per_gpu": seqs, "prompt_len": prompt, "layers": layers, "draft_k": K_DRAFT,
+        "rows_per_step": seqs * (K_DRAFT + 1),
+        "page_size": PAGE, "parallelism": f"replicas x{world}",
+        "l2": "inputs larger than L2 (about 40 GB KV + 4 GB weights read per step)",
+    }
 
 
 def peaks() -> dict:
@@ -305,13 +342,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     lin_ms = op_ms.get("linear_total")
     lin_gbs = lin_bytes / (lin_ms * 1e-3) / 1e9 if lin_ms else None
     step_bytes = att_bytes * shape.layers + lin_bytes + 2 * rows_per_step * shape.hidden * 2
-    # DRAM traffic of one attn_pages launch: an ncu capture of the same kernel on a
-    # 16-sequence case (dram__bytes_read.sum + dram__bytes_write.sum), scaled by this
-    # launch's K/V bytes, with which the kernel's traffic grows (it reads each K/V byte once)
+    # DRAM traffic of one attn_pages launch: the committed ncu capture of the same kernel on
+    # a 16-sequence case, scaled by this launch's K/V bytes, with which the kernel's traffic
+    # grows (it reads each K/V byte once)
     kv_bytes = sum(ctx) * shape.n_kv_heads * shape.head_dim * 2 * 2
-    traffic = round(ATTN_TRAFFIC_CAPTURE[0] * kv_bytes / ATTN_TRAFFIC_CAPTURE[1])
+    cap = attn_traffic_capture()
+    traffic = round(cap["bytes"] * kv_bytes / cap["kv_bytes"]) if cap else None
     cpu = cpu_baseline_sample(args) if not args.no_cpu else None
-    full = (SEQS, PROMPT, shape.layers) == (32, 8192, 36)
     value = rows_per_step * world / (ms_max * 1e-3)
     line = {
         "metric": METRIC,
@@ -326,14 +363,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16 activations x int4 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init weights, random prompt KV pages, random drafts)",
-        "config": {
-            "workload": ("Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])" if full else
-                         f"reduced profiling case: {shape.layers} layers, {SEQS} seqs x {PROMPT} tokens"),
-            "seqs_per_gpu": SEQS, "prompt_len": PROMPT, "layers": shape.layers, "draft_k": K_DRAFT,
-            "rows_per_step": rows_per_step,
-            "page_size": PAGE, "parallelism": f"replicas x{world}",
-            "l2": "inputs larger than L2 (about 40 GB KV + 4 GB weights read per step)",
-        },
+        "config": bench_config(shape.layers, world, SEQS, PROMPT),
         "per_gpu": round(value / world, 2),
         "e2e": {
             "value": round(e2e_rows_all / max(1, e2e_steps) / (e2e_ms_max * 1e-3), 2) if e2e_steps else None,
@@ -355,6 +385,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "unit": "GB/s",
             "frac": round(att_gbs / pk["hbm_gbs"], 4) if att_gbs else None,
             "traffic": traffic,
+            "traffic_source": cap["source"] if cap else None,
             "algorithmic_bytes_per_launch": att_bytes,
             "avg_launch_ms": round(att_ms, 5) if att_ms else None,
         },
@@ -401,13 +432,15 @@ def _ref_linear_ms(lib, M, N, K, threads_note) -> float:
 
 
 def cpu_baseline_sample(args) -> dict | None:
-    """Bounded sample: one Qwen3-8B decoder layer's seven W4 g128 linears (q, k, v, o,
-    gate, up, down) and the LM head at M = 96 verify rows, each timed on its second call
-    (the first warms the thread pool and caches), through the reference's
-    ekernel_linear_w4a16g128_bf16
-    (oracle/_ref/libecpu.so, OpenMP over all host threads), plus one layer of the
-    reference attention arithmetic (torch, oracle restatement) for the 32 sequences;
-    extrapolated to 36 layers + head."""
+    """Bounded sample of the reference's CPU verify step: one Qwen3-8B decoder layer's seven
+    W4 g128 linears (q, k, v, o, gate, up, down) and the LM head at M = 96 verify rows, each
+    timed on its second call (the first warms the thread pool and caches), through the
+    reference's ekernel_linear_w4a16g128_bf16 (oracle/_ref/libecpu.so, OpenMP over all host
+    threads), plus one layer of the reference's attention for the 32 sequences.  The
+    attention runs FullAttention.forward's arithmetic over the paged cache as the reference
+    does it, block gather by torch.cat included (attention.py:98-139), through the oracle's
+    restatement of that module (oracle/model.py attend): the reference's Python modules are
+    not on the GPU box.  The sample is one of 36 layers and is extrapolated to the step."""
     from oracle import reflib
     if not reflib.available():
         return None
@@ -418,11 +451,13 @@ def cpu_baseline_sample(args) -> dict | None:
     lib = reflib.lib()
     M = SEQS * (K_DRAFT + 1)
     H, I, V = 4096, 12288, 151936
+    t0 = time.perf_counter()
     t_layer = 0.0
     for (N, K) in ((4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (I, H), (I, H), (H, I)):
         t_layer += _ref_linear_ms(lib, M, N, K, threads)
     t_head = _ref_linear_ms(lib, M, V, H, threads)
     t_att = _cpu_attention_layer_ms()
+    sample_s = time.perf_counter() - t0
     step_ms = 36 * (t_layer + t_att) + t_head
     return {
         "value": round(M / (step_ms * 1e-3), 3),
@@ -430,37 +465,50 @@ def cpu_baseline_sample(args) -> dict | None:
         "cores": threads,
         "kind": "reference",
         "isa": reflib.isa_name(),
+        "extrapolated": True,
+        "layers_sampled": 1,
+        "sample_s": round(sample_s, 3),
+        "extrapolated_step_ms": round(step_ms, 1),
         "sample": (f"1 of 36 layers (q/k/v/o/gate/up/down W4 g128 linears at M={M} through the reference "
-                   f"ekernel_linear_w4a16g128_bf16: {t_layer:.0f} ms; torch attention of the reference "
-                   f"arithmetic over 32 seqs x {PROMPT + 3} keys: {t_att:.0f} ms) + LM head ({t_head:.0f} ms), "
-                   f"extrapolated to a {step_ms / 1e3:.1f} s step"),
+                   f"ekernel_linear_w4a16g128_bf16: {t_layer:.0f} ms; the reference's paged attention "
+                   f"arithmetic over 32 seqs x {PROMPT + K_DRAFT + 1} keys: {t_att:.0f} ms) + LM head "
+                   f"({t_head:.0f} ms), timed in {sample_s:.1f} s and extrapolated to a {step_ms / 1e3:.1f} s step"),
     }
 
 
+_ATT_CACHE = {}
+
+
 def _cpu_attention_layer_ms() -> float:
-    """One layer of the reference attention arithmetic for all sequences (oracle
-    restatement of attention.py:98-139: gather, GQA expand, bf16 bmm, softmax, bmm)."""
-    import math
+    """One layer of the reference attention for all sequences on the host: each sequence's
+    pages gathered from the paged cache by torch.cat, GQA expansion, bf16 scores, causal
+    mask over the verify rows, fp32 softmax, bf16 P.V (attention.py:98-139, restated in
+    oracle/model.py attend), over a page pool shaped like the bench's."""
     import torch
-    g = torch.Generator().manual_seed(0)
+    from oracle import model as om
     nkv, nh, hd, q = 8, 32, 128, K_DRAFT + 1
     ctx = PROMPT + q
-    k = torch.randn((ctx, nkv, hd), generator=g).to(torch.bfloat16)
-    v = torch.randn((ctx, nkv, hd), generator=g).to(torch.bfloat16)
-    qs = torch.randn((q, nh, hd), generator=g).to(torch.bfloat16)
+    pages = (ctx + PAGE - 1) // PAGE
+    if "kv" not in _ATT_CACHE:
+        g = torch.Generator().manual_seed(0)
+        nb = SEQS * pages + 1
+        _ATT_CACHE["kv"] = (torch.randn((nb, PAGE, nkv, hd), generator=g).to(torch.bfloat16),
+                            torch.randn((nb, PAGE, nkv, hd), generator=g).to(torch.bfloat16))
+        _ATT_CACHE["q"] = torch.randn((q, nh, hd), generator=g).to(torch.bfloat16)
+        _ATT_CACHE["tables"] = [list(range(1 + b * pages, 1 + (b + 1) * pages)) for b in range(SEQS)]
+    kc, vc = _ATT_CACHE["kv"]
+    cfg = om.Qwen3Config(n_heads=nh, n_kv_heads=nkv, head_dim=hd, block_size=PAGE)
     t0 = time.perf_counter()
-    for _ in range(SEQS):
-        fk = k.unsqueeze(2).expand(-1, -1, nh // nkv, -1).reshape(ctx, nh, hd).transpose(0, 1)
-        fv = v.unsqueeze(2).expand(-1, -1, nh // nkv, -1).reshape(ctx, nh, hd).transpose(0, 1)
-        s = torch.bmm(qs.transpose(0, 1), fk.transpose(1, 2)) * (1.0 / math.sqrt(hd))
-        mask = torch.triu(torch.ones(q, ctx, dtype=torch.bool), diagonal=ctx - q + 1)
-        s = s.masked_fill(mask.unsqueeze(0), float("-inf"))
-        a = torch.softmax(s.to(torch.float32), dim=-1).to(torch.bfloat16)
-        torch.bmm(a, fv)
+    for b in range(SEQS):
+        om.attend(cfg, _ATT_CACHE["q"], None, kc, vc, _ATT_CACHE["tables"][b], ctx, True)
     return (time.perf_counter() - t0) * 1e3
 
 
-def run_reference(args, rank: int) -> dict | None:
+def run_reference(args, rank: int, world: int = 1) -> dict | None:
+    """The reference arm: rank 0 times cpu_baseline_sample --steps times (after --warmup
+    untimed samples); each step is one bounded sample, and `value` is the median sample's
+    extrapolated verified tok/s.  ms_per_step is the measured wall time of one sample, so
+    steps x ms_per_step is the timed region; extrapolated_step_ms is the full step."""
     if rank != 0:
         return None
     from oracle import reflib
@@ -469,29 +517,30 @@ def run_reference(args, rank: int) -> dict | None:
     for _ in range(max(0, args.warmup)):  # untimed warm-up samples
         cpu_baseline_sample(args)
     samples = []
-    cpu = None
     for _ in range(max(1, args.steps)):
-        cpu = cpu_baseline_sample(args)
-        samples.append(cpu["value"])
-    value = statistics.median(samples)
+        samples.append(cpu_baseline_sample(args))
+    samples.sort(key=lambda c: c["value"])
+    cpu = samples[len(samples) // 2]
+    value = cpu["value"]
     return {
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": "verified tok/s",
         "n_gpus": 0,
-        "steps": args.steps,
+        "steps": len(samples),
         "warmup": max(0, args.warmup),
-        "ms_per_step": round((SEQS * (K_DRAFT + 1)) / value * 1e3, 1),
+        "ms_per_step": round(statistics.mean(c["sample_s"] for c in samples) * 1e3, 1),
+        "extrapolated": True,
+        "layers_sampled": 1,
+        "extrapolated_step_ms": cpu["extrapolated_step_ms"],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16 activations x int4 weights, fp32 accumulate (AVX2)",
         "data": "synthetic",
-        "config": {"workload": "Qwen3-8B-shaped W4A16 g128 MTP verify step (BASELINE configs[3])",
-                   "seqs_per_gpu": SEQS, "prompt_len": PROMPT, "draft_k": K_DRAFT,
-                   "rows_per_step": SEQS * (K_DRAFT + 1)},
-        "cpu_baseline": dict(cpu, value=value),
+        "config": bench_config(36, world),
+        "cpu_baseline": dict(cpu),
         "e2e": {"value": value, "unit": "verified tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -768,7 +817,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        line = run_reference(args, rank)
+        line = run_reference(args, rank, world)
         if line is not None:
             print(json.dumps(line), flush=True)
         return
