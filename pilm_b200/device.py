@@ -55,6 +55,9 @@ class CudaDevice:
     def memcpy_d2h(self, dst: int, src: int, n: int) -> None:
         self._fn("memcpy_d2h", None, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t)(dst, src, n)
 
+    def memcpy_d2d(self, dst: int, src: int, n: int) -> None:
+        self._fn("memcpy_d2d", None, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t)(dst, src, n)
+
     def synchronize(self) -> int:
         return self._fn("synchronize", ctypes.c_int)()
 

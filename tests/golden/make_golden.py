@@ -33,7 +33,8 @@ import numpy as np
 import torch
 
 REPO = Path(__file__).resolve().parents[2]
-REF_SRC = Path(os.environ.get("PILM_REF_SRC", "/root/reference/src"))
+# the reference's src/ tree: PILM_REF_SRC, else a reference checkout beside this repository
+REF_SRC = Path(os.environ.get("PILM_REF_SRC") or Path(__file__).resolve().parents[3] / "reference" / "src")
 OUT = Path(__file__).resolve().parent
 
 os.environ["PILM_ECPU_LIB"] = str(REPO / "oracle" / "_ref" / "libecpu.so")
