@@ -358,17 +358,26 @@ int ekernel_verify_accept_greedy(const ekernel_accept_desc_t *desc, const int32_
                                  const int32_t *top1, const int32_t *cu_q, int32_t *accept_counts,
                                  int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
 
-/* Rejection-sampling acceptance (no reference implementation; standard speculative
- * sampling with a one-hot greedy draft).  p_i = softmax(logits_i / temperature)
- * restricted to the nucleus {j : mass of strictly more probable tokens < top_p},
- * renormalised.  Draft d_i is accepted iff uniforms[row,0] < p_i(d_i); at the first
- * rejection the next token is sampled (inverse CDF in index order with
- * uniforms[row,1]) from p_i with d_i removed, else the bonus row's p_n.  Outputs and
- * rollback as in ekernel_verify_accept_greedy. */
+/* Rejection-sampling acceptance (no reference implementation: the reference verifies
+ * greedily only, engine.py:373-379; this is standard speculative sampling with a one-hot
+ * greedy draft).  p_i = softmax(logits_i / temperature) restricted to the nucleus
+ * {j : mass of strictly more probable tokens < top_p}, renormalised.  Draft d_i is
+ * accepted iff uniforms[row,0] < p_i(d_i); at the first rejection the next token is
+ * sampled (inverse CDF in index order with uniforms[row,1]) from p_i with d_i removed,
+ * else the bonus row's p_n.  Outputs and rollback as in ekernel_verify_accept_greedy.
+ * Masses are summed in 64-bit fixed point (2^-40), so results do not depend on the
+ * order of summation.  vocab < 2^23. */
 int ekernel_verify_accept_rejection(const ekernel_accept_desc_t *desc, const float *logits,
                                     const int32_t *verify_ids, const int32_t *cu_q, const float *uniforms,
                                     float temperature, float top_p, int32_t *accept_counts,
                                     int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
+
+/* The same over bf16 logits (the LM head's output, read as fp32 like the reference's
+ * lm_head(h).float(), engine.py:480). */
+int ekernel_verify_accept_rejection_bf16(const ekernel_accept_desc_t *desc, const uint16_t *logits,
+                                         const int32_t *verify_ids, const int32_t *cu_q, const float *uniforms,
+                                         float temperature, float top_p, int32_t *accept_counts,
+                                         int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
 
 /* ---- fp32-activation verify path (model dtype float32: the W8A32 configuration,
  * QuantizedW8A32Linear, linear.py:188-233).  The bf16 operations above with every

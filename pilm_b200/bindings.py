@@ -51,6 +51,7 @@ KERNEL_SYMBOLS = [
     "ekernel_argmax_top2_bf16",
     "ekernel_verify_accept_greedy",
     "ekernel_verify_accept_rejection",
+    "ekernel_verify_accept_rejection_bf16",
     "ekernel_linear_bf16",
     "ekernel_repack_w4_kpairs",
     "ekernel_linear_w4a16g128_bf16_kpairs",
@@ -209,6 +210,7 @@ def _configure(lib) -> None:
     lib.ekernel_verify_accept_greedy.argtypes = [ctypes.POINTER(AcceptDesc)] + [_vp] * 7
     lib.ekernel_verify_accept_rejection.argtypes = ([ctypes.POINTER(AcceptDesc)] + [_vp] * 4 +
                                                     [ctypes.c_float, ctypes.c_float] + [_vp] * 4)
+    lib.ekernel_verify_accept_rejection_bf16.argtypes = lib.ekernel_verify_accept_rejection.argtypes
 
 
 def lib():

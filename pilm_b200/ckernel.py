@@ -423,14 +423,22 @@ def verify_accept_greedy(num_seqs, verify_ids, top1, cu_q, accept_counts, next_t
 
 def verify_accept_rejection(num_seqs, logits, verify_ids, cu_q, uniforms, temperature, top_p, accept_counts,
                             next_tokens, context_lens, slot_mapping=None) -> None:
+    """Rejection-sampling acceptance over fp32 or bf16 logits [total_q, vocab] with
+    uniforms [total_q, 2] fp32 (accept test, sample) per row."""
     import ctypes
-    logits = _cuda("logits", logits, torch.float32, 2)
+    if logits.dtype == torch.bfloat16:
+        logits = _cuda("logits", logits, torch.bfloat16, 2)
+        fn, name = abi.lib().ekernel_verify_accept_rejection_bf16, "ekernel_verify_accept_rejection_bf16"
+    else:
+        logits = _cuda("logits", logits, torch.float32, 2)
+        fn, name = abi.lib().ekernel_verify_accept_rejection, "ekernel_verify_accept_rejection"
+    uniforms = _cuda("uniforms", uniforms, torch.float32, 2)
+    if uniforms.shape != (logits.shape[0], 2):
+        raise ValueError(f"uniforms must be [{logits.shape[0]}, 2], got {tuple(uniforms.shape)}")
     d = abi.AcceptDesc(num_seqs, logits.shape[0], logits.shape[1])
     _stream()
-    _check(abi.lib().ekernel_verify_accept_rejection(ctypes.byref(d), logits.data_ptr(), _p(verify_ids), _p(cu_q),
-                                                     _p(uniforms), float(temperature), float(top_p),
-                                                     _p(accept_counts), _p(next_tokens), _p(context_lens),
-                                                     _p(slot_mapping)), "ekernel_verify_accept_rejection")
+    _check(fn(ctypes.byref(d), logits.data_ptr(), _p(verify_ids), _p(cu_q), _p(uniforms), float(temperature),
+              float(top_p), _p(accept_counts), _p(next_tokens), _p(context_lens), _p(slot_mapping)), name)
 
 
 # ---------------------------------------------------------------------------------------

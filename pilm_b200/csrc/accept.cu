@@ -155,20 +155,34 @@ __global__ void greedy_accept(int B, const int32_t *__restrict__ ids, const int3
 }
 
 // ---------------------------------------------------------------------------------
-// Rejection sampling
+// Rejection sampling (standard speculative sampling with a one-hot greedy draft; the
+// reference has none).  Two kernels:
+//   rs_row_stats     one CTA per verify row, all rows in parallel: the row's target
+//                    distribution p = softmax(l / T) restricted to the nucleus {j : mass of
+//                    strictly more probable tokens < top_p}, as its max logit, the nucleus
+//                    cut (the smallest order-preserving key kept) and nucleus mass, and the
+//                    mass of the draft that the row verifies
+//   rs_decide_sample one CTA per sequence: the accept tests u < p(d) row by row from those
+//                    statistics, then the next token by inverse CDF in token-index order
+//                    from the first rejected row with its draft removed, or from the bonus
+//                    row, and the rollback
+// Masses e_j = exp((l_j - mx) / T) <= 1 are summed in unsigned 64-bit fixed point with 40
+// fractional bits.  Integer sums do not depend on the order of summation, so every pass,
+// thread count and launch agrees exactly; V < 2^23 keeps them below 2^63.  The nucleus cut
+// comes from a radix select over the 32-bit keys in three passes (11 + 11 + 10 bits):
+// each pass histograms the masses of the keys in the current bucket by their next digit,
+// so a row costs four reads (max and three histograms) instead of a bisection's ~34.
 // ---------------------------------------------------------------------------------
 constexpr int kRsThreads = 1024;
+constexpr int kRsBins = 2048;
+constexpr double kFix = 1099511627776.0;  // 2^40
 
-__device__ __forceinline__ float block_sum(float v, float *sh) {
-    v = warp_sum(v);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
-    if (lane == 0) sh[warp] = v;
-    __syncthreads();
-    float t = (lane < (int)(blockDim.x >> 5)) ? sh[lane] : 0.f;
-    t = warp_sum(t);
-    return t;
-}
+struct RsRow {
+    float mx;               // max logit
+    uint32_t cut;           // keys >= cut are in the nucleus
+    unsigned long long zn;  // nucleus mass (fixed point)
+    unsigned long long ed;  // mass of the draft this row verifies if in the nucleus, else 0
+};
 
 __device__ __forceinline__ float block_max(float v, float *sh) {
     v = warp_max(v);
@@ -186,121 +200,144 @@ __device__ __forceinline__ uint32_t fkey(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-struct Nucleus {
-    float mx;      // max logit
-    uint32_t cut;  // tokens with fkey(logit) >= cut are in the nucleus
-    float z;       // sum of e_j over the nucleus, e_j = exp((l_j - mx) / T)
-};
-
-// Nucleus of softmax(l / T): {j : mass of strictly more probable tokens < top_p}.
-// Bisection over the ordered float keys finds the smallest cut whose strictly-above
-// mass is < top_p * Z; every token at or above it is kept (ties kept together).
-__device__ Nucleus find_nucleus(const float *x, int V, float T, float top_p, float *sh) {
-    float mx = -INFINITY;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, x[i]);
-    mx = block_max(mx, sh);
-    float z = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) z += expf(__fdiv_rn(x[i] - mx, T));
-    z = block_sum(z, sh);
-    const float target = top_p * z;
-    // smallest key k such that mass(l > key^-1(k-1)...) : search cut in [lo, hi]
-    uint32_t lo = 0u, hi = fkey(mx);  // cut = hi keeps only the maxima (always valid)
-    while (lo < hi) {
-        const uint32_t mid = lo + ((hi - lo) >> 1);
-        // mass strictly above the candidate cut value `mid` must be < target for the
-        // token(s) at `mid` to be kept; keep searching lower cuts while that holds
-        float above = 0.f;
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            const float l = x[i];
-            if (fkey(l) > mid) above += expf(__fdiv_rn(l - mx, T));
-        }
-        above = block_sum(above, sh);
-        if (above < target)
-            hi = mid;
-        else
-            lo = mid + 1;
-    }
-    // `hi` is the smallest key whose strictly-above mass is < target; the nucleus is
-    // every token with key >= the smallest existing key >= hi
-    float zn = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float l = x[i];
-        if (fkey(l) >= hi) zn += expf(__fdiv_rn(l - mx, T));
-    }
-    zn = block_sum(zn, sh);
-    return Nucleus{mx, hi, zn};
+template <typename T>
+__device__ __forceinline__ float logit_at(const T *x, int i) {
+    if constexpr (sizeof(T) == 2) return __bfloat162float(x[i]);
+    else return x[i];
 }
 
-// Inverse-CDF sample in index order over the nucleus with token `skip` removed:
-// smallest j with cumsum(e_j) > u * (sum e_j).  Falls back to the last nonzero index.
-__device__ int sample_index(const float *x, int V, float T, const Nucleus &nu, int skip, float u, float *sh,
-                            float *scan) {
-    const int chunk = (V + blockDim.x - 1) / blockDim.x;
-    const int i0 = threadIdx.x * chunk, i1 = min(V, i0 + chunk);
-    float s = 0.f;
-    int last = -1;
-    for (int i = i0; i < i1; ++i) {
-        const float l = x[i];
-        if (i != skip && fkey(l) >= nu.cut) {
-            s += expf(__fdiv_rn(l - nu.mx, T));
-            last = i;
+__device__ __forceinline__ unsigned long long fix_mass(float l, float mx, float T) {
+    const float e = expf(__fdiv_rn(l - mx, T));  // in [0, 1]
+    return __double2ull_rn((double)e * kFix);
+}
+
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Inclusive suffix sums of `bins` values held two per thread (bins 2t, 2t + 1), in
+// shared memory: sfx[d] = sum of bins[d..].  Block of kRsThreads, kRsBins = 2 x threads.
+__device__ void suffix_sums(const unsigned long long *bins, unsigned long long *sfx, unsigned long long *wsum) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    // reverse order: thread t handles bins kRsBins-1-2t and kRsBins-2-2t, so a prefix scan
+    // over threads is a suffix scan over bins
+    const int hi = kRsBins - 1 - 2 * t, lo = hi - 1;
+    const unsigned long long a = bins[hi], b = bins[lo];
+    unsigned long long v = a + b, x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned long long w = wsum[lane], z = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long y = __shfl_up_sync(0xffffffffu, z, o);
+            if (lane >= o) z += y;
         }
+        wsum[lane] = z - w;  // exclusive over warps
     }
-    // exclusive scan of the chunk sums (sequential over threads for determinism)
     __syncthreads();
-    scan[threadIdx.x] = s;
+    const unsigned long long before = wsum[warp] + x - v;  // sum of bins above `hi`
+    sfx[hi] = before + a;
+    sfx[lo] = before + a + b;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float run = 0.f;
-        for (int t = 0; t < (int)blockDim.x; ++t) {
-            const float v = scan[t];
-            scan[t] = run;
-            run += v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__ logits, int rows, int V,
+                                                            const int32_t *__restrict__ ids, float temp, float top_p,
+                                                            RsRow *__restrict__ out) {
+    pdl_entry();
+    __shared__ float shf[32];
+    __shared__ unsigned long long hist[kRsBins];
+    __shared__ unsigned long long sfx[kRsBins];
+    __shared__ unsigned long long wsum[32];
+    __shared__ int s_digit;
+    const int r = blockIdx.x;
+    const T *x = logits + (size_t)r * V;
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, logit_at(x, i));
+    mx = block_max(mx, shf);
+
+    // radix select of the cut: the lowest present key whose strictly-above mass is < top_p Z
+    constexpr int kBits[3] = {11, 11, 10};
+    uint32_t prefix = 0;           // digits chosen so far
+    int consumed = 0;              // key bits chosen so far
+    unsigned long long above = 0;  // mass of the keys above the current bucket
+    double target = 0.0;
+    unsigned long long at_cut = 0;
+    for (int lv = 0; lv < 3; ++lv) {
+        const int bits = kBits[lv];
+        const int shift = 32 - consumed - bits;
+        for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) hist[d] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < V; i += blockDim.x) {
+            const float l = logit_at(x, i);
+            const uint32_t k = fkey(l);
+            if (consumed == 0 || (k >> (32 - consumed)) == prefix)
+                atomicAdd(&hist[(k >> shift) & ((1u << bits) - 1)], fix_mass(l, mx, temp));
         }
-        scan[blockDim.x] = run;
-    }
-    __syncthreads();
-    const float total = scan[blockDim.x];
-    const float target = u * total;
-    __shared__ int s_pick;
-    __shared__ int s_last;
-    if (threadIdx.x == 0) {
-        s_pick = 0x7fffffff;
-        s_last = -1;
-    }
-    __syncthreads();
-    if (last >= 0) atomicMax(&s_last, last);
-    const float before = scan[threadIdx.x];
-    if (before <= target && before + s > target) {
-        float run = before;
-        for (int i = i0; i < i1; ++i) {
-            const float l = x[i];
-            if (i != skip && fkey(l) >= nu.cut) {
-                run += expf(__fdiv_rn(l - nu.mx, T));
-                if (run > target) {
-                    atomicMin(&s_pick, i);
+        __syncthreads();
+        suffix_sums(hist, sfx, wsum);
+        if (lv == 0) target = (double)top_p * (double)sfx[0];  // top_p x total mass
+        // the lowest non-empty digit whose above-mass (above + bins strictly higher) < target
+        if (threadIdx.x == 0) s_digit = kRsBins;
+        __syncthreads();
+        for (int d = threadIdx.x; d < (1 << bits); d += blockDim.x) {
+            const unsigned long long higher = above + sfx[d] - hist[d];
+            if (hist[d] && (double)higher < target) atomicMin(&s_digit, d);
+        }
+        __syncthreads();
+        int dg = s_digit;
+        if (dg == kRsBins) {  // no mass below target (top_p rounding at the maxima): keep the top digit
+            dg = 0;
+            for (int d = (1 << bits) - 1; d >= 0; --d)
+                if (hist[d]) {
+                    dg = d;
                     break;
                 }
+        }
+        above += sfx[dg] - hist[dg];
+        at_cut = hist[dg];
+        prefix = (prefix << bits) | (uint32_t)dg;
+        consumed += bits;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        RsRow o;
+        o.mx = mx;
+        o.cut = prefix;
+        o.zn = above + at_cut;
+        o.ed = 0;
+        if (r + 1 < rows) {
+            const int d = ids[r + 1];
+            if (d >= 0 && d < V) {
+                const float l = logit_at(x, d);
+                if (fkey(l) >= prefix) o.ed = fix_mass(l, mx, temp);
             }
         }
+        out[r] = o;
     }
-    __syncthreads();
-    int pick = s_pick;
-    if (pick == 0x7fffffff) pick = s_last;
-    __syncthreads();
-    return pick;
 }
 
-// one CTA per sequence
-__global__ void __launch_bounds__(kRsThreads) rejection_accept(const float *__restrict__ logits, int V,
+template <typename T>
+__global__ void __launch_bounds__(kRsThreads) rs_decide_sample(const T *__restrict__ logits, int V,
                                                                 const int32_t *__restrict__ ids,
                                                                 const int32_t *__restrict__ cu_q,
-                                                                const float *__restrict__ uni, float T, float top_p,
+                                                                const float *__restrict__ uni, float temp,
+                                                                const RsRow *__restrict__ stats,
                                                                 int32_t *__restrict__ acc_out,
                                                                 int32_t *__restrict__ next_out,
                                                                 int32_t *__restrict__ ctx, int32_t *__restrict__ slots) {
-    __shared__ float sh[32];
-    __shared__ float scan[kRsThreads + 1];
+    pdl_entry();
+    __shared__ unsigned long long wsum[32];
+    __shared__ int s_row, s_skip, s_acc, s_pick, s_last;
     const int b = blockIdx.x;
     const int q0 = cu_q[b], q_len = cu_q[b + 1] - q0;
     if (q_len <= 0) {
@@ -310,32 +347,120 @@ __global__ void __launch_bounds__(kRsThreads) rejection_accept(const float *__re
         }
         return;
     }
-    int acc = 0, next = -1;
-    for (int i = 0; i < q_len; ++i) {
-        const float *x = logits + (size_t)(q0 + i) * V;
-        const Nucleus nu = find_nucleus(x, V, T, top_p, sh);
-        if (i == q_len - 1) {  // bonus row: every draft accepted
-            next = sample_index(x, V, T, nu, -1, uni[(size_t)(q0 + i) * 2 + 1], sh, scan);
+    if (threadIdx.x == 0) {
+        int acc = 0, row = q0 + q_len - 1, skip = -1;
+        for (int i = 0; i + 1 < q_len; ++i) {
+            const RsRow st = stats[q0 + i];
+            const double pd = st.zn ? (double)st.ed / (double)st.zn : 0.0;
+            if ((double)uni[(size_t)(q0 + i) * 2] < pd) {
+                ++acc;
+                continue;
+            }
+            row = q0 + i;
+            skip = ids[q0 + 1 + i];
             break;
         }
-        const int d = ids[q0 + 1 + i];
-        float pd = 0.f;
-        if (d >= 0 && d < V && fkey(x[d]) >= nu.cut) pd = __fdiv_rn(expf(__fdiv_rn(x[d] - nu.mx, T)), nu.z);
-        if (uni[(size_t)(q0 + i) * 2 + 0] < pd) {
-            ++acc;
-            continue;
-        }
-        next = sample_index(x, V, T, nu, d, uni[(size_t)(q0 + i) * 2 + 1], sh, scan);
-        if (next < 0) next = sample_index(x, V, T, nu, -1, uni[(size_t)(q0 + i) * 2 + 1], sh, scan);
-        break;
+        s_row = row;
+        s_skip = skip;
+        s_acc = acc;
+        s_pick = 0x7fffffff;
+        s_last = -1;
     }
+    __syncthreads();
+    const int row = s_row;
+    const RsRow st = stats[row];
+    int skip = s_skip;
+    unsigned long long total = st.zn;
+    if (skip >= 0) {
+        if (st.ed == st.zn) skip = -1;  // the draft was the whole nucleus: sample from p itself
+        else total -= st.ed;
+    }
+    const T *x = logits + (size_t)row * V;
+    // chunk sums over contiguous index ranges, then the chunk that crosses u x total
+    const int chunk = (V + blockDim.x - 1) / blockDim.x;
+    const int i0 = threadIdx.x * chunk, i1 = min(V, i0 + chunk);
+    unsigned long long s = 0;
+    int last = -1;
+    for (int i = i0; i < i1; ++i) {
+        const float l = logit_at(x, i);
+        if (i != skip && fkey(l) >= st.cut) {
+            s += fix_mass(l, st.mx, temp);
+            last = i;
+        }
+    }
+    if (last >= 0) atomicMax(&s_last, last);
+    // exclusive prefix over threads
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned long long incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned long long w = wsum[lane], z = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long y = __shfl_up_sync(0xffffffffu, z, o);
+            if (lane >= o) z += y;
+        }
+        wsum[lane] = z - w;
+    }
+    __syncthreads();
+    const unsigned long long before = wsum[warp] + incl - s;
+    const double target = (double)uni[(size_t)row * 2 + 1] * (double)total;
+    if ((double)before <= target && (double)(before + s) > target) {
+        unsigned long long run = before;
+        for (int i = i0; i < i1; ++i) {
+            const float l = logit_at(x, i);
+            if (i != skip && fkey(l) >= st.cut) {
+                run += fix_mass(l, st.mx, temp);
+                if ((double)run > target) {
+                    atomicMin(&s_pick, i);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
+        const int acc = s_acc;
+        const int next = s_pick != 0x7fffffff ? s_pick : s_last;
         acc_out[b] = acc;
         next_out[b] = next;
         ctx[b] = ctx[b] - q_len + 1 + acc;
         if (slots)
             for (int j = 1 + acc; j < q_len; ++j) slots[q0 + j] = -1;
     }
+}
+
+template <typename T>
+int launch_rejection(const ekernel_accept_desc_t *desc, const T *logits, const int32_t *verify_ids,
+                     const int32_t *cu_q, const float *uniforms, float temperature, float top_p,
+                     int32_t *accept_counts, int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping,
+                     const char *what) {
+    PILM_REQUIRE(desc && logits && verify_ids && cu_q && uniforms && accept_counts && next_tokens && context_lens,
+                 ECPU_ERR_PARAM, "%s: null argument", what);
+    PILM_REQUIRE(temperature > 0.f && top_p > 0.f && top_p <= 1.f, ECPU_ERR_PARAM,
+                 "%s: temperature must be > 0 and top_p in (0, 1]", what);
+    PILM_REQUIRE(desc->vocab > 0 && desc->vocab < (1u << 23), ECPU_ERR_PARAM, "%s: vocab must be in [1, 2^23)", what);
+    PILM_REQUIRE(desc->total_q <= 0x7fffffff, ECPU_ERR_PARAM, "%s: too many rows", what);
+    if (desc->num_seqs == 0) return ECPU_OK;
+    RsRow *stats = nullptr;
+    if (desc->total_q > 0) {
+        stats = (RsRow *)scratch(kScratchAccept, desc->total_q * sizeof(RsRow));
+        PILM_REQUIRE(stats, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+        launch_pdl(rs_row_stats<T>, dim3((unsigned)desc->total_q), dim3(kRsThreads), 0, logits, (int)desc->total_q,
+                   (int)desc->vocab, verify_ids, temperature, top_p, stats);
+        const int rc = check_launch(what);
+        if (rc != ECPU_OK) return rc;
+    }
+    launch_pdl(rs_decide_sample<T>, dim3((unsigned)desc->num_seqs), dim3(kRsThreads), 0, logits, (int)desc->vocab,
+               verify_ids, cu_q, uniforms, temperature, (const RsRow *)stats, accept_counts, next_tokens,
+               context_lens, slot_mapping);
+    return check_launch(what);
 }
 
 }  // namespace
@@ -377,17 +502,17 @@ int ekernel_verify_accept_rejection(const ekernel_accept_desc_t *desc, const flo
                                     const int32_t *verify_ids, const int32_t *cu_q, const float *uniforms,
                                     float temperature, float top_p, int32_t *accept_counts, int32_t *next_tokens,
                                     int32_t *context_lens, int32_t *slot_mapping) {
-    PILM_REQUIRE(desc && logits && verify_ids && cu_q && uniforms && accept_counts && next_tokens && context_lens,
-                 ECPU_ERR_PARAM, "ekernel_verify_accept_rejection: null argument");
-    PILM_REQUIRE(temperature > 0.f && top_p > 0.f && top_p <= 1.f, ECPU_ERR_PARAM,
-                 "ekernel_verify_accept_rejection: temperature must be > 0 and top_p in (0, 1]");
-    PILM_REQUIRE(desc->vocab > 0 && desc->vocab <= 0x7fffffff, ECPU_ERR_PARAM,
-                 "ekernel_verify_accept_rejection: bad vocab");
-    if (desc->num_seqs == 0) return ECPU_OK;
-    rejection_accept<<<(unsigned)desc->num_seqs, kRsThreads, 0, stream()>>>(
-        logits, (int)desc->vocab, verify_ids, cu_q, uniforms, temperature, top_p, accept_counts, next_tokens,
-        context_lens, slot_mapping);
-    return check_launch("ekernel_verify_accept_rejection");
+    return launch_rejection(desc, logits, verify_ids, cu_q, uniforms, temperature, top_p, accept_counts, next_tokens,
+                            context_lens, slot_mapping, "ekernel_verify_accept_rejection");
+}
+
+int ekernel_verify_accept_rejection_bf16(const ekernel_accept_desc_t *desc, const uint16_t *logits,
+                                         const int32_t *verify_ids, const int32_t *cu_q, const float *uniforms,
+                                         float temperature, float top_p, int32_t *accept_counts,
+                                         int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping) {
+    return launch_rejection(desc, (const __nv_bfloat16 *)logits, verify_ids, cu_q, uniforms, temperature, top_p,
+                            accept_counts, next_tokens, context_lens, slot_mapping,
+                            "ekernel_verify_accept_rejection_bf16");
 }
 
 }  // extern "C"

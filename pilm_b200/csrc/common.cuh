@@ -24,7 +24,7 @@ int num_sms();
 void set_error(const char *fmt, ...);
 // Device scratch owned by the library, one independent buffer per slot so nested
 // calls never alias (grown on demand, never inside stream capture).
-enum ScratchSlot { kScratchSplitK = 0, kScratchAux = 1, kScratchAttn = 2, kScratchSlots = 3 };
+enum ScratchSlot { kScratchSplitK = 0, kScratchAux = 1, kScratchAttn = 2, kScratchAccept = 3, kScratchSlots = 4 };
 void *scratch(int slot, size_t bytes);
 inline void *workspace(size_t bytes) { return scratch(kScratchSplitK, bytes); }
 int *counters(size_t n);  // zero-initialised, self-resetting arrival counters

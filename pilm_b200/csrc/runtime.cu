@@ -24,8 +24,8 @@ struct State {
     char err[512] = {0};
     cudaStream_t stream = nullptr;
     int sync = -1;
-    void *ws[pilm::kScratchSlots] = {nullptr, nullptr, nullptr};
-    size_t ws_bytes[pilm::kScratchSlots] = {0, 0, 0};
+    void *ws[pilm::kScratchSlots] = {};
+    size_t ws_bytes[pilm::kScratchSlots] = {};
     int *ctr = nullptr;
     size_t ctr_n = 0;
     // Outgrown scratch and counter buffers.  CUDA graphs captured earlier still hold

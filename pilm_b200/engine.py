@@ -53,7 +53,8 @@ class MTPVerifyEngine:
     def __init__(self, verifier: Qwen3Verifier, num_blocks: int, block_size: int = 16, max_model_len: int = 65536,
                  max_pages_per_seq: Optional[int] = None, pin_memory: bool = True,
                  max_num_batched_tokens: int = 1 << 30, use_graphs: bool = True, drafter=None, draft_k: int = 0,
-                 page_aligned_chunks: bool = True):
+                 page_aligned_chunks: bool = True, temperature: float = 0.0, top_p: float = 1.0,
+                 sample_seed: int = 0):
         """max_num_batched_tokens is the scheduler's per-pass token budget; the reference
         engine uses one page (16, engine.py:218), which also fixes its page order.
         page_aligned_chunks=False lets a prefill pass run past page boundaries (a long
@@ -64,7 +65,12 @@ class MTPVerifyEngine:
         drafter (pilm_b200.mtp.MTPDrafter) with draft_k > 0 drafts each sequence's next
         tokens on the GPU right after its verify step (in the same graph); verify_step()
         without explicit drafts then uses them, as the reference's speculative loop does
-        with pending_mtp_draft_ids (engine.py:380-408, 527-557)."""
+        with pending_mtp_draft_ids (engine.py:380-408, 527-557).
+        temperature > 0 verifies by rejection sampling from the top-p nucleus of
+        softmax(logits / temperature) instead of greedily (the reference is greedy-only,
+        engine.py:373-379): each step draws two uniforms per verify row, (accept test,
+        sample), from a generator seeded with sample_seed, so a run is reproducible and
+        the same uniforms can be fed to a CPU restatement (``last_uniforms``)."""
         self.v = verifier
         self.device = verifier.device
         self.block_size = block_size
@@ -90,6 +96,12 @@ class MTPVerifyEngine:
         if self.drafter is not None and not use_graphs:
             raise ValueError("the GPU drafter runs inside the captured verify step (use_graphs=True)")
         self.pending: dict[int, list[int]] = {}  # next step's drafts per sequence (from the drafter)
+        if temperature < 0 or not 0 < top_p <= 1:
+            raise ValueError("temperature must be >= 0 and top_p in (0, 1]")
+        self.sampling = (float(temperature), float(top_p)) if temperature > 0 else None
+        self._rng = torch.Generator().manual_seed(sample_seed)
+        self.last_uniforms: Optional[torch.Tensor] = None  # [total_q, 2] of the latest sampled step
+        self._uniforms_staged: Optional[torch.Tensor] = None
 
     # ---- admission -------------------------------------------------------------------
     def add_request(self, prompt: list[int], max_new_tokens: int = 256, eos_token_id: int = -1) -> int:
@@ -197,13 +209,29 @@ class MTPVerifyEngine:
         g = self.graphs.get(key)
         if g is None:
             g = VerifyGraph(self.v, b.num_seqs, b.total_q, b.max_q_len, self.max_pages, self.max_model_len,
-                            self.drafter, self.draft_k)
-            g.load(b)
+                            self.drafter, self.draft_k, self.sampling)
+            g.load(b, self._uniforms_staged)
             g.capture()
             self.graphs[key] = g
         else:
-            g.load(b)
+            g.load(b, self._uniforms_staged)
         return g
+
+    def _draw_uniforms(self, rows: int) -> None:
+        """This step's uniforms [rows, 2] (accept test, sample) from the engine's generator,
+        in a pinned staging buffer (the graph copies them in with the batch)."""
+        self._uniforms_staged = None
+        if self.sampling is None:
+            return
+        u = torch.rand((rows, 2), generator=self._rng)
+        self.last_uniforms = u
+        st = self._staging.get("uniforms")
+        if st is None or st.numel() < 2 * rows:
+            st = torch.empty(max(2 * rows, 1024), dtype=torch.float32, pin_memory=self.pin)
+            self._staging["uniforms"] = st
+        st = st[:2 * rows].view(rows, 2)
+        st.copy_(u)
+        self._uniforms_staged = st
 
     # ---- prefill ----------------------------------------------------------------------
     def prefill(self) -> dict[int, int]:
@@ -262,6 +290,7 @@ class MTPVerifyEngine:
             return []
         B = len(seqs)
         new_drafts = None
+        self._draw_uniforms(int(sum(counts)))
         if self.use_graphs:
             b = self.build_batch(seqs, starts, counts, on_device=False)
             g = self.graph_for(b)
@@ -273,7 +302,11 @@ class MTPVerifyEngine:
             acc = torch.empty(B, dtype=torch.int32, device=self.device)
             nxt = torch.empty(B, dtype=torch.int32, device=self.device)
             ctx = b.context_lens.clone()
-            self.v.verify_greedy(b, acc, nxt, ctx)
+            if self.sampling:
+                self.v.verify_sampled(b, self._uniforms_staged.to(self.device), self.sampling[0], self.sampling[1],
+                                      acc, nxt, ctx)
+            else:
+                self.v.verify_greedy(b, acc, nxt, ctx)
             res = torch.stack([acc, nxt]).to("cpu").tolist()
         if new_drafts is not None:
             self.pending = {s.seq_id: [int(res[2 + j][i]) for j in range(self.draft_k)] for i, s in enumerate(seqs)}

@@ -497,6 +497,21 @@ class Qwen3Verifier:
         self._last_step_launches = abi.launch_count() - n0
         return logits
 
+    def verify_sampled(self, b: VerifyBatch, uniforms: torch.Tensor, temperature: float, top_p: float,
+                       accept_counts: torch.Tensor, next_tokens: torch.Tensor, context_lens: torch.Tensor,
+                       slots: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Verify forward + LM head + rejection-sampling accept and rollback (temperature,
+        top-p nucleus, uniforms [total_q, 2] per row), all on the stream; returns the logits
+        buffer view.  The reference verifies greedily only (engine.py:373-379)."""
+        n0 = abi.launch_count()
+        h = self.forward(b)
+        self.hidden_out = h
+        logits = self.lm_head(h)
+        ck.verify_accept_rejection(b.num_seqs, logits, b.ids, b.cu_q, uniforms, temperature, top_p, accept_counts,
+                                   next_tokens, context_lens, slots)
+        self._last_step_launches = abi.launch_count() - n0
+        return logits
+
 
 class VerifyGraph:
     """The whole verify step (forward, LM head, argmax, accept + rollback) captured as
@@ -508,10 +523,11 @@ class VerifyGraph:
     any batch whose contexts stay within it can be replayed."""
 
     def __init__(self, verifier: "Qwen3Verifier", num_seqs: int, total_q: int, max_q_len: int, max_pages: int,
-                 max_context: int, drafter=None, draft_k: int = 0):
+                 max_context: int, drafter=None, draft_k: int = 0, sampling: Optional[tuple[float, float]] = None):
         """drafter (pilm_b200.mtp.MTPDrafter) and draft_k > 0 add the next step's MTP drafts
         to the graph: k draft steps from the row that produced each sequence's next token,
-        written to ``drafts`` [k, num_seqs]."""
+        written to ``drafts`` [k, num_seqs].  sampling = (temperature, top_p) verifies by
+        rejection sampling with the per-row uniforms ``load`` copies in, instead of greedily."""
         dev = verifier.device
         i32 = dict(dtype=torch.int32, device=dev)
         self.v = verifier
@@ -528,13 +544,19 @@ class VerifyGraph:
                                  cu_q=torch.zeros(num_seqs + 1, **i32), context_lens=torch.zeros(num_seqs, **i32),
                                  max_q_len=max_q_len, max_context=max_context)
         self.ctx_out = torch.zeros(num_seqs, **i32)
+        self.sampling = sampling
+        self.uniforms = torch.zeros((total_q, 2), dtype=torch.float32, device=dev) if sampling else None
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches = 0
 
-    def load(self, b: VerifyBatch) -> None:
+    def load(self, b: VerifyBatch, uniforms: Optional[torch.Tensor] = None) -> None:
         s = self.batch
         if b.total_q != s.total_q or b.num_seqs != s.num_seqs:
             raise ValueError("batch shape differs from the captured graph")
+        if self.sampling:
+            if uniforms is None or tuple(uniforms.shape) != (s.total_q, 2):
+                raise ValueError("a sampling graph needs uniforms [total_q, 2] per step")
+            self.uniforms.copy_(uniforms, non_blocking=True)
         s.ids.copy_(b.ids, non_blocking=True)
         s.positions.copy_(b.positions, non_blocking=True)
         s.slots.copy_(b.slots, non_blocking=True)
@@ -547,7 +569,11 @@ class VerifyGraph:
 
     def _body(self) -> None:
         self.ctx_out.copy_(self.batch.context_lens)
-        self.v.verify_greedy(self.batch, self.acc, self.next, self.ctx_out)
+        if self.sampling:
+            self.v.verify_sampled(self.batch, self.uniforms, self.sampling[0], self.sampling[1], self.acc, self.next,
+                                  self.ctx_out)
+        else:
+            self.v.verify_greedy(self.batch, self.acc, self.next, self.ctx_out)
         if self.drafter is not None:
             self.drafter.draft(self.v.hidden_out, self.batch.cu_q, self.acc, self.next, self.draft_k, self.drafts)
 

@@ -100,3 +100,48 @@ def test_rejection_sampling_decisions_match_oracle(seed):
         assert int(acc[b]) == a
         assert int(nxt[b]) == t
         assert int(ctx[b]) == 100 - (k + 1) + 1 + a
+
+
+@pytest.mark.parametrize("seed", [3, 4])
+def test_rejection_sampling_bf16_logits_vocab_151936(seed):
+    """The LM head's bf16 logits at the Qwen3 vocabulary, ragged rows per sequence (q_len 1
+    to 4, config 3's k = 3), T = 0.8 and top-p 0.95: accept counts, next tokens and the
+    rollback equal the oracle restatement's given the same uniforms (parity unpinned: the
+    reference has no rejection sampling).  Half the drafts are their row's argmax so that
+    acceptance happens; logits scaled so the nucleus is a few hundred tokens."""
+    g = torch.Generator().manual_seed(seed)
+    qlens = [1, 2, 3, 4, 4, 3, 2, 4, 4, 1, 4, 3]
+    B, V, T, P = len(qlens), 151936, 0.8, 0.95
+    cu = [0]
+    for n in qlens:
+        cu.append(cu[-1] + n)
+    R = cu[-1]
+    logits = (torch.randn((R, V), generator=g) * 6).to(torch.bfloat16)
+    uni = torch.rand((R, 2), generator=g)
+    ids = torch.randint(0, V, (R,), generator=g)
+    am = torch.argmax(logits.float(), -1)
+    for b in range(0, B, 2):
+        for j in range(qlens[b] - 1):
+            ids[cu[b] + j + 1] = am[cu[b] + j]
+    i32 = dict(dtype=torch.int32, device=dev())
+    acc, nxt = torch.empty(B, **i32), torch.empty(B, **i32)
+    ctx = torch.full((B,), 1000, **i32)
+    slots = torch.arange(R, **i32)
+    ids_d, cu_d, uni_d = ids.to(torch.int32).to(dev()), torch.tensor(cu, **i32), uni.to(dev())
+    ck.verify_accept_rejection(B, logits.to(dev()), ids_d, cu_d, uni_d, T, P, acc, nxt, ctx, slots)
+    # the fp32 entry point on the same values gives the same decisions
+    acc2, nxt2 = torch.empty(B, **i32), torch.empty(B, **i32)
+    ctx2 = torch.full((B,), 1000, **i32)
+    ck.verify_accept_rejection(B, logits.float().to(dev()), ids_d, cu_d, uni_d, T, P, acc2, nxt2, ctx2)
+    assert acc.tolist() == acc2.tolist() and nxt.tolist() == nxt2.tolist()
+    accepted = 0
+    for b in range(B):
+        rows = slice(cu[b], cu[b + 1])
+        drafts = ids[rows][1:].tolist()
+        a, t = om.rejection_accept(logits[rows].float(), drafts, uni[rows, 0].tolist(), uni[rows, 1].tolist(), T, P)
+        assert (int(acc[b]), int(nxt[b])) == (a, t), b
+        assert int(ctx[b]) == 1000 - qlens[b] + 1 + a
+        s = slots.cpu().tolist()[rows]
+        assert s[:1 + a] == list(range(cu[b], cu[b] + 1 + a)) and all(v == -1 for v in s[1 + a:])
+        accepted += a
+    assert accepted > 0
