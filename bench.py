@@ -546,6 +546,245 @@ def run_reference(args, rank: int, world: int = 1) -> dict | None:
 
 
 # ---------------------------------------------------------------------------------------
+# BASELINE configs 1-3 (python bench.py --config N): one JSON line each
+# ---------------------------------------------------------------------------------------
+
+CONFIGS = {
+    1: dict(name="Qwen3-0.6B-shaped W8A32 (fp32 activations) MTP verify, BASELINE configs[0]", shape="0.6B",
+            fmt="w8a32", seqs=1, k=1, prompt=(128, 128), gen=128, sampling=None),
+    2: dict(name="Qwen3-1.7B-shaped W4A16 g128 MTP verify, BASELINE configs[1]", shape="1.7B", fmt="w4a16g128",
+            seqs=1, k=3, prompt=(512, 512), gen=256, sampling=None),
+    3: dict(name="Qwen3-1.7B-shaped W4A16 g128 MTP verify under continuous batching with rejection sampling "
+                 "(T 0.8, top-p 0.95), BASELINE configs[2]", shape="1.7B", fmt="w4a16g128", seqs=64, k=3,
+            prompt=(128, 2048), gen=256, sampling=(0.8, 0.95), pool_pages=16384),
+}
+
+
+def _config_prompts(cfg, seed):
+    import numpy as np
+    lo, hi = cfg["prompt"]
+    rng = np.random.default_rng(seed)
+    return [int(v) for v in rng.integers(lo, hi + 1, cfg["seqs"])]
+
+
+def cpu_baseline_config(cfg, lens) -> dict | None:
+    """The reference's CPU verify step for configs 1-3 on the host cores: its own linears
+    (oracle/_ref/libecpu.so: ekernel_linear_w8a32 for config 1, ekernel_linear_w4a16g128_bf16
+    otherwise, q/k/v/o/gate/up/down per layer as the reference issues them) plus its paged
+    attention arithmetic (oracle/model.py attend, the torch.cat page gather of
+    attention.py:98-139) and the LM head.  Configs 1 and 2 run every layer on distinct
+    weights (the whole forward, timed on its second run); config 3 (256 rows) samples one
+    layer and extrapolates to 28."""
+    from oracle import reflib
+    if not reflib.available():
+        return None
+    import numpy as np
+    import torch
+    from oracle import model as om
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    torch.set_num_threads(threads)
+    lib = reflib.lib()
+    H, I, V, L = (1024, 3072, 151936, 28) if cfg["shape"] == "0.6B" else (2048, 6144, 151936, 28)
+    nh, nkv, hd = 16, 8, 128
+    M = sum(1 + cfg["k"] for _ in lens)
+    fp32 = cfg["fmt"] == "w8a32"
+    shapes = [(nh * hd, H), (nkv * hd, H), (nkv * hd, H), (H, nh * hd), (I, H), (I, H), (H, I)]
+    rng = np.random.default_rng(7)
+    layers = 1 if cfg["seqs"] > 1 else L
+
+    def weights(N, K):
+        if fp32:
+            return (rng.integers(-127, 128, (N, K), dtype=np.int8), rng.random(N, dtype=np.float32) * 0.01)
+        return (rng.integers(0, 256, (N, K // 2), dtype=np.uint8), rng.random((N, K // 128), dtype=np.float32) * 0.01)
+
+    W = [[weights(N, K) for (N, K) in shapes] for _ in range(layers)]
+    head = weights(V, H)
+    fn = lib.ekernel_linear_w8a32 if fp32 else lib.ekernel_linear_w4a16g128_bf16
+
+    def xin(K):
+        if fp32:
+            return rng.standard_normal((M, K), dtype=np.float32)
+        return (rng.integers(0, 65535, (M, K), dtype=np.uint16) & 0x3FFF) | 0x3C00
+
+    X = {K: xin(K) for K in {H, I, nh * hd}}
+    outs = {N: np.zeros((M, N), np.float32 if fp32 else np.uint16) for N in {nh * hd, nkv * hd, H, I, V}}
+
+    def linear(w, N, K):
+        d = reflib.LinearDesc(M, N, K)
+        assert fn(ctypes.byref(d), X[K].ctypes.data, w[0].ctypes.data, w[1].ctypes.data, outs[N].ctypes.data, 1) == 0
+
+    ocfg = om.Qwen3Config(n_heads=nh, n_kv_heads=nkv, head_dim=hd, block_size=PAGE,
+                          dtype="float32" if fp32 else "bfloat16")
+    dt = torch.float32 if fp32 else torch.bfloat16
+    q = torch.randn((1 + cfg["k"], nh, hd)).to(dt)
+    pages = [(c + PAGE - 1) // PAGE for c in lens]
+    kc = torch.randn((sum(pages) + 1, PAGE, nkv, hd)).to(dt)
+    vc = torch.randn((sum(pages) + 1, PAGE, nkv, hd)).to(dt)
+    tables, off = [], 1
+    for p in pages:
+        tables.append(list(range(off, off + p)))
+        off += p
+
+    def attention():
+        for b, c in enumerate(lens):
+            om.attend(ocfg, q, None, kc, vc, tables[b], c, True)
+
+    def forward():
+        t_lin = t_att = 0.0
+        for li in range(layers):
+            t0 = time.perf_counter()
+            for w, (N, K) in zip(W[li], shapes):
+                linear(w, N, K)
+            t1 = time.perf_counter()
+            attention()
+            t2 = time.perf_counter()
+            t_lin += t1 - t0
+            t_att += t2 - t1
+        t0 = time.perf_counter()
+        linear(head, V, H)
+        return t_lin, t_att, time.perf_counter() - t0
+
+    forward()  # warm-up: thread pool, pages of the outputs
+    t_lin, t_att, t_head = forward()
+    scale = L / layers
+    step_s = scale * (t_lin + t_att) + t_head
+    what = "all 28 layers" if layers == L else f"1 of {L} layers, extrapolated to {L}"
+    return {
+        "value": round(M / step_s, 3), "unit": "verified tok/s", "cores": threads, "kind": "reference",
+        "isa": reflib.isa_name(), "extrapolated": layers != L, "layers_sampled": layers,
+        "sample": (f"{what}: {'W8A32' if fp32 else 'W4A16 g128'} linears at M={M} through the reference library "
+                   f"({t_lin * 1e3:.0f} ms), its paged attention arithmetic over {len(lens)} seqs "
+                   f"({t_att * 1e3:.0f} ms), LM head ({t_head * 1e3:.0f} ms): a {step_s * 1e3:.0f} ms step"),
+    }
+
+
+def run_config(args) -> dict:
+    """Configs 1-3 on one GPU: the verify step from a captured graph on device-resident
+    inputs (value), end to end through MTPVerifyEngine.verify_step with host drafts (e2e),
+    the step's HBM roofline and the reference CPU path."""
+    import torch
+    from pilm_b200 import bindings
+    from pilm_b200.engine import MTPVerifyEngine
+    from pilm_b200.qwen3 import (QWEN3_0_6B, QWEN3_1_7B, PagedKVCache, Qwen3Verifier, Qwen3VerifierF32,
+                                 Qwen3Weights, Qwen3WeightsF32, VerifyGraph)
+    cfg = CONFIGS[args.config]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bindings.init()
+    shape = QWEN3_0_6B if cfg["shape"] == "0.6B" else QWEN3_1_7B
+    fp32 = cfg["fmt"] == "w8a32"
+    seed, k, B = 4321, cfg["k"], cfg["seqs"]
+    lens = _config_prompts(cfg, seed)
+    headroom = cfg["gen"] + 32
+    max_len = max(lens) + headroom + 64
+    num_blocks = cfg.get("pool_pages") or sum((n + headroom + PAGE - 1) // PAGE for n in lens) + 1
+    if fp32:
+        weights = Qwen3WeightsF32.synthetic(shape, seed, dev)
+        kv = PagedKVCache(shape, num_blocks, dev, dtype=torch.float32)
+        ver = Qwen3VerifierF32(weights, kv, max_rows=B * (k + 1), max_pos=max_len, device=dev)
+    else:
+        weights = Qwen3Weights.synthetic(shape, seed, dev)
+        kv = PagedKVCache(shape, num_blocks, dev, fill="random", seed=seed)
+        ver = Qwen3Verifier(weights, kv, max_rows=B * (k + 1), max_pos=max_len, device=dev)
+    T_, P_ = cfg["sampling"] or (0.0, 1.0)
+    eng = MTPVerifyEngine(ver, num_blocks=num_blocks, max_model_len=max_len, temperature=T_, top_p=P_,
+                          sample_seed=seed)
+    g = torch.Generator().manual_seed(seed)
+    for n in lens:
+        sid = eng.add_request(torch.randint(0, shape.vocab, (n,), generator=g).tolist(), max_new_tokens=cfg["gen"])
+        eng.admit_prefilled(sid)
+    for s in eng.sched.running:  # the pending first generated token
+        t = int(torch.randint(0, shape.vocab, (1,), generator=g))
+        s.tokens.append(t)
+        s.outputs.append(t)
+
+    def drafts_for_step():
+        return {s.seq_id: torch.randint(0, shape.vocab, (k,), generator=g).tolist() for s in eng.sched.running}
+
+    # ---- device-resident step: every sequence verifies k drafts (as many as its page allows)
+    from pilm_b200.engine import draft_limit
+    seqs = list(eng.sched.running)
+    counts = []
+    for s in seqs:
+        n = draft_limit(s.num_computed, PAGE, cfg["gen"], k)
+        s.tokens.extend(torch.randint(0, shape.vocab, (n,), generator=g).tolist())
+        eng.pages.allocate(s, 1 + n, eng.max_pages)
+        counts.append(1 + n)
+    batch = eng.build_batch(seqs, [s.num_computed for s in seqs], counts)
+    graph = VerifyGraph(ver, B, batch.total_q, batch.max_q_len, eng.max_pages, eng.max_model_len,
+                        sampling=cfg["sampling"])
+    uni = torch.rand((batch.total_q, 2), generator=g).to(dev) if cfg["sampling"] else None
+    graph.load(batch, uni)
+    graph.capture()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    rows = batch.total_q
+    for s in seqs:
+        del s.tokens[s.num_computed + 1:]
+    # ---- end to end through the engine
+    for _ in range(max(args.warmup, PAGE)):
+        eng.verify_step(drafts_for_step())
+    step_drafts = [drafts_for_step() for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    r0 = eng.stats["verified_rows"]
+    a0, t0c = eng.stats["accepts"], eng.stats["attempts"]
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    for d in step_drafts:
+        eng.verify_step(d)
+    c1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    e2e_ms = c0.elapsed_time(c1) / args.steps
+    e2e_rows = eng.stats["verified_rows"] - r0
+    # ---- roofline: weights + K/V read + appended K/V + logits written, per step
+    ctx = sum(len(s.tokens) for s in seqs)
+    kv_bytes = ctx * kv.bytes_per_token
+    act = 4 if fp32 else 2
+    step_bytes = weights.linear_bytes + kv_bytes + rows * shape.vocab * act + rows * shape.hidden * act
+    pk = peaks()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    flops = 2 * rows * (weights.linear_bytes / (1.0 if fp32 else 0.53125))
+    cpu = None if args.no_cpu else cpu_baseline_config(cfg, [s.num_computed + 1 for s in seqs])
+    return {
+        "metric": METRIC, "config_id": args.config,
+        "value": round(rows / (ms * 1e-3), 2), "unit": "verified tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32 activations x int8 weights" if fp32 else "bf16 activations x int4 weights, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights, random prompt KV pages, random drafts)",
+        "config": {"workload": cfg["name"], "seqs": B, "prompt_lens": f"{min(lens)}-{max(lens)}", "draft_k": k,
+                   "rows_per_step": rows, "page_size": PAGE, "kv_pool_pages": num_blocks,
+                   "verification": (f"rejection sampling T={cfg['sampling'][0]} top-p={cfg['sampling'][1]}"
+                                    if cfg["sampling"] else "greedy"),
+                   "l2": "inputs larger than L2" if step_bytes > L2_BYTES else "inputs fit in L2 (small model)"},
+        "e2e": {"value": round(e2e_rows / args.steps / (e2e_ms * 1e-3), 2), "unit": "verified tok/s",
+                "ms_per_step": round(e2e_ms, 4),
+                "call": "pilm_b200.engine.MTPVerifyEngine.verify_step (host drafts -> host accept results)",
+                "accept_rate": round((eng.stats["accepts"] - a0) / max(1, eng.stats["attempts"] - t0c), 4)},
+        "step_roofline": {"algorithmic_bytes": step_bytes, "weight_bytes": weights.linear_bytes,
+                          "kv_bytes": kv_bytes, "achieved_gbs": round(gbs, 1), "peak": pk["hbm_gbs"],
+                          "peak_source": pk["source"], "frac": round(gbs / pk["hbm_gbs"], 4),
+                          "tflops": round(flops / (ms * 1e-3) / 1e12, 2)},
+        "gpu_launches": graph.launches * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+
+
+# ---------------------------------------------------------------------------------------
 # op sweep: each hot-path kernel alone, over the shapes the configurations use
 # ---------------------------------------------------------------------------------------
 
@@ -801,6 +1040,8 @@ def main():
                     help="linear sweep: comma-separated formats of w4a16g128,w4a16g128_kpairs,w8a32,bf16")
     ap.add_argument("--sweep-ctx", default=None, help="attention sweep: comma-separated context lengths")
     ap.add_argument("--sweep-q", default=None, help="attention sweep: comma-separated rows per sequence")
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="BASELINE configs[0..2] (configs 1-3) on one GPU instead of the config-4 bench line")
     ap.add_argument("--prefill", type=int, default=0,
                     help="time the prefill of one prompt of this many tokens instead of the bench line")
     ap.add_argument("--prefill-chunk", type=int, default=2048, help="prefill: tokens per pass (cross-page chunks)")
@@ -812,6 +1053,9 @@ def main():
         return
     if args.sweep:
         run_sweep(args)
+        return
+    if args.config:
+        print(json.dumps(run_config(args)), flush=True)
         return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

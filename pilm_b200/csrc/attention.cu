@@ -37,6 +37,7 @@ namespace {
 
 constexpr int kHD = 128;         // head_dim supported by the tensor-core path
 constexpr int kWarps = 4;        // warps per attention CTA
+constexpr int kMinPagesPerCta = 8;  // whole-page kernel: pages per CTA at least (short batches)
 constexpr int kStages = 3;       // pages in flight per warp
 constexpr int kPageBytes = 16 * kHD * 2;  // one K (or V) tile of a 16-token page
 constexpr uint32_t kAttnWaitLimit = 1u << 22;  // polls before a page wait gives up
@@ -1054,7 +1055,15 @@ int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnPara
     p.num_blocks = a.num_blocks;
     p.B = (int)desc->num_seqs;
     p.max_q = max_q;
-    p.G = num_sms();
+    // one CTA per SM, but at least kMinPagesPerCta pages each by the host's bound on the
+    // batch's pages (sequences x pages of max_context, a capacity that captured graphs keep):
+    // a short batch split over every SM leaves most CTAs one page or none, and its merge
+    // then walks as many pieces
+    {
+        const long long t_upper = (long long)desc->num_seqs * (long long)((desc->max_context + 15) / 16);
+        const long long g = (t_upper + kMinPagesPerCta - 1) / kMinPagesPerCta;
+        p.G = (int)(g < 1 ? 1 : (g < num_sms() ? g : num_sms()));
+    }
     p.total_q = a.total_q;
     p.scale = a.scale;
     p.err = device_error_word();

@@ -53,50 +53,42 @@ constexpr int kTileRows = 128;   // weight rows per CTA
 constexpr int kMaxNm = 128;      // activation rows per CTA
 constexpr int kRawStages = 8;
 constexpr int kXStages = 4;
+constexpr int kAStages = 4;                          // A buffers in TMEM (64 columns each)
 constexpr int kRawBytes = kTileRows * 64;            // one group of packed weights
 constexpr int kXSubBytes = kMaxNm * 128;             // Nm rows x 64 k bf16 (max)
 constexpr int kXBytes = 2 * kXSubBytes;
 constexpr int kDqWarps = 4;                          // warps 2-5
 constexpr int kFoldWarps = 8;                        // warps 6-13
-constexpr int kXWarp = 2 + kDqWarps + kFoldWarps;    // warp 14: activation loads
 constexpr int kFoldSets = kFoldWarps / 4;            // fold warps per lane quadrant, each a column set
-constexpr int kThreads = (kXWarp + 1) * 32;
+constexpr int kChunksPer = (kMaxNm / 16) / kFoldSets; // 16-column chunks a fold warp holds (at most 4)
+constexpr int kThreads = (2 + kDqWarps + kFoldWarps) * 32;
+constexpr int kTBufs = 2;                            // TMEM partial buffers (kMaxNm columns each)
 constexpr int kTmemCols = 512;
+constexpr int kAColBase = 0;                         // TMEM columns [0, 256): A stages
+constexpr int kAccColBase = kAStages * 64;           // TMEM columns [256, 512): partials
 constexpr uint32_t kWaitLimit = 1u << 20;            // polls before a wait gives up (bounded wait)
 constexpr uint32_t kSleepHintNs = 2000;              // longest sleep of one poll
 
-// TMEM plan of one instantiation.  NC: 16-column chunks of the partial a fold warp holds
-// (the activation tile is 32 NC columns wide at most); NB: partial buffers.  Three
-// buffers (and three A stages) fit for tiles of up to 96 activation rows; 128-row tiles
-// keep two buffers and four A stages.
-template <int NC, int NB>
-struct Plan {
-    static constexpr int kAStages = NB == 3 ? 3 : 4;        // A buffers (64 columns each)
-    static constexpr int kPartCols = 32 * NC;               // columns of one partial buffer
-    static constexpr int kAccColBase = kAStages * 64;
-    static_assert(NC >= 1 && NC <= 4 && (NB == 2 || NB == 3), "plan");
-    static_assert(kAccColBase + NB * kPartCols <= kTmemCols, "TMEM budget");
-};
-
-// Barriers, all on rings indexed by slot i % kSlots for group i:
-//   w_full[q]    the packed weights of group i landed (weights and scales never change, so
-//                they are loaded, and dequantized, before the previous kernel completes)
-//   x_full[q]    the activation tile of group i landed (loaded after griddepcontrol.wait)
+// Every mbarrier operation costs a few hundred cycles inside this kernel, so each group
+// has exactly three, all on rings indexed by slot i % kSlots:
+//   in_full[q]   the TMA copies of group i (packed weights and activations) complete
+//                here: the dequant warps' wait for their inputs
 //   op_full[q]   the MMA issuer's one wait.  One arrival per dequant warp once its rows of
-//                A(i) are in TMEM and the activation tile is in shared memory, and one per
-//                fold warp once it has loaded the partial of group i - NB (the buffer group
-//                i writes; the first NB groups get theirs up front).  The weight producer
-//                also waits here before reusing raw slot i % 8.
+//                A(i) are in TMEM, and one per fold warp once it has loaded group i - 2's
+//                partial (the buffer group i writes; groups 0 and 1 get theirs up front).
+//                The producer also waits here before reusing raw slot i % 8.
 //   mma_done[q]  the issuer's one commit: the fold warps wait for group i's partial, the
-//                dequant warps for A stage reuse, the activation producer for X stage reuse
+//                dequant warps for A stage i % 4 (group i + 4), the producer for X
+//                stage i % 4 (group i + 4)
 // A waiter's parity is (j / kSlots) & 1 for the group j it needs.  No waiter can fall
 // kSlots or more completions behind: every later phase of its slot needs work that the
 // waiter itself has not released yet, so parities never alias.
 constexpr int kSlots = 8;
-static_assert(kSlots == kRawStages && kXStages == 4, "pipeline depths");
+static_assert(kSlots == kRawStages && kXStages == 4 && kAStages == 4 && kTBufs == 2, "pipeline depths");
+static_assert(kAccColBase + kTBufs * kMaxNm <= kTmemCols, "TMEM budget");
 
 struct __align__(8) Barriers {
-    uint64_t w_full[kSlots], x_full[kSlots];
+    uint64_t in_full[kSlots];
     uint64_t op_full[kSlots], mma_done[kSlots];
     uint64_t s_full[2], s_empty[2];
     uint64_t drain;
@@ -276,9 +268,9 @@ __device__ __forceinline__ uint4 dq_word_kpairs(uint32_t w) {
 struct TcParams {
     const float *S;     // scales [N, G] (grouped) or [N] (per-row)
     __nv_bfloat16 *Y;   // [M, N]
-    float *part;        // fp32 pieces of tiles held by several CTAs: [kMaxNm columns][128 rows] each
+    float *part;        // pieces of cut tiles: [P][2][kMaxNm columns][128 rows] fp32
     int *cnt;           // arrivals per (tile, fold warp): zero-initialised, self-resetting
-    float *ws;          // split schedule with a combine pass: fp32 partials [splits, M, N]
+    float *ws;          // split schedule: fp32 partials [splits, M, N] for splitk_combine
     int split_mode;     // 1: CTA c runs split c % splits of tile c / splits (gps groups)
     int splits, gps;
     int *err;           // device error word
@@ -295,14 +287,14 @@ struct TcParams {
 // Two schedules over the units w = t * G + group, each CTA running one contiguous range:
 //  * stream-K (at least one tile per SM): CTA c takes [c U / P, (c+1) U / P), walking
 //    through tiles and their groups in order, so every SM gets the same number of groups
-//    and the rings stream straight across tile boundaries.
+//    and the rings stream straight across tile boundaries.  A tile cut by a range boundary
+//    is reduced in the kernel (the last piece to arrive adds them up).
 //  * split (fewer tiles than SMs): CTA c runs groups [s gps, (s+1) gps) of tile c / splits,
-//    s = c % splits.  With few tiles, stream-K would cut each into many uneven pieces.
-// Either way a tile held by several CTAs is reduced in the kernel: each CTA publishes its
-// fp32 piece, and the last of the tile's CTAs to arrive adds the pieces in CTA order (which
-// is K order, so the sum is deterministic) and writes the tile.
+//    s = c % splits, and writes fp32 partials that splitk_combine sums in split order.  With
+//    few tiles, stream-K would cut each into many pieces and put their reduction on the
+//    critical path.
 __device__ __forceinline__ int unit_begin(int c, const TcParams &p) { return (int)(((unsigned)c * (unsigned)p.U) / (unsigned)p.P); }
-// the CTA whose range holds unit w (stream-K)
+// the CTA whose range holds unit w
 __device__ __forceinline__ int cta_of_unit(int w, const TcParams &p) {
     int c = (int)(((unsigned)w * (unsigned)p.P) / (unsigned)p.U);
     if (c >= p.P) c = p.P - 1;
@@ -310,21 +302,17 @@ __device__ __forceinline__ int cta_of_unit(int w, const TcParams &p) {
     while (c > 0 && unit_begin(c, p) > w) --c;
     return c;
 }
-// CTA c's piece of tile t: under stream-K slot 0 holds its first tile, slot 1 its last;
-// under the split schedule a CTA has one tile
+// a CTA keeps a cut tile's piece in slot 0 for its first tile, slot 1 for its last
 __device__ __forceinline__ float *piece_of(const TcParams &p, int c, int t) {
-    if (p.split_mode) return p.part + (size_t)c * kMaxNm * kTileRows;
     const int slot = t == unit_begin(c, p) / p.G ? 0 : 1;
     return p.part + (size_t)(c * 2 + slot) * kMaxNm * kTileRows;
 }
 
-template <bool KP, int NC, int NB>
+template <bool KP>
 __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant__ CUtensorMap wmap,
                                                          const __grid_constant__ CUtensorMap xmap,
                                                          const __grid_constant__ CUtensorMap smap,
                                                          const TcParams p) {
-    using PL = Plan<NC, NB>;
-    constexpr int NA = PL::kAStages;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     Barriers *bar = reinterpret_cast<Barriers *>(smem + kSmemBar);
@@ -332,9 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
     const int G = p.G;
-    int W0, ng;  // this CTA's first unit and group count (>= 1)
+    int W0, ng, split = 0;  // this CTA's first unit and group count (>= 1)
     if (p.split_mode) {
-        const int split = cta % p.splits;
+        split = cta % p.splits;
         const int gs = split * p.gps;
         W0 = (cta / p.splits) * G + gs;
         ng = min(G, gs + p.gps) - gs;
@@ -343,17 +331,28 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         ng = unit_begin(cta + 1, p) - W0;
     }
 
-    // programmatic dependent launch: the next kernel may launch now.  Only the activation
-    // producer waits for the previous kernel (griddepcontrol.wait): weights and scales are
-    // never written by another kernel, so they are loaded and dequantized into TMEM while
-    // the previous kernel still runs; every global write of this kernel depends on the
-    // activations and therefore follows that wait.
+    // programmatic dependent launch: the next kernel may launch now; this CTA's setup and
+    // an L2 prefetch of its first weight tiles (never written by another kernel) overlap
+    // the previous kernel, and nothing else touches global memory before it completes
     pdl_trigger();
+    if (threadIdx.x == 32 * 2) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+        int t = W0 / G, g = W0 % G;
+        int row0 = (t % p.tiles_n) * kTileRows;
+        for (int i = 0; i < ng && i < kRawStages; ++i) {
+            asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(&wmap), "r"(g * 64),
+                         "r"(row0)
+                         : "memory");
+            if (++g == G) {
+                g = 0;
+                row0 = row0 + kTileRows >= p.tiles_n * kTileRows ? 0 : row0 + kTileRows;
+            }
+        }
+    }
     if (threadIdx.x == 0) {
         // consumer-side barriers take one arrival per warp (lane 0 after __syncwarp)
         for (int i = 0; i < kSlots; ++i) {
-            mbar_init(&bar->w_full[i], 1);  // the producers' arrive.expect_tx
-            mbar_init(&bar->x_full[i], 1);
+            mbar_init(&bar->in_full[i], 1);  // the producer's arrive.expect_tx
             mbar_init(&bar->op_full[i], kDqWarps + kFoldWarps);
             mbar_init(&bar->mma_done[i], 1);
         }
@@ -370,22 +369,30 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
+    pdl_wait();
+
+    const int x_bytes = 2 * p.Nm * 128;
 
     if (warp == 0) {
-        // ---- weights: packed int4 tiles into the raw ring, and group scales into a two-slot
-        // ring (a [128 rows x 16 groups] tile whenever a group starts one; a slot is refilled
-        // once every fold warp has finished with it) ----
+        // ---- TMA: packed weights into the raw ring, activations into the X ring, and
+        // group scales into a two-slot ring: a [128 rows x 16 groups] tile whenever a
+        // group starts one (a slot is refilled once every fold warp has finished with it) ----
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
             if (p.scale_tma) asm volatile("prefetch.tensormap [%0];" ::"l"(&smap) : "memory");
             int issued = 0, s_issued = 0;
             int t = W0 / G, g = W0 % G - 1;
-            int row0 = (t % p.tiles_n) * kTileRows;
+            int row0 = (t % p.tiles_n) * kTileRows, m0 = (t / p.tiles_n) * kMaxNm;
             for (int i = 0; i < ng; ++i) {
-                if (++g == G) {  // next tile: next 128 weight rows (wrapping to the next activation tile)
+                if (++g == G) {  // next tile: next 128 weight rows, or the next activation tile
                     g = 0;
+                    ++t;
                     row0 += kTileRows;
-                    if (row0 >= p.tiles_n * kTileRows) row0 = 0;
+                    if (row0 >= p.tiles_n * kTileRows) {
+                        row0 = 0;
+                        m0 += kMaxNm;
+                    }
                 }
                 if (p.scale_tma && (i == 0 || g % kScaleChunk == 0)) {
                     const int sq = s_issued, slot = sq & 1;
@@ -396,66 +403,39 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     ++s_issued;
                 }
                 // raw slot i % 8 held group i - 8, read by the dequant warps before they
-                // arrived on that group's op_full
+                // arrived on that group's op_full; X stage i % 4 held group i - 4, read by
+                // its MMAs
                 if (i >= kRawStages && !mbar_wait(&bar->op_full[(i - kRawStages) % kSlots],
                                                   (uint32_t)((i - kRawStages) / kSlots) & 1u, abort_flag))
                     break;
-                uint64_t *full = &bar->w_full[i % kSlots];
-                mbar_expect_tx(full, (uint32_t)kRawBytes);
-                tma_load_2d(smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes, &wmap, full, g * 64, row0);
-                ++issued;
-            }
-            // drain: every issued copy has landed before the CTA may exit
-            for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
-                mbar_drain(&bar->w_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
-            for (int c = s_issued > 2 ? s_issued - 2 : 0; c < s_issued; ++c)
-                mbar_drain(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u);
-        }
-        __syncwarp();
-    } else if (warp == kXWarp) {
-        // ---- activations: the tile [Nm rows x 128 k] of every group (two SWIZZLE_128B boxes)
-        // into the X ring, after the previous kernel has completed ----
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
-            pdl_wait();
-            const int x_bytes = 2 * p.Nm * 128;
-            int issued = 0;
-            int t = W0 / G, g = W0 % G - 1;
-            int row0 = (t % p.tiles_n) * kTileRows, m0 = (t / p.tiles_n) * kMaxNm;
-            for (int i = 0; i < ng; ++i) {
-                if (++g == G) {
-                    g = 0;
-                    row0 += kTileRows;
-                    if (row0 >= p.tiles_n * kTileRows) {
-                        row0 = 0;
-                        m0 += kMaxNm;
-                    }
-                }
-                // X stage i % 4 held group i - 4, read by its MMAs
                 if (i >= kXStages && !mbar_wait(&bar->mma_done[(i - kXStages) % kSlots],
                                                 (uint32_t)((i - kXStages) / kSlots) & 1u, abort_flag))
                     break;
-                uint64_t *full = &bar->x_full[i % kSlots];
-                mbar_expect_tx(full, (uint32_t)x_bytes);
+                uint64_t *full = &bar->in_full[i % kSlots];
+                mbar_expect_tx(full, (uint32_t)(kRawBytes + x_bytes));
+                tma_load_2d(smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes, &wmap, full, g * 64, row0);
                 uint8_t *dst = smem + kSmemX + (size_t)(i % kXStages) * kXBytes;
                 tma_load_2d(dst, &xmap, full, g * 128, m0);
                 tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, full, g * 128 + 64, m0);
                 ++issued;
             }
+            // drain: every issued copy has landed before the CTA may exit
             for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
-                mbar_drain(&bar->x_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
+                mbar_drain(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
+            for (int c = s_issued > 2 ? s_issued - 2 : 0; c < s_issued; ++c)
+                mbar_drain(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ---- MMA issuer ----
         if (lane == 0) {
             for (int i = 0; i < ng; ++i) {
-                const int q = i % kSlots, sa = i % NA, sx = i % kXStages, b = i % NB;
+                const int q = i % kSlots, sa = i % kAStages, sx = i % kXStages, b = i % kTBufs;
                 if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
                 tc_fence_after();
-                const uint32_t a_col = tmem + (uint32_t)(sa * 64);
+                const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * 64);
                 const uint32_t x_base = smem_u32(smem + kSmemX + (size_t)sx * kXBytes);
-                const uint32_t d = tmem + (uint32_t)(PL::kAccColBase + b * PL::kPartCols);
+                const uint32_t d = tmem + (uint32_t)(kAccColBase + b * kMaxNm);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const uint64_t bd = sw128_desc(x_base + h * p.Nm * 128);
@@ -472,19 +452,22 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         }
         __syncwarp();
     } else if (warp < 2 + kDqWarps) {
-        // ---- dequant: rows 32 * quad .. + 31 of every group into A stage i % NA.  The first
-        // NA groups are dequantized up front (their weights need no previous kernel); group i
-        // goes to the issuer once its activation tile has landed ----
+        // ---- dequant: rows 32 * quad .. + 31 of every group into A stage i % 4 ----
         const int quad = warp & 3;
         const int rloc = 32 * quad + lane;  // this thread's weight row in the tile = TMEM lane
         const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
         const int sw = (rloc >> 1) & 3;
-        auto dequant = [&](int j) -> bool {
-            if (!mbar_wait_warp(&bar->w_full[j % kSlots], (uint32_t)(j / kSlots) & 1u, abort_flag)) return false;
+        for (int i = 0; i < ng; ++i) {
+            const int sa = i % kAStages;
+            // A stage sa held group i - 4: its MMAs have completed
+            if (i >= kAStages && !mbar_wait_warp(&bar->mma_done[(i - kAStages) % kSlots],
+                                                 (uint32_t)((i - kAStages) / kSlots) & 1u, abort_flag))
+                break;
+            if (!mbar_wait_warp(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
+            tc_fence_after();
             // raw tile written with SWIZZLE_64B: 16-byte chunk c of row r sits at chunk
             // c ^ ((r >> 1) & 3), so 8 consecutive rows hit 8 distinct bank groups
-            const uint8_t *rowp = smem + kSmemRaw + (size_t)(j % kRawStages) * kRawBytes + rloc * 64;
-            const int sa = j % NA;
+            const uint8_t *rowp = smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes + rloc * 64;
 #pragma unroll 2
             for (int c = 0; c < 4; ++c) {  // 16 bytes = 32 k values -> 16 columns
                 const uint4 v = *reinterpret_cast<const uint4 *>(rowp + ((c ^ sw) << 4));
@@ -498,24 +481,10 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     cols[4 * q + 2] = o.z;
                     cols[4 * q + 3] = o.w;
                 }
-                tmem_st16(tmem + lane_addr + (uint32_t)(sa * 64 + 16 * c), cols);
+                tmem_st16(tmem + lane_addr + (uint32_t)(kAColBase + sa * 64 + 16 * c), cols);
             }
             tmem_st_wait();
             tc_fence_before();
-            return true;
-        };
-        bool ok = true;
-        for (int j = 0; j < NA && j < ng && ok; ++j) ok = dequant(j);
-        for (int i = 0; i < ng && ok; ++i) {
-            if (i >= NA) {
-                // A stage i % NA held group i - NA: its MMAs have completed
-                if (!mbar_wait_warp(&bar->mma_done[(i - NA) % kSlots], (uint32_t)((i - NA) / kSlots) & 1u,
-                                    abort_flag))
-                    break;
-                if (!dequant(i)) break;
-            }
-            // the group's activation tile (the MMA's B operand) has landed too
-            if (!mbar_wait_warp(&bar->x_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar->op_full[i % kSlots]);
         }
@@ -526,16 +495,17 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         const int fq = fw >> 2;              // column set 0 .. kFoldSets - 1
         const int rloc = 32 * quad + lane;
         const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
-        const int nc = p.Nm / 16;            // 16-column chunks of the partial (<= 2 NC)
-        const int c_lo = fq * NC, c_hi = min(nc, c_lo + NC);
+        const int nc = p.Nm / 16;            // 16-column chunks of the partial (<= 8)
+        const int per = (nc + kFoldSets - 1) / kFoldSets;  // chunks per set (<= kChunksPer)
+        const int c_lo = fq * per, c_hi = min(nc, c_lo + per);
         const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
-        float2 acc[8 * NC];  // 16-column chunks as fp32 pairs: one packed multiply and add per pair
+        float2 acc[8 * kChunksPer];  // 16-column chunks as fp32 pairs: one packed multiply and add per pair
 #pragma unroll
-        for (int e = 0; e < 8 * NC; ++e) acc[e] = make_float2(0.f, 0.f);
-        // the first NB partial buffers start free
+        for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
+        // partial buffers 0 and 1 start free
         __syncwarp();
         if (lane == 0)
-            for (int i = 0; i < NB && i < ng; ++i) mbar_arrive(&bar->op_full[i]);
+            for (int i = 0; i < kTBufs && i < ng; ++i) mbar_arrive(&bar->op_full[i]);
         int s_seen = 0;   // scale tiles started so far (the producer's sequence)
         int t = W0 / G, g = W0 % G;
         int row = (t % p.tiles_n) * kTileRows + rloc;
@@ -574,47 +544,25 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     break;
                 }
                 tc_fence_after();
-                const uint32_t taddr = tmem + lane_addr + (uint32_t)(PL::kAccColBase + (i % NB) * PL::kPartCols);
-                if constexpr (NC <= 3) {
-                    // load the whole column set, hand the buffer back to the issuer (for group
-                    // i + NB), then fold
-                    uint32_t r[NC][16];
+                const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (i % kTBufs) * kMaxNm);
+                // one 16-column chunk at a time (register budget); the buffer goes back to the
+                // issuer for group i + 2 as soon as the last chunk is in registers
 #pragma unroll
-                    for (int u = 0; u < NC; ++u)
-                        if (c_lo + u < c_hi) tmem_ld16(taddr + 16 * (c_lo + u), r[u]);
+                for (int u = 0; u < kChunksPer; ++u) {
+                    uint32_t r[16];
+                    const bool have = c_lo + u < c_hi;
+                    if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
                     tmem_ld_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0 && i + NB < ng) mbar_arrive(&bar->op_full[(i + NB) % kSlots]);
-#pragma unroll
-                    for (int u = 0; u < NC; ++u) {
-                        if (c_lo + u >= c_hi) continue;
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
-                            const float2 pv = make_float2(__uint_as_float(r[u][2 * e]), __uint_as_float(r[u][2 * e + 1]));
-                            acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
-                        }
+                    if (u == kChunksPer - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0 && i + kTBufs < ng) mbar_arrive(&bar->op_full[(i + kTBufs) % kSlots]);
                     }
-                } else {
-                    // 128-column tiles: one chunk at a time (register budget); the buffer goes
-                    // back once the last chunk is in registers
+                    if (!have) continue;
 #pragma unroll
-                    for (int u = 0; u < NC; ++u) {
-                        uint32_t r[16];
-                        const bool have = c_lo + u < c_hi;
-                        if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
-                        tmem_ld_wait();
-                        if (u == NC - 1) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0 && i + NB < ng) mbar_arrive(&bar->op_full[(i + NB) % kSlots]);
-                        }
-                        if (!have) continue;
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-                            acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
-                        }
+                    for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
+                        const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                        acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
                     }
                 }
             }
@@ -627,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             if (seg_g0 == 0 && last_g == G - 1) {
                 if (row_ok) {
 #pragma unroll
-                    for (int u = 0; u < NC; ++u) {
+                    for (int u = 0; u < kChunksPer; ++u) {
                         if (c_lo + u >= c_hi) continue;
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
@@ -637,12 +585,11 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                         }
                     }
                 }
-            } else if (p.ws) {
+            } else if (p.split_mode) {
                 // split partial for splitk_combine
-                const int split = cta % p.splits;
                 if (row_ok) {
 #pragma unroll
-                    for (int u = 0; u < NC; ++u) {
+                    for (int u = 0; u < kChunksPer; ++u) {
                         if (c_lo + u >= c_hi) continue;
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
@@ -653,11 +600,11 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     }
                 }
             } else {
-                // tile held by several CTAs: publish this piece; the last of the tile's CTAs to
-                // arrive (per fold warp region) sums the pieces in CTA order and writes the tile
+                // cut tile: publish this piece; the last of the tile's CTAs to arrive (per fold
+                // warp region) sums the pieces in CTA order and writes the tile
                 float *pc = piece_of(p, cta, t) + rloc;
 #pragma unroll
-                for (int u = 0; u < NC; ++u) {
+                for (int u = 0; u < kChunksPer; ++u) {
                     if (c_lo + u >= c_hi) continue;
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -668,14 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
                 __threadfence();
                 __syncwarp();
-                int k0, k1;
-                if (p.split_mode) {
-                    k0 = t * p.splits;
-                    k1 = k0 + p.splits - 1;
-                } else {
-                    k0 = cta_of_unit(t * G, p);
-                    k1 = cta_of_unit(t * G + G - 1, p);
-                }
+                const int k0 = cta_of_unit(t * G, p), k1 = cta_of_unit(t * G + G - 1, p);
                 int last = 0;
                 if (lane == 0) last = atomicAdd(p.cnt + (size_t)t * kFoldWarps + fw, 1) == k1 - k0;
                 last = __shfl_sync(0xffffffffu, last, 0);
@@ -683,11 +623,11 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     __threadfence();
                     // sum = 0 + piece(k0) + piece(k0 + 1) + ... in CTA order (deterministic)
 #pragma unroll
-                    for (int e = 0; e < 8 * NC; ++e) acc[e] = make_float2(0.f, 0.f);
+                    for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
                     for (int cc = k0; cc <= k1; ++cc) {
                         const float *pq = piece_of(p, cc, t) + rloc;
 #pragma unroll
-                        for (int u = 0; u < NC; ++u) {
+                        for (int u = 0; u < kChunksPer; ++u) {
                             if (c_lo + u >= c_hi) continue;
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
@@ -699,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     }
                     if (row_ok) {
 #pragma unroll
-                        for (int u = 0; u < NC; ++u) {
+                        for (int u = 0; u < kChunksPer; ++u) {
                             if (c_lo + u >= c_hi) continue;
 #pragma unroll
                             for (int k = 0; k < 16; ++k) {
@@ -713,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
             }
 #pragma unroll
-            for (int e = 0; e < 8 * NC; ++e) acc[e] = make_float2(0.f, 0.f);
+            for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
             // next tile: the next 128 weight rows, or the first of the next activation tile
             g = 0;
             ++t;
@@ -767,29 +707,6 @@ __global__ void __launch_bounds__(256) splitk_combine(const float *__restrict__ 
         o[u] = *reinterpret_cast<const uint32_t *>(&h);
     }
     *reinterpret_cast<uint4 *>(Y + base) = make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-template <bool KP, int NC, int NB>
-void launch_gemm(int P, const CUtensorMap &wmap, const CUtensorMap &xmap, const CUtensorMap &smap, const TcParams &p) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(w4_gemm_tc<KP, NC, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
-        attr_set = true;
-    }
-    launch_pdl(w4_gemm_tc<KP, NC, NB>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
-}
-
-// Partial buffers: three where the tile fits them (NC <= 3), unless PILM_TC_BUFS=2.
-template <bool KP>
-void launch_nc(int nc, int P, const CUtensorMap &wmap, const CUtensorMap &xmap, const CUtensorMap &smap,
-               const TcParams &p) {
-    static const int bufs = (getenv("PILM_TC_BUFS") && getenv("PILM_TC_BUFS")[0] == '2') ? 2 : 3;
-    switch (nc) {
-        case 1: bufs == 3 ? launch_gemm<KP, 1, 3>(P, wmap, xmap, smap, p) : launch_gemm<KP, 1, 2>(P, wmap, xmap, smap, p); break;
-        case 2: bufs == 3 ? launch_gemm<KP, 2, 3>(P, wmap, xmap, smap, p) : launch_gemm<KP, 2, 2>(P, wmap, xmap, smap, p); break;
-        case 3: bufs == 3 ? launch_gemm<KP, 3, 3>(P, wmap, xmap, smap, p) : launch_gemm<KP, 3, 2>(P, wmap, xmap, smap, p); break;
-        default: launch_gemm<KP, 4, 2>(P, wmap, xmap, smap, p); break;
-    }
 }
 
 // ---- host side ---------------------------------------------------------------------------
@@ -847,15 +764,17 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     } else {
         // Split K by a cost model in units of one group's pipeline time: every wave of CTAs
         // pays its groups per CTA plus a fixed prologue and pipeline fill (about 2 groups),
-        // and a split adds the in-kernel reduction of the pieces (about 1).
-        static const double split_cost = (getenv("PILM_TC_COMBINE") && getenv("PILM_TC_COMBINE")[0] == '0') ? 1.0 : 3.0;
+        // and a split adds one combine pass (about 3).  The combine pass wants N % 8 == 0 and
+        // 16-byte aligned output rows.
         double best = 1e30;
-        for (int s = 1; s <= (G < 16 ? G : 16); ++s) {
+        const bool can_split = (N % 8) == 0 && (((uintptr_t)Y) & 15) == 0;
+        const int max_splits = can_split ? (G < 16 ? G : 16) : 1;
+        for (int s = 1; s <= max_splits; ++s) {
             const int g = (G + s - 1) / s;
             const int se = (G + g - 1) / g;
             if (se != s) continue;
             const int waves = (tiles * se + sms - 1) / sms;
-            const double est = waves * (g + 2.0) + (se > 1 ? split_cost : 0.0);
+            const double est = waves * (g + 2.0) + (se > 1 ? 3.0 : 0.0);
             if (est < best - 1e-9) {
                 best = est;
                 splits = se;
@@ -893,35 +812,37 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     p.split_mode = stream_k ? 0 : 1;
     p.splits = splits;
     p.gps = gps;
+    p.ws = nullptr;
     p.grouped = grouped ? 1 : 0;
     p.scale_tma = smap_ok ? 1 : 0;
     // kind::f16 instruction descriptor: D fp32, A/B bf16, K-major both, N = Nm, M = 128
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Nm >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     p.part = nullptr;
     p.cnt = nullptr;
-    p.ws = nullptr;
-    static const bool combine = !(getenv("PILM_TC_COMBINE") && getenv("PILM_TC_COMBINE")[0] == '0');
-    const bool use_combine = !stream_k && splits > 1 && combine && (N % 8) == 0 && (((uintptr_t)Y) & 15) == 0;
-    if (use_combine) {
-        p.ws = (float *)workspace((size_t)splits * M * N * sizeof(float));
-        PILM_REQUIRE(p.ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
-    } else if (stream_k || splits > 1) {
-        const size_t pieces = stream_k ? (size_t)P * 2 : (size_t)P;
-        p.part = (float *)workspace(pieces * kMaxNm * kTileRows * sizeof(float));
+    if (stream_k) {
+        p.part = (float *)workspace((size_t)P * 2 * kMaxNm * kTileRows * sizeof(float));
         p.cnt = counters((size_t)tiles * kFoldWarps);
         PILM_REQUIRE(p.part && p.cnt, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
+    } else if (splits > 1) {
+        p.ws = (float *)workspace((size_t)splits * M * N * sizeof(float));
+        PILM_REQUIRE(p.ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
-    const int nc = (Nm / 16 + kFoldSets - 1) / kFoldSets;  // 16-column chunks per fold warp
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(w4_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        attr_set = true;
+    }
     if (kpairs)
-        launch_nc<true>(nc, P, wmap, xmap, smap, p);
+        launch_pdl(w4_gemm_tc<true>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
     else
-        launch_nc<false>(nc, P, wmap, xmap, smap, p);
+        launch_pdl(w4_gemm_tc<false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
-    if (use_combine) {
+    if (splits > 1) {
         const size_t total8 = (size_t)M * N / 8;
         launch_pdl(splitk_combine, dim3((unsigned)((total8 + 255) / 256)), dim3(256), 0, p.ws, splits, M, N,
-                   grouped ? nullptr : S, Y);
+                                                                            grouped ? nullptr : S, Y);
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }

@@ -663,6 +663,31 @@ class Qwen3WeightsF32(Qwen3Weights):
             })
         return cls(shape, f("embed"), layers, f("final_norm"), W8Linear.quantize(ck_tensors["embed"].to(device)))
 
+    @classmethod
+    def synthetic(cls, shape: Qwen3Shape, seed: int, device) -> "Qwen3WeightsF32":
+        """Seeded random-init fp32 model quantized on the device: N(0, 0.02) weights,
+        int8 per-row (the W8A32 format), fp32 norms of ones (zeros for Gemma norms), fp32
+        embedding and the tied LM head quantized from it."""
+        g = torch.Generator(device=device).manual_seed(seed)
+
+        def lin(n, k):
+            w = torch.randn((n, k), generator=g, device=device, dtype=torch.float32) * 0.02
+            return W8Linear.quantize(w)
+
+        H, I = shape.hidden, shape.intermediate
+        init = torch.zeros if shape.gemma_norm else torch.ones
+        f = dict(dtype=torch.float32, device=device)
+        embed = torch.randn((shape.vocab, H), generator=g, **f) * 0.02
+        layers = []
+        for _ in range(shape.layers):
+            layers.append({
+                "qkv": lin(shape.qkv_rows, H), "o": lin(H, shape.n_heads * shape.head_dim),
+                "gate_up": lin(2 * I, H), "down": lin(H, I),
+                "input_norm": init(H, **f), "post_norm": init(H, **f),
+                "q_norm": init(shape.head_dim, **f), "k_norm": init(shape.head_dim, **f),
+            })
+        return cls(shape, embed, layers, init(H, **f), W8Linear.quantize(embed))
+
 
 class Qwen3VerifierF32(Qwen3Verifier):
     """The verify forward with fp32 activations and KV (model dtype float32, W8A32):
