@@ -1018,6 +1018,19 @@ def run_sweep(args) -> None:
         gbs = nbytes / (ms * 1e-3) / 1e9
         emit({"sweep": "accept", "seqs": B, "k": k, "vocab": V, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
               "frac": round(gbs / peak, 4)})
+        # rejection sampling (T 0.8, top-p 0.95) over the same bf16 logits: four reads of every
+        # row for its nucleus statistics, then two reads of one row per sequence to sample
+        uni = torch.rand((T, 2), device=dev, generator=g)
+
+        def body_rs():
+            for _ in range(4):
+                ctxs.copy_(ctx0)
+                ck.verify_accept_rejection(B, logits, ids, cu, uni, 0.8, 0.95, acc, nxt, ctxs)
+        ms = _graph_ms(body_rs, 4)
+        nbytes = (4 * T + 2 * B) * V * 2
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        emit({"sweep": "accept_rejection", "seqs": B, "k": k, "vocab": V, "temperature": 0.8, "top_p": 0.95,
+              "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
 
 
 def main():

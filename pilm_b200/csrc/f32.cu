@@ -37,6 +37,7 @@ __device__ __forceinline__ float warp_max32(float v) {
 
 __global__ void embedding_f32_kernel(const int32_t *__restrict__ ids, int rows, const float *__restrict__ table,
                                      int vocab, int hidden, float *__restrict__ out, int *__restrict__ err) {
+    pdl_entry();
     const int r = blockIdx.x;
     if (r >= rows) return;
     int id = ids[r];
@@ -51,6 +52,7 @@ __global__ void embedding_f32_kernel(const int32_t *__restrict__ ids, int rows, 
 __global__ void __launch_bounds__(256) add_rmsnorm_f32_kernel(float *__restrict__ res, const float *__restrict__ delta,
                                                               const float *__restrict__ w, int n, float eps,
                                                               int add_one, float *__restrict__ out) {
+    pdl_entry();
     __shared__ float red[8];
     const int row = blockIdx.x;
     float *r = res + (size_t)row * n;
@@ -85,6 +87,7 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
                                        const int32_t *__restrict__ positions, const int32_t *__restrict__ slots,
                                        long long num_slots, float *__restrict__ kc, float *__restrict__ vc,
                                        float *__restrict__ q_out, float *__restrict__ gate_out) {
+    pdl_entry();
     __shared__ float buf[8][kHD];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int item = blockIdx.x * 8 + warp;
@@ -155,15 +158,25 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
     }
 }
 
-// one warp per (query row, head); 4 warps per CTA
-__global__ void attn_f32_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
-                                const int32_t *__restrict__ block_table, const int32_t *__restrict__ cu_q,
-                                const int32_t *__restrict__ ctx_lens, const float *__restrict__ gate,
-                                float *__restrict__ out, int B, int total_q, int nh, int nkv, int max_blocks,
-                                int num_blocks, float scale) {
-    __shared__ float qs[4][kHD];
+// One CTA per (query row, head); its kFA warps take every kFA-th chunk of 32 keys, each
+// with its own online softmax (m, l, o), and the CTA merges the warps' states at the end.
+// In a chunk, lane j scores key k0 + j (one 512-byte key row per lane), then the warp
+// accumulates P V over the chunk's keys with each lane holding 4 of the 128 dims.
+constexpr int kFA = 8;
+__global__ void __launch_bounds__(kFA * 32) attn_f32_kernel(const float *__restrict__ q, const float *__restrict__ kc,
+                                                            const float *__restrict__ vc,
+                                                            const int32_t *__restrict__ block_table,
+                                                            const int32_t *__restrict__ cu_q,
+                                                            const int32_t *__restrict__ ctx_lens,
+                                                            const float *__restrict__ gate, float *__restrict__ out,
+                                                            int B, int total_q, int nh, int nkv, int max_blocks,
+                                                            int num_blocks, float scale) {
+    pdl_entry();
+    __shared__ float qs[kHD];
+    __shared__ float sm[kFA], sl[kFA];
+    __shared__ float4 so[kFA][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int item = blockIdx.x * 4 + warp;
+    const int item = blockIdx.x;
     if (item >= total_q * nh) return;
     const int row = item / nh, h = item % nh;
     int lo = 0, hi = B - 1;  // sequence of this row: largest b with cu_q[b] <= row
@@ -177,14 +190,13 @@ __global__ void attn_f32_kernel(const float *__restrict__ q, const float *__rest
     const int qpos = ctx - q_len + (row - cu_q[b]);
     const int kvh = h / (nh / nkv);
     const float *qrow = q + ((size_t)row * nh + h) * kHD;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) qs[warp][lane + 32 * j] = qrow[lane + 32 * j];
-    __syncwarp();
+    if (threadIdx.x < kHD) qs[threadIdx.x] = qrow[threadIdx.x];
+    __syncthreads();
     const int32_t *bt = block_table + (size_t)b * max_blocks;
     const int last = min(qpos, ctx - 1);  // the last key this row sees
     float m = -INFINITY, l = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k0 = 0; k0 <= last; k0 += 32) {
+    for (int k0 = 32 * warp; k0 <= last; k0 += 32 * kFA) {
         const int key = k0 + lane;
         float s = -INFINITY;
         size_t off = 0;
@@ -197,10 +209,10 @@ __global__ void attn_f32_kernel(const float *__restrict__ q, const float *__rest
 #pragma unroll 8
             for (int d4 = 0; d4 < kHD / 4; ++d4) {
                 const float4 kv = kr[d4];
-                dot = fmaf(qs[warp][4 * d4], kv.x, dot);
-                dot = fmaf(qs[warp][4 * d4 + 1], kv.y, dot);
-                dot = fmaf(qs[warp][4 * d4 + 2], kv.z, dot);
-                dot = fmaf(qs[warp][4 * d4 + 3], kv.w, dot);
+                dot = fmaf(qs[4 * d4], kv.x, dot);
+                dot = fmaf(qs[4 * d4 + 1], kv.y, dot);
+                dot = fmaf(qs[4 * d4 + 2], kv.z, dot);
+                dot = fmaf(qs[4 * d4 + 3], kv.w, dot);
             }
             s = __fmul_rn(dot, scale);
         }
@@ -214,6 +226,7 @@ __global__ void attn_f32_kernel(const float *__restrict__ q, const float *__rest
         o.w *= alpha;
         m = mnew;
         const int n = min(32, last - k0 + 1);
+#pragma unroll 4
         for (int kk = 0; kk < n; ++kk) {
             const float pk = __shfl_sync(0xffffffffu, pl, kk);
             const size_t ok = (size_t)__shfl_sync(0xffffffffu, (unsigned long long)off, kk);
@@ -224,8 +237,33 @@ __global__ void attn_f32_kernel(const float *__restrict__ q, const float *__rest
             o.w = fmaf(pk, vv.w, o.w);
         }
     }
-    const float invl = l > 0.f ? __fdiv_rn(1.0f, l) : 0.f;
-    float r4[4] = {o.x * invl, o.y * invl, o.z * invl, o.w * invl};
+    if (lane == 0) {
+        sm[warp] = m;
+        sl[warp] = l;
+    }
+    so[warp][lane] = o;
+    __syncthreads();
+    if (warp != 0) return;
+    // merge the warps' states in warp order
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kFA; ++w)
+        if (sl[w] > 0.f) M = fmaxf(M, sm[w]);
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kFA; ++w) {
+        if (!(sl[w] > 0.f)) continue;
+        const float f = expf(sm[w] - M);
+        const float4 ow = so[w][lane];
+        L += sl[w] * f;
+        O.x = fmaf(ow.x, f, O.x);
+        O.y = fmaf(ow.y, f, O.y);
+        O.z = fmaf(ow.z, f, O.z);
+        O.w = fmaf(ow.w, f, O.w);
+    }
+    const float invl = L > 0.f ? __fdiv_rn(1.0f, L) : 0.f;
+    float r4[4] = {O.x * invl, O.y * invl, O.z * invl, O.w * invl};
     const size_t ob = (size_t)row * nh * kHD + (size_t)h * kHD + 4 * lane;
     if (gate) {
 #pragma unroll
@@ -235,6 +273,7 @@ __global__ void attn_f32_kernel(const float *__restrict__ q, const float *__rest
 }
 
 __global__ void silu_mul_f32_kernel(const float *__restrict__ gu, size_t rows, int inter, float *__restrict__ out) {
+    pdl_entry();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows * (size_t)inter) return;
     const size_t r = i / inter;
@@ -268,7 +307,7 @@ int ekernel_embedding_f32(const int32_t *ids, size_t rows, const float *table, s
     if (rows == 0) return ECPU_OK;
     int *err = device_error_word();
     PILM_REQUIRE(err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
-    embedding_f32_kernel<<<(unsigned)rows, 256, 0, stream()>>>(ids, (int)rows, table, (int)vocab, (int)hidden, out,
+    launch_pdl(embedding_f32_kernel, dim3((unsigned)rows), dim3(256), 0, ids, (int)rows, table, (int)vocab, (int)hidden, out,
                                                                 err);
     const int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
@@ -281,7 +320,7 @@ int ekernel_add_rmsnorm_f32(float *residual, const float *delta, const float *we
     PILM_REQUIRE(residual && weight && out, ECPU_ERR_PARAM, "%s: null argument", what);
     PILM_REQUIRE(n > 0 && n <= (1u << 24) && rows <= 0x7fffffff, ECPU_ERR_PARAM, "%s: sizes out of range", what);
     if (rows == 0) return ECPU_OK;
-    add_rmsnorm_f32_kernel<<<(unsigned)rows, 256, 0, stream()>>>(residual, delta, weight, (int)n, eps, add_one, out);
+    launch_pdl(add_rmsnorm_f32_kernel, dim3((unsigned)rows), dim3(256), 0, residual, delta, weight, (int)n, eps, add_one, out);
     return check_launch(what);
 }
 
@@ -298,7 +337,7 @@ int ekernel_qk_norm_rope_kv_append_f32(const ekernel_paged_attn_desc_t *desc, co
     PILM_REQUIRE(!desc->output_gate || gate_out, ECPU_ERR_PARAM, "%s: gate_out required when output_gate", what);
     if (desc->total_q == 0) return ECPU_OK;
     const int items = (int)(desc->total_q * (desc->n_heads + desc->n_kv_heads));
-    qk_prologue_f32_kernel<<<(items + 7) / 8, 256, 0, stream()>>>(
+    launch_pdl(qk_prologue_f32_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), 0, 
         qkv, (int)desc->total_q, (int)desc->n_heads, (int)desc->n_kv_heads, (int)desc->qkv_stride, desc->output_gate,
         q_norm_w, k_norm_w, desc->eps, desc->add_one, rope_cos, rope_sin, (int)desc->rope_rows, (int)desc->rot_dim,
         positions, slot_mapping, (long long)desc->num_blocks * (long long)desc->block_size, k_cache, v_cache, q_out,
@@ -317,7 +356,7 @@ int ekernel_paged_attention_verify_f32(const ekernel_paged_attn_desc_t *desc, co
     PILM_REQUIRE(!desc->output_gate || gate, ECPU_ERR_PARAM, "%s: gate required when output_gate", what);
     if (desc->total_q == 0 || desc->num_seqs == 0) return ECPU_OK;
     const int items = (int)(desc->total_q * desc->n_heads);
-    attn_f32_kernel<<<(items + 3) / 4, 128, 0, stream()>>>(
+    launch_pdl(attn_f32_kernel, dim3((unsigned)items), dim3(kFA * 32), 0, 
         q, k_cache, v_cache, block_table, cu_q, context_lens, desc->output_gate ? gate : nullptr, out,
         (int)desc->num_seqs, (int)desc->total_q, (int)desc->n_heads, (int)desc->n_kv_heads,
         (int)desc->max_blocks_per_seq, (int)desc->num_blocks, (float)(1.0 / sqrt((double)kHD)));
@@ -330,7 +369,7 @@ int ekernel_silu_mul_f32(const float *gate_up, size_t rows, size_t inter, float 
     PILM_REQUIRE(inter > 0 && inter <= (1u << 24), ECPU_ERR_PARAM, "%s: sizes out of range", what);
     const size_t total = rows * inter;
     if (total == 0) return ECPU_OK;
-    silu_mul_f32_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream()>>>(gate_up, rows, (int)inter, out);
+    launch_pdl(silu_mul_f32_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, gate_up, rows, (int)inter, out);
     return check_launch(what);
 }
 

@@ -438,6 +438,7 @@ template <int MC>
 __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, int M, int K,
                                                   const int8_t *__restrict__ W, const float *__restrict__ S, int N,
                                                   float *__restrict__ Y) {
+    pdl_entry();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = (blockIdx.x * 8 + warp) * kW8Rows;
     if (n0 >= N) return;
@@ -696,11 +697,11 @@ int ekernel_linear_w8a32(const ekernel_linear_w8a32_desc_t *desc, const float *A
     const unsigned grid = (unsigned)((desc->N + 8 * kW8Rows - 1) / (8 * kW8Rows));
     const int M = (int)desc->M, K = (int)desc->K, N = (int)desc->N;
     if (M == 1)
-        w8a32_gemv<1><<<grid, 256, 0, pilm::stream()>>>(A, M, K, W, scales, N, C);
+        launch_pdl(w8a32_gemv<1>, dim3(grid), dim3(256), 0, A, M, K, W, scales, N, C);
     else if (M == 2)
-        w8a32_gemv<2><<<grid, 256, 0, pilm::stream()>>>(A, M, K, W, scales, N, C);
+        launch_pdl(w8a32_gemv<2>, dim3(grid), dim3(256), 0, A, M, K, W, scales, N, C);
     else
-        w8a32_gemv<4><<<grid, 256, 0, pilm::stream()>>>(A, M, K, W, scales, N, C);
+        launch_pdl(w8a32_gemv<4>, dim3(grid), dim3(256), 0, A, M, K, W, scales, N, C);
     return pilm::check_launch("ekernel_linear_w8a32");
 }
 
