@@ -206,8 +206,34 @@ __device__ __forceinline__ float logit_at(const T *x, int i) {
     else return x[i];
 }
 
-__device__ __forceinline__ unsigned long long fix_mass(float l, float mx, float T) {
-    const float e = expf(__fdiv_rn(l - mx, T));  // in [0, 1]
+// f(i, logit) for every token of a row, spread over the block; bf16 rows on 16-byte
+// boundaries are read 8 logits per load
+template <typename T, typename F>
+__device__ __forceinline__ void row_for_each(const T *x, int V, F &&f) {
+    if constexpr (sizeof(T) == 2) {
+        if ((((uintptr_t)x) & 15) == 0) {
+            const int nv = V >> 3;
+            const uint4 *xv = reinterpret_cast<const uint4 *>(x);
+            for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+                const uint4 w = __ldg(xv + v);
+                const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    f(8 * v + 2 * e, __uint_as_float(wd[e] << 16));
+                    f(8 * v + 2 * e + 1, __uint_as_float(wd[e] & 0xffff0000u));
+                }
+            }
+            for (int i = 8 * nv + threadIdx.x; i < V; i += blockDim.x) f(i, logit_at(x, i));
+            return;
+        }
+    }
+    for (int i = threadIdx.x; i < V; i += blockDim.x) f(i, logit_at(x, i));
+}
+
+// the mass of a token: exp((l - mx) / T) in fixed point; every pass and both kernels use
+// this one function, so their sums agree exactly
+__device__ __forceinline__ unsigned long long rs_mass(float l, float mx, float inv_t) {
+    const float e = expf(-((mx - l) * inv_t));  // in [0, 1]
     return __double2ull_rn((double)e * kFix);
 }
 
@@ -217,8 +243,19 @@ __device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v)
     return v;
 }
 
-// Inclusive suffix sums of `bins` values held two per thread (bins 2t, 2t + 1), in
-// shared memory: sfx[d] = sum of bins[d..].  Block of kRsThreads, kRsBins = 2 x threads.
+// block-wide sum (every thread gets it); wsum holds 32 slots
+__device__ unsigned long long block_sum_u64(unsigned long long v, unsigned long long *wsum) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum_u64(v);
+    __syncthreads();
+    if (lane == 0) wsum[warp] = v;
+    __syncthreads();
+    unsigned long long t = lane < (int)(blockDim.x >> 5) ? wsum[lane] : 0ull;
+    return warp_sum_u64(t);
+}
+
+// Inclusive suffix sums of kRsBins values held two per thread: sfx[d] = sum of bins[d..]
+// (kRsThreads threads).
 __device__ void suffix_sums(const unsigned long long *bins, unsigned long long *sfx, unsigned long long *wsum) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     // reverse order: thread t handles bins kRsBins-1-2t and kRsBins-2-2t, so a prefix scan
@@ -249,77 +286,160 @@ __device__ void suffix_sums(const unsigned long long *bins, unsigned long long *
     __syncthreads();
 }
 
+// Level 0 bins tokens linearly by u = (mx - l) / T: bin floor(u * kRsBins / kRsSpan), the
+// last bin collecting u >= kRsSpan (masses below 2^-57).  A bin index never decreases as
+// the logit decreases, so bins order the tokens by logit, ties kept together.
+constexpr float kRsSpan = 40.f;
+constexpr int kRsGather = 2048;  // tokens of the cut's bin resolved by pairwise comparison
+
+__device__ __forceinline__ int rs_bin(float l, float mx, float inv_t) {
+    const float u = (mx - l) * inv_t;
+    return u < kRsSpan ? min(kRsBins - 1, (int)(u * (kRsBins / kRsSpan))) : kRsBins - 1;
+}
+
+struct RsSmem {
+    unsigned long long hist[kRsBins];  // level-0 masses; later the fallback's histograms
+    unsigned long long sfx[kRsBins];
+    unsigned int cnt[kRsBins];
+    uint32_t gkey[kRsGather];
+    unsigned long long gmass[kRsGather];
+    unsigned long long wsum[32];
+    float shf[32];
+    int s_bin, s_n;
+    uint32_t s_cut;
+};
+
+// Fallback for a cut bin with more than kRsGather tokens: radix select over the 32-bit keys
+// (11 + 11 + 10 bits) of the whole row for the lowest present key whose strictly-above mass
+// is < target; returns the cut and the nucleus mass.
+template <typename T>
+__device__ void rs_radix_cut(const T *x, int V, float mx, float inv_t, double target, RsSmem &sm, uint32_t &cut,
+                             unsigned long long &zn) {
+    constexpr int kBits[3] = {11, 11, 10};
+    uint32_t prefix = 0;
+    int consumed = 0;
+    unsigned long long above = 0, at_cut = 0;
+    for (int lv = 0; lv < 3; ++lv) {
+        const int bits = kBits[lv];
+        const int shift = 32 - consumed - bits;
+        for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) sm.hist[d] = 0;
+        __syncthreads();
+        row_for_each(x, V, [&](int, float l) {
+            const uint32_t k = fkey(l);
+            if (consumed == 0 || (k >> (32 - consumed)) == prefix)
+                atomicAdd(&sm.hist[(k >> shift) & ((1u << bits) - 1)], rs_mass(l, mx, inv_t));
+        });
+        __syncthreads();
+        suffix_sums(sm.hist, sm.sfx, sm.wsum);
+        if (threadIdx.x == 0) sm.s_bin = kRsBins;
+        __syncthreads();
+        for (int d = threadIdx.x; d < (1 << bits); d += blockDim.x) {
+            const unsigned long long higher = above + sm.sfx[d] - sm.hist[d];
+            if (sm.hist[d] && (double)higher < target) atomicMin(&sm.s_bin, d);
+        }
+        __syncthreads();
+        int dg = sm.s_bin;
+        if (dg == kRsBins) dg = 0;
+        above += sm.sfx[dg] - sm.hist[dg];
+        at_cut = sm.hist[dg];
+        prefix = (prefix << bits) | (uint32_t)dg;
+        consumed += bits;
+        __syncthreads();
+    }
+    cut = prefix;
+    zn = above + at_cut;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__ logits, int rows, int V,
                                                             const int32_t *__restrict__ ids, float temp, float top_p,
                                                             RsRow *__restrict__ out) {
     pdl_entry();
-    __shared__ float shf[32];
-    __shared__ unsigned long long hist[kRsBins];
-    __shared__ unsigned long long sfx[kRsBins];
-    __shared__ unsigned long long wsum[32];
-    __shared__ int s_digit;
+    extern __shared__ __align__(16) uint8_t rs_smem_raw[];
+    RsSmem &sm = *reinterpret_cast<RsSmem *>(rs_smem_raw);
     const int r = blockIdx.x;
     const T *x = logits + (size_t)r * V;
+    const float inv_t = __fdiv_rn(1.0f, temp);
     float mx = -INFINITY;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, logit_at(x, i));
-    mx = block_max(mx, shf);
+    row_for_each(x, V, [&](int, float l) { mx = fmaxf(mx, l); });
+    mx = block_max(mx, sm.shf);
 
-    // radix select of the cut: the lowest present key whose strictly-above mass is < top_p Z
-    constexpr int kBits[3] = {11, 11, 10};
-    uint32_t prefix = 0;           // digits chosen so far
-    int consumed = 0;              // key bits chosen so far
-    unsigned long long above = 0;  // mass of the keys above the current bucket
-    double target = 0.0;
-    unsigned long long at_cut = 0;
-    for (int lv = 0; lv < 3; ++lv) {
-        const int bits = kBits[lv];
-        const int shift = 32 - consumed - bits;
-        for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) hist[d] = 0;
-        __syncthreads();
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            const float l = logit_at(x, i);
-            const uint32_t k = fkey(l);
-            if (consumed == 0 || (k >> (32 - consumed)) == prefix)
-                atomicAdd(&hist[(k >> shift) & ((1u << bits) - 1)], fix_mass(l, mx, temp));
+    // level 0: masses and counts per bin
+    for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) {
+        sm.hist[d] = 0;
+        sm.cnt[d] = 0;
+    }
+    __syncthreads();
+    // Tokens in the catch-all bin (u >= kRsSpan) have mass exactly 0 in fixed point, so their
+    // strictly-above mass is the whole total: they are never in the nucleus (top_p <= 1) and
+    // the cut's bin is never theirs.  They are not counted, which keeps the many low-logit
+    // tokens of a row off one contended bin.
+    row_for_each(x, V, [&](int, float l) {
+        const int bn = rs_bin(l, mx, inv_t);
+        if (bn == kRsBins - 1) return;
+        atomicAdd(&sm.hist[bn], rs_mass(l, mx, inv_t));
+        atomicAdd(&sm.cnt[bn], 1u);
+    });
+    __syncthreads();
+    suffix_sums(sm.hist, sm.sfx, sm.wsum);
+    const unsigned long long total = sm.sfx[0];
+    const double target = (double)top_p * (double)total;  // the nucleus keeps above-mass < top_p Z
+    // the cut lies in the last non-empty bin whose higher bins hold less than the target
+    if (threadIdx.x == 0) sm.s_bin = -1;
+    __syncthreads();
+    for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) {
+        const unsigned long long higher = total - sm.sfx[d];  // mass of bins before d
+        if (sm.cnt[d] && (double)higher < target) atomicMax(&sm.s_bin, d);
+    }
+    __syncthreads();
+    const int bstar = sm.s_bin;
+    const unsigned long long base = total - sm.sfx[bstar];  // mass strictly above the cut's bin
+    uint32_t cut;
+    unsigned long long zn;
+    if (sm.cnt[bstar] <= (unsigned)kRsGather) {
+        // gather the bin's tokens; a token's above-mass is base + the masses of the bin's
+        // tokens with a greater key, and the cut is the smallest key whose above-mass < target
+        if (threadIdx.x == 0) {
+            sm.s_n = 0;
+            sm.s_cut = 0xffffffffu;
         }
         __syncthreads();
-        suffix_sums(hist, sfx, wsum);
-        if (lv == 0) target = (double)top_p * (double)sfx[0];  // top_p x total mass
-        // the lowest non-empty digit whose above-mass (above + bins strictly higher) < target
-        if (threadIdx.x == 0) s_digit = kRsBins;
+        row_for_each(x, V, [&](int, float l) {
+            if (rs_bin(l, mx, inv_t) == bstar) {
+                const int slot = atomicAdd(&sm.s_n, 1);
+                sm.gkey[slot] = fkey(l);
+                sm.gmass[slot] = rs_mass(l, mx, inv_t);
+            }
+        });
         __syncthreads();
-        for (int d = threadIdx.x; d < (1 << bits); d += blockDim.x) {
-            const unsigned long long higher = above + sfx[d] - hist[d];
-            if (hist[d] && (double)higher < target) atomicMin(&s_digit, d);
+        const int n = sm.s_n;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t ki = sm.gkey[i];
+            unsigned long long above = base;
+            for (int j = 0; j < n; ++j)
+                if (sm.gkey[j] > ki) above += sm.gmass[j];
+            if ((double)above < target) atomicMin(&sm.s_cut, ki);
         }
         __syncthreads();
-        int dg = s_digit;
-        if (dg == kRsBins) {  // no mass below target (top_p rounding at the maxima): keep the top digit
-            dg = 0;
-            for (int d = (1 << bits) - 1; d >= 0; --d)
-                if (hist[d]) {
-                    dg = d;
-                    break;
-                }
-        }
-        above += sfx[dg] - hist[dg];
-        at_cut = hist[dg];
-        prefix = (prefix << bits) | (uint32_t)dg;
-        consumed += bits;
-        __syncthreads();
+        cut = sm.s_cut;
+        unsigned long long in_bin = 0;
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+            if (sm.gkey[i] >= cut) in_bin += sm.gmass[i];
+        zn = base + block_sum_u64(in_bin, sm.wsum);
+    } else {
+        rs_radix_cut(x, V, mx, inv_t, target, sm, cut, zn);
     }
     if (threadIdx.x == 0) {
         RsRow o;
         o.mx = mx;
-        o.cut = prefix;
-        o.zn = above + at_cut;
+        o.cut = cut;
+        o.zn = zn;
         o.ed = 0;
         if (r + 1 < rows) {
             const int d = ids[r + 1];
             if (d >= 0 && d < V) {
                 const float l = logit_at(x, d);
-                if (fkey(l) >= prefix) o.ed = fix_mass(l, mx, temp);
+                if (fkey(l) >= cut) o.ed = rs_mass(l, mx, inv_t);
             }
         }
         out[r] = o;
@@ -376,17 +496,34 @@ __global__ void __launch_bounds__(kRsThreads) rs_decide_sample(const T *__restri
         else total -= st.ed;
     }
     const T *x = logits + (size_t)row * V;
-    // chunk sums over contiguous index ranges, then the chunk that crosses u x total
-    const int chunk = (V + blockDim.x - 1) / blockDim.x;
-    const int i0 = threadIdx.x * chunk, i1 = min(V, i0 + chunk);
+    const float inv_t = __fdiv_rn(1.0f, temp);
+    // chunk sums over contiguous index ranges (a multiple of 8 logits each, so bf16 rows on
+    // 16-byte boundaries are read 8 logits per load), then the chunk that crosses u x total
+    const int chunk = ((V + blockDim.x * 8 - 1) / (blockDim.x * 8)) * 8;
+    const int i0 = min(V, (int)threadIdx.x * chunk), i1 = min(V, i0 + chunk);
+    const bool vec8 = sizeof(T) == 2 && (((uintptr_t)x) & 15) == 0;
     unsigned long long s = 0;
     int last = -1;
-    for (int i = i0; i < i1; ++i) {
-        const float l = logit_at(x, i);
+    auto visit = [&](int i, float l) {
         if (i != skip && fkey(l) >= st.cut) {
-            s += fix_mass(l, st.mx, temp);
+            s += rs_mass(l, st.mx, inv_t);
             last = i;
         }
+    };
+    if (vec8) {
+        int i = i0;
+        for (; i + 8 <= i1; i += 8) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4 *>(x + i));
+            const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                visit(i + 2 * e, __uint_as_float(wd[e] << 16));
+                visit(i + 2 * e + 1, __uint_as_float(wd[e] & 0xffff0000u));
+            }
+        }
+        for (; i < i1; ++i) visit(i, logit_at(x, i));
+    } else {
+        for (int i = i0; i < i1; ++i) visit(i, logit_at(x, i));
     }
     if (last >= 0) atomicMax(&s_last, last);
     // exclusive prefix over threads
@@ -416,7 +553,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_decide_sample(const T *__restri
         for (int i = i0; i < i1; ++i) {
             const float l = logit_at(x, i);
             if (i != skip && fkey(l) >= st.cut) {
-                run += fix_mass(l, st.mx, temp);
+                run += rs_mass(l, st.mx, inv_t);
                 if ((double)run > target) {
                     atomicMin(&s_pick, i);
                     break;
@@ -452,8 +589,13 @@ int launch_rejection(const ekernel_accept_desc_t *desc, const T *logits, const i
     if (desc->total_q > 0) {
         stats = (RsRow *)scratch(kScratchAccept, desc->total_q * sizeof(RsRow));
         PILM_REQUIRE(stats, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
-        launch_pdl(rs_row_stats<T>, dim3((unsigned)desc->total_q), dim3(kRsThreads), 0, logits, (int)desc->total_q,
-                   (int)desc->vocab, verify_ids, temperature, top_p, stats);
+        static bool attr = false;
+        if (!attr) {
+            cudaFuncSetAttribute(rs_row_stats<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(RsSmem));
+            attr = true;
+        }
+        launch_pdl(rs_row_stats<T>, dim3((unsigned)desc->total_q), dim3(kRsThreads), sizeof(RsSmem), logits,
+                   (int)desc->total_q, (int)desc->vocab, verify_ids, temperature, top_p, stats);
         const int rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
