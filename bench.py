@@ -326,6 +326,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         cycle = run_cycle("w4a16")
         cycle_bf16 = run_cycle("bf16")
     clocks = sampler.stop()
+    # each rank's own timings on stderr (the JSON line carries the max over ranks)
+    print(json.dumps({"rank": rank, "world": world, "ms_per_step": round(ms, 4),
+                      "e2e_ms_per_step": round(e2e_ms, 4) if e2e_steps else None,
+                      "e2e_host_wall_ms_per_step": round(wall_ms, 4) if e2e_steps else None}),
+          file=sys.stderr, flush=True)
     h2d = 4 * (3 * rows_per_step + SEQS * maxp + 2 * SEQS + 1) + 0
     d2h = 4 * 2 * SEQS
 
@@ -348,7 +353,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     kv_bytes = sum(ctx) * shape.n_kv_heads * shape.head_dim * 2 * 2
     cap = attn_traffic_capture()
     traffic = round(cap["bytes"] * kv_bytes / cap["kv_bytes"]) if cap else None
-    cpu = cpu_baseline_sample(args) if not args.no_cpu else None
+    # the CPU baseline runs at N = 1 only: at N > 1 the host's cores serve every rank
+    cpu = cpu_baseline_sample(args) if not args.no_cpu and world == 1 else None
     value = rows_per_step * world / (ms_max * 1e-3)
     line = {
         "metric": METRIC,
