@@ -225,6 +225,13 @@ unsigned long long ekernel_launch_count(void);
  * of its program made the library allocate nothing. */
 unsigned long long ekernel_alloc_count(void);
 
+/* Test hook for the bounded waits of the tensor-core GEMM's pipeline (it has no
+ * counterpart in the reference): later launches give up a wait after `polls` polls
+ * (0: at the first wait not already met), raise the kernel's error word, drain their copies
+ * and MMAs, free their tensor memory and exit, so the call reports ECPU_ERR_KERNEL in
+ * synchronous mode (PILM_CUDA_SYNC=1).  polls < 0 restores the kernel's own limit. */
+int ekernel_set_wait_limit(long long polls);
+
 /* Token embedding gather: out[r,:] = table[ids[r],:] (bf16).  Takes over
  * nn.Embedding in Qwen3Model.forward (model.py:110). */
 int ekernel_embedding_bf16(const int32_t *ids, size_t rows, const uint16_t *table, size_t vocab, size_t hidden,

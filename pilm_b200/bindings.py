@@ -41,6 +41,7 @@ KERNEL_SYMBOLS = [
     "ekernel_synchronize",
     "ekernel_launch_count",
     "ekernel_alloc_count",
+    "ekernel_set_wait_limit",
     "ekernel_embedding_bf16",
     "ekernel_add_rmsnorm_bf16",
     "ekernel_silu_mul_bf16",
@@ -191,6 +192,7 @@ def _configure(lib) -> None:
     lib.ekernel_get_stream.restype = _vp
     lib.ekernel_launch_count.restype = ctypes.c_ulonglong
     lib.ekernel_alloc_count.restype = ctypes.c_ulonglong
+    lib.ekernel_set_wait_limit.argtypes = [ctypes.c_longlong]
     lib.ekernel_embedding_bf16.argtypes = [_vp, _sz, _vp, _sz, _sz, _vp]
     lib.ekernel_add_rmsnorm_bf16.argtypes = [_vp, _vp, _vp, _sz, _sz, ctypes.c_float, _i32, _vp]
     lib.ekernel_silu_mul_bf16.argtypes = [_vp, _sz, _sz, _vp]

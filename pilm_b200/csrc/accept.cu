@@ -169,9 +169,11 @@ __global__ void greedy_accept(int B, const int32_t *__restrict__ ids, const int3
 // Masses e_j = exp((l_j - mx) / T) <= 1 are summed in unsigned 64-bit fixed point with 40
 // fractional bits.  Integer sums do not depend on the order of summation, so every pass,
 // thread count and launch agrees exactly; V < 2^23 keeps them below 2^63.  The nucleus cut
-// comes from a radix select over the 32-bit keys in three passes (11 + 11 + 10 bits):
-// each pass histograms the masses of the keys in the current bucket by their next digit,
-// so a row costs four reads (max and three histograms) instead of a bisection's ~34.
+// takes three reads of the row: its max; a histogram of masses and counts over 2048 linear
+// bins of (mx - l) / T, which locates the bin holding the cut; and a gather of that bin's
+// tokens (at most 2048), among which the cut is found by exact pairwise comparison.  A cut
+// bin with more tokens falls back to a radix select over the 32-bit keys of the whole row
+// (11 + 11 + 10 bits, three more reads).
 // ---------------------------------------------------------------------------------
 constexpr int kRsThreads = 1024;
 constexpr int kRsBins = 2048;

@@ -55,6 +55,9 @@ int check_error_word(const char *what, const char *msg);
 // The same check on a given error word (the allocation-free entry point's own word).
 int check_error_word_at(int *err, const char *what, const char *msg);
 
+// The poll limit set by ekernel_set_wait_limit for pipeline waits (-1: each kernel's own).
+long long wait_limit_override();
+
 // Post-launch check: ECPU_ERR_KERNEL on a launch error; in synchronous mode
 // (PILM_CUDA_SYNC=1) also waits for the stream and reports execution errors.
 int check_launch(const char *what);

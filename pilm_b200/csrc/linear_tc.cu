@@ -144,10 +144,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *b, uint32_t parity
 // Bounded wait: returns false (and raises the CTA abort flag) if the phase never completes.
 // The MMA issuer polls (its waits are nearly always already satisfied); every other role
 // sleeps between polls.  The abort flag is read every 16 polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag,
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag, uint32_t limit,
                                           bool sleep = true) {
     if (mbar_try_wait(b, parity)) return true;  // already complete: no suspend
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (sleep ? mbar_try_wait_sleep(b, parity) : mbar_try_wait(b, parity)) return true;
         if ((i & 15) == 15 && *abort_flag) return false;
     }
@@ -165,8 +165,9 @@ __device__ __forceinline__ void mbar_drain(uint64_t *b, uint32_t parity) {
 // Warp-collective bounded wait: every lane waits (each gets the acquire), then the warp
 // reconverges before the .sync.aligned tcgen05 instructions that follow; a timeout in
 // any lane makes the whole warp give up together.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
-    const bool ok = mbar_wait(b, parity, abort_flag);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *b, uint32_t parity, volatile int *abort_flag,
+                                               uint32_t limit) {
+    const bool ok = mbar_wait(b, parity, abort_flag, limit);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -282,6 +283,7 @@ struct TcParams {
     uint32_t idesc;
     int grouped;
     int scale_tma;      // group scales arrive by TMA (G % 4 == 0, group offsets 16-byte aligned)
+    uint32_t wait_limit;  // polls before a pipeline wait gives up (drains keep kWaitLimit)
 };
 
 // Two schedules over the units w = t * G + group, each CTA running one contiguous range:
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
                 if (p.scale_tma && (i == 0 || g % kScaleChunk == 0)) {
                     const int sq = s_issued, slot = sq & 1;
-                    if (sq >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((sq - 2) >> 1) & 1u, abort_flag)) break;
+                    if (sq >= 2 && !mbar_wait(&bar->s_empty[slot], (uint32_t)((sq - 2) >> 1) & 1u, abort_flag, p.wait_limit)) break;
                     mbar_expect_tx(&bar->s_full[slot], kScaleBytes);
                     tma_load_2d(smem + kSmemScale + (size_t)slot * kScaleBytes, &smap, &bar->s_full[slot],
                                 kScaleChunk * (g / kScaleChunk), row0);
@@ -406,10 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // arrived on that group's op_full; X stage i % 4 held group i - 4, read by
                 // its MMAs
                 if (i >= kRawStages && !mbar_wait(&bar->op_full[(i - kRawStages) % kSlots],
-                                                  (uint32_t)((i - kRawStages) / kSlots) & 1u, abort_flag))
+                                                  (uint32_t)((i - kRawStages) / kSlots) & 1u, abort_flag, p.wait_limit))
                     break;
                 if (i >= kXStages && !mbar_wait(&bar->mma_done[(i - kXStages) % kSlots],
-                                                (uint32_t)((i - kXStages) / kSlots) & 1u, abort_flag))
+                                                (uint32_t)((i - kXStages) / kSlots) & 1u, abort_flag, p.wait_limit))
                     break;
                 uint64_t *full = &bar->in_full[i % kSlots];
                 mbar_expect_tx(full, (uint32_t)(kRawBytes + x_bytes));
@@ -431,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         if (lane == 0) {
             for (int i = 0; i < ng; ++i) {
                 const int q = i % kSlots, sa = i % kAStages, sx = i % kXStages, b = i % kTBufs;
-                if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
+                if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag, p.wait_limit)) break;
                 tc_fence_after();
                 const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * 64);
                 const uint32_t x_base = smem_u32(smem + kSmemX + (size_t)sx * kXBytes);
@@ -461,9 +463,9 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             const int sa = i % kAStages;
             // A stage sa held group i - 4: its MMAs have completed
             if (i >= kAStages && !mbar_wait_warp(&bar->mma_done[(i - kAStages) % kSlots],
-                                                 (uint32_t)((i - kAStages) / kSlots) & 1u, abort_flag))
+                                                 (uint32_t)((i - kAStages) / kSlots) & 1u, abort_flag, p.wait_limit))
                 break;
-            if (!mbar_wait_warp(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) break;
+            if (!mbar_wait_warp(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag, p.wait_limit)) break;
             tc_fence_after();
             // raw tile written with SWIZZLE_64B: 16-byte chunk c of row r sits at chunk
             // c ^ ((r >> 1) & 3), so 8 consecutive rows hit 8 distinct bank groups
@@ -523,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     if (p.scale_tma) {
                         if (i == 0 || g % kScaleChunk == 0) {
                             const int sq = s_seen++;
-                            if (!mbar_wait_warp(&bar->s_full[sq & 1], (uint32_t)(sq >> 1) & 1u, abort_flag)) {
+                            if (!mbar_wait_warp(&bar->s_full[sq & 1], (uint32_t)(sq >> 1) & 1u, abort_flag, p.wait_limit)) {
                                 aborted = true;
                                 break;
                             }
@@ -539,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     }
                 }
                 const float2 sc2 = make_float2(sc, sc);
-                if (!mbar_wait_warp(&bar->mma_done[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag)) {
+                if (!mbar_wait_warp(&bar->mma_done[i % kSlots], (uint32_t)(i / kSlots) & 1u, abort_flag, p.wait_limit)) {
                     aborted = true;
                     break;
                 }
@@ -819,6 +821,7 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Nm >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     p.part = nullptr;
     p.cnt = nullptr;
+    p.wait_limit = wait_limit_override() >= 0 ? (uint32_t)wait_limit_override() : kWaitLimit;
     if (stream_k) {
         p.part = (float *)workspace((size_t)P * 2 * kMaxNm * kTileRows * sizeof(float));
         p.cnt = counters((size_t)tiles * kFoldWarps);
@@ -846,7 +849,13 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
         rc = check_launch(what);
         if (rc != ECPU_OK) return rc;
     }
-    return check_error_word(what, "tensor-core GEMM pipeline timed out");
+    rc = check_error_word(what, "tensor-core GEMM pipeline timed out");
+    if (rc != ECPU_OK && p.cnt) {
+        // CTAs that gave up left some cut tiles' arrival counters short of their reset:
+        // clear them so that the next call starts from zero
+        cudaMemset(p.cnt, 0, (size_t)tiles * kFoldWarps * sizeof(int));
+    }
+    return rc;
 }
 
 }  // namespace pilm

@@ -261,6 +261,9 @@ int *counters(size_t n) {
 }
 
 static unsigned long long g_launches = 0;
+static long long g_wait_limit = -1;
+
+long long wait_limit_override() { return g_wait_limit; }
 
 int check_launch(const char *what) {
     ++g_launches;
@@ -418,6 +421,11 @@ void *ekernel_get_stream(void) { return (void *)g.stream; }
 unsigned long long ekernel_launch_count(void) { return pilm::g_launches; }
 
 unsigned long long ekernel_alloc_count(void) { return pilm::g_lib_allocs; }
+
+int ekernel_set_wait_limit(long long polls) {
+    pilm::g_wait_limit = polls < 0 ? -1 : (polls > 0xffffffffll ? 0xffffffffll : polls);
+    return ECPU_OK;
+}
 
 int ekernel_synchronize(void) {
     cudaError_t e = cudaStreamSynchronize(g.stream);
