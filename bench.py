@@ -15,6 +15,9 @@ over ~8.2K keys per sequence), final norm, LM head, row argmax, greedy accept an
 rollback.  `value` times K such steps on device-resident inputs with CUDA events
 (max over ranks); `e2e` times K steps of the public engine call
 MTPVerifyEngine.verify_step with host drafts in, host accept results out.
+Random drafts are almost never accepted by a random model, so `e2e_accepting` times
+the same call with drafts the model accepts: its own greedy continuation, computed
+untimed beforehand.
 
 --impl reference times the reference's own CPU kernels (oracle/_ref/libecpu.so,
 built from the reference sources) on a bounded sample of the same workload on the
@@ -164,6 +167,33 @@ def reduce_over_ranks(maxes: list[float], sums: list[float], device=None) -> tup
     dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     dist.all_reduce(t_sum, op=dist.ReduceOp.SUM)
     return t_max.tolist()[:len(maxes)], t_sum.tolist()[:len(sums)]
+
+
+def greedy_rollout(eng, n_tokens: int, k: int):
+    """Drafts that the model accepts: run n_tokens steps without drafts (each appends the
+    model's greedy next token), record every running sequence's continuation, then rewind
+    each sequence to where it started.  Its pages stay allocated; the next steps rewrite
+    the same positions.  Returns a function that gives, for the engine's current state,
+    each sequence's next k tokens of that continuation (fewer near its end)."""
+    run = list(eng.sched.running)
+    base = {s.seq_id: (len(s.tokens), len(s.outputs), s.num_computed) for s in run}
+    for _ in range(n_tokens):
+        eng.verify_step({})
+    traj = {s.seq_id: list(s.tokens[base[s.seq_id][0] - 1:]) for s in run}  # [pending, t1, t2, ...]
+    for s in run:
+        nt, no, nc = base[s.seq_id]
+        del s.tokens[nt:]
+        del s.outputs[no:]
+        s.num_computed = nc
+
+    def drafts() -> dict[int, list[int]]:
+        out = {}
+        for s in run:
+            j = len(s.tokens) - base[s.seq_id][0]  # index of the pending token in traj
+            out[s.seq_id] = traj[s.seq_id][j + 1:j + 1 + k]
+        return out
+
+    return drafts
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -325,6 +355,51 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if e2e_steps and not args.no_draft:
         cycle = run_cycle("w4a16")
         cycle_bf16 = run_cycle("bf16")
+
+    def run_accepting() -> dict:
+        """The verify step with drafts that the model accepts: the drafts are the target
+        model's own greedy continuation, computed beforehand (untimed) by steps without
+        drafts, after which every sequence is rewound to where it started (its pages are
+        kept: the timed steps rewrite the same positions with the same K/V).  The timed
+        steps then run the accept, bonus-token and context-advance path with k accepted
+        drafts per sequence wherever the page-boundary cap allows k."""
+        eng.drafter, eng.draft_k, eng.graphs, eng.pending = None, 0, {}, {}
+        n_warm = max(args.warmup, PAGE)
+        ideal_drafts = greedy_rollout(eng, (n_warm + e2e_steps) * (K_DRAFT + 1) + 2, K_DRAFT)
+        eng.graphs = {}
+
+        for _ in range(n_warm):
+            eng.verify_step(ideal_drafts())
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a_rows = a_tokens = a_att = a_acc = 0
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(e2e_steps):
+            d = ideal_drafts()
+            rows_before = eng.stats["verified_rows"]
+            for r in eng.verify_step(d):
+                a_tokens += 1 + r.accepted
+                a_att += len(r.drafts)
+                a_acc += r.accepted
+            a_rows += eng.stats["verified_rows"] - rows_before
+        a1.record(stream)
+        torch.cuda.synchronize()
+        (a_ms,), (a_rows_all, a_tokens_all) = reduce_over_ranks([a0.elapsed_time(a1) / e2e_steps],
+                                                                [float(a_rows), float(a_tokens)], dev)
+        eng.graphs = {}
+        return {
+            "verified_tok_s": round(a_rows_all / e2e_steps / (a_ms * 1e-3), 2),
+            "accepted_tok_s": round(a_tokens_all / e2e_steps / (a_ms * 1e-3), 2),
+            "ms_per_step": round(a_ms, 4),
+            "draft_k": K_DRAFT,
+            "accept_rate": round(a_acc / max(1, a_att), 4),
+            "drafts": "the target model's own greedy continuation (computed untimed beforehand)",
+            "call": "pilm_b200.engine.MTPVerifyEngine.verify_step (host drafts -> host accept results)",
+        }
+
+    accepting = run_accepting() if e2e_steps and not args.no_accepting else None
     clocks = sampler.stop()
     # each rank's own timings on stderr (the JSON line carries the max over ranks)
     print(json.dumps({"rank": rank, "world": world, "ms_per_step": round(ms, 4),
@@ -382,6 +457,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         },
         "cycle": cycle,
         "cycle_bf16_drafter": cycle_bf16,
+        "e2e_accepting": accepting,
         "roofline": {
             "kernel": "attn_pages (+ attn_merge_pages), per layer",
             "bound": "hbm",
@@ -1024,8 +1100,9 @@ def run_sweep(args) -> None:
         gbs = nbytes / (ms * 1e-3) / 1e9
         emit({"sweep": "accept", "seqs": B, "k": k, "vocab": V, "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
               "frac": round(gbs / peak, 4)})
-        # rejection sampling (T 0.8, top-p 0.95) over the same bf16 logits: four reads of every
-        # row for its nucleus statistics, then two reads of one row per sequence to sample
+        # rejection sampling (T 0.8, top-p 0.95) over the same bf16 logits: three reads of every
+        # row for its nucleus statistics (max, bin histogram, gather of the cut's bin), then
+        # two reads of one row per sequence to sample
         uni = torch.rand((T, 2), device=dev, generator=g)
 
         def body_rs():
@@ -1033,7 +1110,7 @@ def run_sweep(args) -> None:
                 ctxs.copy_(ctx0)
                 ck.verify_accept_rejection(B, logits, ids, cu, uni, 0.8, 0.95, acc, nxt, ctxs)
         ms = _graph_ms(body_rs, 4)
-        nbytes = (4 * T + 2 * B) * V * 2
+        nbytes = (3 * T + 2 * B) * V * 2
         gbs = nbytes / (ms * 1e-3) / 1e9
         emit({"sweep": "accept_rejection", "seqs": B, "k": k, "vocab": V, "temperature": 0.8, "top_p": 0.95,
               "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
@@ -1048,6 +1125,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end engine leg (profiling runs)")
     ap.add_argument("--no-draft", action="store_true", help="skip the verify + GPU draft cycle leg")
+    ap.add_argument("--no-accepting", action="store_true",
+                    help="skip the leg whose drafts are accepted (the model's own greedy continuation)")
     ap.add_argument("--seqs", type=int, default=SEQS, help="sequences per GPU (default: the BASELINE config)")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens per sequence")
     ap.add_argument("--layers", type=int, default=0, help="decoder layers (0 = all 36); profiling only")
