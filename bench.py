@@ -806,10 +806,12 @@ def run_config(args) -> dict:
     sampler.start()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     e0.record(stream)
     for _ in range(args.steps):
         graph.replay()
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     rows = batch.total_q

@@ -193,6 +193,21 @@ int ekernel_linear_w4a16g128_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc
 int ekernel_linear_w4a16_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,
                                      const float *scales, uint16_t *C, ekernel_isa_t isa);
 
+/* ekernel_linear_w4a16g128_bf16_kpairs that may leave its result as split-K partial sums
+ * instead of bf16 (no reference counterpart).  When the tensor-core GEMM runs its split
+ * schedule (fewer 128-row weight tiles than SMs) with s splits and s * M * N fp32 values
+ * fit in partials_bytes at partials (16-byte aligned), it writes them there as
+ * [s][M][N] (split order = K order), does not write C, skips its combine pass and sets
+ * *splits = s.  Otherwise it writes C like the plain call and sets *splits = 0.  The
+ * partials are meant for a consumer that sums them itself
+ * (ekernel_add_rmsnorm_bf16_splitk, ekernel_qk_norm_rope_kv_append_splitk). */
+int ekernel_linear_w4a16g128_bf16_kpairs_deferred(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                                  const uint8_t *W, const float *scales, uint16_t *C,
+                                                  float *partials, size_t partials_bytes, int32_t *splits);
+
+/* Bytes of partials a deferred call of this shape leaves on this GPU (0: it writes C). */
+size_t ekernel_linear_w4a16g128_partials_bytes(size_t M, size_t N, size_t K);
+
 /* kernel/api.h:180-186 (kernels.c:1485-1526): rne(x * rsqrt(mean(x^2)+eps) * (w [+1])). */
 int ekernel_rmsnorm_bf16(const uint16_t *x, uint16_t *out, const uint16_t *weight, size_t rows, size_t n,
                          float eps, int add_one);
@@ -243,6 +258,13 @@ int ekernel_embedding_bf16(const int32_t *ids, size_t rows, const uint16_t *tabl
  * out = rne( rne(residual * rsqrt(mean(residual^2)+eps)) * w' ), w' = w or rne(w+1). */
 int ekernel_add_rmsnorm_bf16(uint16_t *residual, const uint16_t *delta, const uint16_t *weight, size_t rows,
                              size_t n, float eps, int add_one, uint16_t *out);
+
+/* The same with the delta given as the split-K partial sums of a deferred W4 linear
+ * ([splits][rows][n] fp32, summed in split order and rounded to bf16: the linear's own
+ * output).  n % 8 == 0, n <= 8192, 16-byte aligned buffers (else ECPU_ERR_UNSUPPORTED). */
+int ekernel_add_rmsnorm_bf16_splitk(uint16_t *residual, const float *partials, int32_t splits,
+                                    const uint16_t *weight, size_t rows, size_t n, float eps, int add_one,
+                                    uint16_t *out);
 
 /* SwiGLU activation with torch bf16 semantics (layers.py:193): h = rne(rne(silu(g)) * u)
  * where gate_up is [rows, 2*inter] with gate in columns [0,inter) and up in
@@ -300,6 +322,17 @@ int ekernel_qk_norm_rope_kv_append(const ekernel_paged_attn_desc_t *desc, const 
                                    const uint16_t *q_norm_w, const uint16_t *k_norm_w, const float *rope_cos,
                                    const float *rope_sin, const int32_t *positions, const int32_t *slot_mapping,
                                    uint16_t *k_cache, uint16_t *v_cache, uint16_t *q_out, uint16_t *gate_out);
+
+/* ekernel_qk_norm_rope_kv_append taking the fused projection as the split-K partial sums
+ * that ekernel_linear_w4a16g128_bf16_kpairs_deferred left ([splits][total_q][qkv_stride]
+ * fp32): each element is their sum in split order rounded to bf16, the value the
+ * projection would have had, so the results are identical.  No reference counterpart:
+ * it saves the GEMM's separate combine pass. */
+int ekernel_qk_norm_rope_kv_append_splitk(const ekernel_paged_attn_desc_t *desc, const float *partials,
+                                          int32_t splits, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                          const float *rope_cos, const float *rope_sin, const int32_t *positions,
+                                          const int32_t *slot_mapping, uint16_t *k_cache, uint16_t *v_cache,
+                                          uint16_t *q_out, uint16_t *gate_out);
 
 /* Paged attention over the verify rows.  q: [total_q, n_heads, hd] (from the call
  * above), block_table [num_seqs, max_blocks_per_seq], cu_q [num_seqs+1] row offsets,

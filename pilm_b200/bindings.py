@@ -57,6 +57,10 @@ KERNEL_SYMBOLS = [
     "ekernel_repack_w4_kpairs",
     "ekernel_linear_w4a16g128_bf16_kpairs",
     "ekernel_linear_w4a16_bf16_kpairs",
+    "ekernel_linear_w4a16g128_bf16_kpairs_deferred",
+    "ekernel_linear_w4a16g128_partials_bytes",
+    "ekernel_add_rmsnorm_bf16_splitk",
+    "ekernel_qk_norm_rope_kv_append_splitk",
     "ekernel_mtp_fc_input_bf16",
     "ekernel_self_attention_bf16",
     "ekernel_embedding_f32",
@@ -180,6 +184,13 @@ def _configure(lib) -> None:
         fn.restype = _i32
     lib.ekernel_linear_w8a16_bf16_argmax.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp, _vp,
                                                      ctypes.POINTER(_sz), ctypes.POINTER(ctypes.c_float), _i32]
+    lib.ekernel_linear_w4a16g128_bf16_kpairs_deferred.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp,
+                                                                  _vp, _vp, _vp, _sz, ctypes.POINTER(_i32)]
+    lib.ekernel_linear_w4a16g128_bf16_kpairs_deferred.restype = _i32
+    lib.ekernel_linear_w4a16g128_partials_bytes.argtypes = [_sz, _sz, _sz]
+    lib.ekernel_linear_w4a16g128_partials_bytes.restype = _sz
+    lib.ekernel_add_rmsnorm_bf16_splitk.argtypes = [_vp, _vp, _i32, _vp, _sz, _sz, ctypes.c_float, _i32, _vp]
+    lib.ekernel_qk_norm_rope_kv_append_splitk.argtypes = [ctypes.POINTER(PagedAttnDesc), _vp, _i32] + [_vp] * 10
     lib.ekernel_linear_bf16.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp, _vp]
     lib.ekernel_linear_bf16.restype = _i32
     lib.ekernel_repack_w4_kpairs.argtypes = [_vp, _sz, _sz, _vp]
@@ -356,6 +367,21 @@ def linear_w4a16g128_bf16_kpairs_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, i
 
 def linear_w4a16_bf16_kpairs_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa=None) -> int:
     return _linear("ekernel_linear_w4a16_bf16_kpairs", a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, isa)
+
+
+def linear_w4a16g128_bf16_kpairs_deferred_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, part_ptr,
+                                              part_bytes) -> tuple[int, int]:
+    """(rc, splits): splits > 0 means the result was left as split-K partial sums at part_ptr
+    ([splits][m][n] fp32) and c_ptr was not written."""
+    d = EkernelLinearW8A32Desc(m, n, k)
+    sp = _i32(0)
+    rc = _load_lib().ekernel_linear_w4a16g128_bf16_kpairs_deferred(ctypes.byref(d), a_ptr, w_ptr, scales_ptr, c_ptr,
+                                                                   part_ptr, part_bytes, ctypes.byref(sp))
+    return int(rc), int(sp.value)
+
+
+def linear_w4a16g128_partials_bytes(m, n, k) -> int:
+    return int(_load_lib().ekernel_linear_w4a16g128_partials_bytes(m, n, k))
 
 
 def linear_bf16_ptr(a_ptr, w_ptr, c_ptr, m, n, k) -> int:

@@ -276,6 +276,25 @@ def add_rmsnorm_bf16(residual: torch.Tensor, delta: Optional[torch.Tensor], weig
     return out
 
 
+def add_rmsnorm_bf16_splitk(residual: torch.Tensor, partials: torch.Tensor, splits: int, weight: torch.Tensor,
+                            eps: float, add_one: bool, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """add_rmsnorm_bf16 with the delta given as a deferred W4 linear's split-K partial sums
+    (partials holds at least [splits, rows, n] fp32): bit-identical to passing the linear's
+    bf16 output."""
+    if residual.device.type != "cuda" or residual.dtype != torch.bfloat16 or not residual.is_contiguous():
+        raise ValueError("residual must be a contiguous CUDA bfloat16 tensor")
+    rows, n = residual.shape
+    if partials.dtype != torch.float32 or partials.numel() < splits * rows * n:
+        raise ValueError("partials must be fp32 with at least splits * rows * n elements")
+    out = _out(out, residual.shape, residual.dtype, residual.device)
+    _stream()
+    _check(abi.lib().ekernel_add_rmsnorm_bf16_splitk(residual.data_ptr(), partials.data_ptr(), int(splits),
+                                                     weight.data_ptr(), rows, n, float(eps), int(add_one),
+                                                     out.data_ptr()),
+           "ekernel_add_rmsnorm_bf16_splitk")
+    return out
+
+
 def mtp_fc_input_bf16(hidden: torch.Tensor, row_base: Optional[torch.Tensor], row_offset: Optional[torch.Tensor],
                       embed: torch.Tensor, tokens: torch.Tensor, w_embed_norm: torch.Tensor,
                       w_hidden_norm: torch.Tensor, eps: float, add_one: bool,
@@ -336,6 +355,21 @@ def qk_norm_rope_kv_append(desc, qkv, q_norm_w, k_norm_w, rope_cos, rope_sin, po
                                                     _p(rope_cos), _p(rope_sin), _p(positions), _p(slot_mapping),
                                                     _p(k_cache), _p(v_cache), _p(q_out), _p(gate_out)),
            "ekernel_qk_norm_rope_kv_append")
+
+
+def qk_norm_rope_kv_append_splitk(desc, partials, splits, q_norm_w, k_norm_w, rope_cos, rope_sin, positions,
+                                  slot_mapping, k_cache, v_cache, q_out, gate_out=None) -> None:
+    """qk_norm_rope_kv_append with the fused projection given as a deferred W4 linear's
+    split-K partial sums ([splits, total_q, qkv_stride] fp32): bit-identical results."""
+    if partials.dtype != torch.float32 or partials.numel() < splits * desc.total_q * desc.qkv_stride:
+        raise ValueError("partials must be fp32 with at least splits * total_q * qkv_stride elements")
+    _stream()
+    import ctypes
+    _check(abi.lib().ekernel_qk_norm_rope_kv_append_splitk(ctypes.byref(desc), _p(partials), int(splits),
+                                                           _p(q_norm_w), _p(k_norm_w), _p(rope_cos), _p(rope_sin),
+                                                           _p(positions), _p(slot_mapping), _p(k_cache), _p(v_cache),
+                                                           _p(q_out), _p(gate_out)),
+           "ekernel_qk_norm_rope_kv_append_splitk")
 
 
 def paged_attention_verify(desc, q, k_cache, v_cache, block_table, cu_q, context_lens, gate, out) -> None:

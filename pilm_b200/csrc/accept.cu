@@ -169,8 +169,9 @@ __global__ void greedy_accept(int B, const int32_t *__restrict__ ids, const int3
 // Masses e_j = exp((l_j - mx) / T) <= 1 are summed in unsigned 64-bit fixed point with 40
 // fractional bits.  Integer sums do not depend on the order of summation, so every pass,
 // thread count and launch agrees exactly; V < 2^23 keeps them below 2^63.  The nucleus cut
-// takes three reads of the row: its max; a histogram of masses and counts over 2048 linear
-// bins of (mx - l) / T, which locates the bin holding the cut; and a gather of that bin's
+// takes three reads of the row: its max; a histogram of masses over 2048 linear bins of
+// (mx - l) / T (one shared-memory atomic per token of nonzero mass), which locates the bin
+// holding the cut; and a gather of that bin's
 // tokens (at most 2048), among which the cut is found by exact pairwise comparison.  A cut
 // bin with more tokens falls back to a radix select over the 32-bit keys of the whole row
 // (11 + 11 + 10 bits, three more reads).
@@ -302,7 +303,6 @@ __device__ __forceinline__ int rs_bin(float l, float mx, float inv_t) {
 struct RsSmem {
     unsigned long long hist[kRsBins];  // level-0 masses; later the fallback's histograms
     unsigned long long sfx[kRsBins];
-    unsigned int cnt[kRsBins];
     uint32_t gkey[kRsGather];
     unsigned long long gmass[kRsGather];
     unsigned long long wsum[32];
@@ -366,54 +366,53 @@ __global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__
     row_for_each(x, V, [&](int, float l) { mx = fmaxf(mx, l); });
     mx = block_max(mx, sm.shf);
 
-    // level 0: masses and counts per bin
-    for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) {
-        sm.hist[d] = 0;
-        sm.cnt[d] = 0;
-    }
+    // level 0: masses per bin.  Only tokens of nonzero fixed-point mass are added: a
+    // token of zero mass has the whole total strictly above it, so it is never in the
+    // nucleus (top_p <= 1); and since masses never grow with distance from the max, a bin
+    // holding only such tokens is followed by such bins only, so "the last bin of nonzero
+    // mass whose higher bins hold less than the target" is the bin of the cut.  The
+    // catch-all bin (u >= kRsSpan) holds masses below 2^-57, zero in fixed point.
+    for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) sm.hist[d] = 0;
     __syncthreads();
-    // Tokens in the catch-all bin (u >= kRsSpan) have mass exactly 0 in fixed point, so their
-    // strictly-above mass is the whole total: they are never in the nucleus (top_p <= 1) and
-    // the cut's bin is never theirs.  They are not counted, which keeps the many low-logit
-    // tokens of a row off one contended bin.
     row_for_each(x, V, [&](int, float l) {
         const int bn = rs_bin(l, mx, inv_t);
         if (bn == kRsBins - 1) return;
-        atomicAdd(&sm.hist[bn], rs_mass(l, mx, inv_t));
-        atomicAdd(&sm.cnt[bn], 1u);
+        const unsigned long long m = rs_mass(l, mx, inv_t);
+        if (m) atomicAdd(&sm.hist[bn], m);
     });
     __syncthreads();
     suffix_sums(sm.hist, sm.sfx, sm.wsum);
     const unsigned long long total = sm.sfx[0];
     const double target = (double)top_p * (double)total;  // the nucleus keeps above-mass < top_p Z
-    // the cut lies in the last non-empty bin whose higher bins hold less than the target
     if (threadIdx.x == 0) sm.s_bin = -1;
     __syncthreads();
     for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) {
         const unsigned long long higher = total - sm.sfx[d];  // mass of bins before d
-        if (sm.cnt[d] && (double)higher < target) atomicMax(&sm.s_bin, d);
+        if (sm.hist[d] && (double)higher < target) atomicMax(&sm.s_bin, d);
+    }
+    if (threadIdx.x == 0) {
+        sm.s_n = 0;
+        sm.s_cut = 0xffffffffu;
     }
     __syncthreads();
     const int bstar = sm.s_bin;
     const unsigned long long base = total - sm.sfx[bstar];  // mass strictly above the cut's bin
     uint32_t cut;
     unsigned long long zn;
-    if (sm.cnt[bstar] <= (unsigned)kRsGather) {
-        // gather the bin's tokens; a token's above-mass is base + the masses of the bin's
-        // tokens with a greater key, and the cut is the smallest key whose above-mass < target
-        if (threadIdx.x == 0) {
-            sm.s_n = 0;
-            sm.s_cut = 0xffffffffu;
-        }
-        __syncthreads();
-        row_for_each(x, V, [&](int, float l) {
-            if (rs_bin(l, mx, inv_t) == bstar) {
-                const int slot = atomicAdd(&sm.s_n, 1);
+    // gather the bin's tokens (slots past kRsGather are counted, not stored); a token's
+    // above-mass is base + the masses of the bin's tokens with a greater key, and the cut
+    // is the smallest key whose above-mass < target
+    row_for_each(x, V, [&](int, float l) {
+        if (rs_bin(l, mx, inv_t) == bstar) {
+            const int slot = atomicAdd(&sm.s_n, 1);
+            if (slot < kRsGather) {
                 sm.gkey[slot] = fkey(l);
                 sm.gmass[slot] = rs_mass(l, mx, inv_t);
             }
-        });
-        __syncthreads();
+        }
+    });
+    __syncthreads();
+    if (sm.s_n <= kRsGather) {
         const int n = sm.s_n;
         for (int i = threadIdx.x; i < n; i += blockDim.x) {
             const uint32_t ki = sm.gkey[i];

@@ -45,7 +45,24 @@ constexpr uint32_t kAttnWaitLimit = 1u << 22;  // polls before a page wait gives
 // ---------------------------------------------------------------------------------
 // Prologue: q/k RMSNorm + RoPE, KV append
 // ---------------------------------------------------------------------------------
-__global__ void qk_prologue(const __nv_bfloat16 *__restrict__ qkv, int total_q, int nh, int nkv, int qkv_stride,
+// The projection row comes as bf16 (qkv) or as split-K partial sums of the W4 linear
+// (part: [splits][total_q][qkv_stride] fp32), summed in split order and rounded to bf16
+// exactly as the GEMM's combine pass would have written them.
+struct QkvSrc {
+    const __nv_bfloat16 *qkv;
+    const float *part;
+    int splits;
+    size_t plane;
+    __device__ __forceinline__ float at(size_t idx) const {
+        return part ? bf16_round(sum_splits(part + idx, splits, plane)) : bf2f(qkv[idx]);
+    }
+    // the element as bf16: copied as it is from the projection, or the rounded sum
+    __device__ __forceinline__ __nv_bfloat16 bf(size_t idx) const {
+        return part ? f2bf(sum_splits(part + idx, splits, plane)) : qkv[idx];
+    }
+};
+
+__global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, int qkv_stride,
                             int gated, const __nv_bfloat16 *__restrict__ qnw, const __nv_bfloat16 *__restrict__ knw,
                             float eps, int add_one, const float *__restrict__ cos_t, const float *__restrict__ sin_t,
                             int rope_rows, int rot_dim, const int32_t *__restrict__ positions,
@@ -60,18 +77,18 @@ __global__ void qk_prologue(const __nv_bfloat16 *__restrict__ qkv, int total_q, 
     if (item >= total_q * heads) return;
     const int row = item / heads, h = item % heads;
     const bool is_q = h < nh;
-    const __nv_bfloat16 *src;
+    size_t src;  // element offset of this head's 128 values
     const int qsec = nh * kHD * (gated ? 2 : 1);
     if (is_q)
-        src = qkv + (size_t)row * qkv_stride + (size_t)h * kHD * (gated ? 2 : 1);
+        src = (size_t)row * qkv_stride + (size_t)h * kHD * (gated ? 2 : 1);
     else
-        src = qkv + (size_t)row * qkv_stride + qsec + (size_t)(h - nh) * kHD;
+        src = (size_t)row * qkv_stride + qsec + (size_t)(h - nh) * kHD;
     const __nv_bfloat16 *nw = is_q ? qnw : knw;
     float x[4];
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        x[j] = bf2f(src[lane + 32 * j]);
+        x[j] = src_in.at(src + lane + 32 * j);
         ss = fmaf(x[j], x[j], ss);
     }
     ss = warp_sum(ss);
@@ -112,10 +129,9 @@ __global__ void qk_prologue(const __nv_bfloat16 *__restrict__ qkv, int total_q, 
 #pragma unroll
         for (int j = 0; j < 4; ++j) qo[lane + 32 * j] = f2bf(y[j]);
         if (gated && gate_out) {
-            const __nv_bfloat16 *gsrc = src + kHD;
             __nv_bfloat16 *go = gate_out + (size_t)row * nh * kHD + (size_t)h * kHD;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) go[lane + 32 * j] = gsrc[lane + 32 * j];
+            for (int j = 0; j < 4; ++j) go[lane + 32 * j] = src_in.bf(src + kHD + lane + 32 * j);
         }
     } else {
         const long long slot = slots[row];
@@ -123,11 +139,11 @@ __global__ void qk_prologue(const __nv_bfloat16 *__restrict__ qkv, int total_q, 
         const int kvh = h - nh;
         __nv_bfloat16 *kd = kc + ((size_t)slot * nkv + kvh) * kHD;
         __nv_bfloat16 *vd = vc + ((size_t)slot * nkv + kvh) * kHD;
-        const __nv_bfloat16 *vsrc = qkv + (size_t)row * qkv_stride + qsec + (size_t)nkv * kHD + (size_t)kvh * kHD;
+        const size_t vsrc = (size_t)row * qkv_stride + qsec + (size_t)nkv * kHD + (size_t)kvh * kHD;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             kd[lane + 32 * j] = f2bf(y[j]);
-            vd[lane + 32 * j] = vsrc[lane + 32 * j];
+            vd[lane + 32 * j] = src_in.bf(vsrc + lane + 32 * j);
         }
     }
 }
@@ -561,6 +577,8 @@ __global__ void attn_merge(const AttnParams p) {
 constexpr int kPMaxKv = 8;       // KV heads per CTA (one consumer warp each)
 constexpr int kPStages = 3;      // pages in flight
 constexpr int kPMaxSeqs = 1024;  // sequences per call (page prefix kept in shared memory)
+constexpr int kPRec = kHD + 4;   // one cut-sequence record: O[128], m, l and two pad floats (16-byte rows)
+constexpr int kMergeHeads = 4;   // heads per merge CTA (one warp each)
 
 struct PageAttnParams {
     const __nv_bfloat16 *q;      // [total_q, nh, 128]
@@ -569,8 +587,7 @@ struct PageAttnParams {
     const int32_t *ctx;          // [B]
     const __nv_bfloat16 *gate;   // [total_q, nh*128] or null
     __nv_bfloat16 *out;          // [total_q, nh*128]
-    float *part;                 // [G][2][max_q][nh][128 + 2]: O, m, l
-    int *prefix;                 // [B+1] pages before each sequence (CTA 0 writes it for the merge)
+    float *part;                 // [G][2][max_q][nh][kPRec]: O, m, l
     int *err;                    // device error word
     int nh, nkv, gsz, max_blocks, num_blocks, B, max_q, G, total_q;
     float scale;
@@ -639,8 +656,6 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (cta == 0)
-        for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.prefix[i] = s_prefix[i];
     const long long T = s_prefix[p.B];
     const long long s_c = ((long long)cta * T) / p.G, e_c = ((long long)(cta + 1) * T) / p.G;
     if (s_c >= e_c) return;
@@ -899,7 +914,7 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
                             p.out[ob + d] = f2bf(v);
                         }
                 } else {
-                    float *rec = p.part + ((((size_t)cta * 2 + slot) * p.max_q + j) * p.nh + head) * (kHD + 2);
+                    float *rec = p.part + ((((size_t)cta * 2 + slot) * p.max_q + j) * p.nh + head) * kPRec;
 #pragma unroll
                     for (int nt = 0; nt < 16; ++nt) {
                         rec[nt * 8 + 2 * c] = o[mt][nt][hh * 2 + 0];
@@ -914,42 +929,57 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
     }
 }
 
-// grid: (nh, max_q, B); block: 128 (one thread per dim).  Combines, in CTA order, the
-// per-CTA partials of a sequence that CTA range boundaries cut; a sequence one CTA holds
-// whole was written by that CTA.  Launched as a programmatic dependent of attn_pages: every
-// CTA waits for that grid first.  The loads of each step are independent of one another,
-// so a CTA waits on three rounds of memory: the metadata, then the pieces' (m, l, O).
-__global__ void attn_merge_pages(const PageAttnParams p) {
-    pdl_entry();
-    const int head = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
-    const int d = threadIdx.x;
+// grid: (ceil(nh / 4), max_q, B); block: 128.  Warp w combines, in CTA order, the pieces
+// that CTA range boundaries cut from head 4 * blockIdx.x + w of row j of sequence b; lane l
+// takes dims 4l .. 4l + 3.  A sequence one CTA holds whole was written by that CTA.  The
+// page ranges come from the context lengths, which the page kernel does not write, so they
+// are worked out before the programmatic-dependent wait: once attn_pages completes, one
+// round of independent loads remains (every piece's m, l and four O values).
+__global__ void __launch_bounds__(kMergeHeads * 32) attn_merge_pages(const PageAttnParams p) {
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = blockIdx.x * kMergeHeads + warp, j = blockIdx.y, b = blockIdx.z;
     const int q0 = p.cu_q[b], q1 = p.cu_q[b + 1];
-    const long long P0 = p.prefix[b], P1 = p.prefix[b + 1], T = p.prefix[p.B];
-    if (j >= q1 - q0 || P1 <= P0 || T <= 0) return;
+    // pages before sequence b (P0), of sequence b and in total (T): the page kernel's prefix
+    long long P0 = 0, T = 0;
+    for (int i0 = 0; i0 < p.B; i0 += 32) {
+        const int i = i0 + lane;
+        int pg = 0;
+        if (i < p.B) {
+            const int cx = p.ctx[i];
+            pg = cx > 0 ? (cx + 15) >> 4 : 0;
+        }
+        T += __reduce_add_sync(0xffffffffu, (unsigned)pg);
+        P0 += __reduce_add_sync(0xffffffffu, (unsigned)(i < b ? pg : 0));
+    }
+    const int cxb = p.ctx[b];
+    const long long P1 = P0 + (cxb > 0 ? (cxb + 15) >> 4 : 0);
+    if (head >= p.nh || j >= q1 - q0 || P1 <= P0 || T <= 0) return;
     const int c0 = cta_of_page(P0, T, p.G), c1 = cta_of_page(P1 - 1, T, p.G);
     if (c0 == c1) return;  // finished by its CTA
-    const size_t ob = (size_t)(q0 + j) * p.nh * kHD + (size_t)head * kHD;
-    const float gt = p.gate ? bf2f(p.gate[ob + d]) : 0.f;
+    const size_t ob = (size_t)(q0 + j) * p.nh * kHD + (size_t)head * kHD + 4 * lane;
+    pdl_wait();
     // CTA c's record for this sequence: slot 0 if the sequence starts inside c's range,
     // slot 1 if it runs on from before; CTAs with an empty range (more CTAs than pages)
     // wrote nothing and are skipped
     constexpr int U = 8;
-    float M = -INFINITY, L = 0.f, O = 0.f;
+    float M = -INFINITY, L = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
     for (int cb = c0; cb <= c1; cb += U) {
-        float m[U], l[U], o[U];
+        float m[U], l[U];
+        float4 o[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             m[u] = -INFINITY;
             l[u] = 0.f;
-            o[u] = 0.f;
+            o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             const int c = cb + u;
             const long long lo = ((long long)c * T) / p.G, hi = ((long long)(c + 1) * T) / p.G;
             if (c <= c1 && lo < hi) {
                 const float *rec =
-                    p.part + ((((size_t)c * 2 + (lo >= P0 ? 0 : 1)) * p.max_q + j) * p.nh + head) * (kHD + 2);
-                m[u] = rec[kHD];
-                l[u] = rec[kHD + 1];
-                o[u] = rec[d];
+                    p.part + ((((size_t)c * 2 + (lo >= P0 ? 0 : 1)) * p.max_q + j) * p.nh + head) * kPRec;
+                m[u] = __ldcg(rec + kHD);
+                l[u] = __ldcg(rec + kHD + 1);
+                o[u] = __ldcg(reinterpret_cast<const float4 *>(rec + 4 * lane));
             }
         }
         float mc = M;
@@ -960,7 +990,8 @@ __global__ void attn_merge_pages(const PageAttnParams p) {
         if (mc > M && L > 0.f) {  // only when the pieces exceed one chunk of U
             const float f = expf(M - mc);
             L *= f;
-            O *= f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) O[e] *= f;
         }
         M = mc;
 #pragma unroll
@@ -968,15 +999,26 @@ __global__ void attn_merge_pages(const PageAttnParams p) {
             if (!(l[u] > 0.f)) continue;
             const float f = expf(m[u] - M);
             L += l[u] * f;
-            O += o[u] * f;
+            O[0] += o[u].x * f;
+            O[1] += o[u].y * f;
+            O[2] += o[u].z * f;
+            O[3] += o[u].w * f;
         }
     }
-    float v = L > 0.f ? bf16_round(__fdiv_rn(O, L)) : 0.f;
-    if (p.gate) {
-        const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt))));
-        v = __fmul_rn(v, sg);
+    __align__(8) __nv_bfloat16 outv[4];
+    uint2 gbits = make_uint2(0u, 0u);
+    if (p.gate) gbits = *reinterpret_cast<const uint2 *>(p.gate + ob);
+    const __nv_bfloat16 *gv = reinterpret_cast<const __nv_bfloat16 *>(&gbits);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        float v = L > 0.f ? bf16_round(__fdiv_rn(O[e], L)) : 0.f;
+        if (p.gate) {
+            const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-bf2f(gv[e])))));
+            v = __fmul_rn(v, sg);
+        }
+        outv[e] = f2bf(v);
     }
-    p.out[ob + d] = f2bf(v);
+    *reinterpret_cast<uint2 *>(p.out + ob) = *reinterpret_cast<const uint2 *>(outv);
 }
 
 // Clear the split partials of every (row, head) so that CTAs which exit early (no
@@ -1068,11 +1110,10 @@ int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnPara
     p.scale = a.scale;
     p.err = device_error_word();
     PILM_REQUIRE(p.err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
-    const size_t part_bytes = (size_t)p.G * 2 * max_q * p.nh * (kHD + 2) * sizeof(float);
-    char *ws = (char *)scratch(kScratchAttn, part_bytes + ((size_t)p.B + 1) * sizeof(int) + 256);
+    const size_t part_bytes = (size_t)p.G * 2 * max_q * p.nh * kPRec * sizeof(float);
+    char *ws = (char *)scratch(kScratchAttn, part_bytes + 256);
     PILM_REQUIRE(ws, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     p.part = (float *)ws;
-    p.prefix = (int *)(ws + part_bytes);
     CUtensorMap maps[2];
     int rc = encode_kv_page_maps(a.kc, a.vc, a.nkv, a.num_blocks, maps, what);
     if (rc != ECPU_OK) return rc;
@@ -1085,8 +1126,8 @@ int launch_attention_pages(const ekernel_paged_attn_desc_t *desc, const AttnPara
     rc = check_error_word(what, "a K/V page load did not complete");
     if (rc != ECPU_OK) return rc;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)p.nh, (unsigned)p.max_q, (unsigned)p.B);
-    cfg.blockDim = dim3(kHD);
+    cfg.gridDim = dim3((unsigned)((p.nh + kMergeHeads - 1) / kMergeHeads), (unsigned)p.max_q, (unsigned)p.B);
+    cfg.blockDim = dim3(kMergeHeads * 32);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream();
     cudaLaunchAttribute attr[1];
@@ -1186,8 +1227,33 @@ int ekernel_qk_norm_rope_kv_append(const ekernel_paged_attn_desc_t *desc, const 
     PILM_REQUIRE(!desc->output_gate || gate_out, ECPU_ERR_PARAM, "%s: gate_out required when output_gate", what);
     if (desc->total_q == 0) return ECPU_OK;
     const int items = (int)(desc->total_q * (desc->n_heads + desc->n_kv_heads));
+    const QkvSrc src{(const __nv_bfloat16 *)qkv, nullptr, 0, 0};
     launch_pdl(qk_prologue, dim3((items + 7) / 8), dim3(256), 0, 
-        (const __nv_bfloat16 *)qkv, (int)desc->total_q, (int)desc->n_heads, (int)desc->n_kv_heads,
+        src, (int)desc->total_q, (int)desc->n_heads, (int)desc->n_kv_heads,
+        (int)desc->qkv_stride, desc->output_gate, (const __nv_bfloat16 *)q_norm_w, (const __nv_bfloat16 *)k_norm_w,
+        desc->eps, desc->add_one, rope_cos, rope_sin, (int)desc->rope_rows, (int)desc->rot_dim, positions,
+        slot_mapping, (long long)desc->num_blocks * (long long)desc->block_size, (__nv_bfloat16 *)k_cache,
+        (__nv_bfloat16 *)v_cache, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)gate_out);
+    return check_launch(what);
+}
+
+int ekernel_qk_norm_rope_kv_append_splitk(const ekernel_paged_attn_desc_t *desc, const float *partials,
+                                          int32_t splits, const uint16_t *q_norm_w, const uint16_t *k_norm_w,
+                                          const float *rope_cos, const float *rope_sin, const int32_t *positions,
+                                          const int32_t *slot_mapping, uint16_t *k_cache, uint16_t *v_cache,
+                                          uint16_t *q_out, uint16_t *gate_out) {
+    const char *what = "ekernel_qk_norm_rope_kv_append_splitk";
+    int rc = check_desc(desc, what);
+    if (rc != ECPU_OK) return rc;
+    PILM_REQUIRE(partials && splits > 0 && q_norm_w && k_norm_w && rope_cos && rope_sin && positions &&
+                     slot_mapping && k_cache && v_cache && q_out,
+                 ECPU_ERR_PARAM, "%s: null argument", what);
+    PILM_REQUIRE(!desc->output_gate || gate_out, ECPU_ERR_PARAM, "%s: gate_out required when output_gate", what);
+    if (desc->total_q == 0) return ECPU_OK;
+    const int items = (int)(desc->total_q * (desc->n_heads + desc->n_kv_heads));
+    const QkvSrc src{nullptr, partials, (int)splits, (size_t)desc->total_q * desc->qkv_stride};
+    launch_pdl(qk_prologue, dim3((items + 7) / 8), dim3(256), 0, 
+        src, (int)desc->total_q, (int)desc->n_heads, (int)desc->n_kv_heads,
         (int)desc->qkv_stride, desc->output_gate, (const __nv_bfloat16 *)q_norm_w, (const __nv_bfloat16 *)k_norm_w,
         desc->eps, desc->add_one, rope_cos, rope_sin, (int)desc->rope_rows, (int)desc->rot_dim, positions,
         slot_mapping, (long long)desc->num_blocks * (long long)desc->block_size, (__nv_bfloat16 *)k_cache,

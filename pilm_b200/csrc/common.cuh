@@ -32,12 +32,20 @@ int *counters(size_t n);  // zero-initialised, self-resetting arrival counters
 // W4 GEMM for M > 16 (tcgen05 path, linear_tc.cu); returns ECPU_ERR_UNSUPPORTED
 // when the shape is not handled there, in which case the caller uses the GEMV.
 // kpairs: the packed weights are in the k-pair nibble order (ekernel_repack_w4_kpairs).
+// defer (optional): when the call runs the split schedule with grouped scales and its
+// [splits][M][N] fp32 partials fit in defer_cap bytes at defer (16-byte aligned), they are
+// left there, Y is not written, no combine pass runs and *defer_splits = splits; otherwise
+// *defer_splits = 0 and Y holds the result.
 int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N,
-                 __nv_bfloat16 *Y, bool grouped, bool kpairs, const char *what);
+                 __nv_bfloat16 *Y, bool grouped, bool kpairs, const char *what, float *defer = nullptr,
+                 size_t defer_cap = 0, int *defer_splits = nullptr);
+// Bytes of split-K partials a deferred call of this shape would leave (0: it would not).
+size_t w4_tc_partials_bytes(int M, int N, int K);
 // Quantized bf16 linear (linear.cu).  qf: 0 = W4 grouped (gs 32/128), 1 = W4 per-row,
 // 2 = W8 per-row.  kpairs (W4 only): weights in the k-pair nibble order.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
-                const char *what, bool kpairs = false);
+                const char *what, bool kpairs = false, float *defer = nullptr, size_t defer_cap = 0,
+                int *defer_splits = nullptr);
 
 // cuTensorMapEncodeTiled, reached through the runtime's driver entry point (no link
 // against libcuda); null if the driver does not provide it.
@@ -99,6 +107,22 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Sum of p[sp * plane] over sp = 0 .. splits - 1, added in split order starting from 0 (as
+// the split-K combine pass adds), with the loads of up to 8 splits issued before the adds
+// so that they wait on memory once, not once per split.
+__device__ __forceinline__ float sum_splits(const float *p, int splits, size_t plane) {
+    float v = 0.f;
+    for (int s0 = 0; s0 < splits; s0 += 8) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = s0 + u < splits ? __ldcs(p + (size_t)(s0 + u) * plane) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (s0 + u < splits) v += t[u];
+    }
+    return v;
+}
 __device__ __forceinline__ float bits2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {

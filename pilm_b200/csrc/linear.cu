@@ -630,7 +630,8 @@ namespace pilm {
 // Shared entry used by the ABI wrappers and by the fused SwiGLU path.
 // qf: 0 = W4 grouped (gs = 32 or 128), 1 = W4 per-row, 2 = W8 per-row.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
-                const char *what, bool kpairs) {
+                const char *what, bool kpairs, float *defer, size_t defer_cap, int *defer_splits) {
+    if (defer_splits) *defer_splits = 0;
     const __nv_bfloat16 *X = (const __nv_bfloat16 *)A;
     __nv_bfloat16 *Y = (__nv_bfloat16 *)C;
     if (M == 0 || N == 0) return ECPU_OK;
@@ -641,7 +642,8 @@ int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, cons
         // above 16 rows the register-dequant GEMV re-reads each activation tile per 16
         // weight rows; the tensor-core GEMM stages it once per 128 (N = 32, 48, ... rows)
         if (M > 16) {
-            int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, kpairs, what);
+            int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, kpairs, what, defer, defer_cap,
+                                  defer_splits);
             if (rc != ECPU_ERR_UNSUPPORTED) return rc;
         }
         // register-dequant GEMV, in slabs of at most 64 activation rows
@@ -815,6 +817,24 @@ int ekernel_linear_w4a16g128_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc
     LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16_kpairs");
     return pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
                              "ekernel_linear_w4a16g128_bf16_kpairs", true);
+}
+
+int ekernel_linear_w4a16g128_bf16_kpairs_deferred(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                                  const uint8_t *W, const float *scales, uint16_t *C,
+                                                  float *partials, size_t partials_bytes, int32_t *splits) {
+    LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16_kpairs_deferred");
+    PILM_REQUIRE(splits, ECPU_ERR_PARAM, "ekernel_linear_w4a16g128_bf16_kpairs_deferred: null splits");
+    int s = 0;
+    const int rc = pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                                     "ekernel_linear_w4a16g128_bf16_kpairs_deferred", true, partials,
+                                     partials ? partials_bytes : 0, &s);
+    *splits = rc == ECPU_OK ? s : 0;
+    return rc;
+}
+
+size_t ekernel_linear_w4a16g128_partials_bytes(size_t M, size_t N, size_t K) {
+    if (M > 0x7fffffff || N > 0x7fffffff || K > 0x7fffffff) return 0;
+    return pilm::w4_tc_partials_bytes((int)M, (int)N, (int)K);
 }
 
 int ekernel_linear_w4a16_bf16_kpairs(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A, const uint8_t *W,

@@ -78,15 +78,57 @@ __global__ void add_rmsnorm_kernel(__nv_bfloat16 *__restrict__ res, const __nv_b
 // held in registers: 16-byte loads/stores, one read of the residual and delta, one
 // block reduction.  n % 8 == 0 and n <= 256 * 8 * VPT.
 template <int VPT>
+// The delta comes as bf16 (delta) or as split-K partial sums of a W4 linear (part:
+// [splits][rows][n] fp32), which are summed in split order and rounded to bf16 exactly as
+// the GEMM's combine pass would have written them.
 __global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__restrict__ res,
                                                               const __nv_bfloat16 *__restrict__ delta,
                                                               const __nv_bfloat16 *__restrict__ w, int n, float eps,
-                                                              int add_one, __nv_bfloat16 *__restrict__ out) {
+                                                              int add_one, __nv_bfloat16 *__restrict__ out,
+                                                              const float *__restrict__ part, int splits,
+                                                              size_t plane) {
     pdl_entry();
     __shared__ float red[8];
     const int row = blockIdx.x;
     __nv_bfloat16 *r = res + (size_t)row * n;
     const __nv_bfloat16 *d = delta ? delta + (size_t)row * n : nullptr;
+    const float *pr = part ? part + (size_t)row * n : nullptr;
+    // partial sums: every element's splits added in split order, the loads of a batch of
+    // splits for all of this thread's elements issued before the adds (16 in flight)
+    float ps[VPT][8];
+    if (pr) {
+        constexpr int SB = VPT <= 2 ? 4 : 2;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ps[v][j] = 0.f;
+        for (int s0 = 0; s0 < splits; s0 += SB) {
+            float4 t[SB][VPT][2];
+#pragma unroll
+            for (int u = 0; u < SB; ++u)
+#pragma unroll
+                for (int v = 0; v < VPT; ++v) {
+                    const int i = (v * 256 + threadIdx.x) * 8;
+                    if (s0 + u < splits && i < n) {
+                        const float *q = pr + (size_t)(s0 + u) * plane + i;
+                        t[u][v][0] = __ldcs(reinterpret_cast<const float4 *>(q));
+                        t[u][v][1] = __ldcs(reinterpret_cast<const float4 *>(q + 4));
+                    }
+                }
+#pragma unroll
+            for (int u = 0; u < SB; ++u)
+#pragma unroll
+                for (int v = 0; v < VPT; ++v) {
+                    const int i = (v * 256 + threadIdx.x) * 8;
+                    if (s0 + u < splits && i < n) {
+                        ps[v][0] += t[u][v][0].x; ps[v][1] += t[u][v][0].y;
+                        ps[v][2] += t[u][v][0].z; ps[v][3] += t[u][v][0].w;
+                        ps[v][4] += t[u][v][1].x; ps[v][5] += t[u][v][1].y;
+                        ps[v][6] += t[u][v][1].z; ps[v][7] += t[u][v][1].w;
+                    }
+                }
+        }
+    }
     float x[VPT][8];
     float ss = 0.f;
 #pragma unroll
@@ -95,14 +137,22 @@ __global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__r
         if (i < n) {
             uint4 rv = *reinterpret_cast<const uint4 *>(r + i);
             const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
-            if (d) {
-                uint4 dv = *reinterpret_cast<const uint4 *>(d + i);
-                const __nv_bfloat16 *de = reinterpret_cast<const __nv_bfloat16 *>(&dv);
+            if (d || pr) {
+                float dl[8];
+                if (pr) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) dl[j] = bf16_round(ps[v][j]);
+                } else {
+                    uint4 dv = *reinterpret_cast<const uint4 *>(d + i);
+                    const __nv_bfloat16 *de = reinterpret_cast<const __nv_bfloat16 *>(&dv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) dl[j] = bf2f(de[j]);
+                }
                 uint4 o;
                 __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&o);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    oe[j] = f2bf(__fadd_rn(bf2f(re[j]), bf2f(de[j])));
+                    oe[j] = f2bf(__fadd_rn(bf2f(re[j]), dl[j]));
                     x[v][j] = bf2f(oe[j]);
                 }
                 *reinterpret_cast<uint4 *>(r + i) = o;
@@ -248,17 +298,39 @@ int ekernel_add_rmsnorm_bf16(uint16_t *residual, const uint16_t *delta, const ui
     if (vec) {
         const __nv_bfloat16 *dl = (const __nv_bfloat16 *)delta;
         if (n <= 256 * 8 * 2)
-            launch_pdl(add_rmsnorm_row_kernel<2>, dim3((unsigned)rows), dim3(256), 0, 
-                (__nv_bfloat16 *)residual, dl, (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out);
+            launch_pdl(add_rmsnorm_row_kernel<2>, dim3((unsigned)rows), dim3(256), 0, (__nv_bfloat16 *)residual, dl,
+                       (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out,
+                       (const float *)nullptr, 0, (size_t)0);
         else
-            launch_pdl(add_rmsnorm_row_kernel<4>, dim3((unsigned)rows), dim3(256), 0, 
-                (__nv_bfloat16 *)residual, dl, (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out);
+            launch_pdl(add_rmsnorm_row_kernel<4>, dim3((unsigned)rows), dim3(256), 0, (__nv_bfloat16 *)residual, dl,
+                       (const __nv_bfloat16 *)weight, (int)n, eps, add_one, (__nv_bfloat16 *)out,
+                       (const float *)nullptr, 0, (size_t)0);
         return check_launch("ekernel_add_rmsnorm_bf16");
     }
     launch_pdl(add_rmsnorm_kernel, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, 
         (__nv_bfloat16 *)residual, (const __nv_bfloat16 *)delta, (const __nv_bfloat16 *)weight, (int)rows, (int)n,
         eps, add_one, (__nv_bfloat16 *)out);
     return check_launch("ekernel_add_rmsnorm_bf16");
+}
+
+int ekernel_add_rmsnorm_bf16_splitk(uint16_t *residual, const float *partials, int32_t splits, const uint16_t *weight,
+                                    size_t rows, size_t n, float eps, int add_one, uint16_t *out) {
+    const char *what = "ekernel_add_rmsnorm_bf16_splitk";
+    PILM_REQUIRE(residual && partials && weight && out && rows > 0 && n > 0 && splits > 0, ECPU_ERR_PARAM,
+                 "%s: bad argument", what);
+    PILM_REQUIRE((n % 8) == 0 && n <= 256 * 8 * 4 &&
+                     ((((uintptr_t)residual) | ((uintptr_t)out) | ((uintptr_t)weight) | ((uintptr_t)partials)) & 15) == 0,
+                 ECPU_ERR_UNSUPPORTED, "%s: needs n %% 8 == 0, n <= 8192 and 16-byte aligned buffers", what);
+    const size_t plane = rows * n;
+    if (n <= 256 * 8 * 2)
+        launch_pdl(add_rmsnorm_row_kernel<2>, dim3((unsigned)rows), dim3(256), 0, (__nv_bfloat16 *)residual,
+                   (const __nv_bfloat16 *)nullptr, (const __nv_bfloat16 *)weight, (int)n, eps, add_one,
+                   (__nv_bfloat16 *)out, partials, (int)splits, plane);
+    else
+        launch_pdl(add_rmsnorm_row_kernel<4>, dim3((unsigned)rows), dim3(256), 0, (__nv_bfloat16 *)residual,
+                   (const __nv_bfloat16 *)nullptr, (const __nv_bfloat16 *)weight, (int)n, eps, add_one,
+                   (__nv_bfloat16 *)out, partials, (int)splits, plane);
+    return check_launch(what);
 }
 
 int ekernel_swiglu_bf16(const uint16_t *gate, const uint16_t *up, uint16_t *out, size_t n) {

@@ -102,6 +102,25 @@ class W4Linear:
             raise RuntimeError(f"ekernel_linear_w4a16g128_bf16_kpairs failed: rc={rc}: {abi.last_error()}")
         return out
 
+    def deferred(self, x: torch.Tensor, out: torch.Tensor, partials: torch.Tensor) -> int:
+        """The linear, leaving its result as split-K partial sums in partials when its GEMM
+        runs the split schedule and they fit (returns the split count; out is not written),
+        else writing out (returns 0).  A consumer that sums the partials itself saves the
+        GEMM's combine pass."""
+        ck._stream()
+        rc, sp = abi.linear_w4a16g128_bf16_kpairs_deferred_ptr(
+            x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(), out.data_ptr(), x.shape[0],
+            self.out_features, self.in_features, partials.data_ptr(), partials.numel() * partials.element_size())
+        if rc != 0:
+            raise RuntimeError(f"ekernel_linear_w4a16g128_bf16_kpairs_deferred failed: rc={rc}: {abi.last_error()}")
+        return sp
+
+    def partials_bytes(self, max_rows: int) -> int:
+        """Most bytes of partials a deferred call of up to max_rows rows leaves.  The split
+        count is fixed within each 128-row band of M, so the band ends bound it."""
+        return max(abi.linear_w4a16g128_partials_bytes(min(max_rows, 128 * t), self.out_features, self.in_features)
+                   for t in range(1, (max_rows + 127) // 128 + 1))
+
 
 class Qwen3Weights:
     def __init__(self, shape: Qwen3Shape, embed: torch.Tensor, layers: list[dict], final_norm: torch.Tensor,
@@ -292,6 +311,19 @@ class Qwen3Verifier:
         i32 = dict(dtype=torch.int32, device=device)
         self.top1 = torch.empty((max_rows,), **i32)
         self.margin = torch.empty((max_rows,), dtype=torch.float32, device=device)
+        # Split-K partials of the q/k/v, o and down projections, summed by the kernel that
+        # consumes them (QK-norm/RoPE/KV-append, residual add + RMSNorm) instead of a
+        # separate combine pass; the results are bit-identical either way.  One buffer:
+        # each projection's partials are consumed before the next projection runs.
+        self.defer_splitk = True
+        need = 0
+        for L in weights.layers:
+            for k in ("qkv", "o", "down"):
+                if isinstance(L.get(k), W4Linear):
+                    need = max(need, L[k].partials_bytes(max_rows))
+            break  # every layer has the same shapes
+        need = min(need, 256 << 20)  # calls whose partials exceed this write bf16 and combine
+        self.part = torch.empty((need + 3) // 4, dtype=torch.float32, device=device) if need else None
         # optional CUDA-event timing of the attention and linear launches (bench.py)
         self.op_timing = False
         # passes of more than 16 query rows per KV head: run on the per-head kernel (False),
@@ -378,37 +410,55 @@ class Qwen3Verifier:
         adesc, ab = view if view is not None else (desc, b)
         res, h = self.residual[:T], self.h[:T]
         ck.embedding_bf16(b.ids, self.w.embed, out=res)
-        delta = None
+        part = self.part if self.defer_splitk else None
+
+        def linear(lin, x, out) -> int:  # split count of partials left in part, else 0 (out written)
+            if part is None:
+                lin(x, out=out)
+                return 0
+            return lin.deferred(x, out, part)
+
+        def add_norm(delta, sp, w):
+            if sp:
+                ck.add_rmsnorm_bf16_splitk(res, part, sp, w, s.eps, s.gemma_norm, out=h)
+            else:
+                ck.add_rmsnorm_bf16(res, delta, w, s.eps, s.gemma_norm, out=h)
+
+        delta, delta_sp = None, 0
         for li, L in enumerate(self.w.layers):
-            ck.add_rmsnorm_bf16(res, delta, L["input_norm"], s.eps, s.gemma_norm, out=h)
+            add_norm(delta, delta_sp, L["input_norm"])
             e = self._ev("linear_qkv")
-            L["qkv"](h, out=self.qkv[:T])
+            sp = linear(L["qkv"], h, self.qkv[:T])
             if e is not None:
                 e.record()
-            ck.qk_norm_rope_kv_append(desc, self.qkv[:T], L["q_norm"], L["k_norm"], self.cos, self.sin, b.positions,
-                                      b.slots, self.kv.k[li], self.kv.v[li], self.q[:T],
-                                      self.gate[:T] if s.gated else None)
+            gate = self.gate[:T] if s.gated else None
+            if sp:
+                ck.qk_norm_rope_kv_append_splitk(desc, part, sp, L["q_norm"], L["k_norm"], self.cos, self.sin,
+                                                 b.positions, b.slots, self.kv.k[li], self.kv.v[li], self.q[:T], gate)
+            else:
+                ck.qk_norm_rope_kv_append(desc, self.qkv[:T], L["q_norm"], L["k_norm"], self.cos, self.sin,
+                                          b.positions, b.slots, self.kv.k[li], self.kv.v[li], self.q[:T], gate)
             e = self._ev("attention")
             ck.paged_attention_verify(adesc, self.q[:T], self.kv.k[li], self.kv.v[li], ab.block_table, ab.cu_q,
                                       ab.context_lens, self.gate[:T] if s.gated else None, self.attn[:T])
             if e is not None:
                 e.record()
             e = self._ev("linear_o")
-            L["o"](self.attn[:T], out=self.o[:T])
+            sp = linear(L["o"], self.attn[:T], self.o[:T])
             if e is not None:
                 e.record()
-            ck.add_rmsnorm_bf16(res, self.o[:T], L["post_norm"], s.eps, s.gemma_norm, out=h)
+            add_norm(self.o[:T], sp, L["post_norm"])
             e = self._ev("linear_gate_up")
             L["gate_up"](h, out=self.gu[:T])
             if e is not None:
                 e.record()
             ck.silu_mul_bf16(self.gu[:T], s.intermediate, out=self.act[:T])
             e = self._ev("linear_down")
-            L["down"](self.act[:T], out=self.mlp[:T])
+            delta_sp = linear(L["down"], self.act[:T], self.mlp[:T])
             if e is not None:
                 e.record()
             delta = self.mlp[:T]
-        ck.add_rmsnorm_bf16(res, delta, self.w.final_norm, s.eps, s.gemma_norm, out=h)
+        add_norm(delta, delta_sp, self.w.final_norm)
         return h
 
     def time_attention(self, b: VerifyBatch, reps: int = 2) -> float:
