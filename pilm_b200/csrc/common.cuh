@@ -125,6 +125,11 @@ __device__ __forceinline__ float sum_splits(const float *p, int splits, size_t p
 }
 __device__ __forceinline__ float bits2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

@@ -63,12 +63,20 @@ __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
 // the B fragment of the same thread carries A[m, k] for exactly those k (gathered
 // with byte permutes from one 16-byte load), so every MMA slot pairs W[n,k] with
 // A[m,k] for the same k and the 8 steps of a group sum the whole group.
-template <int RT, int NT, bool GROUPED, bool KP>
+template <int RT, int NT, bool GROUPED, bool KP, bool PF>
 __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
     const __nv_bfloat16 *__restrict__ X, int M, int K, const uint8_t *__restrict__ W,
     const float *__restrict__ S, int N, __nv_bfloat16 *__restrict__ Y, float *__restrict__ ws,
     int *__restrict__ ctr, int splits, int groups_per_split) {
-    pdl_entry();
+    // PF: weights are never written by another kernel, so this CTA's weight slab is
+    // prefetched into L2 before the wait for the previous kernel, and the fetch overlaps
+    // that kernel's tail.  In the model's layer chain (a norm, SwiGLU or attention kernel
+    // before each linear) that took 3% off a config 2 step (M = 4).  It is used for grids
+    // of one wave at M <= 8 only: CTAs of later waves start after the previous kernel has
+    // ended, and at M = 16 or for back-to-back launches of large shapes the variant
+    // measured up to 24% slower alone.
+    if (PF) pdl_trigger();
+    else pdl_entry();
     constexpr int ROWS = 16 * RT;
     constexpr int NACC = RT * NT * 4;
     __shared__ float red[kGemvWarps][NACC][32];
@@ -110,6 +118,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int j = 0; j < 4; ++j) acc[rt][nt][j] = 0.f;
+
+    // the slab: rows [row_base, row_base + ROWS), bytes [64 g0, 64 g1) of each (one row per
+    // lane of the last warp; every address and size is a multiple of 64 bytes).  Loading
+    // each warp's next group a loop iteration ahead as well was slower (more registers).
+    if (PF && warp == kGemvWarps - 1 && lane < ROWS && row_base + lane < N)
+        prefetch_l2_bulk(W + (size_t)(row_base + lane) * ldw + (size_t)g0 * 64, (uint32_t)(g1 - g0) * 64u);
+    if (PF) pdl_wait();
 
     for (int g = g0 + warp; g < g1; g += kGemvWarps) {
         uint4 wq[RT][2];
@@ -591,8 +606,17 @@ int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const flo
         PILM_REQUIRE(ws && ctr, ECPU_ERR_MEM, "%s: workspace allocation failed", what);
     }
     dim3 grid(tiles, splits);
-    launch_pdl(w4_gemv_mma<RT, NT, GROUPED, KP>, dim3(grid), dim3(kGemvWarps * 32), 0, X, M, K, W, S, N, Y, ws, ctr,
-                                                                                     splits, gps);
+    static int per_sm = 0;  // resident CTAs per SM of the prefetching instantiation
+    if (NT == 1 && per_sm == 0 &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w4_gemv_mma<RT, NT, GROUPED, KP, true>,
+                                                      kGemvWarps * 32, 0) != cudaSuccess)
+        per_sm = 1;
+    if (NT == 1 && tiles * splits <= per_sm * pilm::num_sms())  // M <= 8, the grid is one wave
+        launch_pdl(w4_gemv_mma<RT, NT, GROUPED, KP, true>, dim3(grid), dim3(kGemvWarps * 32), 0, X, M, K, W, S, N,
+                   Y, ws, ctr, splits, gps);
+    else
+        launch_pdl(w4_gemv_mma<RT, NT, GROUPED, KP, false>, dim3(grid), dim3(kGemvWarps * 32), 0, X, M, K, W, S, N,
+                   Y, ws, ctr, splits, gps);
     return pilm::check_launch(what);
 }
 
