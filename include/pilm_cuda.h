@@ -208,6 +208,18 @@ int ekernel_linear_w4a16g128_bf16_kpairs_deferred(const ekernel_linear_w8a32_des
 /* Bytes of partials a deferred call of this shape leaves on this GPU (0: it writes C). */
 size_t ekernel_linear_w4a16g128_partials_bytes(size_t M, size_t N, size_t K);
 
+/* ekernel_linear_w4a16g128_bf16_kpairs that, on its stream-K schedule (at least one 128-row
+ * weight tile per SM and M > 16: an LM head), also folds each output row's argmax into
+ * row_keys[m] (uint64, zero before the call): atomicMax of (order-preserving bits of the
+ * bf16 output << 32) | (0xFFFFFFFF - n), so the largest value wins with ties going to the
+ * smallest n, NaN never wins and -0 equals +0, as in a first-max argmax over the bf16
+ * logits.  *fused = 1 when it did; 0 when it only wrote C (then run
+ * ekernel_argmax_top2_bf16 as usual).  The fused LM head -> acceptance of the verify
+ * step (engine.py:479-503); no reference counterpart. */
+int ekernel_linear_w4a16g128_bf16_kpairs_argmax(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                                const uint8_t *W, const float *scales, uint16_t *C,
+                                                uint64_t *row_keys, int32_t *fused);
+
 /* kernel/api.h:180-186 (kernels.c:1485-1526): rne(x * rsqrt(mean(x^2)+eps) * (w [+1])). */
 int ekernel_rmsnorm_bf16(const uint16_t *x, uint16_t *out, const uint16_t *weight, size_t rows, size_t n,
                          float eps, int add_one);
@@ -397,6 +409,15 @@ int ekernel_argmax_top2_bf16(const ekernel_accept_desc_t *desc, const uint16_t *
 int ekernel_verify_accept_greedy(const ekernel_accept_desc_t *desc, const int32_t *verify_ids,
                                  const int32_t *top1, const int32_t *cu_q, int32_t *accept_counts,
                                  int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping);
+
+/* ekernel_verify_accept_greedy taking the row argmax keys of
+ * ekernel_linear_w4a16g128_bf16_kpairs_argmax: decodes each row's key into top1 (optional
+ * output) and resets the key to 0 for the next step, then accepts and rolls back as the
+ * greedy call does. */
+int ekernel_verify_accept_greedy_keys(const ekernel_accept_desc_t *desc, const int32_t *verify_ids,
+                                      uint64_t *row_keys, const int32_t *cu_q, int32_t *accept_counts,
+                                      int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping,
+                                      int32_t *top1);
 
 /* Rejection-sampling acceptance (no reference implementation: the reference verifies
  * greedily only, engine.py:373-379; this is standard speculative sampling with a one-hot

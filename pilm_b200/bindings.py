@@ -59,6 +59,8 @@ KERNEL_SYMBOLS = [
     "ekernel_linear_w4a16_bf16_kpairs",
     "ekernel_linear_w4a16g128_bf16_kpairs_deferred",
     "ekernel_linear_w4a16g128_partials_bytes",
+    "ekernel_linear_w4a16g128_bf16_kpairs_argmax",
+    "ekernel_verify_accept_greedy_keys",
     "ekernel_add_rmsnorm_bf16_splitk",
     "ekernel_qk_norm_rope_kv_append_splitk",
     "ekernel_mtp_fc_input_bf16",
@@ -187,6 +189,10 @@ def _configure(lib) -> None:
     lib.ekernel_linear_w4a16g128_bf16_kpairs_deferred.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp,
                                                                   _vp, _vp, _vp, _sz, ctypes.POINTER(_i32)]
     lib.ekernel_linear_w4a16g128_bf16_kpairs_deferred.restype = _i32
+    lib.ekernel_linear_w4a16g128_bf16_kpairs_argmax.argtypes = [ctypes.POINTER(EkernelLinearW8A32Desc), _vp, _vp,
+                                                                _vp, _vp, _vp, ctypes.POINTER(_i32)]
+    lib.ekernel_linear_w4a16g128_bf16_kpairs_argmax.restype = _i32
+    lib.ekernel_verify_accept_greedy_keys.argtypes = [ctypes.POINTER(AcceptDesc)] + [_vp] * 8
     lib.ekernel_linear_w4a16g128_partials_bytes.argtypes = [_sz, _sz, _sz]
     lib.ekernel_linear_w4a16g128_partials_bytes.restype = _sz
     lib.ekernel_add_rmsnorm_bf16_splitk.argtypes = [_vp, _vp, _i32, _vp, _sz, _sz, ctypes.c_float, _i32, _vp]
@@ -378,6 +384,16 @@ def linear_w4a16g128_bf16_kpairs_deferred_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m
     rc = _load_lib().ekernel_linear_w4a16g128_bf16_kpairs_deferred(ctypes.byref(d), a_ptr, w_ptr, scales_ptr, c_ptr,
                                                                    part_ptr, part_bytes, ctypes.byref(sp))
     return int(rc), int(sp.value)
+
+
+def linear_w4a16g128_bf16_kpairs_argmax_ptr(a_ptr, w_ptr, scales_ptr, c_ptr, m, n, k, keys_ptr) -> tuple[int, int]:
+    """(rc, fused): fused = 1 when the call also folded each output row's argmax into the
+    uint64 keys at keys_ptr (which must be zero before the call)."""
+    d = EkernelLinearW8A32Desc(m, n, k)
+    f = _i32(0)
+    rc = _load_lib().ekernel_linear_w4a16g128_bf16_kpairs_argmax(ctypes.byref(d), a_ptr, w_ptr, scales_ptr, c_ptr,
+                                                                 keys_ptr, ctypes.byref(f))
+    return int(rc), int(f.value)
 
 
 def linear_w4a16g128_partials_bytes(m, n, k) -> int:

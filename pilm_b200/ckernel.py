@@ -455,6 +455,21 @@ def verify_accept_greedy(num_seqs, verify_ids, top1, cu_q, accept_counts, next_t
                                                   _p(slot_mapping)), "ekernel_verify_accept_greedy")
 
 
+def verify_accept_greedy_keys(num_seqs, verify_ids, row_keys, cu_q, accept_counts, next_tokens, context_lens,
+                              slot_mapping=None, top1=None) -> None:
+    """Greedy acceptance from the row argmax keys of a fused LM head
+    (linear_w4a16g128_bf16_kpairs_argmax); the keys are reset to 0, top1 (optional) gets
+    the decoded row argmaxes."""
+    import ctypes
+    if row_keys.dtype != torch.int64 or row_keys.numel() < verify_ids.shape[0]:
+        raise ValueError("row_keys must be int64 (uint64 bits) with one entry per verify row")
+    d = abi.AcceptDesc(num_seqs, verify_ids.shape[0], 0)
+    _stream()
+    _check(abi.lib().ekernel_verify_accept_greedy_keys(ctypes.byref(d), _p(verify_ids), _p(row_keys), _p(cu_q),
+                                                       _p(accept_counts), _p(next_tokens), _p(context_lens),
+                                                       _p(slot_mapping), _p(top1)), "ekernel_verify_accept_greedy_keys")
+
+
 def verify_accept_rejection(num_seqs, logits, verify_ids, cu_q, uniforms, temperature, top_p, accept_counts,
                             next_tokens, context_lens, slot_mapping=None) -> None:
     """Rejection-sampling acceptance over fp32 or bf16 logits [total_q, vocab] with

@@ -154,6 +154,45 @@ __global__ void greedy_accept(int B, const int32_t *__restrict__ ids, const int3
         for (int j = 1 + acc; j < q_len; ++j) slots[q0 + j] = -1;
 }
 
+// The same acceptance from row argmax keys that the LM-head GEMM folded in
+// (ekernel_linear_w4a16g128_bf16_kpairs_argmax: value bits << 32 | (0xFFFFFFFF - index)
+// per row): each row's key is decoded into top1 and reset to 0 for the next step.
+__global__ void greedy_accept_keys(int B, const int32_t *__restrict__ ids, unsigned long long *__restrict__ keys,
+                                   const int32_t *__restrict__ cu_q, int32_t *__restrict__ acc_out,
+                                   int32_t *__restrict__ next_out, int32_t *__restrict__ ctx,
+                                   int32_t *__restrict__ slots, int32_t *__restrict__ top1) {
+    pdl_entry();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int q0 = cu_q[b], q_len = cu_q[b + 1] - q0;
+    if (q_len <= 0) {
+        acc_out[b] = 0;
+        next_out[b] = -1;
+        return;
+    }
+    int acc = 0, next = -1;
+    bool matching = true;
+    for (int j = 0; j < q_len; ++j) {
+        const unsigned long long k = keys[q0 + j];
+        const int t = k ? (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+        keys[q0 + j] = 0ull;
+        if (top1) top1[q0 + j] = t;
+        if (matching) {
+            if (j < q_len - 1 && t == ids[q0 + 1 + j]) {
+                ++acc;
+            } else {
+                matching = false;
+                next = t;
+            }
+        }
+    }
+    acc_out[b] = acc;
+    next_out[b] = next;
+    ctx[b] = ctx[b] - q_len + 1 + acc;
+    if (slots)
+        for (int j = 1 + acc; j < q_len; ++j) slots[q0 + j] = -1;
+}
+
 // ---------------------------------------------------------------------------------
 // Rejection sampling (standard speculative sampling with a one-hot greedy draft; the
 // reference has none).  Two kernels:
@@ -639,6 +678,19 @@ int ekernel_verify_accept_greedy(const ekernel_accept_desc_t *desc, const int32_
     launch_pdl(greedy_accept, dim3((unsigned)((desc->num_seqs + 127) / 128)), dim3(128), 0, 
         (int)desc->num_seqs, verify_ids, top1, cu_q, accept_counts, next_tokens, context_lens, slot_mapping);
     return check_launch("ekernel_verify_accept_greedy");
+}
+
+int ekernel_verify_accept_greedy_keys(const ekernel_accept_desc_t *desc, const int32_t *verify_ids,
+                                      uint64_t *row_keys, const int32_t *cu_q, int32_t *accept_counts,
+                                      int32_t *next_tokens, int32_t *context_lens, int32_t *slot_mapping,
+                                      int32_t *top1) {
+    PILM_REQUIRE(desc && verify_ids && row_keys && cu_q && accept_counts && next_tokens && context_lens,
+                 ECPU_ERR_PARAM, "ekernel_verify_accept_greedy_keys: null argument");
+    if (desc->num_seqs == 0) return ECPU_OK;
+    launch_pdl(greedy_accept_keys, dim3((unsigned)((desc->num_seqs + 127) / 128)), dim3(128), 0, (int)desc->num_seqs,
+               verify_ids, (unsigned long long *)row_keys, cu_q, accept_counts, next_tokens, context_lens,
+               slot_mapping, top1);
+    return check_launch("ekernel_verify_accept_greedy_keys");
 }
 
 int ekernel_verify_accept_rejection(const ekernel_accept_desc_t *desc, const float *logits,

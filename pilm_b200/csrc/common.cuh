@@ -36,16 +36,20 @@ int *counters(size_t n);  // zero-initialised, self-resetting arrival counters
 // [splits][M][N] fp32 partials fit in defer_cap bytes at defer (16-byte aligned), they are
 // left there, Y is not written, no combine pass runs and *defer_splits = splits; otherwise
 // *defer_splits = 0 and Y holds the result.
+// amax (optional, k-pair weights): when the call runs the stream-K schedule it also folds
+// every output row m's argmax over n into amax[m] (atomicMax of an order-preserving key:
+// value bits << 32 | (0xFFFFFFFF - n)) and sets *amax_done = 1; else *amax_done = 0.
 int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N,
                  __nv_bfloat16 *Y, bool grouped, bool kpairs, const char *what, float *defer = nullptr,
-                 size_t defer_cap = 0, int *defer_splits = nullptr);
+                 size_t defer_cap = 0, int *defer_splits = nullptr, unsigned long long *amax = nullptr,
+                 int *amax_done = nullptr);
 // Bytes of split-K partials a deferred call of this shape would leave (0: it would not).
 size_t w4_tc_partials_bytes(int M, int N, int K);
 // Quantized bf16 linear (linear.cu).  qf: 0 = W4 grouped (gs 32/128), 1 = W4 per-row,
 // 2 = W8 per-row.  kpairs (W4 only): weights in the k-pair nibble order.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
                 const char *what, bool kpairs = false, float *defer = nullptr, size_t defer_cap = 0,
-                int *defer_splits = nullptr);
+                int *defer_splits = nullptr, unsigned long long *amax = nullptr, int *amax_done = nullptr);
 
 // cuTensorMapEncodeTiled, reached through the runtime's driver entry point (no link
 // against libcuda); null if the driver does not provide it.

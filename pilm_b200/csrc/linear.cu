@@ -654,8 +654,10 @@ namespace pilm {
 // Shared entry used by the ABI wrappers and by the fused SwiGLU path.
 // qf: 0 = W4 grouped (gs = 32 or 128), 1 = W4 per-row, 2 = W8 per-row.
 int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, const float *S, int N, void *C,
-                const char *what, bool kpairs, float *defer, size_t defer_cap, int *defer_splits) {
+                const char *what, bool kpairs, float *defer, size_t defer_cap, int *defer_splits,
+                unsigned long long *amax, int *amax_done) {
     if (defer_splits) *defer_splits = 0;
+    if (amax_done) *amax_done = 0;
     const __nv_bfloat16 *X = (const __nv_bfloat16 *)A;
     __nv_bfloat16 *Y = (__nv_bfloat16 *)C;
     if (M == 0 || N == 0) return ECPU_OK;
@@ -667,7 +669,7 @@ int linear_bf16(int qf, int gs, const void *A, int M, int K, const void *W, cons
         // weight rows; the tensor-core GEMM stages it once per 128 (N = 32, 48, ... rows)
         if (M > 16) {
             int rc = linear_w4_tc(X, M, K, (const uint8_t *)W, S, N, Y, qf == 0, kpairs, what, defer, defer_cap,
-                                  defer_splits);
+                                  defer_splits, amax, amax_done);
             if (rc != ECPU_ERR_UNSUPPORTED) return rc;
         }
         // register-dequant GEMV, in slabs of at most 64 activation rows
@@ -853,6 +855,19 @@ int ekernel_linear_w4a16g128_bf16_kpairs_deferred(const ekernel_linear_w8a32_des
                                      "ekernel_linear_w4a16g128_bf16_kpairs_deferred", true, partials,
                                      partials ? partials_bytes : 0, &s);
     *splits = rc == ECPU_OK ? s : 0;
+    return rc;
+}
+
+int ekernel_linear_w4a16g128_bf16_kpairs_argmax(const ekernel_linear_w8a32_desc_t *desc, const uint16_t *A,
+                                                const uint8_t *W, const float *scales, uint16_t *C,
+                                                uint64_t *row_keys, int32_t *fused) {
+    LINEAR_ARGS_OK("ekernel_linear_w4a16g128_bf16_kpairs_argmax");
+    PILM_REQUIRE(row_keys && fused, ECPU_ERR_PARAM, "ekernel_linear_w4a16g128_bf16_kpairs_argmax: null argument");
+    int done = 0;
+    const int rc = pilm::linear_bf16(0, 128, A, (int)desc->M, (int)desc->K, W, scales, (int)desc->N, C,
+                                     "ekernel_linear_w4a16g128_bf16_kpairs_argmax", true, nullptr, 0, nullptr,
+                                     (unsigned long long *)row_keys, &done);
+    *fused = rc == ECPU_OK ? done : 0;
     return rc;
 }
 

@@ -285,7 +285,20 @@ struct TcParams {
     int grouped;
     int scale_tma;      // group scales arrive by TMA (G % 4 == 0, group offsets 16-byte aligned)
     uint32_t wait_limit;  // polls before a pipeline wait gives up (drains keep kWaitLimit)
+    unsigned long long *amax;  // AM: per output row, the max of argmax_key over the row's outputs
 };
+
+// Order-preserving key of output value f at column (vocab index) idx: the largest key is
+// the largest value, ties going to the smallest index; NaN never wins and -0 equals +0,
+// as in a first-max row argmax (row_top2).
+__device__ __forceinline__ unsigned long long argmax_key(float f, int idx) {
+    if (f != f) return 0ull;
+    uint32_t b = f == 0.f ? 0u : __float_as_uint(f);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+
+
 
 // Two schedules over the units w = t * G + group, each CTA running one contiguous range:
 //  * stream-K (at least one tile per SM): CTA c takes [c U / P, (c+1) U / P), walking
@@ -311,12 +324,19 @@ __device__ __forceinline__ float *piece_of(const TcParams &p, int c, int t) {
     return p.part + (size_t)(c * 2 + slot) * kMaxNm * kTileRows;
 }
 
-template <bool KP>
+// AM: also fold each finished output row's argmax (over the tile's weight rows, the
+// vocabulary of an LM head) into p.amax by atomicMax of argmax_key (stream-K schedule).
+template <bool KP, bool AM>
 __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant__ CUtensorMap wmap,
                                                          const __grid_constant__ CUtensorMap xmap,
                                                          const __grid_constant__ CUtensorMap smap,
                                                          const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
+    // AM: each fold warp's running argmax key per output row over every tile it writes
+    // (its own slots, so no atomics inside the loop); at the end the CTA takes the max over
+    // its warps and makes one global atomicMax per row (one per tile and warp, on the same
+    // few words, cost 0.2 ms per LM-head call)
+    __shared__ unsigned long long s_amax[AM ? kFoldWarps * kMaxNm : 1];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     Barriers *bar = reinterpret_cast<Barriers *>(smem + kSmemBar);
     volatile int *abort_flag = &bar->abort_flag;
@@ -368,6 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) tmem_alloc(&bar->tmem_base, kTmemCols);
+    if (AM)
+        for (int i = threadIdx.x; i < kFoldWarps * kMaxNm; i += blockDim.x) s_amax[i] = 0ull;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -503,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         const int c_lo = fq * per, c_hi = min(nc, c_lo + per);
         const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
         float2 acc[8 * kChunksPer];  // 16-column chunks as fp32 pairs: one packed multiply and add per pair
+
 #pragma unroll
         for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
         // partial buffers 0 and 1 start free
@@ -575,19 +598,33 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             const float sr = (p.grouped || !row_ok) ? 1.0f : __ldg(p.S + row);
             const int m0 = (t / p.tiles_n) * kMaxNm;
             const int mlim = min(p.Nm, p.M - m0);
-            if (seg_g0 == 0 && last_g == G - 1) {
-                if (row_ok) {
+            // the finished tile: bf16 outputs, and under AM each output row's argmax over the
+            // warp's 32 weight rows folded into s_amax (ml < mlim is the same for the whole warp)
+            auto write_tile = [&]() {
 #pragma unroll
-                    for (int u = 0; u < kChunksPer; ++u) {
-                        if (c_lo + u >= c_hi) continue;
+                for (int u = 0; u < kChunksPer; ++u) {
+                    if (c_lo + u >= c_hi) continue;
 #pragma unroll
-                        for (int k = 0; k < 16; ++k) {
-                            const int ml = 16 * (c_lo + u) + k;  // activation row in the tile
-                            const float a = (k & 1) ? acc[u * 8 + (k >> 1)].y : acc[u * 8 + (k >> 1)].x;
-                            if (ml < mlim) p.Y[(size_t)(m0 + ml) * p.N + row] = f2bf(a * sr);
+                    for (int k = 0; k < 16; ++k) {
+                        const int ml = 16 * (c_lo + u) + k;  // activation row in the tile
+                        if (ml >= mlim) continue;
+                        const float a = (k & 1) ? acc[u * 8 + (k >> 1)].y : acc[u * 8 + (k >> 1)].x;
+                        const __nv_bfloat16 v = f2bf(a * sr);
+                        if (row_ok) p.Y[(size_t)(m0 + ml) * p.N + row] = v;
+                        if (AM) {  // the warp's max key: max of the value words, then of the index words
+                            const unsigned long long key = row_ok ? argmax_key(bf2f(v), row) : 0ull;
+                            const uint32_t hi = (uint32_t)(key >> 32);
+                            const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
+                            const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)key : 0u);
+                            const unsigned long long wk = ((unsigned long long)mhi << 32) | mlo;
+                            unsigned long long *slot = &s_amax[fw * kMaxNm + ml];  // this warp's own: no atomics
+                            if (lane == 0 && wk > *slot) *slot = wk;
                         }
                     }
                 }
+            };
+            if (seg_g0 == 0 && last_g == G - 1) {
+                write_tile();
             } else if (p.split_mode) {
                 // split partial for splitk_combine
                 if (row_ok) {
@@ -640,18 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                             }
                         }
                     }
-                    if (row_ok) {
-#pragma unroll
-                        for (int u = 0; u < kChunksPer; ++u) {
-                            if (c_lo + u >= c_hi) continue;
-#pragma unroll
-                            for (int k = 0; k < 16; ++k) {
-                                const int ml = 16 * (c_lo + u) + k;
-                                const float a = (k & 1) ? acc[u * 8 + (k >> 1)].y : acc[u * 8 + (k >> 1)].x;
-                                if (ml < mlim) p.Y[(size_t)(m0 + ml) * p.N + row] = f2bf(a * sr);
-                            }
-                        }
-                    }
+                    write_tile();
                     if (lane == 0) p.cnt[(size_t)t * kFoldWarps + fw] = 0;  // self-reset for the next launch
                 }
             }
@@ -671,6 +697,13 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     if (*abort_flag) {
         if (threadIdx.x == 0) atomicExch(p.err, 1);
     }
+    if (AM)  // one activation tile (M <= 128): output row m is column m of every fold warp
+        for (int i = threadIdx.x; i < p.Nm; i += blockDim.x) {
+            unsigned long long k = 0ull;
+#pragma unroll
+            for (int w = 0; w < kFoldWarps; ++w) k = s_amax[w * kMaxNm + i] > k ? s_amax[w * kMaxNm + i] : k;
+            if (k) atomicMax(p.amax + i, k);
+        }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -767,8 +800,10 @@ size_t w4_tc_partials_bytes(int M, int N, int K) {
 }
 
 int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
-                 bool grouped, bool kpairs, const char *what, float *defer, size_t defer_cap, int *defer_splits) {
+                 bool grouped, bool kpairs, const char *what, float *defer, size_t defer_cap, int *defer_splits,
+                 unsigned long long *amax, int *amax_done) {
     if (defer_splits) *defer_splits = 0;
+    if (amax_done) *amax_done = 0;
     static const bool disabled = getenv("PILM_DISABLE_TC") && getenv("PILM_DISABLE_TC")[0] == '1';
     if (disabled || M <= 16 || (K % 128) != 0 || N < 1) return ECPU_ERR_UNSUPPORTED;
     if ((((uintptr_t)X) & 15) || (((uintptr_t)W) & 15)) return ECPU_ERR_UNSUPPORTED;
@@ -846,6 +881,10 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     p.part = nullptr;
     p.cnt = nullptr;
     p.wait_limit = wait_limit_override() >= 0 ? (uint32_t)wait_limit_override() : kWaitLimit;
+    // the fused argmax needs every output written by this kernel: stream-K only (the split
+    // schedule's outputs come from the combine pass), k-pair weights, one activation tile
+    const bool am = amax && amax_done && stream_k && kpairs && plan.tiles_m == 1;
+    p.amax = am ? amax : nullptr;
     if (stream_k) {
         p.part = (float *)workspace((size_t)P * 2 * kMaxNm * kTileRows * sizeof(float));
         p.cnt = counters((size_t)tiles * kFoldWarps);
@@ -861,16 +900,20 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     }
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(w4_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
-        cudaFuncSetAttribute(w4_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
         attr_set = true;
     }
-    if (kpairs)
-        launch_pdl(w4_gemm_tc<true>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+    if (am)
+        launch_pdl(w4_gemm_tc<true, true>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+    else if (kpairs)
+        launch_pdl(w4_gemm_tc<true, false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
     else
-        launch_pdl(w4_gemm_tc<false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+        launch_pdl(w4_gemm_tc<false, false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
+    if (am) *amax_done = 1;
     if (splits > 1 && !(defer_splits && *defer_splits)) {
         const size_t total8 = (size_t)M * N / 8;
         launch_pdl(splitk_combine, dim3((unsigned)((total8 + 255) / 256)), dim3(256), 0, p.ws, splits, M, N,

@@ -115,6 +115,18 @@ class W4Linear:
             raise RuntimeError(f"ekernel_linear_w4a16g128_bf16_kpairs_deferred failed: rc={rc}: {abi.last_error()}")
         return sp
 
+    def with_argmax(self, x: torch.Tensor, out: torch.Tensor, row_keys: torch.Tensor) -> bool:
+        """The linear (out written as usual) that, on its stream-K schedule, also folds each
+        output row's argmax into row_keys (int64 holding uint64 keys, zero before the call);
+        returns whether it did (else the caller takes the argmax from out)."""
+        ck._stream()
+        rc, fused = abi.linear_w4a16g128_bf16_kpairs_argmax_ptr(
+            x.data_ptr(), self.qweight.data_ptr(), self.scales.data_ptr(), out.data_ptr(), x.shape[0],
+            self.out_features, self.in_features, row_keys.data_ptr())
+        if rc != 0:
+            raise RuntimeError(f"ekernel_linear_w4a16g128_bf16_kpairs_argmax failed: rc={rc}: {abi.last_error()}")
+        return bool(fused)
+
     def partials_bytes(self, max_rows: int) -> int:
         """Most bytes of partials a deferred call of up to max_rows rows leaves.  The split
         count is fixed within each 128-row band of M, so the band ends bound it."""
@@ -311,6 +323,14 @@ class Qwen3Verifier:
         i32 = dict(dtype=torch.int32, device=device)
         self.top1 = torch.empty((max_rows,), **i32)
         self.margin = torch.empty((max_rows,), dtype=torch.float32, device=device)
+        # fuse_lm_argmax: greedy verification with the row argmax folded into the LM-head
+        # GEMM (its stream-K schedule) and the accept kernel decoding and re-zeroing these
+        # keys, instead of a separate row top-2 pass over the logits.  Off by default: on
+        # the Qwen3-8B bench step the fused form measured 0.03 ms slower (the extra work in
+        # the GEMM's tile write-out delays its MMA pipeline by more than the 15 us top-2 pass
+        # costs).  Other LM-head shapes take row_top2 either way.
+        self.fuse_lm_argmax = False
+        self.row_keys = torch.zeros((max_rows,), dtype=torch.int64, device=device)
         # Split-K partials of the q/k/v, o and down projections, summed by the kernel that
         # consumes them (QK-norm/RoPE/KV-append, residual add + RMSNorm) instead of a
         # separate combine pass; the results are bit-identical either way.  One buffer:
@@ -539,11 +559,23 @@ class Qwen3Verifier:
         n0 = abi.launch_count()
         h = self.forward(b)
         self.hidden_out = h  # normed hidden states of the rows (the MTP drafter's input)
-        logits = self.lm_head(h)
         T = b.total_q
-        ck.argmax_top2(logits, self.top1[:T], None, self.margin[:T])
-        ck.verify_accept_greedy(b.num_seqs, b.ids, self.top1[:T], b.cu_q, accept_counts, next_tokens, context_lens,
-                                slots)
+        fused = False
+        if self.fuse_lm_argmax and isinstance(self.w.lm_head, W4Linear):
+            e = self._ev("lm_head")
+            fused = self.w.lm_head.with_argmax(h, self.logits[:T], self.row_keys[:T])
+            if e is not None:
+                e.record()
+            logits = self.logits[:T]
+        else:
+            logits = self.lm_head(h)
+        if fused:
+            ck.verify_accept_greedy_keys(b.num_seqs, b.ids, self.row_keys[:T], b.cu_q, accept_counts, next_tokens,
+                                         context_lens, slots, top1=self.top1[:T])
+        else:
+            ck.argmax_top2(logits, self.top1[:T], None, self.margin[:T])
+            ck.verify_accept_greedy(b.num_seqs, b.ids, self.top1[:T], b.cu_q, accept_counts, next_tokens,
+                                    context_lens, slots)
         self._last_step_launches = abi.launch_count() - n0
         return logits
 
