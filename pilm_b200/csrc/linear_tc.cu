@@ -60,7 +60,7 @@ constexpr int kXBytes = 2 * kXSubBytes;
 constexpr int kDqWarps = 4;                          // warps 2-5
 constexpr int kFoldWarps = 8;                        // warps 6-13
 constexpr int kFoldSets = kFoldWarps / 4;            // fold warps per lane quadrant, each a column set
-constexpr int kChunksPer = (kMaxNm / 16) / kFoldSets; // 16-column chunks a fold warp holds (at most 4)
+static_assert((kMaxNm / 16) / kFoldSets == 4, "a fold warp holds at most 4 chunks of 16 partial columns (CH)");
 constexpr int kThreads = (2 + kDqWarps + kFoldWarps) * 32;
 constexpr int kTBufs = 2;                            // TMEM partial buffers (kMaxNm columns each)
 constexpr int kTmemCols = 512;
@@ -326,7 +326,8 @@ __device__ __forceinline__ float *piece_of(const TcParams &p, int c, int t) {
 
 // AM: also fold each finished output row's argmax (over the tile's weight rows, the
 // vocabulary of an LM head) into p.amax by atomicMax of argmax_key (stream-K schedule).
-template <bool KP, bool AM>
+// CH: 16-column chunks of the partial per fold warp (3: Nm <= 96, 4: Nm <= 128).
+template <bool KP, bool AM, int CH>
 __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant__ CUtensorMap wmap,
                                                          const __grid_constant__ CUtensorMap xmap,
                                                          const __grid_constant__ CUtensorMap smap,
@@ -521,13 +522,13 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         const int rloc = 32 * quad + lane;
         const uint32_t lane_addr = (uint32_t)(32 * quad) << 16;
         const int nc = p.Nm / 16;            // 16-column chunks of the partial (<= 8)
-        const int per = (nc + kFoldSets - 1) / kFoldSets;  // chunks per set (<= kChunksPer)
+        const int per = (nc + kFoldSets - 1) / kFoldSets;  // chunks per set (<= CH)
         const int c_lo = fq * per, c_hi = min(nc, c_lo + per);
         const float *sring = reinterpret_cast<const float *>(smem + kSmemScale);
-        float2 acc[8 * kChunksPer];  // 16-column chunks as fp32 pairs: one packed multiply and add per pair
+        float2 acc[8 * CH];  // 16-column chunks as fp32 pairs: one packed multiply and add per pair
 
 #pragma unroll
-        for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
+        for (int e = 0; e < 8 * CH; ++e) acc[e] = make_float2(0.f, 0.f);
         // partial buffers 0 and 1 start free
         __syncwarp();
         if (lane == 0)
@@ -571,24 +572,47 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
                 tc_fence_after();
                 const uint32_t taddr = tmem + lane_addr + (uint32_t)(kAccColBase + (i % kTBufs) * kMaxNm);
-                // one 16-column chunk at a time (register budget); the buffer goes back to the
-                // issuer for group i + 2 as soon as the last chunk is in registers
+                if constexpr (CH <= 3) {
+                    // all chunks into registers with one wait, the buffer straight back to the
+                    // issuer for group i + 2, then the arithmetic (2-3% faster than holding
+                    // the buffer through the chunks' arithmetic; four chunks do not fit)
+                    uint32_t r[CH][16];
 #pragma unroll
-                for (int u = 0; u < kChunksPer; ++u) {
-                    uint32_t r[16];
-                    const bool have = c_lo + u < c_hi;
-                    if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
+                    for (int u = 0; u < CH; ++u)
+                        if (c_lo + u < c_hi) tmem_ld16(taddr + 16 * (c_lo + u), r[u]);
                     tmem_ld_wait();
-                    if (u == kChunksPer - 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0 && i + kTBufs < ng) mbar_arrive(&bar->op_full[(i + kTBufs) % kSlots]);
-                    }
-                    if (!have) continue;
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0 && i + kTBufs < ng) mbar_arrive(&bar->op_full[(i + kTBufs) % kSlots]);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
-                        const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-                        acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
+                    for (int u = 0; u < CH; ++u) {
+                        if (c_lo + u >= c_hi) continue;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
+                            const float2 pv = make_float2(__uint_as_float(r[u][2 * e]), __uint_as_float(r[u][2 * e + 1]));
+                            acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
+                        }
+                    }
+                } else {
+                    // one 16-column chunk at a time (register budget); the buffer goes back to
+                    // the issuer for group i + 2 as soon as the last chunk is in registers
+#pragma unroll
+                    for (int u = 0; u < CH; ++u) {
+                        uint32_t r[16];
+                        const bool have = c_lo + u < c_hi;
+                        if (have) tmem_ld16(taddr + 16 * (c_lo + u), r);
+                        tmem_ld_wait();
+                        if (u == CH - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0 && i + kTBufs < ng) mbar_arrive(&bar->op_full[(i + kTBufs) % kSlots]);
+                        }
+                        if (!have) continue;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {  // acc += rn(p * s), per element as the reference
+                            const float2 pv = make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+                            acc[u * 8 + e] = __fadd2_rn(acc[u * 8 + e], p.grouped ? __fmul2_rn(pv, sc2) : pv);
+                        }
                     }
                 }
             }
@@ -602,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             // warp's 32 weight rows folded into s_amax (ml < mlim is the same for the whole warp)
             auto write_tile = [&]() {
 #pragma unroll
-                for (int u = 0; u < kChunksPer; ++u) {
+                for (int u = 0; u < CH; ++u) {
                     if (c_lo + u >= c_hi) continue;
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
@@ -629,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // split partial for splitk_combine
                 if (row_ok) {
 #pragma unroll
-                    for (int u = 0; u < kChunksPer; ++u) {
+                    for (int u = 0; u < CH; ++u) {
                         if (c_lo + u >= c_hi) continue;
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
@@ -644,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 // warp region) sums the pieces in CTA order and writes the tile
                 float *pc = piece_of(p, cta, t) + rloc;
 #pragma unroll
-                for (int u = 0; u < kChunksPer; ++u) {
+                for (int u = 0; u < CH; ++u) {
                     if (c_lo + u >= c_hi) continue;
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -663,11 +687,11 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                     __threadfence();
                     // sum = 0 + piece(k0) + piece(k0 + 1) + ... in CTA order (deterministic)
 #pragma unroll
-                    for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
+                    for (int e = 0; e < 8 * CH; ++e) acc[e] = make_float2(0.f, 0.f);
                     for (int cc = k0; cc <= k1; ++cc) {
                         const float *pq = piece_of(p, cc, t) + rloc;
 #pragma unroll
-                        for (int u = 0; u < kChunksPer; ++u) {
+                        for (int u = 0; u < CH; ++u) {
                             if (c_lo + u >= c_hi) continue;
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
@@ -682,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 }
             }
 #pragma unroll
-            for (int e = 0; e < 8 * kChunksPer; ++e) acc[e] = make_float2(0.f, 0.f);
+            for (int e = 0; e < 8 * CH; ++e) acc[e] = make_float2(0.f, 0.f);
             // next tile: the next 128 weight rows, or the first of the next activation tile
             g = 0;
             ++t;
@@ -900,17 +924,30 @@ int linear_w4_tc(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const f
     }
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(w4_gemm_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
-        cudaFuncSetAttribute(w4_gemm_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
-        cudaFuncSetAttribute(w4_gemm_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<false, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true, true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<false, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
+        cudaFuncSetAttribute(w4_gemm_tc<true, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemTotal);
         attr_set = true;
     }
-    if (am)
-        launch_pdl(w4_gemm_tc<true, true>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
-    else if (kpairs)
-        launch_pdl(w4_gemm_tc<true, false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
-    else
-        launch_pdl(w4_gemm_tc<false, false>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+    // fold chunks per warp: half of the Nm / 16 partial columns
+    if (Nm <= 96) {
+        if (am)
+            launch_pdl(w4_gemm_tc<true, true, 3>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+        else if (kpairs)
+            launch_pdl(w4_gemm_tc<true, false, 3>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+        else
+            launch_pdl(w4_gemm_tc<false, false, 3>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+    } else {
+        if (am)
+            launch_pdl(w4_gemm_tc<true, true, 4>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+        else if (kpairs)
+            launch_pdl(w4_gemm_tc<true, false, 4>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+        else
+            launch_pdl(w4_gemm_tc<false, false, 4>, dim3(P), dim3(kThreads), kSmemTotal, wmap, xmap, smap, p);
+    }
     int rc = check_launch(what);
     if (rc != ECPU_OK) return rc;
     if (am) *amax_done = 1;
