@@ -69,7 +69,7 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
                             const int32_t *__restrict__ slots, long long num_slots, __nv_bfloat16 *__restrict__ kc,
                             __nv_bfloat16 *__restrict__ vc, __nv_bfloat16 *__restrict__ q_out,
                             __nv_bfloat16 *__restrict__ gate_out) {
-    pdl_entry();
+    pdl_trigger();
     __shared__ float buf[8][kHD];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int item = blockIdx.x * 8 + warp;
@@ -84,6 +84,26 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
     else
         src = (size_t)row * qkv_stride + qsec + (size_t)(h - nh) * kHD;
     const __nv_bfloat16 *nw = is_q ? qnw : knw;
+    // The norm weights, RoPE tables, positions and slots are constant or written by the
+    // host before the step, so they are read before the wait for the previous kernel; the
+    // projection (its output) after it.
+    const int pos = positions[row];
+    const int nf = rot_dim >> 1;
+    const bool pos_ok = pos >= 0 && pos < rope_rows;
+    const long long slot = is_q ? -1 : slots[row];
+    float wv[4], cv[4], sv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int d = lane + 32 * j;
+        float wf = bf2f(nw[d]);
+        if (add_one) wf = bf16_round(__fadd_rn(wf, 1.0f));
+        wv[j] = wf;
+        const int f = d < nf ? d : d - nf;
+        const bool rot = d < rot_dim && pos_ok;
+        cv[j] = rot ? cos_t[(size_t)pos * nf + f] : 1.f;
+        sv[j] = rot ? sin_t[(size_t)pos * nf + f] : 0.f;
+    }
+    pdl_wait();
     float x[4];
     float ss = 0.f;
 #pragma unroll
@@ -97,14 +117,9 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
     for (int j = 0; j < 4; ++j) {
         const int d = lane + 32 * j;
         float xn = bf16_round(__fmul_rn(x[j], inv));
-        float wf = bf2f(nw[d]);
-        if (add_one) wf = bf16_round(__fadd_rn(wf, 1.0f));
-        buf[warp][d] = bf16_round(__fmul_rn(xn, wf));
+        buf[warp][d] = bf16_round(__fmul_rn(xn, wv[j]));
     }
     __syncwarp();
-    const int pos = positions[row];
-    const int nf = rot_dim >> 1;
-    const bool pos_ok = pos >= 0 && pos < rope_rows;
     float y[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -112,8 +127,7 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
         float v = buf[warp][d];
         if (d < rot_dim && pos_ok) {
             // out_first = a*cos - b*sin ; out_second = a*sin + b*cos  (layers.py:161-164)
-            const int f = d < nf ? d : d - nf;
-            const float cs = cos_t[(size_t)pos * nf + f], sn = sin_t[(size_t)pos * nf + f];
+            const float cs = cv[j], sn = sv[j];
             if (d < nf) {
                 const float b = buf[warp][d + nf];
                 v = __fsub_rn(__fmul_rn(v, cs), __fmul_rn(b, sn));
@@ -134,7 +148,6 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
             for (int j = 0; j < 4; ++j) go[lane + 32 * j] = src_in.bf(src + kHD + lane + 32 * j);
         }
     } else {
-        const long long slot = slots[row];
         if (slot < 0 || slot >= num_slots) return;  // rejected / padded rows are not written
         const int kvh = h - nh;
         __nv_bfloat16 *kd = kc + ((size_t)slot * nkv + kvh) * kHD;
@@ -619,9 +632,11 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
     __shared__ __align__(8) uint64_t full_bar[kPStages], empty_bar[kPStages];
     __shared__ int s_blk_ok[kPStages];  // the stage's block id was valid (else zero its tiles)
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    // the merge kernel may be scheduled now: it waits for this grid's completion before it
-    // reads anything; this grid waits for its own predecessor (programmatic dependent launch)
-    pdl_entry();
+    // the merge kernel may be scheduled now (programmatic dependent launch).  The page
+    // prefix comes from the context lengths, which the host writes before the step, so it
+    // is worked out before the wait for the previous kernel (which appends this step's
+    // K/V and writes the queries).
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkv = p.nkv;
     const int cta = blockIdx.x;
@@ -659,6 +674,7 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
     const long long T = s_prefix[p.B];
     const long long s_c = ((long long)cta * T) / p.G, e_c = ((long long)(cta + 1) * T) / p.G;
     if (s_c >= e_c) return;
+    pdl_wait();
     // largest b with prefix[b] <= x (sequences without pages are skipped)
     auto seq_of = [&](long long x) {
         int lo = 0, hi = p.B - 1;

@@ -87,7 +87,7 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
                                        const int32_t *__restrict__ positions, const int32_t *__restrict__ slots,
                                        long long num_slots, float *__restrict__ kc, float *__restrict__ vc,
                                        float *__restrict__ q_out, float *__restrict__ gate_out) {
-    pdl_entry();
+    pdl_trigger();
     __shared__ float buf[8][kHD];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int item = blockIdx.x * 8 + warp;
@@ -99,6 +99,25 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
     const float *src = is_q ? qkv + (size_t)row * qkv_stride + (size_t)h * kHD * (gated ? 2 : 1)
                             : qkv + (size_t)row * qkv_stride + qsec + (size_t)(h - nh) * kHD;
     const float *nw = is_q ? qnw : knw;
+    // norm weights, RoPE tables, positions and slots (constant or host-written) before the
+    // wait for the previous kernel, the projection after it
+    const int pos = positions[row];
+    const int nf = rot_dim >> 1;
+    const bool pos_ok = pos >= 0 && pos < rope_rows;
+    const long long slot = is_q ? -1 : slots[row];
+    float wv[4], cv[4], sv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int d = lane + 32 * j;
+        float wf = nw[d];
+        if (add_one) wf = __fadd_rn(wf, 1.0f);
+        wv[j] = wf;
+        const int f = d < nf ? d : d - nf;
+        const bool rot = d < rot_dim && pos_ok;
+        cv[j] = rot ? cos_t[(size_t)pos * nf + f] : 1.f;
+        sv[j] = rot ? sin_t[(size_t)pos * nf + f] : 0.f;
+    }
+    pdl_wait();
     float x[4];
     float ss = 0.f;
 #pragma unroll
@@ -111,22 +130,16 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int d = lane + 32 * j;
-        float wf = nw[d];
-        if (add_one) wf = __fadd_rn(wf, 1.0f);
-        buf[warp][d] = __fmul_rn(wf, __fmul_rn(x[j], inv));
+        buf[warp][d] = __fmul_rn(wv[j], __fmul_rn(x[j], inv));
     }
     __syncwarp();
-    const int pos = positions[row];
-    const int nf = rot_dim >> 1;
-    const bool pos_ok = pos >= 0 && pos < rope_rows;
     float y[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int d = lane + 32 * j;
         float v = buf[warp][d];
         if (d < rot_dim && pos_ok) {
-            const int f = d < nf ? d : d - nf;
-            const float cs = cos_t[(size_t)pos * nf + f], sn = sin_t[(size_t)pos * nf + f];
+            const float cs = cv[j], sn = sv[j];
             if (d < nf)
                 v = __fsub_rn(__fmul_rn(v, cs), __fmul_rn(buf[warp][d + nf], sn));
             else
@@ -144,7 +157,6 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
             for (int j = 0; j < 4; ++j) go[lane + 32 * j] = src[kHD + lane + 32 * j];
         }
     } else {
-        const long long slot = slots[row];
         if (slot < 0 || slot >= num_slots) return;  // rejected / padded rows are not written
         const int kvh = h - nh;
         float *kd = kc + ((size_t)slot * nkv + kvh) * kHD;
