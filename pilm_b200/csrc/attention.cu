@@ -449,10 +449,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) attn_verify(const __grid_const
                         ls += pv;
                     }
                 lrow[mt][hh] = lrow[mt][hh] * alpha + ls;
+                // once the running maxima settle, alpha is exactly 1 for every row: skip the
+                // multiplies (a product by 1 is exact, so results are unchanged)
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-                for (int nt = 0; nt < 16; ++nt) {
-                    o[mt][nt][hh * 2 + 0] *= alpha;
-                    o[mt][nt][hh * 2 + 1] *= alpha;
+                    for (int nt = 0; nt < 16; ++nt) {
+                        o[mt][nt][hh * 2 + 0] *= alpha;
+                        o[mt][nt][hh * 2 + 1] *= alpha;
+                    }
                 }
             }
             pa[mt][0] = pack_bf16(sacc[mt][0][0], sacc[mt][0][1]);
@@ -870,10 +874,14 @@ __global__ void __launch_bounds__((kPMaxKv + 1) * 32, 1) attn_pages(const __grid
                                 ls += pv;
                             }
                         lrow[mt][hh] = lrow[mt][hh] * alpha + ls;
+                        // once the running maxima settle, alpha is exactly 1 for every row:
+                        // skip the multiplies (a product by 1 is exact)
+                        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-                        for (int nt = 0; nt < 16; ++nt) {
-                            o[mt][nt][hh * 2 + 0] *= alpha;
-                            o[mt][nt][hh * 2 + 1] *= alpha;
+                            for (int nt = 0; nt < 16; ++nt) {
+                                o[mt][nt][hh * 2 + 0] *= alpha;
+                                o[mt][nt][hh * 2 + 1] *= alpha;
+                            }
                         }
                     }
                     pa[mt][0] = pack_bf16(sacc[mt][0][0], sacc[mt][0][1]);

@@ -132,6 +132,32 @@ def test_many_ragged_sequences_nan_past_context():
     run_case(32, 8, ctxs=ctxs, qlens=qlens, seed=8, poison=True)
 
 
+def test_rows_17_to_32_per_kv_head_qwen3_8b_heads():
+    """17 to 32 query rows per KV head (q_len 5 to 8 with 4 query heads per KV head, mixed with
+    shorter passes in the same call): beyond the whole-page kernel's one 16-row tile.  40
+    ragged sequences; the slots past each context in its last page are NaN."""
+    import random
+    rnd = random.Random(17)
+    ctxs, qlens = [], []
+    for _ in range(40):
+        q = rnd.choice([1, 3, 5, 6, 8])
+        st = 16 * rnd.randint(0, 40) + rnd.randint(0, 16 - q)
+        ctxs.append(st + q)
+        qlens.append(q)
+    run_case(32, 8, ctxs=ctxs, qlens=qlens, seed=18, poison=True)
+
+
+def test_rows_17_to_32_per_kv_head_two_kv_heads():
+    """The same range of rows per KV head with two KV heads (8 query heads)."""
+    run_case(8, 2, ctxs=[40, 112, 16, 136, 704], qlens=[5, 8, 1, 6, 7], seed=19, poison=True)
+
+
+def test_rows_17_to_32_per_kv_head_gated_gemma():
+    """Gated attention with Gemma norms, 2 query heads per KV head and q_len up to 16 (32 rows
+    per KV head)."""
+    run_case(16, 8, ctxs=[30, 77, 496, 16], qlens=[12, 9, 16, 16], gated=True, gemma=True, seed=20)
+
+
 def prefill_case(nh, nkv, qlens, prefixes, gated=False, seed=0):
     """Prompt chunks (q_len positions after a cached prefix) straight into the attention
     entry point: post-RoPE queries against paged caches whose slots past each context

@@ -49,6 +49,12 @@ def test_attention_qwen3_8b_heads_32k():
     run_case(32, 8, ctxs=ctxs, qlens=[3, 4, 1], seed=22, poison=True)
 
 
+def test_attention_qwen3_8b_heads_8k_q5():
+    """Eight sequences of 7K-9K keys at k = 4 (five verify rows each, twenty rows per KV
+    head, more than the whole-page kernel's one 16-row tile)."""
+    run_case(32, 8, ctxs=_ragged_contexts(8, 440, 570, 5, seed=23), qlens=[5] * 8, seed=23, poison=True)
+
+
 def _cut_tiles(N, K, sms):
     """Tiles that a stream-K range boundary [c U / P, ...) cuts, for P = sms CTAs."""
     tiles, G = (N + 127) // 128, K // 128
