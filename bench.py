@@ -274,6 +274,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     rows_per_step = batch.total_q
     (ms_max,), _ = reduce_over_ranks([ms], [], dev)
     # per-kernel timings for the rooflines (CUDA events, same stream, back-to-back launches)
+    timeline = graph_timeline(graph) if args.timeline else None
     op_ms = {"attention": ver.time_attention(graph.batch)}
     op_ms["attention_total"] = op_ms["attention"] * shape.layers
     op_ms.update(ver.time_linears(rows_per_step))
@@ -489,6 +490,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "cpu_baseline": cpu,
         "acceptance": {"attempts": eng.stats["attempts"], "accepts": eng.stats["accepts"]},
     }
+    if timeline:
+        line["timeline"] = timeline
     return line
 
 
@@ -815,6 +818,7 @@ def run_config(args) -> dict:
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     rows = batch.total_q
+    timeline = graph_timeline(graph) if args.timeline else None
     for s in seqs:
         del s.tokens[s.num_computed + 1:]
     # ---- end to end through the engine
@@ -865,6 +869,7 @@ def run_config(args) -> dict:
         "gpu_launches": graph.launches * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
+        **({"timeline": timeline} if timeline else {}),
     }
 
 
@@ -924,6 +929,53 @@ def run_prefill(args) -> None:
               flush=True)
         del ver, kv
         torch.cuda.empty_cache()
+
+
+def graph_timeline(graph, replays: int = 3) -> dict:
+    """Where a captured step's time goes, on the device: CUPTI kernel records (torch.profiler)
+    of `replays` graph replays, the middle one kept.  Kernels overlap at programmatic
+    dependent launches, so each kernel is charged only the part of its span after every
+    earlier kernel has ended (its share of the critical path); the shares add up to the
+    step.  Taken outside the timed region."""
+    import re
+    from collections import Counter, defaultdict
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(replays):
+            graph.replay()
+        torch.cuda.synchronize()
+    evs = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                 if e.device_type == torch.autograd.DeviceType.CUDA)
+    n = len(evs) // replays
+    step = evs[n * (replays // 2):n * (replays // 2 + 1)]
+    if not step:
+        return {}
+
+    def short(name: str) -> str:
+        name = name.replace("void ", "").replace("(anonymous namespace)::", "").replace("pilm::", "")
+        m = re.match(r"[\w:]+", name)
+        return m.group(0) if m else name[:40]
+
+    crit, span, cnt = defaultdict(float), defaultdict(float), Counter()
+    gaps, prev_end = 0.0, step[0][0]
+    for s0, e0, name in step:
+        k = short(name)
+        span[k] += e0 - s0
+        cnt[k] += 1
+        gaps += max(0.0, s0 - prev_end)
+        crit[k] += max(0.0, e0 - max(s0, prev_end))
+        prev_end = max(prev_end, e0)
+    total = step[-1][1] - step[0][0]
+    return {"step_ms": round(total / 1e3, 4), "kernels": len(step), "idle_ms": round(gaps / 1e3, 4),
+            "critical_ms": {k: round(crit[k] / 1e3, 4) for k in sorted(crit, key=lambda k: -crit[k])},
+            "launches": {k: cnt[k] for k in sorted(crit, key=lambda k: -crit[k])},
+            "span_ms": {k: round(span[k] / 1e3, 4) for k in sorted(crit, key=lambda k: -crit[k])},
+            "how": "CUPTI kernel records of one graph replay (torch.profiler); a kernel's critical time is "
+                   "its span after every earlier kernel has ended"}
 
 
 def _graph_ms(body, calls: int, iters: int = 5) -> float:
@@ -1126,6 +1178,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end engine leg (profiling runs)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="add the step's per-kernel critical-path times (CUPTI records of one graph replay, "
+                         "taken after the timed region)")
     ap.add_argument("--no-draft", action="store_true", help="skip the verify + GPU draft cycle leg")
     ap.add_argument("--no-accepting", action="store_true",
                     help="skip the leg whose drafts are accepted (the model's own greedy continuation)")

@@ -53,6 +53,34 @@ __device__ __forceinline__ uint32_t word_of(const uint4 &v, int i) {
     return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
+// One group of one 16-row tile against one 8-row activation tile (w4_gemv_mma with RT = NT
+// = 1): the weight words w0 (rows r) and w1 (rows r + 8) and the four activation words of
+// the thread, into the fp32 group partial d, exactly as the general loop in w4_gemv_mma.
+template <bool KP>
+__device__ __forceinline__ void gemv_group_dot(uint4 w0, uint4 w1, uint4 x0, uint4 x1, uint4 x2, uint4 x3,
+                                               float (&d)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 xw = i == 0 ? x0 : (i == 1 ? x1 : (i == 2 ? x2 : x3));
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            uint32_t b0, b1;
+            if (KP) {  // nibble pairs (2hh, 2hh+4) and (2hh+1, 2hh+5) are k (4hh, 4hh+1), (4hh+2, 4hh+3)
+                b0 = hh ? xw.z : xw.x;
+                b1 = hh ? xw.w : xw.y;
+            } else {
+                const uint32_t lo = hh ? xw.y : xw.x;
+                const uint32_t hi = hh ? xw.w : xw.z;
+                b0 = __byte_perm(lo, hi, 0x5410);
+                b1 = __byte_perm(lo, hi, 0x7632);
+            }
+            const uint32_t wr = word_of(w0, i), wr8 = word_of(w1, i);
+            mma16816(d, dq_pair(wr >> (8 * hh)), dq_pair(wr8 >> (8 * hh)), dq_pair(wr >> (8 * hh + 4)),
+                     dq_pair(wr8 >> (8 * hh + 4)), b0, b1);
+        }
+    }
+}
+
 // Register-dequant W4 GEMV on tensor cores.
 //
 // Tile: a warp owns RT row tiles of 16 output rows and NT batch tiles of 8 rows of A.
@@ -126,6 +154,53 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
         prefetch_l2_bulk(W + (size_t)(row_base + lane) * ldw + (size_t)g0 * 64, (uint32_t)(g1 - g0) * 64u);
     if (PF) pdl_wait();
 
+    if constexpr (RT == 1 && NT == 1) {
+        // One 16-row tile and one activation tile (the small projections at M <= 8): the
+        // next group's weights, scales and activations are loaded before this group's math,
+        // so a warp's groups wait on memory once, not once each.
+        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0, x0 = w0, x1 = w0, x2 = w0, x3 = w0;
+        float s0 = 0.f, s1 = 0.f;
+        int g = g0 + warp;
+        if (g < g1) {
+            if (rv[0][0]) w0 = ldg_nc_v4(wp[0][0] + (size_t)g * 64);
+            if (rv[0][1]) w1 = ldg_nc_v4(wp[0][1] + (size_t)g * 64);
+            if (GROUPED && rv[0][0]) s0 = __ldg(S + (size_t)rows[0][0] * G + g);
+            if (GROUPED && rv[0][1]) s1 = __ldg(S + (size_t)rows[0][1] * G + g);
+            if (xv[0]) {
+                x0 = ldg_v4(xp[0] + (size_t)g * 128);
+                x1 = ldg_v4(xp[0] + (size_t)g * 128 + 8);
+                x2 = ldg_v4(xp[0] + (size_t)g * 128 + 16);
+                x3 = ldg_v4(xp[0] + (size_t)g * 128 + 24);
+            }
+        }
+        for (; g < g1; g += kGemvWarps) {
+            const int gn = g + kGemvWarps;
+            uint4 nw0 = make_uint4(0, 0, 0, 0), nw1 = nw0, nx0 = nw0, nx1 = nw0, nx2 = nw0, nx3 = nw0;
+            float ns0 = 0.f, ns1 = 0.f;
+            if (gn < g1) {
+                if (rv[0][0]) nw0 = ldg_nc_v4(wp[0][0] + (size_t)gn * 64);
+                if (rv[0][1]) nw1 = ldg_nc_v4(wp[0][1] + (size_t)gn * 64);
+                if (GROUPED && rv[0][0]) ns0 = __ldg(S + (size_t)rows[0][0] * G + gn);
+                if (GROUPED && rv[0][1]) ns1 = __ldg(S + (size_t)rows[0][1] * G + gn);
+                if (xv[0]) {
+                    nx0 = ldg_v4(xp[0] + (size_t)gn * 128);
+                    nx1 = ldg_v4(xp[0] + (size_t)gn * 128 + 8);
+                    nx2 = ldg_v4(xp[0] + (size_t)gn * 128 + 16);
+                    nx3 = ldg_v4(xp[0] + (size_t)gn * 128 + 24);
+                }
+            }
+            float part[4] = {0.f, 0.f, 0.f, 0.f};
+            gemv_group_dot<KP>(w0, w1, x0, x1, x2, x3, part);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (GROUPED)  // reference: acc = acc + dot_g * s[n,g], product rounded first
+                    acc[0][0][j] = __fadd_rn(acc[0][0][j], __fmul_rn(part[j], (j >> 1) ? s1 : s0));
+                else
+                    acc[0][0][j] = __fadd_rn(acc[0][0][j], part[j]);
+            }
+            w0 = nw0, w1 = nw1, x0 = nx0, x1 = nx1, x2 = nx2, x3 = nx3, s0 = ns0, s1 = ns1;
+        }
+    } else {
     for (int g = g0 + warp; g < g1; g += kGemvWarps) {
         uint4 wq[RT][2];
 #pragma unroll
@@ -192,6 +267,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4_gemv_mma(
                     else
                         acc[rt][nt][j] = __fadd_rn(acc[rt][nt][j], part[rt][nt][j]);
                 }
+    }
     }
 
 #pragma unroll
@@ -583,14 +659,17 @@ __global__ void argmax_bf16_row(const __nv_bfloat16 *__restrict__ v, int n, int 
     }
 }
 
+// split_k: spread short grids over more CTAs by splitting K (partials reduced by the last
+// CTA of each row tile); false keeps one CTA per row tile, which saves that reduction's
+// round trip where the grid is already wide enough.
 template <int RT, int NT, bool GROUPED, bool KP>
 int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
-               const char *what) {
+               const char *what, bool split_k = true) {
     const int tiles = (N + 16 * RT - 1) / (16 * RT);
     const int G = K >> 7;
     const int target = 2 * pilm::num_sms();
     int splits = 1;
-    if (tiles < target) {
+    if (split_k && tiles < target) {
         splits = (target + tiles - 1) / tiles;
         int max_splits = G / kGemvWarps;  // keep every warp busy
         if (max_splits < 1) max_splits = 1;
@@ -623,6 +702,13 @@ int launch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const flo
 template <bool GROUPED, bool KP>
 int dispatch_mma(const __nv_bfloat16 *X, int M, int K, const uint8_t *W, const float *S, int N, __nv_bfloat16 *Y,
                  const char *what) {
+    // M <= 8.  Projections narrow enough for fewer than two 32-row tiles per SM and with at
+    // most 32 groups (each warp then walks at most 4 of them): 16-row tiles, no split-K, and
+    // the next group's loads in flight during the current group's math.  Measured at M = 4:
+    // 2048 x 4096 6.0 -> 4.2 us, 2048 x 2048 5.8 -> 4.1 us, 4096 x 6144 8.2 -> 7.4 us; wider
+    // or deeper shapes keep the 32-row tiles and split-K (16-row tiles there were 5-40% slower).
+    if (M <= 8 && (N + 31) / 32 < 2 * pilm::num_sms() && (K >> 7) <= 4 * kGemvWarps)
+        return launch_mma<1, 1, GROUPED, KP>(X, M, K, W, S, N, Y, what, false);
     if (M <= 8) return launch_mma<2, 1, GROUPED, KP>(X, M, K, W, S, N, Y, what);
     if (M <= 16) return launch_mma<2, 2, GROUPED, KP>(X, M, K, W, S, N, Y, what);
     if (M <= 32) return launch_mma<1, 4, GROUPED, KP>(X, M, K, W, S, N, Y, what);
