@@ -106,9 +106,13 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
     pdl_wait();
     float x[4];
     float ss = 0.f;
+    // a K head's V values, loaded with its K values (they are only copied to the cache)
+    const size_t vsrc = (size_t)row * qkv_stride + qsec + (size_t)nkv * kHD + (size_t)(h - nh) * kHD;
+    __nv_bfloat16 vv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         x[j] = src_in.at(src + lane + 32 * j);
+        if (!is_q) vv[j] = src_in.bf(vsrc + lane + 32 * j);
         ss = fmaf(x[j], x[j], ss);
     }
     ss = warp_sum(ss);
@@ -152,11 +156,10 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
         const int kvh = h - nh;
         __nv_bfloat16 *kd = kc + ((size_t)slot * nkv + kvh) * kHD;
         __nv_bfloat16 *vd = vc + ((size_t)slot * nkv + kvh) * kHD;
-        const size_t vsrc = (size_t)row * qkv_stride + qsec + (size_t)nkv * kHD + (size_t)kvh * kHD;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             kd[lane + 32 * j] = f2bf(y[j]);
-            vd[lane + 32 * j] = src_in.bf(vsrc + lane + 32 * j);
+            vd[lane + 32 * j] = vv[j];
         }
     }
 }
