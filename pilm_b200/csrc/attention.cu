@@ -1103,6 +1103,532 @@ int encode_kv_page_maps(const __nv_bfloat16 *kc, const __nv_bfloat16 *vc, int nk
     return ECPU_OK;
 }
 
+// ---------------------------------------------------------------------------------
+// Prefill-sized passes on 5th-generation tensor cores (tcgen05 + TMEM): flash attention
+// over the paged cache for 128 query rows per CTA.
+//
+// A CTA owns one KV head and 128 / gsz consecutive query positions of one sequence, so its
+// 128 rows are (position, query head of the group) pairs, row r = position * gsz + head.
+// TMA loads the Q tile once (two 64-dim SWIZZLE_128B halves), and the K and V blocks of 128
+// keys (8 pages, 16 boxes each) into two two-stage rings: a K stage is free again once the
+// scores that read it are done, a V stage once the P V product is, so K runs ahead of V.
+// Per KV block j:
+//   S(j) = Q K(j)^T      8 x tcgen05.mma M=128 N=128 K=16, both operands K-major in shared
+//                        memory, into one of two TMEM score buffers
+//   softmax (8 warps)    two threads per row, each 64 keys: the scores rounded as the
+//                        reference's bf16 bmm and scale are, the causal / context mask, the
+//                        running max (shared by the pair) and sum; P = exp(S - max) as bf16
+//                        into one of two TMEM P buffers, and O rescaled in TMEM when a
+//                        row's max moved
+//   O += P(j) V(j)       8 x tcgen05.mma M=128 N=128 K=16, A = P from TMEM, B = V as it lies
+//                        in the cache (keys x dims, an MN-major SWIZZLE_128B operand)
+// S(j + 1) is issued before PV(j), so the tensor pipe works on the next block while the
+// softmax warps work on this one.  The causal and context masks are those of the other
+// attention kernels (a key is seen by a row iff key <= the row's position and key <
+// context), so the results agree with them up to fp32 summation order.
+// Warps: 0 TMA producer of Q and K, 2 of V, 1 TMEM owner and MMA issuer (its lanes also zero
+// the V rows past the context, and K and V of pages with an invalid block id), 4-11 softmax
+// and epilogue,
+// two per TMEM lane quadrant (one half of the keys of each block, one half of O's dims).
+// Every mbarrier wait is bounded; a wait that gives up sets the device error word.
+// ---------------------------------------------------------------------------------
+constexpr int kPfRows = 128;                   // query rows per CTA (MMA M)
+constexpr int kPfKeys = 128;                   // keys per KV block
+constexpr int kPfHalf = kPfKeys * 128;         // one 64-dim half of a K or V block: 16 KB
+constexpr int kPfKV = 2 * kPfHalf;             // K (or V) block: 32 KB
+constexpr int kPfQ = kPfRows * kHD * 2;        // Q tile: 32 KB
+constexpr int kPfThreads = 12 * 32;  // Q/K producer, issuer, V producer, one idle, 8 softmax
+constexpr int kPfTmemCols = 512;               // S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512)
+constexpr int kPfStages = 2;                 // K blocks in flight, and V blocks
+constexpr size_t kPfSmemK = kPfQ;                                  // K ring
+constexpr size_t kPfSmemV = kPfSmemK + kPfStages * (size_t)kPfKV;  // V ring
+constexpr size_t kPfSmemBar = kPfSmemV + kPfStages * (size_t)kPfKV;
+struct __align__(8) PfBars {
+    uint64_t q_full, k_full[kPfStages], k_empty[kPfStages], v_full[kPfStages], v_empty[kPfStages];
+    uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], drain;
+    uint64_t pair_max[4][2], pair_sum[4];  // the two softmax warps of a lane quadrant: row maxima, row sums
+    uint32_t tmem_base;
+    int abort_flag;
+};
+constexpr size_t kPfSmemTotal = kPfSmemBar + sizeof(PfBars) + 1024;
+static_assert(kPfSmemTotal <= 227 * 1024, "shared memory budget");
+
+struct PfParams {
+    const int32_t *block_table;  // [B, max_blocks]
+    const int32_t *cu_q;         // [B+1]
+    const int32_t *ctx;          // [B]
+    const __nv_bfloat16 *gate;   // [total_q, nh*128] or null
+    __nv_bfloat16 *out;          // [total_q, nh*128]
+    int *err;
+    int nh, gsz, ppt, tiles, max_blocks, num_blocks;
+    float scale;
+};
+
+__device__ __forceinline__ uint32_t pf_s32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void pf_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void pf_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void pf_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(pf_s32(bar))
+                 : "memory");
+}
+// K-major SWIZZLE_128B operand: 8-row x 128-byte atoms, 1024 bytes between 8-row groups
+__device__ __forceinline__ uint64_t pf_kdesc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// MN-major SWIZZLE_128B operand (V: key rows of 64 contiguous dims): 1024 bytes between
+// 8-key groups (stride byte offset), kPfHalf bytes between the two 64-dim halves (leading
+// byte offset)
+__device__ __forceinline__ uint64_t pf_mndesc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFF) >> 4) | ((uint64_t)(kPfHalf >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void pf_mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void pf_mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void pf_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void pf_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void pf_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void pf_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// bounded wait shared by a warp: every lane waits, the warp reconverges, a timeout in any
+// lane (or an abort raised elsewhere) ends it for all
+__device__ __forceinline__ bool pf_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag) {
+    bool ok = false;
+    for (uint32_t i = 0; i < kAttnWaitLimit; ++i) {
+        if (mbar_try_wait(b, parity)) {
+            ok = true;
+            break;
+        }
+        if ((i & 255) == 255 && *abort_flag) break;
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) *abort_flag = 1;
+    return ok;
+}
+
+// grid: (sequences x tiles, n_kv); block: 256.  qmap: q as (dim, head, row) with 64 x gsz x
+// ppt boxes; kmap / vmap: the caches as (dim, head, slot) with 64 x 1 x 16 boxes.
+__global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_constant__ CUtensorMap qmap,
+                                                                 const __grid_constant__ CUtensorMap kmap,
+                                                                 const __grid_constant__ CUtensorMap vmap,
+                                                                 const PfParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint32_t s_inv[2][kPfStages];  // [K, V][stage]: pages inside the context with an invalid block id
+    __shared__ float s_pmax[2][2][kPfRows];  // [block parity][key half][row]: partial row maxima
+    __shared__ float s_psum[2][kPfRows];     // [key half][row]: partial row sums
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    PfBars *bar = reinterpret_cast<PfBars *>(smem + kPfSmemBar);
+    volatile int *abort_flag = &bar->abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    // the tile: heaviest (last positions, most keys) first.  cu_q and the context lengths
+    // are host-written before the step, so they are read before the wait.
+    const int b = blockIdx.x / p.tiles, t = p.tiles - 1 - blockIdx.x % p.tiles;
+    const int kvh = blockIdx.y;
+    const int q0 = p.cu_q[b], q_len = p.cu_q[b + 1] - q0, ctx = p.ctx[b];
+    const int pos0 = t * p.ppt;
+    if (pos0 >= q_len) return;
+    const int p0 = ctx - q_len;                          // position of the sequence's first query row
+    const int kmax = min(ctx, p0 + pos0 + p.ppt);        // keys that any row of the tile sees
+    const int nb = (kmax + kPfKeys - 1) / kPfKeys;
+    const int ctx_pages = (ctx + 15) >> 4;
+    const int32_t *bt = p.block_table + (size_t)b * p.max_blocks;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar->q_full, 1);
+        for (int i = 0; i < kPfStages; ++i) {
+            mbar_init(&bar->k_full[i], 1);
+            mbar_init(&bar->k_empty[i], 1);
+            mbar_init(&bar->v_full[i], 1);
+            mbar_init(&bar->v_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bar->s_full[i], 1);
+            mbar_init(&bar->s_free[i], 8);
+            mbar_init(&bar->p_full[i], 8);
+            mbar_init(&bar->pv_done[i], 1);
+        }
+        mbar_init(&bar->drain, 1);
+        for (int q = 0; q < 4; ++q) {
+            mbar_init(&bar->pair_max[q][0], 64);
+            mbar_init(&bar->pair_max[q][1], 64);
+            mbar_init(&bar->pair_sum[q], 64);
+        }
+        bar->abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(pf_s32(&bar->tmem_base)),
+                     "r"(kPfTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    pf_fence_before();
+    __syncthreads();
+    pf_fence_after();
+    const uint32_t tmem = bar->tmem_base;
+    pdl_wait();
+
+    if (warp == 0 || warp == 2) {
+        // ---- producers: warp 0 Q once and the K blocks, warp 2 the V blocks, each block's 8
+        // pages into a two-stage ring ----
+        const bool is_k = warp == 0;
+        const CUtensorMap *map = is_k ? &kmap : &vmap;
+        uint64_t *full = is_k ? bar->k_full : bar->v_full;
+        uint64_t *empty = is_k ? bar->k_empty : bar->v_empty;
+        int issued = 0;
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+            if (is_k) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"(&qmap) : "memory");
+                mbar_expect_tx(&bar->q_full, kPfQ);
+                for (int h = 0; h < 2; ++h)
+                    tma_load_3d(pf_s32(smem) + h * (kPfQ / 2), &qmap, &bar->q_full, 64 * h, kvh * p.gsz, q0 + pos0);
+            }
+        }
+        for (int j = 0; j < nb; ++j) {
+            const int st = j % kPfStages;
+            // block ids of the block's 8 pages, one per lane (invalid ones load page 0,
+            // which the issuer warp zeroes)
+            int blk = 0;
+            bool inv = false;  // a page inside the context whose block id is out of range
+            if (lane < 8) {
+                const int pg = 8 * j + lane;
+                if (pg < ctx_pages) {
+                    blk = pg < p.max_blocks ? bt[pg] : -1;
+                    inv = blk < 0 || blk >= p.num_blocks;
+                }
+                if (inv) blk = 0;
+            }
+            const uint32_t inv_mask = __ballot_sync(0xffffffffu, inv);
+            if (j >= kPfStages && !pf_wait(&empty[st], (uint32_t)((j - kPfStages) / kPfStages) & 1u, abort_flag)) break;
+            const uint32_t base = pf_s32(smem + (is_k ? kPfSmemK : kPfSmemV)) + (uint32_t)st * kPfKV;
+            int blks[8];
+#pragma unroll
+            for (int pg = 0; pg < 8; ++pg) blks[pg] = __shfl_sync(0xffffffffu, blk, pg);
+            if (lane == 0) {
+                s_inv[is_k ? 0 : 1][st] = inv_mask;  // published by the arrive below
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_expect_tx(&full[st], kPfKV);
+#pragma unroll
+                for (int pg = 0; pg < 8; ++pg)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        tma_load_3d(base + (uint32_t)(h * kPfHalf + pg * 2048), map, &full[st], 64 * h, kvh, blks[pg] * 16);
+            }
+            ++issued;
+        }
+        // drain: every copy issued has landed before the CTA may exit
+        if (lane == 0) {
+            if (is_k) mbar_wait_bounded(&bar->q_full, 0);
+            for (int j = issued > kPfStages ? issued - kPfStages : 0; j < issued; ++j)
+                mbar_wait_bounded(&full[j % kPfStages], (uint32_t)(j / kPfStages) & 1u);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---- MMA issuer (lane 0); the warp zeroes what must not reach the MMAs ----
+        const uint32_t idesc_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPfKeys >> 3) << 17) |
+                                 ((uint32_t)(kPfRows >> 4) << 24);
+        const uint32_t idesc_pv = idesc_s | (1u << 16);  // B (V) MN-major; N = 128 dims
+        const uint32_t q_s = pf_s32(smem);
+        // the rows of a stage that must not reach the MMAs: rows of keys past the context
+        // (V only: their P is 0, but 0 x NaN is NaN) and whole pages with an invalid block id
+        auto zero_rows = [&](uint8_t *stage, int j, uint32_t inv_mask, bool is_v) {
+            const int key0 = j * kPfKeys;
+            if (!(is_v && key0 + kPfKeys > ctx) && !inv_mask) return;
+            for (int pg = 0; pg < 8; ++pg) {
+                const int k16 = key0 + pg * 16;
+                const bool invalid = (inv_mask >> pg) & 1u;
+                const int r0 = invalid ? 0 : (is_v ? max(0, min(16, ctx - k16)) : 16);
+                if (r0 >= 16) continue;
+                for (int idx = lane; idx < (16 - r0) * 16; idx += 32) {  // 16-byte chunks, both halves
+                    const int row = pg * 16 + r0 + (idx >> 4), ch = idx & 15;
+                    const size_t off = (size_t)(ch >> 3) * kPfHalf + (size_t)row * 128 + ((ch & 7) << 4);
+                    *reinterpret_cast<uint4 *>(stage + off) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+        };
+        auto issue_s = [&](int j) -> bool {
+            const int st = j % kPfStages, sb = j & 1;  // K stage, S buffer
+            if (j == 0 && !pf_wait(&bar->q_full, 0, abort_flag)) return false;
+            if (!pf_wait(&bar->k_full[st], (uint32_t)(j / kPfStages) & 1u, abort_flag)) return false;
+            if (j >= 2 && !pf_wait(&bar->s_free[sb], (uint32_t)((j - 2) >> 1) & 1u, abort_flag)) return false;
+            uint8_t *kst = smem + kPfSmemK + (size_t)st * kPfKV;
+            zero_rows(kst, j, s_inv[0][st], false);
+            pf_fence_after();
+            if (lane == 0) {
+                const uint32_t k_s = pf_s32(kst);
+                const uint32_t d = tmem + (uint32_t)(sb * 128);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {  // K = 16 dims per MMA: 32 bytes of each 128-byte row
+                    const uint32_t off = (uint32_t)((ks >> 2) * (kPfQ / 2));
+                    pf_mma_ss(d, pf_kdesc(q_s + off) + 2 * (ks & 3), pf_kdesc(k_s + (uint32_t)((ks >> 2) * kPfHalf)) + 2 * (ks & 3),
+                              idesc_s, ks > 0 ? 1u : 0u);
+                }
+                pf_commit(&bar->s_full[sb]);
+                pf_commit(&bar->k_empty[st]);
+            }
+            __syncwarp();
+            return true;
+        };
+        bool ok = issue_s(0);
+        for (int j = 0; ok && j < nb; ++j) {
+            const int st = j % kPfStages, sb = j & 1;  // V stage, P buffer
+            if (j + 1 < nb && !issue_s(j + 1)) break;
+            if (!pf_wait(&bar->v_full[st], (uint32_t)(j / kPfStages) & 1u, abort_flag)) break;
+            uint8_t *vst = smem + kPfSmemV + (size_t)st * kPfKV;
+            zero_rows(vst, j, s_inv[1][st], true);
+            if (!pf_wait(&bar->p_full[sb], (uint32_t)(j >> 1) & 1u, abort_flag)) break;
+            pf_fence_after();
+            if (lane == 0) {
+                const uint32_t v_s = pf_s32(vst);
+                const uint32_t pa = tmem + (uint32_t)(384 + sb * 64);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)  // K = 16 keys per MMA: 8 TMEM columns of P, 16 key rows of V
+                    pf_mma_ts(tmem + 256u, pa + (uint32_t)(8 * ks), pf_mndesc(v_s + (uint32_t)(ks * 2048)), idesc_pv,
+                              (j > 0 || ks > 0) ? 1u : 0u);
+                pf_commit(&bar->pv_done[sb]);
+                pf_commit(&bar->v_empty[st]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) {
+            pf_commit(&bar->drain);
+            mbar_wait_bounded(&bar->drain, 0);
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ---- softmax and epilogue: two warps per row quadrant, each one half of the keys of
+        // a block (64 columns of S, 32 of P) and one half of the dims of O; the row maxima
+        // and, at the end, the row sums are exchanged through shared memory ----
+        const int q4 = warp & 3, half = (warp - 4) >> 2;
+        const int r = 32 * q4 + lane;
+        const uint32_t lane_addr = (uint32_t)(32 * q4) << 16;
+        const int pos = r / p.gsz, g = r % p.gsz;
+        const int qp = p0 + pos0 + pos;                  // this row's position (its last key)
+        const int qp_min = p0 + pos0;                    // the tile's first position
+        const bool row_ok = pos0 + pos < q_len;
+        float m = -INFINITY, l = 0.f;
+        bool failed = false;
+        for (int j = 0; j < nb; ++j) {
+            const int st = j & 1;
+            if (!pf_wait(&bar->s_full[st], (uint32_t)(j >> 1) & 1u, abort_flag)) {
+                failed = true;
+                break;
+            }
+            pf_fence_after();
+            float s[64];
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t u[32];
+                pf_ld32(tmem + lane_addr + (uint32_t)(st * 128 + 64 * half + 32 * c), u);
+                pf_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) s[32 * c + e] = __uint_as_float(u[e]);
+            }
+            pf_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar->s_free[st]);
+            // scores = bmm(q, k^T) in bf16, then * scale in bf16 (attention.py:128-129); a
+            // block whose keys every row of the tile sees needs no mask
+            const int k0 = j * kPfKeys + 64 * half;
+            const bool masked = (j + 1) * kPfKeys - 1 > qp_min || (j + 1) * kPfKeys > ctx;
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                float v = bf16_round(__fmul_rn(bf16_round(s[c]), p.scale));
+                if (masked && (k0 + c > qp || k0 + c >= ctx)) v = -INFINITY;
+                s[c] = v;
+                mx4[c & 3] = fmaxf(mx4[c & 3], v);
+            }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            s_pmax[st][half][r] = mx;
+            mbar_arrive(&bar->pair_max[q4][st]);  // every lane: each publishes its own row's value
+            if (!pf_wait(&bar->pair_max[q4][st], (uint32_t)(j >> 1) & 1u, abort_flag)) {
+                failed = true;
+                break;
+            }
+            const float mnew = fmaxf(m, fmaxf(mx, s_pmax[st][half ^ 1][r]));
+            const float alpha = (m == -INFINITY || mnew == -INFINITY) ? 1.f : __expf(m - mnew);
+            // PV(j - 1) has completed: O holds blocks < j, and P buffer st (PV(j - 2)) is free
+            if (j >= 1 && !pf_wait(&bar->pv_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort_flag)) {
+                failed = true;
+                break;
+            }
+            pf_fence_after();
+            if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t u[32];
+                    pf_ld32(tmem + lane_addr + (uint32_t)(256 + 64 * half + 32 * c), u);
+                    pf_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+                    pf_st32(tmem + lane_addr + (uint32_t)(256 + 64 * half + 32 * c), u);
+                }
+            }
+            float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t u[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const float a0 = s[2 * e], a1 = s[2 * e + 1];
+                const float p0v = (a0 == -INFINITY) ? 0.f : __expf(a0 - mnew);
+                const float p1v = (a1 == -INFINITY) ? 0.f : __expf(a1 - mnew);
+                ls4[e & 3] += p0v + p1v;
+                u[e] = pack_bf16(p0v, p1v);
+            }
+            pf_st32(tmem + lane_addr + (uint32_t)(384 + st * 64 + 32 * half), u);
+            l = l * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+            m = mnew;
+            pf_st_wait();
+            pf_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar->p_full[st]);
+        }
+        // the row sum over both halves of every block
+        s_psum[half][r] = l;
+        mbar_arrive(&bar->pair_sum[q4]);
+        if (!failed && pf_wait(&bar->pair_sum[q4], 0u, abort_flag) &&
+            pf_wait(&bar->pv_done[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag)) {
+            const float lt = l + s_psum[half ^ 1][r];
+            pf_fence_after();
+            const int qrow = q0 + pos0 + pos, head = kvh * p.gsz + g;
+            const size_t ob = ((size_t)qrow * p.nh + head) * kHD + 64 * half;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t u[32];
+                pf_ld32(tmem + lane_addr + (uint32_t)(256 + 64 * half + 32 * c), u);
+                pf_ld_wait();
+                if (row_ok) {
+#pragma unroll
+                    for (int e8 = 0; e8 < 4; ++e8) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e2 = 0; e2 < 4; ++e2) {
+                            float v2[2];
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int e = 8 * e8 + 2 * e2 + h;
+                                const int d = 32 * c + e;
+                                float v = lt > 0.f ? bf16_round(__fdiv_rn(__uint_as_float(u[e]), lt)) : 0.f;
+                                if (p.gate) {
+                                    const float gt = bf2f(p.gate[ob + d]);
+                                    const float sg = bf16_round(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt))));
+                                    v = __fmul_rn(v, sg);
+                                }
+                                v2[h] = v;
+                            }
+                            w[e2] = pack_bf16(v2[0], v2[1]);
+                        }
+                        *reinterpret_cast<uint4 *>(p.out + ob + 32 * c + 8 * e8) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- teardown ----
+    pf_fence_before();
+    __syncthreads();
+    if (*abort_flag && threadIdx.x == 0) atomicExch(p.err, 1);
+    if (warp == 1) {
+        pf_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols) : "memory");
+    }
+}
+
+// Prefill-sized passes (at least 64 query rows per KV head, at least one CTA per SM) on
+// the tcgen05 kernel; ECPU_ERR_UNSUPPORTED (nothing launched) for other shapes: fewer rows
+// or CTAs, a query group that does not divide 128 rows, or q not 16-byte aligned.  PILM_ATTN_TC=0 leaves every pass to
+// the other kernels.
+int launch_attention_prefill_tc(const ekernel_paged_attn_desc_t *desc, const AttnParams &a, const char *what) {
+    static const bool off = getenv("PILM_ATTN_TC") && getenv("PILM_ATTN_TC")[0] == '0';
+    const int max_q = (int)(desc->max_q_len ? desc->max_q_len : 1);
+    if (off || a.gsz < 1 || a.gsz > 16 || (kPfRows % a.gsz) != 0 || max_q * a.gsz < 64 ||
+        (((uintptr_t)a.q) & 15) != 0)
+        return ECPU_ERR_UNSUPPORTED;
+    // a CTA streams its whole key range (no split over keys), so fewer CTAs than SMs leave
+    // SMs idle: such passes (a few long sequences with short chunks) stay on the per-head
+    // kernel, which splits the keys
+    const int tiles = (max_q + kPfRows / a.gsz - 1) / (kPfRows / a.gsz);
+    if ((long long)desc->num_seqs * tiles * a.nkv < num_sms()) return ECPU_ERR_UNSUPPORTED;
+    TensorMapEncodeTiledFn enc = tensor_map_encoder();
+    PILM_REQUIRE(enc, ECPU_ERR_UNSUPPORTED, "%s: cuTensorMapEncodeTiled is unavailable", what);
+    PfParams p;
+    p.block_table = a.block_table;
+    p.cu_q = a.cu_q;
+    p.ctx = a.ctx;
+    p.gate = a.gate;
+    p.out = a.out;
+    p.err = device_error_word();
+    PILM_REQUIRE(p.err, ECPU_ERR_MEM, "%s: error word allocation failed", what);
+    p.nh = a.nh;
+    p.gsz = a.gsz;
+    p.ppt = kPfRows / a.gsz;
+    p.tiles = (max_q + p.ppt - 1) / p.ppt;
+    p.max_blocks = a.max_blocks;
+    p.num_blocks = a.num_blocks;
+    p.scale = a.scale;
+    CUtensorMap qmap;
+    {
+        // q [total_q, nh, 128] as (dim, head, row): a box of 64 dims x gsz heads x ppt rows
+        // lands as [row][head][64 dims], the Q tile's row r = position * gsz + head
+        cuuint64_t dims[3] = {(cuuint64_t)kHD, (cuuint64_t)a.nh, (cuuint64_t)a.total_q};
+        cuuint64_t strides[2] = {(cuuint64_t)kHD * 2, (cuuint64_t)a.nh * kHD * 2};
+        cuuint32_t box[3] = {64, (cuuint32_t)a.gsz, (cuuint32_t)p.ppt};
+        cuuint32_t es[3] = {1, 1, 1};
+        const CUresult r = enc(&qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void *)a.q, dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        PILM_REQUIRE(r == CUDA_SUCCESS, ECPU_ERR_PARAM, "%s: the query tensor map was rejected (error %d)", what, (int)r);
+    }
+    CUtensorMap maps[2];
+    int rc = encode_kv_maps(a.kc, a.vc, a.nkv, a.num_blocks, maps, what);
+    if (rc != ECPU_OK) return rc;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(attn_prefill_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmemTotal);
+        attr = true;
+    }
+    launch_pdl(attn_prefill_tc, dim3((unsigned)(desc->num_seqs * p.tiles), (unsigned)a.nkv), dim3(kPfThreads),
+               kPfSmemTotal, qmap, maps[0], maps[1], p);
+    rc = check_launch(what);
+    if (rc != ECPU_OK) return rc;
+    return check_error_word(what, "a prefill attention wait did not complete");
+}
+
 // The whole-page persistent kernel and its merge; ECPU_ERR_UNSUPPORTED (nothing launched)
 // for shapes it does not take: more than 8 KV heads, more than 1024 sequences, or more
 // than 16 query rows per KV head (q_len x n_heads / n_kv; more would spill registers).
@@ -1319,7 +1845,10 @@ int ekernel_paged_attention_verify(const ekernel_paged_attn_desc_t *desc, const 
     // narrowed to fp32 (the bf16 kernel's opmath type)
     p.scale = (float)(1.0 / sqrt((double)kHD));
 
-    // whole pages per CTA where the shape allows it, else the per-head split kernel
+    // prefill-sized passes on tensor cores; whole pages per CTA where the shape allows it;
+    // else the per-head split kernel
+    rc = launch_attention_prefill_tc(desc, p, what);
+    if (rc != ECPU_ERR_UNSUPPORTED) return rc;
     rc = launch_attention_pages(desc, p, what);
     if (rc != ECPU_ERR_UNSUPPORTED) return rc;
 
