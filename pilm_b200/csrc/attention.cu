@@ -1165,6 +1165,12 @@ struct PfParams {
 };
 
 __device__ __forceinline__ uint32_t pf_s32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// two floats rounded to bf16 (nearest even) by one conversion, returned as floats
+__device__ __forceinline__ float2 bf16x2_round(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return __bfloat1622float2(h);
+}
+
 __device__ __forceinline__ void pf_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void pf_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void pf_commit(uint64_t *bar) {
@@ -1467,11 +1473,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_co
             const bool masked = (j + 1) * kPfKeys - 1 > qp_min || (j + 1) * kPfKeys > ctx;
             float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                float v = bf16_round(__fmul_rn(bf16_round(s[c]), p.scale));
-                if (masked && (k0 + c > qp || k0 + c >= ctx)) v = -INFINITY;
-                s[c] = v;
-                mx4[c & 3] = fmaxf(mx4[c & 3], v);
+            for (int c = 0; c < 64; c += 2) {
+                // two scores per bf16x2 conversion (each rounded to nearest even, as alone)
+                float2 v = bf16x2_round(s[c], s[c + 1]);
+                v = bf16x2_round(__fmul_rn(v.x, p.scale), __fmul_rn(v.y, p.scale));
+                if (masked) {
+                    if (k0 + c > qp || k0 + c >= ctx) v.x = -INFINITY;
+                    if (k0 + c + 1 > qp || k0 + c + 1 >= ctx) v.y = -INFINITY;
+                }
+                s[c] = v.x;
+                s[c + 1] = v.y;
+                mx4[c & 3] = fmaxf(mx4[c & 3], v.x);
+                mx4[(c + 1) & 3] = fmaxf(mx4[(c + 1) & 3], v.y);
             }
             const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             s_pmax[st][half][r] = mx;
@@ -1501,13 +1514,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_co
             }
             float ls4[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t u[32];
+            if (masked) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const float a0 = s[2 * e], a1 = s[2 * e + 1];
-                const float p0v = (a0 == -INFINITY) ? 0.f : __expf(a0 - mnew);
-                const float p1v = (a1 == -INFINITY) ? 0.f : __expf(a1 - mnew);
-                ls4[e & 3] += p0v + p1v;
-                u[e] = pack_bf16(p0v, p1v);
+                for (int e = 0; e < 32; ++e) {
+                    const float a0 = s[2 * e], a1 = s[2 * e + 1];
+                    const float p0v = (a0 == -INFINITY) ? 0.f : __expf(a0 - mnew);
+                    const float p1v = (a1 == -INFINITY) ? 0.f : __expf(a1 - mnew);
+                    ls4[e & 3] += p0v + p1v;
+                    u[e] = pack_bf16(p0v, p1v);
+                }
+            } else {  // every score finite: no -inf tests
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const float p0v = __expf(s[2 * e] - mnew), p1v = __expf(s[2 * e + 1] - mnew);
+                    ls4[e & 3] += p0v + p1v;
+                    u[e] = pack_bf16(p0v, p1v);
+                }
             }
             pf_st32(tmem + lane_addr + (uint32_t)(384 + st * 64 + 32 * half), u);
             l = l * alpha + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
