@@ -1446,6 +1446,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_co
         const int qp = p0 + pos0 + pos;                  // this row's position (its last key)
         const int qp_min = p0 + pos0;                    // the tile's first position
         const bool row_ok = pos0 + pos < q_len;
+        // a quadrant whose 32 rows are all past the sequence's queries (short passes: 20 rows
+        // of a 128-row tile at q_len 5 with 4 query heads per KV head) skips the softmax; it
+        // still takes each block's s_full before its arrivals, so the barriers keep phase
+        const bool skip = __all_sync(0xffffffffu, !row_ok);
         float m = -INFINITY, l = 0.f;
         bool failed = false;
         for (int j = 0; j < nb; ++j) {
@@ -1453,6 +1457,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_co
             if (!pf_wait(&bar->s_full[st], (uint32_t)(j >> 1) & 1u, abort_flag)) {
                 failed = true;
                 break;
+            }
+            if (skip) {
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&bar->s_free[st]);
+                    mbar_arrive(&bar->p_full[st]);
+                }
+                continue;
             }
             pf_fence_after();
             float s[64];
@@ -1541,8 +1553,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_co
         }
         // the row sum over both halves of every block
         s_psum[half][r] = l;
-        mbar_arrive(&bar->pair_sum[q4]);
-        if (!failed && pf_wait(&bar->pair_sum[q4], 0u, abort_flag) &&
+        if (!skip) mbar_arrive(&bar->pair_sum[q4]);
+        if (!failed && !skip && pf_wait(&bar->pair_sum[q4], 0u, abort_flag) &&
             pf_wait(&bar->pv_done[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag)) {
             const float lt = l + s_psum[half ^ 1][r];
             pf_fence_after();
@@ -1598,6 +1610,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc(const __grid_co
 int launch_attention_prefill_tc(const ekernel_paged_attn_desc_t *desc, const AttnParams &a, const char *what) {
     static const bool off = getenv("PILM_ATTN_TC") && getenv("PILM_ATTN_TC")[0] == '0';
     const int max_q = (int)(desc->max_q_len ? desc->max_q_len : 1);
+    // at least 64 rows per KV head: below that the softmax chain per 128-key block (which
+    // does not shrink with fewer valid rows) makes it no faster than the per-head kernel
     if (off || a.gsz < 1 || a.gsz > 16 || (kPfRows % a.gsz) != 0 || max_q * a.gsz < 64 ||
         (((uintptr_t)a.q) & 15) != 0)
         return ECPU_ERR_UNSUPPORTED;

@@ -50,9 +50,9 @@ def test_attention_qwen3_8b_heads_32k():
 
 
 def test_attention_qwen3_8b_heads_8k_q5():
-    """Eight sequences of 7K-9K keys at k = 4 (five verify rows each, twenty rows per KV
+    """Twenty sequences of 7K-9K keys at k = 4 (five verify rows each, twenty rows per KV
     head, more than the whole-page kernel's one 16-row tile)."""
-    run_case(32, 8, ctxs=_ragged_contexts(8, 440, 570, 5, seed=23), qlens=[5] * 8, seed=23, poison=True)
+    run_case(32, 8, ctxs=_ragged_contexts(20, 440, 570, 5, seed=23), qlens=[5] * 20, seed=23, poison=True)
 
 
 def _cut_tiles(N, K, sms):
