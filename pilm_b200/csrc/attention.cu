@@ -53,13 +53,6 @@ struct QkvSrc {
     const float *part;
     int splits;
     size_t plane;
-    __device__ __forceinline__ float at(size_t idx) const {
-        return part ? bf16_round(sum_splits(part + idx, splits, plane)) : bf2f(qkv[idx]);
-    }
-    // the element as bf16: copied as it is from the projection, or the rounded sum
-    __device__ __forceinline__ __nv_bfloat16 bf(size_t idx) const {
-        return part ? f2bf(sum_splits(part + idx, splits, plane)) : qkv[idx];
-    }
 };
 
 __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, int qkv_stride,
@@ -103,18 +96,54 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
         cv[j] = rot ? cos_t[(size_t)pos * nf + f] : 1.f;
         sv[j] = rot ? sin_t[(size_t)pos * nf + f] : 0.f;
     }
+    // The values only copied through, loaded with the head's own: a K head's V values (to
+    // the cache), a gated Q head's gate values (to gate_out).
+    const bool has_aux = !is_q || (gated && gate_out);
+    const size_t asrc = is_q ? src + kHD : (size_t)row * qkv_stride + qsec + (size_t)nkv * kHD + (size_t)(h - nh) * kHD;
     pdl_wait();
     float x[4];
-    float ss = 0.f;
-    // a K head's V values, loaded with its K values (they are only copied to the cache)
-    const size_t vsrc = (size_t)row * qkv_stride + qsec + (size_t)nkv * kHD + (size_t)(h - nh) * kHD;
     __nv_bfloat16 vv[4];
+    if (src_in.part) {
+        // every split of the lane's 4 values (and 4 aux values) is loaded before the adds,
+        // which run per element in split order from 0 as the combine pass adds: one wait
+        // on memory for up to 4 splits, not one per element
+        float xs[4] = {0.f, 0.f, 0.f, 0.f}, as[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s0 = 0; s0 < src_in.splits; s0 += 4) {
+            float tx[4][4], ta[4][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        x[j] = src_in.at(src + lane + 32 * j);
-        if (!is_q) vv[j] = src_in.bf(vsrc + lane + 32 * j);
-        ss = fmaf(x[j], x[j], ss);
+            for (int u = 0; u < 4; ++u) {
+                const bool ok = s0 + u < src_in.splits;
+                const float *pl = src_in.part + (size_t)(s0 + u) * src_in.plane;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    tx[u][j] = ok ? __ldcs(pl + src + lane + 32 * j) : 0.f;
+                    ta[u][j] = ok && has_aux ? __ldcs(pl + asrc + lane + 32 * j) : 0.f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (s0 + u < src_in.splits)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        xs[j] += tx[u][j];
+                        as[j] += ta[u][j];
+                    }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[j] = bf16_round(xs[j]);
+            vv[j] = f2bf(as[j]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[j] = bf2f(src_in.qkv[src + lane + 32 * j]);
+            vv[j] = has_aux ? src_in.qkv[asrc + lane + 32 * j] : __float2bfloat16_rn(0.f);
+        }
     }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = fmaf(x[j], x[j], ss);
     ss = warp_sum(ss);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)kHD), eps)));
 #pragma unroll
@@ -146,10 +175,10 @@ __global__ void qk_prologue(const QkvSrc src_in, int total_q, int nh, int nkv, i
         __nv_bfloat16 *qo = q_out + ((size_t)row * nh + h) * kHD;
 #pragma unroll
         for (int j = 0; j < 4; ++j) qo[lane + 32 * j] = f2bf(y[j]);
-        if (gated && gate_out) {
+        if (has_aux) {
             __nv_bfloat16 *go = gate_out + (size_t)row * nh * kHD + (size_t)h * kHD;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) go[lane + 32 * j] = src_in.bf(src + kHD + lane + 32 * j);
+            for (int j = 0; j < 4; ++j) go[lane + 32 * j] = vv[j];
         }
     } else {
         if (slot < 0 || slot >= num_slots) return;  // rejected / padded rows are not written

@@ -112,21 +112,6 @@ __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// Sum of p[sp * plane] over sp = 0 .. splits - 1, added in split order starting from 0 (as
-// the split-K combine pass adds), with the loads of up to 8 splits issued before the adds
-// so that they wait on memory once, not once per split.
-__device__ __forceinline__ float sum_splits(const float *p, int splits, size_t plane) {
-    float v = 0.f;
-    for (int s0 = 0; s0 < splits; s0 += 8) {
-        float t[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) t[u] = s0 + u < splits ? __ldcs(p + (size_t)(s0 + u) * plane) : 0.f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (s0 + u < splits) v += t[u];
-    }
-    return v;
-}
 __device__ __forceinline__ float bits2f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 
 // Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16).

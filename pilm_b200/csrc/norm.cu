@@ -87,12 +87,26 @@ __global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__r
                                                               int add_one, __nv_bfloat16 *__restrict__ out,
                                                               const float *__restrict__ part, int splits,
                                                               size_t plane) {
-    pdl_entry();
+    pdl_trigger();
     __shared__ float red[8];
     const int row = blockIdx.x;
     __nv_bfloat16 *r = res + (size_t)row * n;
     const __nv_bfloat16 *d = delta ? delta + (size_t)row * n : nullptr;
     const float *pr = part ? part + (size_t)row * n : nullptr;
+    // The norm weights are constant: read before the wait for the previous kernel.  The
+    // residual is read with the partial sums, so that the row waits on memory once.
+    uint4 wv[VPT], rv[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = (v * 256 + threadIdx.x) * 8;
+        if (i < n) wv[v] = *reinterpret_cast<const uint4 *>(w + i);
+    }
+    pdl_wait();
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = (v * 256 + threadIdx.x) * 8;
+        if (i < n) rv[v] = *reinterpret_cast<const uint4 *>(r + i);
+    }
     // partial sums: every element's splits added in split order, the loads of a batch of
     // splits for all of this thread's elements issued before the adds (16 in flight)
     float ps[VPT][8];
@@ -135,8 +149,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__r
     for (int v = 0; v < VPT; ++v) {
         const int i = (v * 256 + threadIdx.x) * 8;
         if (i < n) {
-            uint4 rv = *reinterpret_cast<const uint4 *>(r + i);
-            const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
+            const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv[v]);
             if (d || pr) {
                 float dl[8];
                 if (pr) {
@@ -176,8 +189,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_row_kernel(__nv_bfloat16 *__r
     for (int v = 0; v < VPT; ++v) {
         const int i = (v * 256 + threadIdx.x) * 8;
         if (i < n) {
-            uint4 wv = *reinterpret_cast<const uint4 *>(w + i);
-            const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv);
+            const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv[v]);
             uint4 ov;
             __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&ov);
 #pragma unroll

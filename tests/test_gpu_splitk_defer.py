@@ -84,9 +84,11 @@ def test_add_rmsnorm_from_partials_is_bit_identical(K, N):
         assert torch.equal(ra, rb) and torch.equal(ha, hb)
 
 
-@pytest.mark.parametrize("nh,nkv,gated,M", [(32, 8, False, 96), (8, 2, True, 48)])
-def test_qk_prologue_from_partials_is_bit_identical(nh, nkv, gated, M):
-    hd, K = 128, (4096 if nh == 32 else 1024)
+# (8, 2, True, 40, 4096) runs 7 splits: the prologue adds them in two batches of loads
+@pytest.mark.parametrize("nh,nkv,gated,M,K", [(32, 8, False, 96, 4096), (8, 2, True, 48, 1024),
+                                              (8, 2, True, 40, 4096)])
+def test_qk_prologue_from_partials_is_bit_identical(nh, nkv, gated, M, K):
+    hd = 128
     N = nh * hd * (2 if gated else 1) + 2 * nkv * hd
     lin, x = _w4(N, K, N), _x(M, K, 5)
     shape = Qwen3Shape(hidden=K, layers=1, n_heads=nh, n_kv_heads=nkv, head_dim=hd, intermediate=256, vocab=256,
