@@ -90,6 +90,7 @@ static_assert(kAccColBase + kTBufs * kMaxNm <= kTmemCols, "TMEM budget");
 
 struct __align__(8) Barriers {
     uint64_t in_full[kSlots];
+    uint64_t x_pre[kXStages];  // activations of the first kXStages groups (loaded after the wait)
     uint64_t op_full[kSlots], mma_done[kSlots];
     uint64_t s_full[2], s_empty[2];
     uint64_t drain;
@@ -364,9 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         int t = W0 / G, g = W0 % G;
         int row0 = (t % p.tiles_n) * kTileRows;
         for (int i = 0; i < ng && i < kRawStages; ++i) {
-            asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(&wmap), "r"(g * 64),
-                         "r"(row0)
-                         : "memory");
+            if (i >= kXStages)  // the first kXStages groups are copied to shared memory directly
+                asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(&wmap),
+                             "r"(g * 64), "r"(row0)
+                             : "memory");
             if (++g == G) {
                 g = 0;
                 row0 = row0 + kTileRows >= p.tiles_n * kTileRows ? 0 : row0 + kTileRows;
@@ -380,6 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             mbar_init(&bar->op_full[i], kDqWarps + kFoldWarps);
             mbar_init(&bar->mma_done[i], 1);
         }
+        for (int i = 0; i < kXStages; ++i) mbar_init(&bar->x_pre[i], 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bar->s_full[i], 1);
             mbar_init(&bar->s_empty[i], kFoldWarps);
@@ -395,7 +398,13 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bar->tmem_base;
-    pdl_wait();
+    // No wait for the previous kernel here.  The first npre groups' weights (and their
+    // scale tile) are copied and dequantized into TMEM while it runs: the dequant and MMA
+    // warps touch only shared memory and TMEM.  The producer waits before it copies
+    // activations (that kernel's output), the fold warps before they write.
+    // (At most two scale tiles may be requested before the fold warps release one: with a
+    // single group per tile (G = 1) every group starts a scale tile, so only two go early.)
+    const int npre = min(ng, G >= 2 ? kXStages : 2);
 
     const int x_bytes = 2 * p.Nm * 128;
 
@@ -410,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             int issued = 0, s_issued = 0;
             int t = W0 / G, g = W0 % G - 1;
             int row0 = (t % p.tiles_n) * kTileRows, m0 = (t / p.tiles_n) * kMaxNm;
+            int pre_g[kXStages], pre_m0[kXStages];
             for (int i = 0; i < ng; ++i) {
                 if (++g == G) {  // next tile: next 128 weight rows, or the next activation tile
                     g = 0;
@@ -438,6 +448,25 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                                                 (uint32_t)((i - kXStages) / kSlots) & 1u, abort_flag, p.wait_limit))
                     break;
                 uint64_t *full = &bar->in_full[i % kSlots];
+                if (i < npre) {
+                    // weights only: in_full(i) completes without the activations, which
+                    // land on x_pre(i) once the previous kernel has completed
+                    mbar_expect_tx(full, (uint32_t)kRawBytes);
+                    tma_load_2d(smem + kSmemRaw + (size_t)i * kRawBytes, &wmap, full, g * 64, row0);
+                    pre_g[i] = g;
+                    pre_m0[i] = m0;
+                    ++issued;
+                    if (i == npre - 1) {
+                        pdl_wait();
+                        for (int j = 0; j < npre; ++j) {
+                            uint8_t *dst = smem + kSmemX + (size_t)j * kXBytes;
+                            mbar_expect_tx(&bar->x_pre[j], (uint32_t)x_bytes);
+                            tma_load_2d(dst, &xmap, &bar->x_pre[j], pre_g[j] * 128, pre_m0[j]);
+                            tma_load_2d(dst + (size_t)p.Nm * 128, &xmap, &bar->x_pre[j], pre_g[j] * 128 + 64, pre_m0[j]);
+                        }
+                    }
+                    continue;
+                }
                 mbar_expect_tx(full, (uint32_t)(kRawBytes + x_bytes));
                 tma_load_2d(smem + kSmemRaw + (size_t)(i % kRawStages) * kRawBytes, &wmap, full, g * 64, row0);
                 uint8_t *dst = smem + kSmemX + (size_t)(i % kXStages) * kXBytes;
@@ -450,6 +479,8 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
                 mbar_drain(&bar->in_full[i % kSlots], (uint32_t)(i / kSlots) & 1u);
             for (int c = s_issued > 2 ? s_issued - 2 : 0; c < s_issued; ++c)
                 mbar_drain(&bar->s_full[c & 1], (uint32_t)(c >> 1) & 1u);
+            if (issued >= npre)  // the activation copies of the first groups were issued
+                for (int j = 0; j < npre; ++j) mbar_drain(&bar->x_pre[j], 0);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -458,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
             for (int i = 0; i < ng; ++i) {
                 const int q = i % kSlots, sa = i % kAStages, sx = i % kXStages, b = i % kTBufs;
                 if (!mbar_wait(&bar->op_full[q], (uint32_t)(i / kSlots) & 1u, abort_flag, p.wait_limit)) break;
+                if (i < npre && !mbar_wait(&bar->x_pre[i], 0, abort_flag, p.wait_limit)) break;
                 tc_fence_after();
                 const uint32_t a_col = tmem + (uint32_t)(kAColBase + sa * 64);
                 const uint32_t x_base = smem_u32(smem + kSmemX + (size_t)sx * kXBytes);
@@ -533,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4_gemm_tc(const __grid_constant_
         __syncwarp();
         if (lane == 0)
             for (int i = 0; i < kTBufs && i < ng; ++i) mbar_arrive(&bar->op_full[i]);
+        pdl_wait();  // before the first write (outputs, pieces, counters)
         int s_seen = 0;   // scale tiles started so far (the producer's sequence)
         int t = W0 / G, g = W0 % G;
         int row = (t % p.tiles_n) * kTileRows + rloc;
