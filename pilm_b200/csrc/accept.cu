@@ -339,15 +339,24 @@ __device__ __forceinline__ int rs_bin(float l, float mx, float inv_t) {
     return u < kRsSpan ? min(kRsBins - 1, (int)(u * (kRsBins / kRsSpan))) : kRsBins - 1;
 }
 
+// Level 0 adds each token's mass to one of kRsSub copies of the histogram (warp w to copy
+// w % kRsSub): lanes of a warp still collide on bins near the mode, but warps no longer
+// collide with most other warps.  Integer sums, so the copies' sum is the same whatever
+// the split.  After the copies are summed, sub[0] is the histogram (hist) and sub[1] its
+// suffix sums (sfx); sub[2] and sub[3] hold the gather of the cut's bin.
+constexpr int kRsSub = 4;
+static_assert(kRsGather <= kRsBins, "the gather fits in one histogram copy");
+
 struct RsSmem {
-    unsigned long long hist[kRsBins];  // level-0 masses; later the fallback's histograms
-    unsigned long long sfx[kRsBins];
-    uint32_t gkey[kRsGather];
-    unsigned long long gmass[kRsGather];
+    unsigned long long sub[kRsSub][kRsBins];
     unsigned long long wsum[32];
     float shf[32];
     int s_bin, s_n;
     uint32_t s_cut;
+    __device__ unsigned long long *hist() { return sub[0]; }  // level-0 masses; later the fallback's histograms
+    __device__ unsigned long long *sfx() { return sub[1]; }
+    __device__ unsigned long long *gmass() { return sub[2]; }
+    __device__ uint32_t *gkey() { return reinterpret_cast<uint32_t *>(sub[3]); }
 };
 
 // Fallback for a cut bin with more than kRsGather tokens: radix select over the 32-bit keys
@@ -363,26 +372,26 @@ __device__ void rs_radix_cut(const T *x, int V, float mx, float inv_t, double ta
     for (int lv = 0; lv < 3; ++lv) {
         const int bits = kBits[lv];
         const int shift = 32 - consumed - bits;
-        for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) sm.hist[d] = 0;
+        for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) sm.hist()[d] = 0;
         __syncthreads();
         row_for_each(x, V, [&](int, float l) {
             const uint32_t k = fkey(l);
             if (consumed == 0 || (k >> (32 - consumed)) == prefix)
-                atomicAdd(&sm.hist[(k >> shift) & ((1u << bits) - 1)], rs_mass(l, mx, inv_t));
+                atomicAdd(&sm.hist()[(k >> shift) & ((1u << bits) - 1)], rs_mass(l, mx, inv_t));
         });
         __syncthreads();
-        suffix_sums(sm.hist, sm.sfx, sm.wsum);
+        suffix_sums(sm.hist(), sm.sfx(), sm.wsum);
         if (threadIdx.x == 0) sm.s_bin = kRsBins;
         __syncthreads();
         for (int d = threadIdx.x; d < (1 << bits); d += blockDim.x) {
-            const unsigned long long higher = above + sm.sfx[d] - sm.hist[d];
-            if (sm.hist[d] && (double)higher < target) atomicMin(&sm.s_bin, d);
+            const unsigned long long higher = above + sm.sfx()[d] - sm.hist()[d];
+            if (sm.hist()[d] && (double)higher < target) atomicMin(&sm.s_bin, d);
         }
         __syncthreads();
         int dg = sm.s_bin;
         if (dg == kRsBins) dg = 0;
-        above += sm.sfx[dg] - sm.hist[dg];
-        at_cut = sm.hist[dg];
+        above += sm.sfx()[dg] - sm.hist()[dg];
+        at_cut = sm.hist()[dg];
         prefix = (prefix << bits) | (uint32_t)dg;
         consumed += bits;
         __syncthreads();
@@ -411,23 +420,31 @@ __global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__
     // holding only such tokens is followed by such bins only, so "the last bin of nonzero
     // mass whose higher bins hold less than the target" is the bin of the cut.  The
     // catch-all bin (u >= kRsSpan) holds masses below 2^-57, zero in fixed point.
-    for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) sm.hist[d] = 0;
+    for (int d = threadIdx.x; d < kRsSub * kRsBins; d += blockDim.x) (&sm.sub[0][0])[d] = 0;
     __syncthreads();
+    unsigned long long *mine = sm.sub[(threadIdx.x >> 5) % kRsSub];
     row_for_each(x, V, [&](int, float l) {
         const int bn = rs_bin(l, mx, inv_t);
         if (bn == kRsBins - 1) return;
         const unsigned long long m = rs_mass(l, mx, inv_t);
-        if (m) atomicAdd(&sm.hist[bn], m);
+        if (m) atomicAdd(&mine[bn], m);
     });
     __syncthreads();
-    suffix_sums(sm.hist, sm.sfx, sm.wsum);
-    const unsigned long long total = sm.sfx[0];
+    for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) {
+        unsigned long long v = sm.sub[0][d];
+#pragma unroll
+        for (int c = 1; c < kRsSub; ++c) v += sm.sub[c][d];
+        sm.sub[0][d] = v;
+    }
+    __syncthreads();
+    suffix_sums(sm.hist(), sm.sfx(), sm.wsum);
+    const unsigned long long total = sm.sfx()[0];
     const double target = (double)top_p * (double)total;  // the nucleus keeps above-mass < top_p Z
     if (threadIdx.x == 0) sm.s_bin = -1;
     __syncthreads();
     for (int d = threadIdx.x; d < kRsBins; d += blockDim.x) {
-        const unsigned long long higher = total - sm.sfx[d];  // mass of bins before d
-        if (sm.hist[d] && (double)higher < target) atomicMax(&sm.s_bin, d);
+        const unsigned long long higher = total - sm.sfx()[d];  // mass of bins before d
+        if (sm.hist()[d] && (double)higher < target) atomicMax(&sm.s_bin, d);
     }
     if (threadIdx.x == 0) {
         sm.s_n = 0;
@@ -435,7 +452,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__
     }
     __syncthreads();
     const int bstar = sm.s_bin;
-    const unsigned long long base = total - sm.sfx[bstar];  // mass strictly above the cut's bin
+    const unsigned long long base = total - sm.sfx()[bstar];  // mass strictly above the cut's bin
     uint32_t cut;
     unsigned long long zn;
     // gather the bin's tokens (slots past kRsGather are counted, not stored); a token's
@@ -445,8 +462,8 @@ __global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__
         if (rs_bin(l, mx, inv_t) == bstar) {
             const int slot = atomicAdd(&sm.s_n, 1);
             if (slot < kRsGather) {
-                sm.gkey[slot] = fkey(l);
-                sm.gmass[slot] = rs_mass(l, mx, inv_t);
+                sm.gkey()[slot] = fkey(l);
+                sm.gmass()[slot] = rs_mass(l, mx, inv_t);
             }
         }
     });
@@ -454,17 +471,17 @@ __global__ void __launch_bounds__(kRsThreads) rs_row_stats(const T *__restrict__
     if (sm.s_n <= kRsGather) {
         const int n = sm.s_n;
         for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const uint32_t ki = sm.gkey[i];
+            const uint32_t ki = sm.gkey()[i];
             unsigned long long above = base;
             for (int j = 0; j < n; ++j)
-                if (sm.gkey[j] > ki) above += sm.gmass[j];
+                if (sm.gkey()[j] > ki) above += sm.gmass()[j];
             if ((double)above < target) atomicMin(&sm.s_cut, ki);
         }
         __syncthreads();
         cut = sm.s_cut;
         unsigned long long in_bin = 0;
         for (int i = threadIdx.x; i < n; i += blockDim.x)
-            if (sm.gkey[i] >= cut) in_bin += sm.gmass[i];
+            if (sm.gkey()[i] >= cut) in_bin += sm.gmass()[i];
         zn = base + block_sum_u64(in_bin, sm.wsum);
     } else {
         rs_radix_cut(x, V, mx, inv_t, target, sm, cut, zn);
