@@ -48,10 +48,10 @@ __global__ void embedding_f32_kernel(const int32_t *__restrict__ ids, int rows, 
     for (int i = threadIdx.x; i < hidden; i += blockDim.x) out[(size_t)r * hidden + i] = table[(size_t)id * hidden + i];
 }
 
-// one CTA (256 threads) per row
-__global__ void __launch_bounds__(256) add_rmsnorm_f32_kernel(float *__restrict__ res, const float *__restrict__ delta,
-                                                              const float *__restrict__ w, int n, float eps,
-                                                              int add_one, float *__restrict__ out) {
+// one CTA (256 threads) per row, any n (the rows above 8192 values)
+__global__ void __launch_bounds__(256) add_rmsnorm_f32_loop(float *__restrict__ res, const float *__restrict__ delta,
+                                                            const float *__restrict__ w, int n, float eps,
+                                                            int add_one, float *__restrict__ out) {
     pdl_entry();
     __shared__ float red[8];
     const int row = blockIdx.x;
@@ -76,6 +76,59 @@ __global__ void __launch_bounds__(256) add_rmsnorm_f32_kernel(float *__restrict_
         float wf = w[i];
         if (add_one) wf = __fadd_rn(wf, 1.0f);
         out[(size_t)row * n + i] = __fmul_rn(wf, __fmul_rn(r[i], inv));
+    }
+}
+
+// The same with the row in registers (VPT values a thread, n <= 256 VPT): the norm
+// weights are read before the wait for the previous kernel, the residual and delta in one
+// batch after it.  Each thread's squares are added in index order, as the strided loop adds
+// them.
+template <int VPT>
+__global__ void __launch_bounds__(256) add_rmsnorm_f32_kernel(float *__restrict__ res, const float *__restrict__ delta,
+                                                              const float *__restrict__ w, int n, float eps,
+                                                              int add_one, float *__restrict__ out) {
+    pdl_trigger();
+    __shared__ float red[8];
+    const int row = blockIdx.x;
+    float *r = res + (size_t)row * n;
+    float wv[VPT], x[VPT], d[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = threadIdx.x + 256 * v;
+        wv[v] = i < n ? w[i] : 0.f;
+    }
+    pdl_wait();
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = threadIdx.x + 256 * v;
+        x[v] = i < n ? r[i] : 0.f;
+        d[v] = i < n && delta ? delta[(size_t)row * n + i] : 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = threadIdx.x + 256 * v;
+        if (i >= n) continue;
+        if (delta) {
+            x[v] = __fadd_rn(x[v], d[v]);
+            r[i] = x[v];
+        }
+        ss = fmaf(x[v], x[v], ss);
+    }
+    ss = warp_sum32(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red[k];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)n), eps)));
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+        const int i = threadIdx.x + 256 * v;
+        if (i >= n) continue;
+        float wf = wv[v];
+        if (add_one) wf = __fadd_rn(wf, 1.0f);
+        out[(size_t)row * n + i] = __fmul_rn(wf, __fmul_rn(x[v], inv));
     }
 }
 
@@ -172,10 +225,13 @@ __global__ void qk_prologue_f32_kernel(const float *__restrict__ qkv, int total_
 
 // One CTA per (query row, head); its kFA warps take every kFA-th chunk of 32 keys, each
 // with its own online softmax (m, l, o), and the CTA merges the warps' states at the end.
-// In a chunk, lane j scores key k0 + j (one 512-byte key row per lane), then the warp
-// accumulates P V over the chunk's keys with each lane holding 4 of the 128 dims.
+// In a chunk each lane holds 4 of the 128 dims: every key row is one coalesced 512-byte
+// load, a lane forms its 4-dim part of all 32 dot products, and a transposing butterfly
+// (31 shuffles) leaves key k0 + j's score in lane j.  The warp then accumulates P V over
+// the chunk's keys the same way, lane by dims.  The chunk's 32 key rows are loaded at
+// once, and its 32 value rows are in flight during the score reduction and the softmax.
 constexpr int kFA = 8;
-__global__ void __launch_bounds__(kFA * 32) attn_f32_kernel(const float *__restrict__ q, const float *__restrict__ kc,
+__global__ void __launch_bounds__(kFA * 32, 1) attn_f32_kernel(const float *__restrict__ q, const float *__restrict__ kc,
                                                             const float *__restrict__ vc,
                                                             const int32_t *__restrict__ block_table,
                                                             const int32_t *__restrict__ cu_q,
@@ -183,13 +239,15 @@ __global__ void __launch_bounds__(kFA * 32) attn_f32_kernel(const float *__restr
                                                             const float *__restrict__ gate, float *__restrict__ out,
                                                             int B, int total_q, int nh, int nkv, int max_blocks,
                                                             int num_blocks, float scale) {
-    pdl_entry();
-    __shared__ float qs[kHD];
+    pdl_trigger();
     __shared__ float sm[kFA], sl[kFA];
     __shared__ float4 so[kFA][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int item = blockIdx.x;
     if (item >= total_q * nh) return;
+    // The row's sequence, query length and context come from host-written metadata, so
+    // they are worked out before the wait for the previous kernel (which appends this
+    // step's K/V and writes the queries).
     const int row = item / nh, h = item % nh;
     int lo = 0, hi = B - 1;  // sequence of this row: largest b with cu_q[b] <= row
     while (lo < hi) {
@@ -202,32 +260,55 @@ __global__ void __launch_bounds__(kFA * 32) attn_f32_kernel(const float *__restr
     const int qpos = ctx - q_len + (row - cu_q[b]);
     const int kvh = h / (nh / nkv);
     const float *qrow = q + ((size_t)row * nh + h) * kHD;
-    if (threadIdx.x < kHD) qs[threadIdx.x] = qrow[threadIdx.x];
-    __syncthreads();
+    pdl_wait();
+    const float4 q4 = reinterpret_cast<const float4 *>(qrow)[lane];  // dims 4 lane .. 4 lane + 3
     const int32_t *bt = block_table + (size_t)b * max_blocks;
     const int last = min(qpos, ctx - 1);  // the last key this row sees
     float m = -INFINITY, l = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k0 = 32 * warp; k0 <= last; k0 += 32 * kFA) {
         const int key = k0 + lane;
-        float s = -INFINITY;
-        size_t off = 0;
+        const int n = min(32, last - k0 + 1);  // keys of this chunk the row sees
+        size_t off = 0;                        // element offset of key k0 + lane's row
         if (key <= last) {
             int blk = bt[key >> 4];
             if (blk < 0 || blk >= num_blocks) blk = 0;
             off = (((size_t)blk * 16 + (key & 15)) * nkv + kvh) * kHD;
-            const float4 *kr = reinterpret_cast<const float4 *>(kc + off);
-            float dot = 0.f;
-#pragma unroll 8
-            for (int d4 = 0; d4 < kHD / 4; ++d4) {
-                const float4 kv = kr[d4];
-                dot = fmaf(qs[4 * d4], kv.x, dot);
-                dot = fmaf(qs[4 * d4 + 1], kv.y, dot);
-                dot = fmaf(qs[4 * d4 + 2], kv.z, dot);
-                dot = fmaf(qs[4 * d4 + 3], kv.w, dot);
-            }
-            s = __fmul_rn(dot, scale);
         }
+        // The row loads are unconditional, so that all are in flight at once: a key past
+        // `last` reads row 0 of the cache (offset 0, always allocated); its score is
+        // replaced by -inf and its P V term skipped.
+        float4 kv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const size_t oj = (size_t)__shfl_sync(0xffffffffu, (unsigned long long)off, j);
+            kv[j] = reinterpret_cast<const float4 *>(kc + oj)[lane];
+        }
+        // p[j]: this lane's 4-dim part of key k0 + j's dot product
+        float p[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            p[j] = fmaf(q4.w, kv[j].w, fmaf(q4.z, kv[j].z, fmaf(q4.y, kv[j].y, __fmul_rn(q4.x, kv[j].x))));
+        float4 vv[32];
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) {
+            const size_t ok = (size_t)__shfl_sync(0xffffffffu, (unsigned long long)off, kk);
+            vv[kk] = reinterpret_cast<const float4 *>(vc + ok)[lane];
+        }
+        // butterfly: at offset sh a lane keeps the half of its sums whose key index has bit
+        // sh equal to its own lane bit and adds its partner's copy of that half; after five
+        // rounds p[0] is the full dot product of key k0 + lane
+#pragma unroll
+        for (int sh = 16; sh >= 1; sh >>= 1) {
+            const bool upper = (lane & sh) != 0;
+#pragma unroll
+            for (int j = 0; j < sh; ++j) {
+                const float keep = upper ? p[j + sh] : p[j];
+                const float send = upper ? p[j] : p[j + sh];
+                p[j] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
+            }
+        }
+        const float s = key <= last ? __fmul_rn(p[0], scale) : -INFINITY;
         const float mnew = fmaxf(m, warp_max32(s));
         const float alpha = (m == -INFINITY) ? 0.f : expf(m - mnew);
         const float pl = (s == -INFINITY) ? 0.f : expf(s - mnew);
@@ -237,16 +318,15 @@ __global__ void __launch_bounds__(kFA * 32) attn_f32_kernel(const float *__restr
         o.z *= alpha;
         o.w *= alpha;
         m = mnew;
-        const int n = min(32, last - k0 + 1);
-#pragma unroll 4
-        for (int kk = 0; kk < n; ++kk) {
+#pragma unroll
+        for (int kk = 0; kk < 32; ++kk) {  // in key order over the keys the row sees
             const float pk = __shfl_sync(0xffffffffu, pl, kk);
-            const size_t ok = (size_t)__shfl_sync(0xffffffffu, (unsigned long long)off, kk);
-            const float4 vv = reinterpret_cast<const float4 *>(vc + ok)[lane];
-            o.x = fmaf(pk, vv.x, o.x);
-            o.y = fmaf(pk, vv.y, o.y);
-            o.z = fmaf(pk, vv.z, o.z);
-            o.w = fmaf(pk, vv.w, o.w);
+            if (kk < n) {
+                o.x = fmaf(pk, vv[kk].x, o.x);
+                o.y = fmaf(pk, vv[kk].y, o.y);
+                o.z = fmaf(pk, vv[kk].z, o.z);
+                o.w = fmaf(pk, vv[kk].w, o.w);
+            }
         }
     }
     if (lane == 0) {
@@ -332,7 +412,17 @@ int ekernel_add_rmsnorm_f32(float *residual, const float *delta, const float *we
     PILM_REQUIRE(residual && weight && out, ECPU_ERR_PARAM, "%s: null argument", what);
     PILM_REQUIRE(n > 0 && n <= (1u << 24) && rows <= 0x7fffffff, ECPU_ERR_PARAM, "%s: sizes out of range", what);
     if (rows == 0) return ECPU_OK;
-    launch_pdl(add_rmsnorm_f32_kernel, dim3((unsigned)rows), dim3(256), 0, residual, delta, weight, (int)n, eps, add_one, out);
+    const dim3 grid((unsigned)rows), block(256);
+    if (n <= 1024)
+        launch_pdl(add_rmsnorm_f32_kernel<4>, grid, block, 0, residual, delta, weight, (int)n, eps, add_one, out);
+    else if (n <= 2048)
+        launch_pdl(add_rmsnorm_f32_kernel<8>, grid, block, 0, residual, delta, weight, (int)n, eps, add_one, out);
+    else if (n <= 4096)
+        launch_pdl(add_rmsnorm_f32_kernel<16>, grid, block, 0, residual, delta, weight, (int)n, eps, add_one, out);
+    else if (n <= 8192)
+        launch_pdl(add_rmsnorm_f32_kernel<32>, grid, block, 0, residual, delta, weight, (int)n, eps, add_one, out);
+    else
+        launch_pdl(add_rmsnorm_f32_loop, grid, block, 0, residual, delta, weight, (int)n, eps, add_one, out);
     return check_launch(what);
 }
 
