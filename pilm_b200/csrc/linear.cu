@@ -525,10 +525,10 @@ __device__ __forceinline__ float i8_to_f32(uint32_t w, int e) {
     return __uint_as_float(t) - 8388736.0f;
 }
 
-// Weights and scales are never written by another kernel: the row scales are read before
-// the wait for the previous kernel, and with PF (grids of one wave) each warp also
-// bulk-prefetches its rows into L2 first, so that the weight fetch overlaps that kernel.
-template <int MC, bool PF>
+// The row scales are never written by another kernel: they are read before the wait for
+// the previous kernel.  (An L2 prefetch of the warp's weight rows there as well made the
+// GEMV faster but its neighbours in the config 1 step slower by as much: not kept.)
+template <int MC>
 __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, int M, int K,
                                                   const int8_t *__restrict__ W, const float *__restrict__ S, int N,
                                                   float *__restrict__ Y) {
@@ -546,7 +546,6 @@ __global__ void __launch_bounds__(256) w8a32_gemv(const float *__restrict__ X, i
         w[r] = W + (size_t)(rv[r] ? n0 + r : n0) * K;
         sc[r] = rv[r] ? __ldg(S + n0 + r) : 0.f;
     }
-    if (PF && vec && lane < kW8Rows && n0 + lane < N) prefetch_l2_bulk(W + (size_t)(n0 + lane) * K, (uint32_t)K);
     pdl_wait();
     for (int m0 = 0; m0 < M; m0 += MC) {
         const int mc = min(MC, M - m0);
@@ -739,20 +738,6 @@ __global__ void repack_w4_kpairs(const uint32_t *__restrict__ in, uint32_t *out,
 
 bool aligned16(const void *p) { return (((uintptr_t)p) & 15) == 0; }
 
-// The prefetching form when the grid is one wave (every CTA resident while the previous
-// kernel runs); later waves would only add L2 requests.
-template <int MC>
-void launch_w8a32(unsigned grid, const float *A, int M, int K, const int8_t *W, const float *S, int N, float *C) {
-    static int per_sm = 0;
-    if (per_sm == 0 &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w8a32_gemv<MC, true>, 256, 0) != cudaSuccess)
-        per_sm = 1;
-    if ((long long)grid <= (long long)per_sm * pilm::num_sms())
-        launch_pdl(w8a32_gemv<MC, true>, dim3(grid), dim3(256), 0, A, M, K, W, S, N, C);
-    else
-        launch_pdl(w8a32_gemv<MC, false>, dim3(grid), dim3(256), 0, A, M, K, W, S, N, C);
-}
-
 }  // namespace
 
 namespace pilm {
@@ -831,11 +816,11 @@ int ekernel_linear_w8a32(const ekernel_linear_w8a32_desc_t *desc, const float *A
     const unsigned grid = (unsigned)((desc->N + 8 * kW8Rows - 1) / (8 * kW8Rows));
     const int M = (int)desc->M, K = (int)desc->K, N = (int)desc->N;
     if (M == 1)
-        launch_w8a32<1>(grid, A, M, K, W, scales, N, C);
+        launch_pdl(w8a32_gemv<1>, dim3(grid), dim3(256), 0, A, M, K, W, scales, N, C);
     else if (M == 2)
-        launch_w8a32<2>(grid, A, M, K, W, scales, N, C);
+        launch_pdl(w8a32_gemv<2>, dim3(grid), dim3(256), 0, A, M, K, W, scales, N, C);
     else
-        launch_w8a32<4>(grid, A, M, K, W, scales, N, C);
+        launch_pdl(w8a32_gemv<4>, dim3(grid), dim3(256), 0, A, M, K, W, scales, N, C);
     return pilm::check_launch("ekernel_linear_w8a32");
 }
 
