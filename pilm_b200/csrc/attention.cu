@@ -1011,7 +1011,11 @@ __global__ void __launch_bounds__(kMergeHeads * 32) attn_merge_pages(const PageA
     const int cxb = p.ctx[b];
     const long long P1 = P0 + (cxb > 0 ? (cxb + 15) >> 4 : 0);
     if (head >= p.nh || j >= q1 - q0 || P1 <= P0 || T <= 0) return;
-    const int c0 = cta_of_page(P0, T, p.G), c1 = cta_of_page(P1 - 1, T, p.G);
+    // The range bounds c T / G are 64-bit divisions: lanes work them out in parallel and
+    // share them, instead of every lane repeating all of them (they dominated the kernel's
+    // instructions).  Lane 0 finds the first CTA, lane 1 the last.
+    const int cl = cta_of_page(lane == 0 ? P0 : P1 - 1, T, p.G);
+    const int c0 = __shfl_sync(0xffffffffu, cl, 0), c1 = __shfl_sync(0xffffffffu, cl, 1);
     if (c0 == c1) return;  // finished by its CTA
     const size_t ob = (size_t)(q0 + j) * p.nh * kHD + (size_t)head * kHD + 4 * lane;
     pdl_wait();
@@ -1021,6 +1025,12 @@ __global__ void __launch_bounds__(kMergeHeads * 32) attn_merge_pages(const PageA
     constexpr int U = 8;
     float M = -INFINITY, L = 0.f, O[4] = {0.f, 0.f, 0.f, 0.f};
     for (int cb = c0; cb <= c1; cb += U) {
+        // lane u < U: the page range [lo, hi) of CTA cb + u
+        long long lo_l = 0, hi_l = 0;
+        if (lane < U) {
+            lo_l = ((long long)(cb + lane) * T) / p.G;
+            hi_l = ((long long)(cb + lane + 1) * T) / p.G;
+        }
         float m[U], l[U];
         float4 o[U];
 #pragma unroll
@@ -1029,7 +1039,7 @@ __global__ void __launch_bounds__(kMergeHeads * 32) attn_merge_pages(const PageA
             l[u] = 0.f;
             o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             const int c = cb + u;
-            const long long lo = ((long long)c * T) / p.G, hi = ((long long)(c + 1) * T) / p.G;
+            const long long lo = __shfl_sync(0xffffffffu, lo_l, u), hi = __shfl_sync(0xffffffffu, hi_l, u);
             if (c <= c1 && lo < hi) {
                 const float *rec =
                     p.part + ((((size_t)c * 2 + (lo >= P0 ? 0 : 1)) * p.max_q + j) * p.nh + head) * kPRec;
